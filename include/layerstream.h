@@ -1,0 +1,156 @@
+/*
+ * layerstream_b200 — C ABI of the B200-native speculative-decode verify path.
+ *
+ * This is the boundary a host in the reference's language binds (a Rust `extern "C"` block, or
+ * ctypes). Every entry point takes plain pointers and sizes, returns 0 on success and a negative
+ * status on error (never aborts, never throws across the boundary), and leaves a message that
+ * ls_last_error() returns. Errors are values, as in the reference, where every fallible call
+ * returns Result<_, String>.
+ *
+ * Threading: one caller thread per LsModel at a time (the reference's Model is `&mut self`).
+ * Device memory is owned by the LsModel; host buffers passed in are copied and not retained.
+ *
+ * Reference interfaces replaced (paths inside themaker00001/layerstream):
+ *   LsModel                      <- model::Model (src/model.rs:16-26) + provider::Provider (src/provider.rs:39-55)
+ *   ls_model_open                <- weights::ModelFiles::open_quantized (src/weights.rs:391-423)
+ *                                   + provider::ResidentProvider::load (src/provider.rs:69-81)
+ *                                   / provider::StreamProvider::new (src/provider.rs:182-223)
+ *                                   + model::Model::new (src/model.rs:58-77)
+ *   ls_forward                   <- model::Model::forward (src/model.rs:111-119)
+ *   ls_forward_multi             <- model::Model::forward_multi (src/model.rs:124-133)
+ *   ls_verify                    <- the verify step of spec::speculative_greedy (src/spec.rs:110-139):
+ *                                   forward_multi + argmax + longest-prefix acceptance + truncate
+ *   ls_truncate / ls_pos / ls_reset <- model::Model::truncate / pos / reset (src/model.rs:84-103,137-140)
+ *   ls_speculative_greedy        <- spec::speculative_greedy (src/spec.rs:57-152)
+ *   ls_quantize_model            <- quant::quantize_model (src/quant.rs:158-251)
+ *   ls_model_report              <- provider::ProviderReport (src/provider.rs:29-37) + source::IoStats (src/source.rs:13-21)
+ */
+#ifndef LAYERSTREAM_B200_H
+#define LAYERSTREAM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef struct LsModel LsModel;
+
+/* Status codes. */
+#define LS_OK 0
+#define LS_ERR_ARG -1      /* bad request: the reference's Err(String) cases */
+#define LS_ERR_IO -2       /* file missing, damaged or of the wrong format */
+#define LS_ERR_CUDA -3     /* a CUDA call failed */
+#define LS_ERR_DEVICE -4   /* a kernel reported an error status (e.g. a bounded wait gave up) */
+
+/* Residency modes (src/provider.rs): every layer in HBM, or N HBM slots filled per pass from
+ * pinned host memory by cudaMemcpyAsync on a side stream. */
+#define LS_MODE_RESIDENT 0
+#define LS_MODE_STREAM 1
+
+typedef struct LsModelInfo {
+  uint64_t hidden, inter, layers, heads, kv_heads, head_dim, vocab, max_ctx;
+  int32_t bits, group, embed_bits, embed_group; /* bits 16 = bf16 */
+  float eps, rope_theta;
+  uint64_t layer_bytes;        /* bytes of one stored layer block */
+  uint64_t embed_row_bytes;    /* bytes of one stored embedding row */
+  uint64_t weight_bytes;       /* layers * layer_bytes + vocab * embed_row_bytes */
+} LsModelInfo;
+
+/* src/provider.rs:29-37, src/source.rs:13-21 */
+typedef struct LsReport {
+  uint64_t resident_weight_bytes; /* device bytes holding weights */
+  uint64_t bytes_read;            /* bytes moved host->device for weights since open */
+  uint64_t wait_ns;               /* host time blocked on streamed data */
+  uint64_t passes;                /* forward passes run */
+} LsReport;
+
+/* src/spec.rs:16-39 */
+typedef struct LsSpecStats {
+  uint64_t target_passes, drafted, accepted, draft_forwards;
+  double target_secs, draft_secs, first_secs, decode_secs;
+} LsSpecStats;
+
+/* Copies the last error message of this thread into buf (NUL-terminated); returns its length. */
+int ls_last_error(char *buf, size_t cap);
+
+/* Opens a quantized `.lsq` file (src/weights.rs:327-423 format) on CUDA device `device`.
+ * mode: LS_MODE_RESIDENT or LS_MODE_STREAM; slots: HBM layer slots when streaming (>= 1).
+ * max_ctx: KV-cache capacity in tokens, reserved up front (src/model.rs:67-68). */
+int ls_model_open(const char *lsq_path, int device, uint64_t max_ctx, int mode, int slots, LsModel **out);
+int ls_model_free(LsModel *m);
+int ls_model_info(const LsModel *m, LsModelInfo *out);
+int ls_model_report(const LsModel *m, LsReport *out);
+
+int ls_pos(const LsModel *m, uint64_t *pos);
+int ls_reset(LsModel *m);
+int ls_truncate(LsModel *m, uint64_t pos);
+
+/* Pushes n tokens (prefill, 128-token chunks) and returns the last position's logits (vocab
+ * floats, may be NULL) and its greedy token (first maximum; may be NULL). */
+int ls_forward(LsModel *m, const uint32_t *ids, uint64_t n, float *logits, uint32_t *argmax);
+
+/* One pass over t <= 128 tokens returning the logits at the last n positions (n * vocab floats). */
+int ls_forward_multi(LsModel *m, const uint32_t *ids, uint64_t t, uint64_t n, float *logits);
+
+/* The verify step. block = [a, d_1 .. d_k] (n = k + 1 <= 33 tokens). One pass over the weights,
+ * the greedy token at every position computed on the device, then m = the longest prefix with
+ * argmax(pos i) == d_{i+1}, next = argmax(pos m). The cache keeps exactly [a, d_1 .. d_m]
+ * (pos advances by m + 1). Only (m, next) cross back to the host. */
+int ls_verify(LsModel *m, const uint32_t *block, uint64_t n, uint32_t *accepted_m, uint32_t *next);
+
+/* spec::speculative_greedy: generates up to max_new tokens with `target`, `draft` guessing k at a
+ * time. Both models must be fresh and share a vocabulary. out_tokens holds max_new entries.
+ * draft may be NULL: then a prompt-lookup drafter (longest recent n-gram match in the token
+ * history, an addition to the reference) proposes the guesses. */
+int ls_speculative_greedy(LsModel *target, LsModel *draft, const uint32_t *prompt, uint64_t plen, uint64_t max_new,
+                          uint64_t k, const uint32_t *eos, uint64_t neos, uint32_t *out_tokens, uint64_t *out_len,
+                          LsSpecStats *stats);
+
+/* quant::quantize_model: reads a BF16 safetensors model directory (config.json +
+ * model.safetensors) and writes a new `.lsq` file (must not exist). The group quantization with
+ * its clip search runs on CUDA device `device`; bytes equal the reference's quantizer's. */
+int ls_quantize_model(const char *src_dir, const char *out_path, int bits, int group, int embed_bits, int embed_group,
+                      int clip_search, int device, double *rel_rmse);
+
+/* ---- kernel-level entry points (microbenchmarks and parity tests) ---------------------------- */
+
+/* y[t][r] = dot(stored row r, x[t]) for t < M, with W given as `rows` stored rows in the .lsq
+ * row format (packed ints then bf16 scales, src/weights.rs:26-31). Host buffers; the call
+ * uploads, repacks, runs the verify-path GEMV kernel and copies y back. Mirrors
+ * kernels::matmul (src/kernels.rs:196-203). iters > 1 repeats the kernel and returns the mean
+ * kernel time in *ms (may be NULL). */
+int ls_qgemv_host(int bits, int group, const uint8_t *rows_raw, uint64_t rows, uint64_t cols, const float *x, uint64_t M,
+                  float *y, int iters, double *ms);
+
+/* The same GEMV on device buffers prepared once by ls_qweights_upload (for timing loops). */
+typedef struct LsQWeights LsQWeights;
+int ls_qweights_upload(int device, int bits, int group, const uint8_t *rows_raw, uint64_t rows, uint64_t cols,
+                       LsQWeights **out);
+int ls_qweights_free(LsQWeights *w);
+/* x_dev: M x cols f32, y_dev: M x rows f32, both device pointers; stream: a cudaStream_t or NULL. */
+int ls_qgemv_device(const LsQWeights *w, const float *x_dev, uint64_t M, float *y_dev, void *stream);
+
+/* Embedding gather + dequantisation of n stored rows (ids index `rows` stored rows in the .lsq row
+ * format) into out (n x cols floats), through the same repack and gather kernels the model uses.
+ * Mirrors kernels::dequant_row (src/kernels.rs:95-121); the result is bit-exact. */
+int ls_dequant_rows_host(int bits, int group, const uint8_t *rows_raw, uint64_t rows, uint64_t cols, const uint32_t *ids,
+                         uint64_t n, float *out);
+
+/* Device bytes a kernel of this library reads per GEMV call (weights + scales + x + y). */
+uint64_t ls_qgemv_bytes(int bits, int group, uint64_t rows, uint64_t cols, uint64_t M);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LAYERSTREAM_B200_H */

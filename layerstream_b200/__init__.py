@@ -1,0 +1,236 @@
+"""layerstream_b200: the speculative-decode verify path of layerstream on NVIDIA B200 (sm_100a).
+
+Python binding (ctypes) of ``liblayerstream_b200.so``, whose C ABI is ``include/layerstream.h``.
+The names mirror the reference's Rust API (``model::Model``, ``spec::speculative_greedy``,
+``quant::quantize_model``): errors are raised as ``LayerstreamError`` carrying the library's message.
+There is no CPU fallback: without the built library (and a CUDA device) every call fails.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liblayerstream_b200.so")
+
+MODE_RESIDENT = 0
+MODE_STREAM = 1
+
+
+class LayerstreamError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+class ModelInfo(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("hidden", "inter", "layers", "heads", "kv_heads", "head_dim", "vocab", "max_ctx")] + [
+        (n, C.c_int32) for n in ("bits", "group", "embed_bits", "embed_group")
+    ] + [("eps", C.c_float), ("rope_theta", C.c_float), ("layer_bytes", C.c_uint64), ("embed_row_bytes", C.c_uint64),
+         ("weight_bytes", C.c_uint64)]
+
+
+class Report(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("resident_weight_bytes", "bytes_read", "wait_ns", "passes")]
+
+
+class SpecStats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("target_passes", "drafted", "accepted", "draft_forwards")] + [
+        (n, C.c_double) for n in ("target_secs", "draft_secs", "first_secs", "decode_secs")
+    ]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+_lib = None
+
+# C signatures of include/layerstream.h
+_SIGS = {
+    "ls_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
+    "ls_model_open": (C.c_int, [C.c_char_p, C.c_int, C.c_uint64, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "ls_model_free": (C.c_int, [C.c_void_p]),
+    "ls_model_info": (C.c_int, [C.c_void_p, C.POINTER(ModelInfo)]),
+    "ls_model_report": (C.c_int, [C.c_void_p, C.POINTER(Report)]),
+    "ls_pos": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64)]),
+    "ls_reset": (C.c_int, [C.c_void_p]),
+    "ls_truncate": (C.c_int, [C.c_void_p, C.c_uint64]),
+    "ls_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.POINTER(C.c_uint32)]),
+    "ls_forward_multi": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p]),
+    "ls_verify": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+    "ls_speculative_greedy": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_void_p,
+                                        C.c_uint64, C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(SpecStats)]),
+    "ls_quantize_model": (C.c_int, [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                    C.POINTER(C.c_double)]),
+    "ls_qgemv_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p,
+                                C.c_int, C.POINTER(C.c_double)]),
+    "ls_qweights_upload": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.POINTER(C.c_void_p)]),
+    "ls_qweights_free": (C.c_int, [C.c_void_p]),
+    "ls_qgemv_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p]),
+    "ls_qgemv_bytes": (C.c_uint64, [C.c_int, C.c_int, C.c_uint64, C.c_uint64, C.c_uint64]),
+    "ls_dequant_rows_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p]),
+}
+
+
+def lib():
+    """Loads the CUDA library (raises if it has not been built: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m layerstream_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(rc: int):
+    if rc != 0:
+        buf = C.create_string_buffer(4096)
+        lib().ls_last_error(buf, 4096)
+        raise LayerstreamError(rc, buf.value.decode(errors="replace"))
+
+
+def _u32(a):
+    return np.ascontiguousarray(a, dtype=np.uint32)
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class Model:
+    """``model::Model`` (src/model.rs) backed by CUDA: a `.lsq` model resident in HBM or streamed
+    through ``slots`` HBM layer slots from pinned host memory."""
+
+    def __init__(self, path: str, device: int = 0, max_ctx: int = 1024, mode: str = "resident", slots: int = 2):
+        h = C.c_void_p()
+        md = {"resident": MODE_RESIDENT, "stream": MODE_STREAM}[mode]
+        _check(lib().ls_model_open(str(path).encode(), device, max_ctx, md, slots, C.byref(h)))
+        self._h = h
+        info = ModelInfo()
+        _check(lib().ls_model_info(h, C.byref(info)))
+        self.info = info
+        self.vocab = info.vocab
+        self.max_ctx = max_ctx
+        self.mode = mode
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().ls_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def pos(self) -> int:
+        p = C.c_uint64()
+        _check(lib().ls_pos(self._h, C.byref(p)))
+        return p.value
+
+    def reset(self):
+        _check(lib().ls_reset(self._h))
+
+    def truncate(self, pos: int):
+        _check(lib().ls_truncate(self._h, pos))
+
+    def forward(self, tokens, want_logits: bool = True):
+        """Returns the last position's logits (and keeps the greedy token in ``self.last_argmax``)."""
+        t = _u32(tokens)
+        out = np.empty(self.vocab, np.float32) if want_logits else None
+        a = C.c_uint32()
+        _check(lib().ls_forward(self._h, _p(t), t.size, _p(out) if out is not None else None, C.byref(a)))
+        self.last_argmax = a.value
+        return out if want_logits else a.value
+
+    def forward_multi(self, tokens, n: int) -> np.ndarray:
+        t = _u32(tokens)
+        out = np.empty((max(n, 1), self.vocab), np.float32)
+        _check(lib().ls_forward_multi(self._h, _p(t), t.size, n, _p(out)))
+        return out
+
+    def verify(self, block):
+        """The verify step: returns (m, next) and keeps [a, d_1 .. d_m] in the cache."""
+        b = _u32(block)
+        m, nxt = C.c_uint32(), C.c_uint32()
+        _check(lib().ls_verify(self._h, _p(b), b.size, C.byref(m), C.byref(nxt)))
+        return m.value, nxt.value
+
+    def report(self) -> dict:
+        r = Report()
+        _check(lib().ls_model_report(self._h, C.byref(r)))
+        return {n: getattr(r, n) for n, _ in r._fields_}
+
+
+def speculative_greedy(target: Model, draft: Model | None, prompt, max_new: int, k: int, eos=()):
+    """``spec::speculative_greedy`` (src/spec.rs:57-152). ``draft=None`` uses the prompt-lookup drafter."""
+    p = _u32(prompt)
+    e = _u32(list(eos) if len(eos) else [0])
+    out = np.zeros(max(max_new, 1), np.uint32)
+    n = C.c_uint64()
+    st = SpecStats()
+    _check(lib().ls_speculative_greedy(target._h, draft._h if draft is not None else None, _p(p), p.size, max_new, k, _p(e),
+                                       len(eos), _p(out), C.byref(n), C.byref(st)))
+    return out[: n.value].tolist(), st.as_dict()
+
+
+def quantize_model(src_dir: str, out_path: str, body=(8, 64), embed=None, clip: bool = True, device: int = 0) -> float:
+    """``quant::quantize_model`` (src/quant.rs:158-251) with the group quantization on the GPU."""
+    eb, eg = embed if embed else body
+    r = C.c_double()
+    _check(lib().ls_quantize_model(str(src_dir).encode(), str(out_path).encode(), body[0], body[1], eb, eg, int(clip), device,
+                                   C.byref(r)))
+    return r.value
+
+
+def qgemv(bits: int, group: int, rows_raw: np.ndarray, rows: int, cols: int, x: np.ndarray, iters: int = 1):
+    """y = W x through the verify-path GEMV kernel; W in the stored row format. Returns (y, ms)."""
+    w = np.ascontiguousarray(rows_raw, np.uint8)
+    xx = np.ascontiguousarray(x, np.float32).reshape(-1, cols)
+    y = np.empty((xx.shape[0], rows), np.float32)
+    ms = C.c_double()
+    _check(lib().ls_qgemv_host(bits, group, _p(w), rows, cols, _p(xx), xx.shape[0], _p(y), iters, C.byref(ms)))
+    return y, ms.value
+
+
+def dequant_rows(bits: int, group: int, rows_raw: np.ndarray, rows: int, cols: int, ids) -> np.ndarray:
+    """Embedding gather + dequantisation of stored rows `ids` on the GPU (bit-exact)."""
+    w = np.ascontiguousarray(rows_raw, np.uint8)
+    i = _u32(ids)
+    out = np.empty((i.size, cols), np.float32)
+    _check(lib().ls_dequant_rows_host(bits, group, _p(w), rows, cols, _p(i), i.size, _p(out)))
+    return out
+
+
+class QWeights:
+    """A quantized matrix uploaded once (device planes) for timing the GEMV on device buffers."""
+
+    def __init__(self, bits: int, group: int, rows_raw: np.ndarray, rows: int, cols: int, device: int = 0):
+        h = C.c_void_p()
+        w = np.ascontiguousarray(rows_raw, np.uint8)
+        _check(lib().ls_qweights_upload(device, bits, group, _p(w), rows, cols, C.byref(h)))
+        self._h, self.rows, self.cols, self.bits, self.group = h, rows, cols, bits, group
+
+    def gemv(self, x_ptr: int, M: int, y_ptr: int, stream: int = 0):
+        _check(lib().ls_qgemv_device(self._h, C.c_void_p(x_ptr), M, C.c_void_p(y_ptr), C.c_void_p(stream)))
+
+    def bytes(self, M: int) -> int:
+        return lib().ls_qgemv_bytes(self.bits, self.group, self.rows, self.cols, M)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().ls_qweights_free(self._h)
+            self._h = None
+
+
+SYMBOLS = tuple(_SIGS)

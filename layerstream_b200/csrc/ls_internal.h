@@ -1,0 +1,206 @@
+// Internal declarations shared by the host code and the CUDA kernels of layerstream_b200.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace ls {
+
+// ---- errors ----------------------------------------------------------------------------------
+
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define LS_THROW(code, msg) throw ::ls::Error((code), (msg))
+#define LS_CUDA(expr)                                                                                   \
+  do {                                                                                                  \
+    cudaError_t _e = (expr);                                                                            \
+    if (_e != cudaSuccess)                                                                              \
+      throw ::ls::Error(-3, std::string(#expr) + ": " + cudaGetErrorString(_e) + " (" __FILE__ ":" +   \
+                                std::to_string(__LINE__) + ")");                                        \
+  } while (0)
+
+// ---- formats (src/weights.rs) ----------------------------------------------------------------
+
+struct WeightFormat {
+  int bits = 16;  // 16 = bf16; 8 or 4 = grouped symmetric integers with bf16 scales
+  int group = 0;
+  bool quant() const { return bits != 16; }
+  bool operator==(const WeightFormat& o) const { return bits == o.bits && group == o.group; }
+  // src/weights.rs:26-31
+  size_t row_bytes(size_t cols) const {
+    return quant() ? cols * (size_t)bits / 8 + cols / (size_t)group * 2 : cols * 2;
+  }
+};
+
+struct Config {
+  WeightFormat format, embed_format;
+  size_t hidden = 0, inter = 0, layers = 0, heads = 0, kv_heads = 0, head_dim = 0, vocab = 0, max_pos = 0;
+  float eps = 0, rope_theta = 0;
+  size_t kv_dim() const { return kv_heads * head_dim; }
+  size_t embed_row_bytes() const { return embed_format.row_bytes(hidden); }
+};
+
+// Tensor slots inside a stored layer block (src/weights.rs:158-171).
+enum Slot { T_INPUT_NORM = 0, T_DOWN, T_GATE, T_UP, T_POST_NORM, T_K_B, T_K_W, T_O_W, T_Q_B, T_Q_W, T_V_B, T_V_W, N_SLOTS };
+
+struct LayerLayout {
+  size_t off[N_SLOTS] = {0}, len[N_SLOTS] = {0};
+  size_t total = 0;
+};
+
+Config parse_config(const std::string& json_text);
+LayerLayout layer_layout_for(const Config& c);
+bool matrix_shape(int slot, const Config& c, size_t* rows, size_t* cols);
+std::vector<size_t> tensor_shape(int slot, const Config& c);
+extern const char* const kSlotSuffix[N_SLOTS];
+
+// A `.lsq` file opened for reading (src/weights.rs:327-423).
+struct LsqFile {
+  std::string path;
+  std::string config_text;
+  Config cfg;
+  LayerLayout layout;
+  uint64_t data_start = 0, embed_start = 0, norm_start = 0;
+  size_t embed_bytes = 0, norm_bytes = 0;
+  static LsqFile open(const std::string& path);
+};
+
+// A BF16 safetensors model directory (src/weights.rs:271-324).
+struct SafetensorsModel {
+  std::string dir, file, config_text;
+  Config cfg;
+  LayerLayout layout;
+  std::vector<uint64_t> layer_start;
+  uint64_t embed_start = 0, norm_start = 0;
+  size_t embed_len = 0, norm_len = 0;
+  static SafetensorsModel open(const std::string& dir);
+};
+
+std::string inject_quant(const std::string& config_text, WeightFormat body, WeightFormat embed);
+std::string lsq_header_bytes(const std::string& config_text, size_t layer_bytes, size_t embed_bytes, size_t norm_bytes);
+std::string read_file_text(const std::string& path);
+void pread_all(int fd, void* buf, size_t n, uint64_t off);
+
+// ---- device layout of a quantized matrix --------------------------------------------------------
+//
+// A matrix of R rows x C columns is stored on the device as two planes, both tiled by 32 rows so
+// that one warp (lane = row) reads 512 contiguous bytes per step:
+//   data  : tile-major [R/32][C*bits/128 chunks][32 rows][16 B]  (the row's packed ints, unchanged)
+//   scales: tile-major [R/32][C/G groups][32 rows] bf16
+// R is padded up to a multiple of 32 with zero rows. Byte values are the file's, only moved.
+
+struct QMat {
+  const uint8_t* data = nullptr;    // tiled data plane
+  const uint16_t* scales = nullptr; // tiled scale plane (bf16 bits)
+  int rows = 0, rows_pad = 0, cols = 0, bits = 8, group = 64;
+  __host__ __device__ size_t data_bytes() const { return (size_t)rows_pad * cols * bits / 8; }
+  __host__ __device__ size_t scale_bytes() const { return (size_t)rows_pad * (cols / group) * 2; }
+  __host__ __device__ int chunks() const { return cols * bits / 128; }
+  __host__ __device__ int groups() const { return cols / group; }
+};
+
+inline int pad32(int r) { return (r + 31) / 32 * 32; }
+
+// Row sources of a repacked matrix: up to 3 stacked segments (e.g. q | k | v), optionally with
+// rows interleaved in blocks of 16 between two segments (gate/up, for the SwiGLU epilogue).
+struct RepackSrc {
+  const uint8_t* seg[3] = {nullptr, nullptr, nullptr};
+  int seg_rows[3] = {0, 0, 0};
+  int nseg = 1;
+  int interleave16 = 0;  // 1: dest tile of 32 = 16 rows of seg0 then the same 16 rows of seg1
+};
+
+// ---- kernels (ls_kernels.cu) -------------------------------------------------------------------
+
+enum Epilogue { EPI_STORE = 0, EPI_BIAS_STORE = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+
+// Argmax partial: value then index, combined so that a larger value wins and, on equal values,
+// the smaller index wins (src/spec.rs:41-49 first-maximum rule).
+struct ArgPart {
+  float v;
+  uint32_t i;
+};
+
+// Device control block of one model: the token block and position, and the verify result.
+struct Ctl {
+  int32_t pos0;         // tokens already in the cache
+  int32_t M;            // tokens in this pass
+  int32_t n_logits;     // positions whose logits/argmax are wanted (the last n_logits)
+  int32_t mode;         // 0 = forward (pos += M), 1 = verify (pos += m + 1)
+  uint32_t tokens[128]; // the block (max PREFILL_CHUNK)
+  // results
+  uint32_t argmax[128]; // greedy token at each wanted position
+  int32_t m;            // accepted prefix length (verify)
+  uint32_t next;        // argmax at position m (verify) / at the last position (forward)
+  int32_t err;          // nonzero if a kernel detected a bad input
+  int32_t pad;
+};
+
+struct GemvLaunch {
+  QMat w;
+  const float* x = nullptr;  // [M][x_stride] f32
+  int x_stride = 0;
+  int M = 0;
+  int m_base = 0;  // first token row of x for this launch (token groups)
+  // optional RMSNorm prologue over the full row of x (K == hidden)
+  const uint16_t* norm_bf16 = nullptr;
+  const float* norm_f32 = nullptr;
+  float eps = 0;
+  // epilogue
+  int epi = EPI_STORE;
+  float* y = nullptr;          // output [M][y_stride]
+  int y_stride = 0;
+  const uint16_t* bias = nullptr;
+  // argmax epilogue
+  ArgPart* arg_parts = nullptr;  // [n_row_ctas][M]
+  unsigned* arg_ticket = nullptr;
+  Ctl* ctl = nullptr;            // accept/advance target of the last CTA
+  int n_valid_rows = 0;          // valid rows of this matrix (ignores padding)
+  int row_offset = 0;            // vocabulary id of row 0 (head streamed in chunks)
+  int part_tile_offset = 0;      // first arg_parts tile of this launch
+  int finalize = 1;              // 1: the last CTA reduces all parts and applies the acceptance rule
+  int n_part_tiles = 0;          // tiles over all launches of this pass (finalize)
+  float* logits = nullptr;       // optional full logits [M][logits_stride]
+  int logits_stride = 0;
+  // split-K
+  int ksplit = 1;
+  float* partial = nullptr;  // [row_ctas][ksplit][M][32]
+  unsigned* tickets = nullptr;
+};
+
+void launch_gemv(const GemvLaunch& g, cudaStream_t s);
+void launch_repack(const RepackSrc& src, int bits, int group, int cols, uint8_t* data, uint16_t* scales, int rows_pad,
+                   cudaStream_t s);
+void launch_embed(const QMat& e, const Ctl* ctl, float* x, int hidden, int M, cudaStream_t s);
+// Streaming mode: rows read in the file layout through a mapped pinned-host pointer.
+void launch_embed_raw(const uint8_t* table, size_t row_bytes, int bits, int group, const Ctl* ctl, float* x, int hidden,
+                      int vocab, int M, cudaStream_t s);
+void launch_advance(Ctl* ctl, cudaStream_t s);
+void launch_argmax_finalize(const ArgPart* parts, int nparts, int M, Ctl* ctl, cudaStream_t s);
+
+struct AttnLaunch {
+  const float* qkv = nullptr;  // [M][qkv_stride] f32: q | k | v (pre-RoPE, bias added)
+  int qkv_stride = 0;
+  uint16_t* k_cache = nullptr;  // [kv_heads][max_ctx][hd] f16 bits
+  uint16_t* v_cache = nullptr;
+  const float2* rope = nullptr;  // [max_ctx][hd/2] (cos, sin)
+  const Ctl* ctl = nullptr;
+  float* out = nullptr;  // [M][heads*hd]
+  float* part = nullptr; // split partials
+  unsigned* tickets = nullptr;
+  int heads = 0, kv_heads = 0, hd = 0, max_ctx = 0, M = 0, split = 64, max_splits = 0;
+};
+void launch_attention(const AttnLaunch& a, cudaStream_t s);
+
+void launch_set_ctl(Ctl* ctl, int pos0, int M, int n_logits, int mode, const uint32_t* tokens_dev_or_null, cudaStream_t s);
+void launch_quantize_rows(const uint16_t* src_bf16, int rows, int cols, int bits, int group, int clip, uint8_t* dst,
+                          double* err_norm, cudaStream_t s);
+
+}  // namespace ls

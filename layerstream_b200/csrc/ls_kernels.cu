@@ -1,0 +1,881 @@
+// CUDA kernels of the verify path, written for sm_100a.
+//
+//   gemv_kernel        dequant-fused skinny GEMV for M <= 16 rows per token group: int8 / int4 weights
+//                      with bf16 group scales, 128-bit coalesced loads of a 32-row tiled layout,
+//                      in-register unpacking, optional RMSNorm prologue, and fused epilogues
+//                      (bias, residual add, SwiGLU, LM-head argmax + longest-prefix acceptance).
+//                      Replaces kernels::matmul_q8 / matmul_q4 (src/kernels.rs:53-92,123-203) and the
+//                      norm / bias / silu / residual / argmax steps around them (src/model.rs:240-298,
+//                      src/model.rs:190-216, src/spec.rs:41-49,120-127).
+//   attention_kernel   causal GQA attention of the M block rows over the f16 KV cache with RoPE applied
+//                      from a host-computed table and the block's new K/V appended. Split across CTAs
+//                      along the context with an online softmax and a deterministic combine.
+//                      Replaces src/model.rs:249-282 and kernels::rope_inplace / softmax_inplace.
+//   embed_kernel       embedding row gather + dequantisation (src/kernels.rs:95-121), bit-exact.
+//   repack_kernel      file row layout -> tiled device planes (a byte move, no arithmetic).
+//   quantize_kernel    quant::quantize_group / quantize_row (src/quant.rs:35-104), bit-exact.
+#include <cuda_fp16.h>
+#include <math_constants.h>
+
+#include "ls_internal.h"
+
+namespace ls {
+
+// ------------------------------------------------------------------------------------------------
+// small helpers
+// ------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// signed int8 byte k of a word -> float, exact: 0x4B0000xx is 2^23 + xx.
+__device__ __forceinline__ float s8_to_f(uint32_t wx /* word ^ 0x80808080 */, int k) {
+  return __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7440u + k)) - 8388736.0f;
+}
+// nibble (value + 8 stored) -> float value, exact.
+__device__ __forceinline__ float u4_to_f(uint32_t w, int shift) {
+  return __uint_as_float(((w >> shift) & 0xFu) | 0x4B000000u) - 8388616.0f;
+}
+
+__device__ __forceinline__ bool arg_better(float v2, uint32_t i2, float v1, uint32_t i1) {
+  return v2 > v1 || (v2 == v1 && i2 < i1);
+}
+
+__device__ __forceinline__ void warp_argmax(float& v, uint32_t& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+    uint32_t i2 = __shfl_xor_sync(0xffffffffu, i, o);
+    if (arg_better(v2, i2, v, i)) {
+      v = v2;
+      i = i2;
+    }
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Last-CTA election: every thread has finished its global writes; returns true in exactly one CTA
+// (the last of `total` to arrive), which then reads the others' writes. Resets the ticket.
+__device__ __forceinline__ bool last_cta(unsigned* ticket, unsigned total) {
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned t = atomicAdd(ticket, 1u);
+    s_last = (t == total - 1);
+    if (s_last) *ticket = 0u;
+  }
+  __syncthreads();
+  if (s_last) __threadfence();
+  return s_last != 0;
+}
+
+// ------------------------------------------------------------------------------------------------
+// GEMV
+// ------------------------------------------------------------------------------------------------
+
+constexpr int GEMV_WARPS = 4;
+constexpr int GEMV_THREADS = GEMV_WARPS * 32;
+
+// Reduces the per-tile argmax parts of every token (first-maximum rule), then applies the
+// acceptance rule of src/spec.rs:121-125 (verify) or records the next token (forward).
+// Run by one whole CTA of GEMV_THREADS threads.
+__device__ void argmax_finalize_block(const ArgPart* parts, int ntiles, int M, Ctl* ctl) {
+  __shared__ float s_v[GEMV_WARPS];
+  __shared__ uint32_t s_i[GEMV_WARPS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = 0; t < M; t++) {
+    float v = -CUDART_INF_F;
+    uint32_t idx = 0xffffffffu;
+    for (int k = threadIdx.x; k < ntiles; k += GEMV_THREADS) {
+      const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(parts + (size_t)k * M + t));
+      const ArgPart p{__uint_as_float(raw.x), raw.y};
+      if (arg_better(p.v, p.i, v, idx)) {
+        v = p.v;
+        idx = p.i;
+      }
+    }
+    warp_argmax(v, idx);
+    if (lane == 0) {
+      s_v[warp] = v;
+      s_i[warp] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < GEMV_WARPS; w++)
+        if (arg_better(s_v[w], s_i[w], v, idx)) {
+          v = s_v[w];
+          idx = s_i[w];
+        }
+      ctl->argmax[t] = idx;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    if (ctl->mode == 1) {
+      // longest prefix of guesses the target agrees with, then the correction (or bonus) token;
+      // the cache keeps [a, d_1 .. d_m]
+      int m = 0;
+      while (m < M - 1 && ctl->argmax[m] == ctl->tokens[m + 1]) m++;
+      ctl->m = m;
+      ctl->next = ctl->argmax[m];
+      ctl->pos0 += m + 1;
+    } else {
+      ctl->m = 0;
+      ctl->next = ctl->argmax[M - 1];
+      ctl->pos0 += ctl->M;
+      if (ctl->mode == 2) ctl->tokens[0] = ctl->next;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(GEMV_THREADS) argmax_finalize_kernel(const ArgPart* parts, int ntiles, int M, Ctl* ctl) {
+  argmax_finalize_block(parts, ntiles, M, ctl);
+}
+
+void launch_argmax_finalize(const ArgPart* parts, int nparts, int M, Ctl* ctl, cudaStream_t s) {
+  argmax_finalize_kernel<<<1, GEMV_THREADS, 0, s>>>(parts, nparts, M, ctl);
+  LS_CUDA(cudaGetLastError());
+}
+
+// One 16-byte chunk of a row times the staged activations of up to MT tokens, accumulated into
+// tot[t] with the chunk's group scale(s).
+template <int BITS, bool G16, int MT>
+__device__ __forceinline__ void gemv_chunk(const uint4 wv, int c, int col0, int ncol, int group, const uint16_t* sb,
+                                           const float* __restrict__ xs, int Mloc, float (&tot)[MT]) {
+  const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+  if constexpr (BITS == 8) {
+    const float s = bf16f(sb[(size_t)((c * 16) / group) * 32]);
+    float wf[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t wx = wd[k] ^ 0x80808080u;
+#pragma unroll
+      for (int b = 0; b < 4; b++) wf[4 * k + b] = s8_to_f(wx, b);
+    }
+    const float* xc = xs + (c * 16 - col0);
+#pragma unroll
+    for (int t = 0; t < MT; t++) {
+      if (t < Mloc) {
+        const float4* xp = reinterpret_cast<const float4*>(xc + t * ncol);
+        float p = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float4 xv = xp[q];
+          p = fmaf(wf[4 * q + 0], xv.x, p);
+          p = fmaf(wf[4 * q + 1], xv.y, p);
+          p = fmaf(wf[4 * q + 2], xv.z, p);
+          p = fmaf(wf[4 * q + 3], xv.w, p);
+        }
+        tot[t] = fmaf(s, p, tot[t]);
+      }
+    }
+  } else {
+    // low nibble of byte j = weight j, high nibble = weight j + group/2 (inside the group)
+    float wl[16], wh[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+#pragma unroll
+      for (int b = 0; b < 4; b++) {
+        wl[4 * k + b] = u4_to_f(wd[k], 8 * b);
+        wh[4 * k + b] = u4_to_f(wd[k], 8 * b + 4);
+      }
+    }
+    if constexpr (G16) {
+      // the chunk holds groups 2c (bytes 0..7) and 2c+1 (bytes 8..15); columns 32c .. 32c+31
+      const float s0 = bf16f(sb[(size_t)(2 * c) * 32]);
+      const float s1 = bf16f(sb[(size_t)(2 * c + 1) * 32]);
+      const float* xc = xs + (c * 32 - col0);
+#pragma unroll
+      for (int t = 0; t < MT; t++) {
+        if (t < Mloc) {
+          const float4* xp = reinterpret_cast<const float4*>(xc + t * ncol);
+          float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+          for (int q = 0; q < 2; q++) {
+            const float4 lo = xp[q], hi = xp[2 + q];
+            p0 = fmaf(wl[4 * q + 0], lo.x, p0);
+            p0 = fmaf(wl[4 * q + 1], lo.y, p0);
+            p0 = fmaf(wl[4 * q + 2], lo.z, p0);
+            p0 = fmaf(wl[4 * q + 3], lo.w, p0);
+            p0 = fmaf(wh[4 * q + 0], hi.x, p0);
+            p0 = fmaf(wh[4 * q + 1], hi.y, p0);
+            p0 = fmaf(wh[4 * q + 2], hi.z, p0);
+            p0 = fmaf(wh[4 * q + 3], hi.w, p0);
+            const float4 lo1 = xp[4 + q], hi1 = xp[6 + q];
+            p1 = fmaf(wl[8 + 4 * q + 0], lo1.x, p1);
+            p1 = fmaf(wl[8 + 4 * q + 1], lo1.y, p1);
+            p1 = fmaf(wl[8 + 4 * q + 2], lo1.z, p1);
+            p1 = fmaf(wl[8 + 4 * q + 3], lo1.w, p1);
+            p1 = fmaf(wh[8 + 4 * q + 0], hi1.x, p1);
+            p1 = fmaf(wh[8 + 4 * q + 1], hi1.y, p1);
+            p1 = fmaf(wh[8 + 4 * q + 2], hi1.z, p1);
+            p1 = fmaf(wh[8 + 4 * q + 3], hi1.w, p1);
+          }
+          tot[t] = fmaf(s0, p0, tot[t]);
+          tot[t] = fmaf(s1, p1, tot[t]);
+        }
+      }
+    } else {
+      const int half = group >> 1;
+      const int g = (c * 32) / group;
+      const int j0 = (c * 16) % half;
+      const float s = bf16f(sb[(size_t)g * 32]);
+      const float* xlo = xs + (g * group + j0 - col0);
+      const float* xhi = xlo + half;
+#pragma unroll
+      for (int t = 0; t < MT; t++) {
+        if (t < Mloc) {
+          const float4* lp = reinterpret_cast<const float4*>(xlo + t * ncol);
+          const float4* hp = reinterpret_cast<const float4*>(xhi + t * ncol);
+          float p = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const float4 lo = lp[q], hi = hp[q];
+            p = fmaf(wl[4 * q + 0], lo.x, p);
+            p = fmaf(wl[4 * q + 1], lo.y, p);
+            p = fmaf(wl[4 * q + 2], lo.z, p);
+            p = fmaf(wl[4 * q + 3], lo.w, p);
+            p = fmaf(wh[4 * q + 0], hi.x, p);
+            p = fmaf(wh[4 * q + 1], hi.y, p);
+            p = fmaf(wh[4 * q + 2], hi.z, p);
+            p = fmaf(wh[4 * q + 3], hi.w, p);
+          }
+          tot[t] = fmaf(s, p, tot[t]);
+        }
+      }
+    }
+  }
+}
+
+// Split boundaries in chunks, aligned so that each CTA covers whole groups (int4, group >= 32).
+__host__ __device__ inline void gemv_split(int nch, int bits, int group, int ksplit, int ks, int* c0, int* c1) {
+  const int U = (bits == 4 && group >= 32) ? group / 32 : 1;
+  const int nu = nch / U;
+  *c0 = (int)((long long)ks * nu / ksplit) * U;
+  *c1 = (int)((long long)(ks + 1) * nu / ksplit) * U;
+}
+
+template <int BITS, bool G16, int MT>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvLaunch g) {
+  extern __shared__ __align__(16) float smem[];
+  __shared__ float s_inv[MT];
+  const int tile = blockIdx.x, ks = blockIdx.y, z = blockIdx.z;
+  const int ntiles = gridDim.x, nz = gridDim.z;
+  const int m0 = z * MT;
+  const int Mloc = min(MT, g.M - m0);
+  const int nch = g.w.chunks();
+  int c0, c1;
+  gemv_split(nch, BITS, g.w.group, g.ksplit, ks, &c0, &c1);
+  constexpr int WPC = 128 / BITS;
+  const int col0 = c0 * WPC, ncol = (c1 - c0) * WPC;
+  float* xs = smem;                       // [MT][ncol]
+  float* red = smem + MT * ncol;          // [GEMV_WARPS][MT][32]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // ---- prologue: RMSNorm statistics over the full rows (only when a norm is fused) ----
+  const bool has_norm = g.norm_bf16 != nullptr || g.norm_f32 != nullptr;
+  if (has_norm) {
+    for (int t = warp; t < Mloc; t += GEMV_WARPS) {
+      const float* xr = g.x + (size_t)(m0 + t) * g.x_stride;
+      float ss = 0.f;
+      for (int i = lane; i < g.w.cols; i += 32) ss = fmaf(xr[i], xr[i], ss);
+      ss = warp_sum(ss);
+      if (lane == 0) s_inv[t] = 1.0f / sqrtf(ss / (float)g.w.cols + g.eps);
+    }
+    __syncthreads();
+  }
+  // ---- stage the activations (normalised if requested) ----
+  for (int i = threadIdx.x; i < Mloc * ncol; i += GEMV_THREADS) {
+    const int t = i / ncol, cc = i - t * ncol;
+    float v = g.x[(size_t)(m0 + t) * g.x_stride + col0 + cc];
+    if (has_norm) {
+      const float w = g.norm_bf16 ? bf16f(g.norm_bf16[col0 + cc]) : g.norm_f32[col0 + cc];
+      v = v * s_inv[t] * w;
+    }
+    xs[t * ncol + cc] = v;
+  }
+  __syncthreads();
+
+  // ---- main loop: lane = row of the 32-row tile; warps stride the chunks ----
+  float tot[MT];
+#pragma unroll
+  for (int t = 0; t < MT; t++) tot[t] = 0.f;
+  const uint8_t* db = g.w.data + (size_t)tile * nch * 512 + lane * 16;
+  const uint16_t* sb = g.w.scales + (size_t)tile * g.w.groups() * 32 + lane;
+  constexpr int U = 4;
+  int c = c0 + warp;
+  for (; c + (U - 1) * GEMV_WARPS < c1; c += U * GEMV_WARPS) {
+    uint4 wv[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) wv[u] = ld_stream_v4(db + (size_t)(c + u * GEMV_WARPS) * 512);
+#pragma unroll
+    for (int u = 0; u < U; u++)
+      gemv_chunk<BITS, G16, MT>(wv[u], c + u * GEMV_WARPS, col0, ncol, g.w.group, sb, xs, Mloc, tot);
+  }
+  for (; c < c1; c += GEMV_WARPS) {
+    const uint4 wv = ld_stream_v4(db + (size_t)c * 512);
+    gemv_chunk<BITS, G16, MT>(wv, c, col0, ncol, g.w.group, sb, xs, Mloc, tot);
+  }
+
+  // ---- reduce the warps' partial sums in a fixed order ----
+#pragma unroll
+  for (int t = 0; t < MT; t++) red[(warp * MT + t) * 32 + lane] = tot[t];
+  __syncthreads();
+  float y[MT];
+  if (warp == 0) {
+#pragma unroll
+    for (int t = 0; t < MT; t++) {
+      float a = 0.f;
+#pragma unroll
+      for (int w = 0; w < GEMV_WARPS; w++) a += red[(w * MT + t) * 32 + lane];
+      y[t] = a;
+    }
+  }
+  // ---- split-K: the last CTA of this (token group, tile) sums the partials in order ----
+  if (g.ksplit > 1) {
+    float* part = g.partial + ((size_t)(z * ntiles + tile) * g.ksplit) * MT * 32;
+    if (warp == 0) {
+#pragma unroll
+      for (int t = 0; t < MT; t++) part[((size_t)ks * MT + t) * 32 + lane] = y[t];
+    }
+    if (!last_cta(g.tickets + z * ntiles + tile, (unsigned)g.ksplit)) return;
+    if (warp == 0) {
+#pragma unroll
+      for (int t = 0; t < MT; t++) {
+        float a = 0.f;
+        for (int k = 0; k < g.ksplit; k++) a += __ldcg(part + ((size_t)k * MT + t) * 32 + lane);
+        y[t] = a;
+      }
+    }
+  }
+
+  // ---- epilogue ----
+  const int r = tile * 32 + lane;
+  if (g.epi == EPI_ARGMAX) {
+    if (warp == 0) {
+#pragma unroll
+      for (int t = 0; t < MT; t++) {
+        if (t < Mloc) {
+          float v = (r < g.n_valid_rows) ? y[t] : -CUDART_INF_F;
+          uint32_t idx = (uint32_t)(r + g.row_offset);
+          if (g.logits && r < g.n_valid_rows) g.logits[(size_t)(m0 + t) * g.logits_stride + g.row_offset + r] = y[t];
+          warp_argmax(v, idx);
+          if (lane == 0) g.arg_parts[(size_t)(tile + g.part_tile_offset) * g.M + m0 + t] = ArgPart{v, idx};
+        }
+      }
+    }
+    if (!g.finalize) return;
+    if (!last_cta(g.arg_ticket, (unsigned)(ntiles * nz))) return;
+    argmax_finalize_block(g.arg_parts, g.n_part_tiles ? g.n_part_tiles : ntiles, g.M, g.ctl);
+    return;
+  }
+  if (warp != 0) return;
+  if (g.epi == EPI_SWIGLU) {
+    // rows interleaved in 16s: lanes 0..15 hold gate rows, lanes 16..31 the matching up rows
+#pragma unroll
+    for (int t = 0; t < MT; t++) {
+      const float u = __shfl_down_sync(0xffffffffu, y[t], 16);
+      if (t < Mloc && lane < 16) {
+        const int j = tile * 16 + lane;
+        const float gt = y[t];
+        g.y[(size_t)(m0 + t) * g.y_stride + j] = gt / (1.0f + expf(-gt)) * u;
+      }
+    }
+    return;
+  }
+  if (r >= g.w.rows) return;
+#pragma unroll
+  for (int t = 0; t < MT; t++) {
+    if (t < Mloc) {
+      float* dst = g.y + (size_t)(m0 + t) * g.y_stride + r;
+      if (g.epi == EPI_RESID) *dst += y[t];
+      else if (g.epi == EPI_BIAS_STORE) *dst = y[t] + bf16f(g.bias[r]);
+      else *dst = y[t];
+    }
+  }
+}
+
+template <int BITS, bool G16, int MT>
+static void launch_gemv_t(const GemvLaunch& g, cudaStream_t s) {
+  const int nch = g.w.chunks();
+  int maxcol = 0;
+  for (int ks = 0; ks < g.ksplit; ks++) {
+    int c0, c1;
+    gemv_split(nch, g.w.bits, g.w.group, g.ksplit, ks, &c0, &c1);
+    maxcol = max(maxcol, (c1 - c0) * (128 / BITS));
+  }
+  const size_t smem = (size_t)MT * maxcol * 4 + (size_t)GEMV_WARPS * MT * 32 * 4;
+  static int configured[64] = {0};  // per device: the attribute is a per-device setting
+  int dev = 0;
+  LS_CUDA(cudaGetDevice(&dev));
+  if (smem > 48 * 1024 && configured[dev & 63] < (int)smem) {
+    LS_CUDA(cudaFuncSetAttribute(gemv_kernel<BITS, G16, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured[dev & 63] = (int)smem;
+  }
+  dim3 grid(g.w.rows_pad / 32, g.ksplit, (g.M + MT - 1) / MT);
+  gemv_kernel<BITS, G16, MT><<<grid, GEMV_THREADS, smem, s>>>(g);
+  LS_CUDA(cudaGetLastError());
+}
+
+template <int BITS, bool G16>
+static void launch_gemv_b(const GemvLaunch& g, cudaStream_t s) {
+  if (g.M <= 1) return launch_gemv_t<BITS, G16, 1>(g, s);
+  if (g.M <= 2) return launch_gemv_t<BITS, G16, 2>(g, s);
+  if (g.M <= 4) return launch_gemv_t<BITS, G16, 4>(g, s);
+  if (g.M <= 8) return launch_gemv_t<BITS, G16, 8>(g, s);
+  return launch_gemv_t<BITS, G16, 16>(g, s);
+}
+
+void launch_gemv(const GemvLaunch& g, cudaStream_t s) {
+  if (g.M <= 0) return;
+  if (g.w.bits == 8) return launch_gemv_b<8, false>(g, s);
+  if (g.w.group == 16) return launch_gemv_b<4, true>(g, s);
+  return launch_gemv_b<4, false>(g, s);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Attention
+// ------------------------------------------------------------------------------------------------
+
+constexpr int ATT_THREADS = 128;
+constexpr int ATT_TILE = 64;
+
+__device__ __forceinline__ float f16_round(float v) { return __half2float(__float2half_rn(v)); }
+
+template <int HD>
+__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch a) {
+  extern __shared__ __align__(16) float sm[];
+  constexpr int HP = HD + 1;  // padded row: conflict-free column access
+  constexpr int HALF = HD / 2;
+  const int hh = blockIdx.x, slot = blockIdx.y, nslot = gridDim.y;
+  const int group = a.heads / a.kv_heads;
+  const int g = hh / group;
+  const int M = a.M;
+  const int pos0 = a.ctl->pos0;
+  const int total = pos0 + M;
+  const int ntiles = (total + ATT_TILE - 1) / ATT_TILE;
+  const int H = a.heads * HD, KV = a.kv_heads * HD;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* qs = sm;                       // [M][HD]
+  float* Ks = qs + M * HD;              // [64][HP]
+  float* Vs = Ks + ATT_TILE * HP;       // [64][HP]
+  float* st = Vs + ATT_TILE * HP;       // [M][HD + 2]  (m, l, acc)
+  const float scale = 1.0f / sqrtf((float)HD);
+
+  for (int i = threadIdx.x; i < M * HALF; i += ATT_THREADS) {
+    const int t = i / HALF, d = i - t * HALF;
+    const float2 cs = a.rope[(size_t)(pos0 + t) * HALF + d];
+    const float* q = a.qkv + (size_t)t * a.qkv_stride + hh * HD;
+    const float x1 = q[d], x2 = q[d + HALF];
+    qs[t * HD + d] = x1 * cs.x - x2 * cs.y;
+    qs[t * HD + d + HALF] = x2 * cs.x + x1 * cs.y;
+  }
+  for (int i = threadIdx.x; i < M * (HD + 2); i += ATT_THREADS) st[i] = (i % (HD + 2) == 0) ? -CUDART_INF_F : 0.f;
+  __syncthreads();
+
+  const bool writer = (hh % group) == 0;
+  for (int tile = slot; tile < ntiles; tile += nslot) {
+    const int p0 = tile * ATT_TILE;
+    for (int i = threadIdx.x; i < ATT_TILE * HALF; i += ATT_THREADS) {
+      const int pl = i / HALF, d = i - pl * HALF;
+      const int p = p0 + pl;
+      float k1 = 0.f, k2 = 0.f, v1 = 0.f, v2 = 0.f;
+      if (p < pos0) {
+        const size_t base = ((size_t)g * a.max_ctx + p) * HD;
+        k1 = __half2float(__ushort_as_half(a.k_cache[base + d]));
+        k2 = __half2float(__ushort_as_half(a.k_cache[base + d + HALF]));
+        v1 = __half2float(__ushort_as_half(a.v_cache[base + d]));
+        v2 = __half2float(__ushort_as_half(a.v_cache[base + d + HALF]));
+      } else if (p < total) {
+        const int t = p - pos0;
+        const float* kr = a.qkv + (size_t)t * a.qkv_stride + H + g * HD;
+        const float* vr = a.qkv + (size_t)t * a.qkv_stride + H + KV + g * HD;
+        const float2 cs = a.rope[(size_t)p * HALF + d];
+        const float x1 = kr[d], x2 = kr[d + HALF];
+        k1 = f16_round(x1 * cs.x - x2 * cs.y);
+        k2 = f16_round(x2 * cs.x + x1 * cs.y);
+        v1 = f16_round(vr[d]);
+        v2 = f16_round(vr[d + HALF]);
+        if (writer) {
+          const size_t base = ((size_t)g * a.max_ctx + p) * HD;
+          a.k_cache[base + d] = __half_as_ushort(__float2half_rn(k1));
+          a.k_cache[base + d + HALF] = __half_as_ushort(__float2half_rn(k2));
+          a.v_cache[base + d] = __half_as_ushort(__float2half_rn(v1));
+          a.v_cache[base + d + HALF] = __half_as_ushort(__float2half_rn(v2));
+        }
+      }
+      Ks[pl * HP + d] = k1;
+      Ks[pl * HP + d + HALF] = k2;
+      Vs[pl * HP + d] = v1;
+      Vs[pl * HP + d + HALF] = v2;
+    }
+    __syncthreads();
+    for (int t = warp; t < M; t += ATT_THREADS / 32) {
+      const int ctx = pos0 + t + 1;
+      if (p0 >= ctx) continue;
+      const float* q = qs + t * HD;
+      float s0 = -CUDART_INF_F, s1 = -CUDART_INF_F;
+      if (p0 + lane < ctx) {
+        float acc = 0.f;
+#pragma unroll 16
+        for (int d = 0; d < HD; d++) acc = fmaf(q[d], Ks[lane * HP + d], acc);
+        s0 = acc * scale;
+      }
+      if (p0 + 32 + lane < ctx) {
+        float acc = 0.f;
+#pragma unroll 16
+        for (int d = 0; d < HD; d++) acc = fmaf(q[d], Ks[(lane + 32) * HP + d], acc);
+        s1 = acc * scale;
+      }
+      const float tmax = warp_max(fmaxf(s0, s1));
+      float* S = st + t * (HD + 2);
+      const float m_old = S[0];
+      const float m_new = fmaxf(m_old, tmax);
+      const float corr = (m_old == -CUDART_INF_F) ? 0.f : expf(m_old - m_new);
+      const float e0 = (s0 == -CUDART_INF_F) ? 0.f : expf(s0 - m_new);
+      const float e1 = (s1 == -CUDART_INF_F) ? 0.f : expf(s1 - m_new);
+      const float lsum = warp_sum(e0 + e1);
+      constexpr int DPL = (HD + 31) / 32;  // value dims owned by each lane
+      float acc[DPL];
+#pragma unroll
+      for (int j = 0; j < DPL; j++) {
+        const int d = lane + 32 * j;
+        acc[j] = (d < HD) ? S[2 + d] * corr : 0.f;
+      }
+#pragma unroll 8
+      for (int pl = 0; pl < 32; pl++) {
+        const float e = __shfl_sync(0xffffffffu, e0, pl);
+#pragma unroll
+        for (int j = 0; j < DPL; j++)
+          if (lane + 32 * j < HD) acc[j] = fmaf(e, Vs[pl * HP + lane + 32 * j], acc[j]);
+      }
+#pragma unroll 8
+      for (int pl = 0; pl < 32; pl++) {
+        const float e = __shfl_sync(0xffffffffu, e1, pl);
+#pragma unroll
+        for (int j = 0; j < DPL; j++)
+          if (lane + 32 * j < HD) acc[j] = fmaf(e, Vs[(pl + 32) * HP + lane + 32 * j], acc[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < DPL; j++)
+        if (lane + 32 * j < HD) S[2 + lane + 32 * j] = acc[j];
+      __syncwarp();
+      if (lane == 0) {
+        S[1] = S[1] * corr + lsum;
+        S[0] = m_new;
+      }
+      __syncwarp();
+    }
+    __syncthreads();
+  }
+
+  // partial (m, l, acc) of this CTA for every token, then the combine in the last CTA of the head
+  float* part = a.part + ((size_t)hh * nslot + slot) * M * (HD + 2);
+  for (int i = threadIdx.x; i < M * (HD + 2); i += ATT_THREADS) part[i] = st[i];
+  if (!last_cta(a.tickets + hh, (unsigned)nslot)) return;
+  const float* all = a.part + (size_t)hh * nslot * M * (HD + 2);
+  for (int i = threadIdx.x; i < M * HD; i += ATT_THREADS) {
+    const int t = i / HD, d = i - t * HD;
+    float mx = -CUDART_INF_F;
+    for (int s = 0; s < nslot; s++) mx = fmaxf(mx, __ldcg(all + ((size_t)s * M + t) * (HD + 2)));
+    float L = 0.f, acc = 0.f;
+    for (int s = 0; s < nslot; s++) {
+      const float* P = all + ((size_t)s * M + t) * (HD + 2);
+      const float ms = __ldcg(P);
+      if (ms == -CUDART_INF_F) continue;
+      const float w = expf(ms - mx);
+      L += __ldcg(P + 1) * w;
+      acc += __ldcg(P + 2 + d) * w;
+    }
+    a.out[(size_t)t * H + hh * HD + d] = acc / L;
+  }
+}
+
+template <int HD>
+static void launch_attention_t(const AttnLaunch& a, size_t smem, cudaStream_t s) {
+  static size_t configured[64] = {0};
+  int dev = 0;
+  LS_CUDA(cudaGetDevice(&dev));
+  if (smem > 48 * 1024 && smem > configured[dev & 63]) {
+    LS_CUDA(cudaFuncSetAttribute(attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured[dev & 63] = smem;
+  }
+  attention_kernel<HD><<<dim3(a.heads, a.max_splits), ATT_THREADS, smem, s>>>(a);
+  LS_CUDA(cudaGetLastError());
+}
+
+void launch_attention(const AttnLaunch& a, cudaStream_t s) {
+  const size_t smem = ((size_t)a.M * a.hd + 2 * ATT_TILE * (a.hd + 1) + (size_t)a.M * (a.hd + 2)) * 4;
+  switch (a.hd) {
+    case 16: return launch_attention_t<16>(a, smem, s);
+    case 32: return launch_attention_t<32>(a, smem, s);
+    case 64: return launch_attention_t<64>(a, smem, s);
+    case 128: return launch_attention_t<128>(a, smem, s);
+    default:
+      LS_THROW(-1, "head dimension " + std::to_string(a.hd) + " is not supported by the CUDA attention kernel (16, 32, 64, 128)");
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Embedding gather + dequantisation (bit-exact with src/kernels.rs:95-121)
+// ------------------------------------------------------------------------------------------------
+
+__global__ void embed_kernel(const QMat e, const Ctl* ctl, float* x, int hidden, int vocab) {
+  const int t = blockIdx.x;
+  const uint32_t tok = ctl->tokens[t];
+  float* xr = x + (size_t)t * hidden;
+  if (tok >= (uint32_t)vocab) {
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x) xr[c] = 0.f;
+    if (threadIdx.x == 0) const_cast<Ctl*>(ctl)->err = 1;
+    return;
+  }
+  const int nch = e.chunks();
+  const uint8_t* row = e.data + ((size_t)(tok / 32) * nch) * 512 + (tok % 32) * 16;
+  const uint16_t* sc = e.scales + (size_t)(tok / 32) * e.groups() * 32 + (tok % 32);
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    float q;
+    int g = c / e.group;
+    if (e.bits == 8) {
+      const int ch = c / 16, b = c % 16;
+      q = (float)(int8_t)row[(size_t)ch * 512 + b];
+    } else {
+      const int half = e.group / 2;
+      const int j = c % e.group;
+      const int byte_in_row = g * half + (j < half ? j : j - half);
+      const uint8_t by = row[(size_t)(byte_in_row / 16) * 512 + byte_in_row % 16];
+      q = (float)((j < half ? (by & 15) : (by >> 4)) - 8);
+    }
+    xr[c] = q * bf16f(sc[(size_t)g * 32]);
+  }
+}
+
+void launch_embed(const QMat& e, const Ctl* ctl, float* x, int hidden, int M, cudaStream_t s) {
+  embed_kernel<<<M, 256, 0, s>>>(e, ctl, x, hidden, e.rows);
+  LS_CUDA(cudaGetLastError());
+}
+
+// Streaming mode: the embedding table stays in pinned host memory in the file layout; the rows of
+// the block's tokens are read through the mapped pointer (one row per token crosses the link).
+__global__ void embed_raw_kernel(const uint8_t* table, size_t row_bytes, int bits, int group, const Ctl* ctl, float* x,
+                                 int hidden, int vocab) {
+  const int t = blockIdx.x;
+  const uint32_t tok = ctl->tokens[t];
+  float* xr = x + (size_t)t * hidden;
+  if (tok >= (uint32_t)vocab) {
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x) xr[c] = 0.f;
+    if (threadIdx.x == 0) const_cast<Ctl*>(ctl)->err = 1;
+    return;
+  }
+  const uint8_t* row = table + (size_t)tok * row_bytes;
+  const uint8_t* sc = row + (size_t)hidden * bits / 8;
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    const int g = c / group;
+    float q;
+    if (bits == 8) {
+      q = (float)(int8_t)row[c];
+    } else {
+      const int half = group / 2, j = c % group;
+      const uint8_t by = row[(size_t)g * half + (j < half ? j : j - half)];
+      q = (float)((j < half ? (by & 15) : (by >> 4)) - 8);
+    }
+    xr[c] = q * __uint_as_float((uint32_t)(sc[2 * g] | (sc[2 * g + 1] << 8)) << 16);
+  }
+}
+
+void launch_embed_raw(const uint8_t* table, size_t row_bytes, int bits, int group, const Ctl* ctl, float* x, int hidden,
+                      int vocab, int M, cudaStream_t s) {
+  embed_raw_kernel<<<M, 256, 0, s>>>(table, row_bytes, bits, group, ctl, x, hidden, vocab);
+  LS_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------------------------------------
+// Repack: stored rows (packed ints ‖ bf16 scales, src/weights.rs:26-31) -> tiled planes
+// ------------------------------------------------------------------------------------------------
+
+__global__ void repack_kernel(const RepackSrc src, int bits, int group, int cols, uint8_t* data, uint16_t* scales,
+                              int rows_pad) {
+  const int d = blockIdx.x;
+  const int tile = d / 32, lr = d % 32;
+  const size_t dbytes = (size_t)cols * bits / 8;
+  const size_t row_bytes = dbytes + (size_t)cols / group * 2;
+  const int nch = cols * bits / 128, ng = cols / group;
+  // find the source row
+  const uint8_t* s = nullptr;
+  if (src.interleave16) {
+    const int seg = lr < 16 ? 0 : 1;
+    const int sr = tile * 16 + (lr & 15);
+    if (sr < src.seg_rows[seg]) s = src.seg[seg] + (size_t)sr * row_bytes;
+  } else {
+    int r = d;
+    for (int k = 0; k < src.nseg; k++) {
+      if (r < src.seg_rows[k]) {
+        s = src.seg[k] + (size_t)r * row_bytes;
+        break;
+      }
+      r -= src.seg_rows[k];
+    }
+  }
+  for (int i = threadIdx.x; i < nch * 16; i += blockDim.x) {
+    const int ch = i / 16, b = i % 16;
+    data[((size_t)tile * nch + ch) * 512 + lr * 16 + b] = s ? s[(size_t)ch * 16 + b] : (uint8_t)0;
+  }
+  for (int gi = threadIdx.x; gi < ng; gi += blockDim.x) {
+    uint16_t v = 0;
+    if (s) v = (uint16_t)(s[dbytes + 2 * gi] | (s[dbytes + 2 * gi + 1] << 8));
+    scales[((size_t)tile * ng + gi) * 32 + lr] = v;
+  }
+}
+
+void launch_repack(const RepackSrc& src, int bits, int group, int cols, uint8_t* data, uint16_t* scales, int rows_pad,
+                   cudaStream_t s) {
+  repack_kernel<<<rows_pad, 128, 0, s>>>(src, bits, group, cols, data, scales, rows_pad);
+  LS_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------------------------------------
+// Control block
+// ------------------------------------------------------------------------------------------------
+
+__global__ void set_ctl_kernel(Ctl* ctl, int pos0, int M, int n_logits, int mode, const uint32_t* toks, int ntok) {
+  if (threadIdx.x == 0) {
+    if (pos0 >= 0) ctl->pos0 = pos0;
+    if (M >= 0) ctl->M = M;
+    if (n_logits >= 0) ctl->n_logits = n_logits;
+    if (mode >= 0) ctl->mode = mode;
+    ctl->err = 0;
+  }
+  if (toks)
+    for (int i = threadIdx.x; i < ntok; i += blockDim.x) ctl->tokens[i] = toks[i];
+}
+
+void launch_set_ctl(Ctl* ctl, int pos0, int M, int n_logits, int mode, const uint32_t* tokens_dev, cudaStream_t s) {
+  set_ctl_kernel<<<1, 128, 0, s>>>(ctl, pos0, M, n_logits, mode, tokens_dev, tokens_dev ? M : 0);
+  LS_CUDA(cudaGetLastError());
+}
+
+__global__ void advance_kernel(Ctl* ctl) {
+  if (threadIdx.x == 0) ctl->pos0 += ctl->M;
+}
+void launch_advance(Ctl* ctl, cudaStream_t s) {
+  advance_kernel<<<1, 32, 0, s>>>(ctl);
+  LS_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------------------------------------
+// Quantizer: one thread per (row, group); float steps written with explicit _rn intrinsics so that
+// nothing is contracted into an FMA (the Rust reference never fuses).
+// ------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float bf16_round_dev(float v) {
+  const uint32_t b = __float_as_uint(v);
+  if ((b & 0x7fffffffu) > 0x7f800000u) return v;
+  const uint32_t lsb = (b >> 16) & 1u;
+  return __uint_as_float((b + 0x7fffu + lsb) & 0xffff0000u);
+}
+
+__device__ __forceinline__ float qround_dev(float v, float inv, float qmax) {
+  float r = roundf(__fmul_rn(v, inv));
+  r = r < -qmax ? -qmax : r;
+  r = r > qmax ? qmax : r;
+  return r;
+}
+
+__constant__ float kClips[9] = {1.0f, 0.95f, 0.9f, 0.85f, 0.8f, 0.75f, 0.7f, 0.65f, 0.6f};
+
+__global__ void quantize_kernel(const uint16_t* src, int rows, int cols, int bits, int group, int clip, uint8_t* dst,
+                                double* err_norm) {
+  const long long gi = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int ng = cols / group;
+  if (gi >= (long long)rows * ng) return;
+  const int r = (int)(gi / ng), g = (int)(gi % ng);
+  const uint16_t* w = src + (size_t)r * cols + (size_t)g * group;
+  const size_t dbytes = (size_t)cols * bits / 8;
+  uint8_t* out = dst + (size_t)r * (dbytes + (size_t)ng * 2);
+  const float qmax = bits == 8 ? 127.0f : 7.0f;
+  float amax = 0.0f;
+  double norm = 0.0;
+  for (int i = 0; i < group; i++) {
+    const float v = bf16f(w[i]);
+    amax = fmaxf(amax, fabsf(v));
+    norm += (double)__fmul_rn(v, v);
+  }
+  float best_s = 0.0f;
+  double best_e = CUDART_INF;
+  if (amax != 0.0f && isfinite(amax)) {
+    const int nclip = clip ? 9 : 1;
+    for (int ci = 0; ci < nclip; ci++) {
+      const float s = bf16_round_dev(__fdiv_rn(__fmul_rn(kClips[ci], amax), qmax));
+      if (s == 0.0f) continue;
+      const float inv = __fdiv_rn(1.0f, s);
+      double e = 0.0;
+      for (int i = 0; i < group; i++) {
+        const float v = bf16f(w[i]);
+        const float d = __fsub_rn(v, __fmul_rn(qround_dev(v, inv, qmax), s));
+        e += (double)__fmul_rn(d, d);
+      }
+      if (e < best_e) {
+        best_e = e;
+        best_s = s;
+      }
+    }
+  }
+  double err;
+  if (best_s == 0.0f) {
+    err = 0.0;
+    for (int i = 0; i < group; i++) {
+      const float v = bf16f(w[i]);
+      err += (double)__fmul_rn(v, v);
+    }
+  } else {
+    err = best_e;
+  }
+  const float inv = best_s == 0.0f ? 0.0f : __fdiv_rn(1.0f, best_s);
+  if (bits == 8) {
+    for (int i = 0; i < group; i++) {
+      const int8_t q = best_s == 0.0f ? 0 : (int8_t)qround_dev(bf16f(w[i]), inv, qmax);
+      out[(size_t)g * group + i] = (uint8_t)q;
+    }
+  } else {
+    const int half = group / 2;
+    for (int j = 0; j < half; j++) {
+      const int qa = best_s == 0.0f ? 0 : (int)qround_dev(bf16f(w[j]), inv, qmax);
+      const int qb = best_s == 0.0f ? 0 : (int)qround_dev(bf16f(w[j + half]), inv, qmax);
+      out[(size_t)g * half + j] = (uint8_t)((qa + 8) | ((qb + 8) << 4));
+    }
+  }
+  const uint16_t sb = (uint16_t)(__float_as_uint(best_s) >> 16);
+  out[dbytes + 2 * g] = (uint8_t)(sb & 0xff);
+  out[dbytes + 2 * g + 1] = (uint8_t)(sb >> 8);
+  if (err_norm) {
+    atomicAdd(err_norm, err);
+    atomicAdd(err_norm + 1, norm);
+  }
+}
+
+void launch_quantize_rows(const uint16_t* src_bf16, int rows, int cols, int bits, int group, int clip, uint8_t* dst,
+                          double* err_norm, cudaStream_t s) {
+  const long long n = (long long)rows * (cols / group);
+  const int th = 128;
+  quantize_kernel<<<(unsigned)((n + th - 1) / th), th, 0, s>>>(src_bf16, rows, cols, bits, group, clip, dst, err_norm);
+  LS_CUDA(cudaGetLastError());
+}
+
+}  // namespace ls

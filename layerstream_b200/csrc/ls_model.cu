@@ -1,0 +1,1135 @@
+// Host runtime of the verify path: model loading (resident or streamed layer slots), the per-pass
+// kernel sequence (captured once per shape in a CUDA graph), the greedy speculative loop and the
+// C ABI declared in include/layerstream.h.
+//
+// Reference counterparts: model::Model (src/model.rs:16-220), provider::{ResidentProvider,
+// StreamProvider} (src/provider.rs:61-337), spec::speculative_greedy (src/spec.rs:57-152),
+// quant::quantize_model (src/quant.rs:158-251).
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <tuple>
+
+#include "layerstream.h"
+#include "ls_internal.h"
+
+using namespace ls;
+
+namespace {
+
+constexpr int kPrefillChunk = 128;  // src/model.rs:14
+constexpr int kHeadRows = 4096;     // src/provider.rs:21
+constexpr int kMaxDraft = 32;       // src/spec.rs:52
+constexpr int kMaxT = kPrefillChunk;
+
+thread_local std::string g_err;
+
+double now_s() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+// Device planes of one quantized matrix carved out of a larger allocation.
+QMat carve(uint8_t*& p, int rows, int cols, const WeightFormat& f) {
+  QMat m;
+  m.rows = rows;
+  m.rows_pad = pad32(rows);
+  m.cols = cols;
+  m.bits = f.bits;
+  m.group = f.group;
+  m.data = p;
+  p += align256(m.data_bytes());
+  m.scales = reinterpret_cast<uint16_t*>(p);
+  p += align256(m.scale_bytes());
+  return m;
+}
+
+size_t qmat_bytes(int rows, int cols, const WeightFormat& f) {
+  QMat m;
+  m.rows = rows;
+  m.rows_pad = pad32(rows);
+  m.cols = cols;
+  m.bits = f.bits;
+  m.group = f.group;
+  return align256(m.data_bytes()) + align256(m.scale_bytes());
+}
+
+struct LayerW {
+  QMat qkv, o, gu, down;
+  uint16_t* in_norm = nullptr;
+  uint16_t* post_norm = nullptr;
+  uint16_t* qkv_bias = nullptr;  // q_b | k_b | v_b
+};
+
+void check_gpu_format(const Config& c) {
+  for (const WeightFormat* f : {&c.format, &c.embed_format}) {
+    if (!f->quant()) LS_THROW(LS_ERR_ARG, "the CUDA path reads quantized (.lsq) models; bf16 weights are not supported yet");
+    if (f->group & (f->group - 1)) LS_THROW(LS_ERR_ARG, "the CUDA path needs a power-of-two group size, not " + std::to_string(f->group));
+  }
+  if (c.head_dim != 16 && c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128)
+    LS_THROW(LS_ERR_ARG, "head dimension " + std::to_string(c.head_dim) + " is not supported by the CUDA path");
+  if (c.inter % 16) LS_THROW(LS_ERR_ARG, "intermediate size must be a multiple of 16");
+}
+
+}  // namespace
+
+struct LsModel {
+  int device = 0;
+  LsqFile file;
+  Config cfg;
+  int mode = LS_MODE_RESIDENT, slots = 1;
+  size_t max_ctx = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr, copy_stream = nullptr;
+  std::vector<void*> dev_allocs;
+  std::vector<void*> host_allocs;
+
+  std::vector<LayerW> layers;  // resident: one per layer; stream: one per slot
+  QMat embed;                  // resident: the whole tiled table (also the LM head)
+  std::vector<QMat> head_slot; // stream: head chunk planes per slot
+  float* final_norm = nullptr;
+
+  // streaming
+  uint8_t* host_model = nullptr;      // pinned copy of the file's data (layers, embedding, norm)
+  const uint8_t* host_embed_dev = nullptr;  // device-visible pointer to the embedding in host_model
+  std::vector<uint8_t*> raw_slot;
+  std::vector<cudaEvent_t> ev_loaded, ev_free;
+  size_t raw_slot_bytes = 0;
+
+  // cache, tables and activations
+  uint16_t *kc = nullptr, *vc = nullptr;
+  float2* rope = nullptr;
+  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *hbuf = nullptr, *logits = nullptr;
+  ArgPart* arg_parts = nullptr;
+  unsigned *tickets = nullptr, *arg_ticket = nullptr, *att_tickets = nullptr;
+  float *partial = nullptr, *att_part = nullptr;
+  size_t partial_floats = 0, att_part_floats = 0;
+  int att_slots = 1;
+  Ctl* ctl = nullptr;
+  Ctl* ctl_host = nullptr;
+
+  std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;
+  size_t pos = 0;
+  uint64_t bytes_read = 0, wait_ns = 0, passes = 0, resident_weight_bytes = 0;
+
+  ~LsModel() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    for (auto e : ev_loaded) cudaEventDestroy(e);
+    for (auto e : ev_free) cudaEventDestroy(e);
+    for (void* p : dev_allocs) cudaFree(p);
+    for (void* p : host_allocs) cudaFreeHost(p);
+    if (stream) cudaStreamDestroy(stream);
+    if (copy_stream) cudaStreamDestroy(copy_stream);
+  }
+
+  template <class T>
+  T* dalloc(size_t n) {
+    void* p = nullptr;
+    LS_CUDA(cudaMalloc(&p, std::max<size_t>(n * sizeof(T), 16)));
+    dev_allocs.push_back(p);
+    LS_CUDA(cudaMemsetAsync(p, 0, std::max<size_t>(n * sizeof(T), 16), stream));
+    return reinterpret_cast<T*>(p);
+  }
+  template <class T>
+  T* halloc(size_t n, unsigned flags = cudaHostAllocDefault) {
+    void* p = nullptr;
+    LS_CUDA(cudaHostAlloc(&p, std::max<size_t>(n * sizeof(T), 16), flags));
+    host_allocs.push_back(p);
+    return reinterpret_cast<T*>(p);
+  }
+
+  size_t layer_plane_bytes() const {
+    const size_t h = cfg.hidden, kv = cfg.kv_dim(), I = cfg.inter;
+    return qmat_bytes((int)(h + 2 * kv), (int)h, cfg.format) + qmat_bytes((int)h, (int)h, cfg.format) +
+           qmat_bytes((int)(2 * I), (int)h, cfg.format) + qmat_bytes((int)h, (int)I, cfg.format) + align256(h * 2) * 2 +
+           align256((h + 2 * kv) * 2);
+  }
+
+  LayerW carve_layer(uint8_t*& p) {
+    const int h = (int)cfg.hidden, kv = (int)cfg.kv_dim(), I = (int)cfg.inter;
+    LayerW w;
+    w.qkv = carve(p, h + 2 * kv, h, cfg.format);
+    w.o = carve(p, h, h, cfg.format);
+    w.gu = carve(p, 2 * I, h, cfg.format);
+    w.down = carve(p, h, I, cfg.format);
+    w.in_norm = reinterpret_cast<uint16_t*>(p);
+    p += align256((size_t)h * 2);
+    w.post_norm = reinterpret_cast<uint16_t*>(p);
+    p += align256((size_t)h * 2);
+    w.qkv_bias = reinterpret_cast<uint16_t*>(p);
+    p += align256((size_t)(h + 2 * kv) * 2);
+    return w;
+  }
+
+  // Raw layer block on the device (file layout) -> tiled planes of `w`.
+  void repack_layer(const uint8_t* raw, LayerW& w, cudaStream_t s) {
+    const LayerLayout& L = file.layout;
+    const int h = (int)cfg.hidden, kv = (int)cfg.kv_dim(), I = (int)cfg.inter;
+    RepackSrc q;
+    q.nseg = 3;
+    q.seg[0] = raw + L.off[T_Q_W];
+    q.seg_rows[0] = h;
+    q.seg[1] = raw + L.off[T_K_W];
+    q.seg_rows[1] = kv;
+    q.seg[2] = raw + L.off[T_V_W];
+    q.seg_rows[2] = kv;
+    launch_repack(q, w.qkv.bits, w.qkv.group, h, const_cast<uint8_t*>(w.qkv.data), const_cast<uint16_t*>(w.qkv.scales),
+                  w.qkv.rows_pad, s);
+    RepackSrc o;
+    o.seg[0] = raw + L.off[T_O_W];
+    o.seg_rows[0] = h;
+    launch_repack(o, w.o.bits, w.o.group, h, const_cast<uint8_t*>(w.o.data), const_cast<uint16_t*>(w.o.scales), w.o.rows_pad, s);
+    RepackSrc gu;
+    gu.nseg = 2;
+    gu.interleave16 = 1;
+    gu.seg[0] = raw + L.off[T_GATE];
+    gu.seg_rows[0] = I;
+    gu.seg[1] = raw + L.off[T_UP];
+    gu.seg_rows[1] = I;
+    launch_repack(gu, w.gu.bits, w.gu.group, h, const_cast<uint8_t*>(w.gu.data), const_cast<uint16_t*>(w.gu.scales),
+                  w.gu.rows_pad, s);
+    RepackSrc d;
+    d.seg[0] = raw + L.off[T_DOWN];
+    d.seg_rows[0] = h;
+    launch_repack(d, w.down.bits, w.down.group, I, const_cast<uint8_t*>(w.down.data), const_cast<uint16_t*>(w.down.scales),
+                  w.down.rows_pad, s);
+    LS_CUDA(cudaMemcpyAsync(w.in_norm, raw + L.off[T_INPUT_NORM], (size_t)h * 2, cudaMemcpyDeviceToDevice, s));
+    LS_CUDA(cudaMemcpyAsync(w.post_norm, raw + L.off[T_POST_NORM], (size_t)h * 2, cudaMemcpyDeviceToDevice, s));
+    LS_CUDA(cudaMemcpyAsync(w.qkv_bias, raw + L.off[T_Q_B], (size_t)h * 2, cudaMemcpyDeviceToDevice, s));
+    LS_CUDA(cudaMemcpyAsync(w.qkv_bias + h, raw + L.off[T_K_B], (size_t)kv * 2, cudaMemcpyDeviceToDevice, s));
+    LS_CUDA(cudaMemcpyAsync(w.qkv_bias + h + kv, raw + L.off[T_V_B], (size_t)kv * 2, cudaMemcpyDeviceToDevice, s));
+  }
+
+  void repack_embed_rows(const uint8_t* raw_rows, int first, int rows, QMat& dst, cudaStream_t s) {
+    // dst holds the whole table (resident) or one chunk (stream, first == 0)
+    const int nch = dst.chunks(), ng = dst.groups();
+    RepackSrc e;
+    e.seg[0] = raw_rows;
+    e.seg_rows[0] = rows;
+    uint8_t* d = const_cast<uint8_t*>(dst.data) + (size_t)(first / 32) * nch * 512;
+    uint16_t* sc = const_cast<uint16_t*>(dst.scales) + (size_t)(first / 32) * ng * 32;
+    launch_repack(e, dst.bits, dst.group, dst.cols, d, sc, pad32(rows), s);
+  }
+
+  void open(const char* path, int dev, uint64_t mctx, int md, int nslots) {
+    file = LsqFile::open(path);
+    cfg = file.cfg;
+    check_gpu_format(cfg);
+    device = dev;
+    LS_CUDA(cudaSetDevice(device));
+    if (mctx == 0) LS_THROW(LS_ERR_ARG, "max_ctx must be positive");
+    max_ctx = mctx;
+    mode = md;
+    if (mode != LS_MODE_RESIDENT && mode != LS_MODE_STREAM) LS_THROW(LS_ERR_ARG, "mode must be resident or stream");
+    slots = std::max(1, nslots);
+    LS_CUDA(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device));
+    LS_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    LS_CUDA(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking));
+
+    const size_t h = cfg.hidden, kv = cfg.kv_dim(), I = cfg.inter, V = cfg.vocab, L = cfg.layers;
+    const size_t lt = file.layout.total, rb = cfg.embed_row_bytes();
+    int fd = ::open(path, O_RDONLY);
+    if (fd < 0) LS_THROW(LS_ERR_IO, std::string(path) + ": cannot open");
+    struct FdGuard {
+      int fd;
+      ~FdGuard() { ::close(fd); }
+    } guard{fd};
+
+    // final norm (src/weights.rs:408-411): bf16 -> f32, resident in both modes
+    std::vector<uint16_t> nb(h);
+    pread_all(fd, nb.data(), h * 2, file.norm_start);
+    std::vector<float> nf(h);
+    for (size_t i = 0; i < h; i++) {
+      uint32_t u = (uint32_t)nb[i] << 16;
+      std::memcpy(&nf[i], &u, 4);
+    }
+    final_norm = dalloc<float>(h);
+    LS_CUDA(cudaMemcpyAsync(final_norm, nf.data(), h * 4, cudaMemcpyHostToDevice, stream));
+    LS_CUDA(cudaStreamSynchronize(stream));
+
+    if (mode == LS_MODE_RESIDENT) {
+      const size_t per = layer_plane_bytes();
+      uint8_t* base = dalloc<uint8_t>(per * L + qmat_bytes((int)V, (int)h, cfg.embed_format));
+      resident_weight_bytes = per * L + qmat_bytes((int)V, (int)h, cfg.embed_format);
+      uint8_t* p = base;
+      for (size_t l = 0; l < L; l++) layers.push_back(carve_layer(p));
+      embed = carve(p, (int)V, (int)h, cfg.embed_format);
+      // load through two pinned staging buffers and one device raw buffer
+      const size_t chunk_rows = std::min<size_t>(kHeadRows, V);
+      const size_t stage = std::max(lt, chunk_rows * rb);
+      uint8_t* hst[2] = {halloc<uint8_t>(stage), halloc<uint8_t>(stage)};
+      uint8_t* raw[2] = {dalloc<uint8_t>(stage), dalloc<uint8_t>(stage)};
+      cudaEvent_t done[2];
+      LS_CUDA(cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming));
+      LS_CUDA(cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming));
+      bool used[2] = {false, false};
+      int k = 0;
+      auto step = [&](uint64_t off, size_t n, const std::function<void(const uint8_t*)>& after) {
+        if (used[k]) LS_CUDA(cudaEventSynchronize(done[k]));
+        pread_all(fd, hst[k], n, off);
+        LS_CUDA(cudaMemcpyAsync(raw[k], hst[k], n, cudaMemcpyHostToDevice, stream));
+        after(raw[k]);
+        LS_CUDA(cudaEventRecord(done[k], stream));
+        used[k] = true;
+        k ^= 1;
+      };
+      for (size_t l = 0; l < L; l++)
+        step(file.data_start + l * lt, lt, [&](const uint8_t* r) { repack_layer(r, layers[l], stream); });
+      for (size_t first = 0; first < V; first += chunk_rows) {
+        const size_t rows = std::min(chunk_rows, V - first);
+        step(file.embed_start + first * rb, rows * rb, [&](const uint8_t* r) { repack_embed_rows(r, (int)first, (int)rows, embed, stream); });
+      }
+      LS_CUDA(cudaStreamSynchronize(stream));
+      cudaEventDestroy(done[0]);
+      cudaEventDestroy(done[1]);
+    } else {
+      // pinned, device-mapped host copy of the whole model; HBM holds `slots` layer-sized slots
+      const size_t data_bytes = (size_t)(file.norm_start - file.data_start);
+      host_model = halloc<uint8_t>(data_bytes, cudaHostAllocMapped);
+      const size_t step_bytes = 64ull << 20;
+      for (size_t off = 0; off < data_bytes; off += step_bytes)
+        pread_all(fd, host_model + off, std::min(step_bytes, data_bytes - off), file.data_start + off);
+      void* dp = nullptr;
+      LS_CUDA(cudaHostGetDevicePointer(&dp, host_model + (file.embed_start - file.data_start), 0));
+      host_embed_dev = reinterpret_cast<const uint8_t*>(dp);
+      const size_t chunk_rows = std::min<size_t>(kHeadRows, V);
+      raw_slot_bytes = std::max(lt, chunk_rows * rb);
+      const size_t per = layer_plane_bytes();
+      const size_t head_per = qmat_bytes((int)chunk_rows, (int)h, cfg.embed_format);
+      for (int s = 0; s < slots; s++) {
+        raw_slot.push_back(dalloc<uint8_t>(raw_slot_bytes));
+        uint8_t* p = dalloc<uint8_t>(per);
+        layers.push_back(carve_layer(p));
+        uint8_t* hp = dalloc<uint8_t>(head_per);
+        head_slot.push_back(carve(hp, (int)chunk_rows, (int)h, cfg.embed_format));
+        cudaEvent_t a, b;
+        LS_CUDA(cudaEventCreateWithFlags(&a, cudaEventDisableTiming));
+        LS_CUDA(cudaEventCreateWithFlags(&b, cudaEventDisableTiming));
+        ev_loaded.push_back(a);
+        ev_free.push_back(b);
+      }
+      resident_weight_bytes = (size_t)slots * (raw_slot_bytes + per + head_per);
+    }
+
+    // KV cache [L][kv_heads][max_ctx][hd] f16 and the RoPE table, computed here with the same float
+    // steps as src/model.rs:62-65 and src/kernels.rs:242-252 (so the angles match the CPU path)
+    kc = dalloc<uint16_t>(L * kv * max_ctx);
+    vc = dalloc<uint16_t>(L * kv * max_ctx);
+    const size_t half = cfg.head_dim / 2;
+    std::vector<float> inv(half);
+    for (size_t i = 0; i < half; i++)
+      inv[i] = (float)(1.0 / std::pow((double)cfg.rope_theta, (double)(2 * i) / (double)cfg.head_dim));
+    std::vector<float2> tab(max_ctx * half);
+    for (size_t p = 0; p < max_ctx; p++)
+      for (size_t i = 0; i < half; i++) {
+        float ang = (float)p * inv[i];
+        tab[p * half + i] = make_float2(cosf(ang), sinf(ang));
+      }
+    rope = dalloc<float2>(max_ctx * half);
+    LS_CUDA(cudaMemcpyAsync(rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, stream));
+
+    // activations for up to one prefill chunk
+    x = dalloc<float>(kMaxT * h);
+    qkv = dalloc<float>(kMaxT * (h + 2 * kv));
+    attn = dalloc<float>(kMaxT * h);
+    hbuf = dalloc<float>(kMaxT * I);
+    logits = dalloc<float>((size_t)(kMaxDraft + 1) * V);
+    const size_t vtiles = (size_t)pad32((int)V) / 32;
+    arg_parts = dalloc<ArgPart>(vtiles * kMaxT);
+    const size_t max_tiles = std::max<size_t>({(size_t)pad32((int)(h + 2 * kv)), (size_t)2 * I, h}) / 32;
+    tickets = dalloc<unsigned>(max_tiles * (kMaxT / 16 + 1));
+    partial_floats = (size_t)max_tiles * 32 * 16 * 32 * (kMaxT / 16 + 1);
+    partial = dalloc<float>(partial_floats);
+    arg_ticket = dalloc<unsigned>(1);
+    att_slots = (int)std::max<size_t>(1, std::min<size_t>(16, (max_ctx + 63) / 64));
+    att_part_floats = cfg.heads * (size_t)att_slots * kMaxT * (cfg.head_dim + 2);
+    att_part = dalloc<float>(att_part_floats);
+    att_tickets = dalloc<unsigned>(cfg.heads);
+    ctl = dalloc<Ctl>(1);
+    ctl_host = halloc<Ctl>(1);
+    std::memset(ctl_host, 0, sizeof(Ctl));
+    LS_CUDA(cudaStreamSynchronize(stream));
+  }
+
+  // ---- the pass --------------------------------------------------------------------------------
+
+  int pick_ksplit(const QMat& w, int M) const {
+    const int tiles = w.rows_pad / 32;
+    const int nz = (M + 15) / 16;
+    const int U = (w.bits == 4 && w.group >= 32) ? w.group / 32 : 1;
+    const int units = w.chunks() / U;
+    const int by_work = std::max(1, units * U / 16);  // keep >= 16 chunks per CTA
+    const int want = std::max(1, (2 * num_sms) / std::max(1, tiles * nz));
+    return std::max(1, std::min({want, by_work, units, 32}));
+  }
+
+  void gemv(const QMat& w, const float* xin, int x_stride, int M, int epi, float* y, int y_stride, const uint16_t* norm_bf16,
+            const float* norm_f32, const uint16_t* bias, cudaStream_t s) {
+    GemvLaunch g;
+    g.w = w;
+    g.x = xin;
+    g.x_stride = x_stride;
+    g.M = M;
+    g.norm_bf16 = norm_bf16;
+    g.norm_f32 = norm_f32;
+    g.eps = cfg.eps;
+    g.epi = epi;
+    g.y = y;
+    g.y_stride = y_stride;
+    g.bias = bias;
+    g.ksplit = (epi == EPI_ARGMAX) ? 1 : pick_ksplit(w, M);
+    g.partial = partial;
+    g.tickets = tickets;
+    launch_gemv(g, s);
+  }
+
+  void head(const QMat& w, const float* xin, int n, bool want_logits, int row_offset, int n_valid, int part_tile_offset,
+            int finalize, int n_part_tiles, cudaStream_t s) {
+    GemvLaunch g;
+    g.w = w;
+    g.x = xin;
+    g.x_stride = (int)cfg.hidden;
+    g.M = n;
+    g.norm_f32 = final_norm;
+    g.eps = cfg.eps;
+    g.epi = EPI_ARGMAX;
+    g.arg_parts = arg_parts;
+    g.arg_ticket = arg_ticket;
+    g.ctl = ctl;
+    g.n_valid_rows = n_valid;
+    g.row_offset = row_offset;
+    g.part_tile_offset = part_tile_offset;
+    g.finalize = finalize;
+    g.n_part_tiles = n_part_tiles;
+    g.logits = want_logits ? logits : nullptr;
+    g.logits_stride = (int)cfg.vocab;
+    launch_gemv(g, s);
+  }
+
+  void layer_compute(const LayerW& W, size_t l, int T, cudaStream_t s) {
+    const int h = (int)cfg.hidden, kv = (int)cfg.kv_dim(), I = (int)cfg.inter;
+    gemv(W.qkv, x, h, T, EPI_BIAS_STORE, qkv, h + 2 * kv, W.in_norm, nullptr, W.qkv_bias, s);
+    AttnLaunch a;
+    a.qkv = qkv;
+    a.qkv_stride = h + 2 * kv;
+    a.k_cache = kc + l * cfg.kv_dim() * max_ctx;
+    a.v_cache = vc + l * cfg.kv_dim() * max_ctx;
+    a.rope = rope;
+    a.ctl = ctl;
+    a.out = attn;
+    a.part = att_part;
+    a.tickets = att_tickets;
+    a.heads = (int)cfg.heads;
+    a.kv_heads = (int)cfg.kv_heads;
+    a.hd = (int)cfg.head_dim;
+    a.max_ctx = (int)max_ctx;
+    a.M = T;
+    a.max_splits = att_slots;
+    launch_attention(a, s);
+    gemv(W.o, attn, h, T, EPI_RESID, x, h, nullptr, nullptr, nullptr, s);
+    gemv(W.gu, x, h, T, EPI_SWIGLU, hbuf, I, W.post_norm, nullptr, nullptr, s);
+    gemv(W.down, hbuf, I, T, EPI_RESID, x, h, nullptr, nullptr, nullptr, s);
+  }
+
+  // Enqueues one pass over T tokens already in ctl->tokens (pos0 in ctl). n_logits > 0 runs the
+  // LM head on the last n_logits positions with the device argmax (and the acceptance rule when
+  // ctl->mode == 1); otherwise only advances pos0.
+  void enqueue_pass(int T, int n_logits, bool want_logits) {
+    const int h = (int)cfg.hidden;
+    const size_t V = cfg.vocab;
+    if (mode == LS_MODE_RESIDENT) {
+      launch_embed(embed, ctl, x, h, T, stream);
+      for (size_t l = 0; l < cfg.layers; l++) layer_compute(layers[l], l, T, stream);
+      if (n_logits > 0) {
+        head(embed, x + (size_t)(T - n_logits) * h, n_logits, want_logits, 0, (int)V, 0, 1, 0, stream);
+      } else {
+        launch_advance(ctl, stream);
+      }
+      return;
+    }
+    // streaming: items are layers 0..L-1 then head chunks; each slot is refilled by a copy on the
+    // side stream once the compute that used it has finished (src/provider.rs:234-268)
+    launch_embed_raw(host_embed_dev, cfg.embed_row_bytes(), cfg.embed_format.bits, cfg.embed_format.group, ctl, x, h,
+                     (int)V, T, stream);
+    bytes_read += (uint64_t)T * cfg.embed_row_bytes();
+    const size_t L = cfg.layers;
+    const size_t chunk_rows = std::min<size_t>(kHeadRows, V);
+    const size_t nchunks = n_logits > 0 ? (V + chunk_rows - 1) / chunk_rows : 0;
+    const size_t items = L + nchunks;
+    const size_t lt = file.layout.total, rb = cfg.embed_row_bytes();
+    size_t issued = 0;
+    auto issue = [&](size_t it) {
+      const int s = (int)(it % slots);
+      LS_CUDA(cudaStreamWaitEvent(copy_stream, ev_free[s], 0));
+      const uint8_t* src;
+      size_t n;
+      if (it < L) {
+        src = host_model + it * lt;
+        n = lt;
+      } else {
+        const size_t c = it - L, first = c * chunk_rows, rows = std::min(chunk_rows, V - first);
+        src = host_model + (file.embed_start - file.data_start) + first * rb;
+        n = rows * rb;
+      }
+      LS_CUDA(cudaMemcpyAsync(raw_slot[s], src, n, cudaMemcpyHostToDevice, copy_stream));
+      LS_CUDA(cudaEventRecord(ev_loaded[s], copy_stream));
+      bytes_read += n;
+    };
+    const int vtiles_total = pad32((int)V) / 32;
+    (void)vtiles_total;
+    int part_tiles = 0;
+    for (size_t it = 0; it < items; it++) {
+      while (issued < items && issued < it + (size_t)slots) issue(issued++);
+      const int s = (int)(it % slots);
+      LS_CUDA(cudaStreamWaitEvent(stream, ev_loaded[s], 0));
+      if (it < L) {
+        repack_layer(raw_slot[s], layers[s], stream);
+        LS_CUDA(cudaEventRecord(ev_free[s], stream));  // the raw slot may be refilled now
+        layer_compute(layers[s], it, T, stream);
+      } else {
+        const size_t c = it - L, first = c * chunk_rows, rows = std::min(chunk_rows, V - first);
+        QMat hq = head_slot[s];
+        hq.rows = (int)rows;
+        hq.rows_pad = pad32((int)rows);
+        repack_embed_rows(raw_slot[s], 0, (int)rows, hq, stream);
+        LS_CUDA(cudaEventRecord(ev_free[s], stream));
+        head(hq, x + (size_t)(T - n_logits) * h, n_logits, want_logits, (int)first, (int)rows, part_tiles, 0, 0, stream);
+        part_tiles += hq.rows_pad / 32;
+      }
+    }
+    if (n_logits > 0) launch_argmax_finalize(arg_parts, part_tiles, n_logits, ctl, stream);
+    else launch_advance(ctl, stream);
+  }
+
+  void run_pass(int T, int n_logits, bool want_logits) {
+    passes++;
+    if (mode != LS_MODE_RESIDENT) {
+      enqueue_pass(T, n_logits, want_logits);
+      return;
+    }
+    auto key = std::make_tuple(T, n_logits, (int)want_logits);
+    auto it = graphs.find(key);
+    if (it == graphs.end()) {
+      cudaGraph_t graph;
+      LS_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+      try {
+        enqueue_pass(T, n_logits, want_logits);
+      } catch (...) {
+        cudaStreamEndCapture(stream, &graph);
+        throw;
+      }
+      LS_CUDA(cudaStreamEndCapture(stream, &graph));
+      cudaGraphExec_t exec;
+      LS_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+      cudaGraphDestroy(graph);
+      it = graphs.emplace(key, exec).first;
+    }
+    LS_CUDA(cudaGraphLaunch(it->second, stream));
+  }
+
+  // ---- host API --------------------------------------------------------------------------------
+
+  void check_request(const uint32_t* ids, uint64_t n) const {
+    if (n == 0) LS_THROW(LS_ERR_ARG, "no tokens to process");
+    if (pos + n > max_ctx)
+      LS_THROW(LS_ERR_ARG, "context is full: " + std::to_string(pos) + " cached + " + std::to_string(n) +
+                               " new tokens exceeds the limit of " + std::to_string(max_ctx));
+    for (uint64_t i = 0; i < n; i++)
+      if (ids[i] >= cfg.vocab) LS_THROW(LS_ERR_ARG, "token id " + std::to_string(ids[i]) + " is outside the vocabulary");
+  }
+
+  void push_ctl(int T, int n_logits, int md, const uint32_t* ids) {
+    ctl_host->pos0 = (int32_t)pos;
+    ctl_host->M = T;
+    ctl_host->n_logits = n_logits;
+    ctl_host->mode = md;
+    std::memcpy(ctl_host->tokens, ids, (size_t)T * 4);
+    ctl_host->err = 0;
+    LS_CUDA(cudaMemcpyAsync(ctl, ctl_host, sizeof(Ctl), cudaMemcpyHostToDevice, stream));
+  }
+
+  void fetch_result() {
+    LS_CUDA(cudaMemcpyAsync(&ctl_host->argmax, &ctl->argmax, sizeof(Ctl) - offsetof(Ctl, argmax), cudaMemcpyDeviceToHost, stream));
+    LS_CUDA(cudaStreamSynchronize(stream));
+    if (ctl_host->err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
+  }
+
+  // src/model.rs:111-119
+  uint32_t forward(const uint32_t* ids, uint64_t n, float* logits_out) {
+    check_request(ids, n);
+    const uint64_t nchunks = (n + kPrefillChunk - 1) / kPrefillChunk;
+    uint32_t tok = 0;
+    for (uint64_t c = 0; c < nchunks; c++) {
+      const uint64_t a = c * kPrefillChunk, b = std::min<uint64_t>(n, a + kPrefillChunk);
+      const bool last = c + 1 == nchunks;
+      push_ctl((int)(b - a), last ? 1 : 0, 0, ids + a);
+      run_pass((int)(b - a), last ? 1 : 0, last && logits_out != nullptr);
+      if (last && logits_out)
+        LS_CUDA(cudaMemcpyAsync(logits_out, logits, cfg.vocab * 4, cudaMemcpyDeviceToHost, stream));
+      fetch_result();
+      pos += b - a;
+      tok = ctl_host->next;
+    }
+    return tok;
+  }
+
+  // src/model.rs:124-133
+  void forward_multi(const uint32_t* ids, uint64_t t, uint64_t n, float* logits_out) {
+    check_request(ids, t);
+    if (n == 0 || n > t) LS_THROW(LS_ERR_ARG, "asked for logits at " + std::to_string(n) + " positions of " + std::to_string(t) + " tokens");
+    if (t > (uint64_t)kPrefillChunk) LS_THROW(LS_ERR_ARG, "forward_multi takes at most 128 tokens at a time");
+    if (n > (uint64_t)kMaxDraft + 1) LS_THROW(LS_ERR_ARG, "forward_multi returns logits for at most 33 positions");
+    push_ctl((int)t, (int)n, 0, ids);
+    run_pass((int)t, (int)n, logits_out != nullptr);
+    if (logits_out) LS_CUDA(cudaMemcpyAsync(logits_out, logits, n * cfg.vocab * 4, cudaMemcpyDeviceToHost, stream));
+    fetch_result();
+    pos += t;
+  }
+
+  // the verify step of src/spec.rs:110-139
+  void verify(const uint32_t* block, uint64_t n, uint32_t* m_out, uint32_t* next_out) {
+    check_request(block, n);
+    if (n > (uint64_t)kMaxDraft + 1) LS_THROW(LS_ERR_ARG, "a verify block holds at most 33 tokens");
+    push_ctl((int)n, (int)n, 1, block);
+    run_pass((int)n, (int)n, false);
+    fetch_result();
+    pos += (size_t)ctl_host->m + 1;
+    *m_out = (uint32_t)ctl_host->m;
+    *next_out = ctl_host->next;
+  }
+
+  void truncate(uint64_t p) {
+    if (p > pos) LS_THROW(LS_ERR_ARG, "cannot truncate to " + std::to_string(p) + ": only " + std::to_string(pos) + " tokens are cached");
+    pos = p;
+  }
+};
+
+// ------------------------------------------------------------------------------------------------
+// Greedy speculative decoding (src/spec.rs:57-152)
+// ------------------------------------------------------------------------------------------------
+
+namespace {
+
+// Prompt-lookup drafter (an addition to the reference): proposes the tokens that followed the most
+// recent earlier occurrence of the longest suffix n-gram (n = 3, 2, 1) of the history.
+std::vector<uint32_t> lookup_draft(const std::vector<uint32_t>& hist, size_t kk) {
+  std::vector<uint32_t> out;
+  if (kk == 0 || hist.size() < 2) return out;
+  for (size_t n = std::min<size_t>(3, hist.size() - 1); n >= 1; n--) {
+    const size_t tail = hist.size() - n;
+    for (size_t s = tail; s-- > 0;) {
+      bool ok = true;
+      for (size_t j = 0; j < n && ok; j++) ok = hist[s + j] == hist[tail + j];
+      if (!ok) continue;
+      for (size_t j = s + n; j < hist.size() && out.size() < kk; j++) out.push_back(hist[j]);
+      return out;
+    }
+  }
+  return out;
+}
+
+}  // namespace
+
+static void speculative_greedy(LsModel& target, LsModel* draft, const uint32_t* prompt, uint64_t plen, uint64_t max_new,
+                               uint64_t k, const uint32_t* eos, uint64_t neos, uint32_t* out_tokens, uint64_t* out_len,
+                               LsSpecStats* st) {
+  if (k == 0 || k > (uint64_t)kMaxDraft) LS_THROW(LS_ERR_ARG, "k must be between 1 and 32, not " + std::to_string(k));
+  if (plen == 0 || max_new == 0) LS_THROW(LS_ERR_ARG, "need a prompt and at least one token to generate");
+  if (target.pos != 0 || (draft && draft->pos != 0)) LS_THROW(LS_ERR_ARG, "both models must start with an empty cache");
+  if (draft && draft->cfg.vocab != target.cfg.vocab) LS_THROW(LS_ERR_ARG, "the draft and the target must share a vocabulary");
+  const uint64_t need = plen + max_new + k;
+  if (need > target.max_ctx || (draft && need > draft->max_ctx))
+    LS_THROW(LS_ERR_ARG, "prompt + max_new + k = " + std::to_string(need) + " tokens exceed the context limit");
+  auto is_eos = [&](uint32_t t) {
+    for (uint64_t i = 0; i < neos; i++)
+      if (eos[i] == t) return true;
+    return false;
+  };
+  std::memset(st, 0, sizeof *st);
+  const double t0 = now_s();
+  uint32_t a = target.forward(prompt, plen, nullptr);
+  if (draft) draft->forward(prompt, plen, nullptr);
+  st->first_secs = now_s() - t0;
+  std::vector<uint32_t> out{a};
+  std::vector<uint32_t> hist(prompt, prompt + plen);
+  hist.push_back(a);
+  bool stop = is_eos(a);
+  const double td = now_s();
+  while (!stop && out.size() < max_new) {
+    const uint64_t kk = std::min<uint64_t>(k, max_new - out.size() - 1);
+    double ts = now_s();
+    std::vector<uint32_t> drafts;
+    if (draft) {
+      uint32_t cur = a;
+      for (uint64_t i = 0; i < kk; i++) {
+        cur = draft->forward(&cur, 1, nullptr);
+        st->draft_forwards++;
+        drafts.push_back(cur);
+      }
+    } else {
+      drafts = lookup_draft(hist, kk);
+    }
+    st->draft_secs += now_s() - ts;
+    std::vector<uint32_t> block{a};
+    block.insert(block.end(), drafts.begin(), drafts.end());
+    const size_t p = target.pos;
+    ts = now_s();
+    uint32_t m = 0, next = 0;
+    target.verify(block.data(), block.size(), &m, &next);
+    st->target_secs += now_s() - ts;
+    st->target_passes++;
+    st->drafted += drafts.size();
+    st->accepted += m;
+    for (uint32_t i = 0; i <= m; i++) {
+      const uint32_t tok = i < m ? drafts[i] : next;
+      out.push_back(tok);
+      hist.push_back(tok);
+      if (is_eos(tok) || out.size() == max_new) {
+        stop = true;
+        break;
+      }
+    }
+    if (draft) {
+      const size_t want = p + m + 1;
+      if (draft->pos > want) {
+        draft->truncate(want);
+      } else if (draft->pos < want) {
+        ts = now_s();
+        const size_t from = draft->pos - p;
+        draft->forward(block.data() + from, m + 1 - from, nullptr);
+        st->draft_forwards++;
+        st->draft_secs += now_s() - ts;
+      }
+    }
+    a = next;
+  }
+  st->decode_secs = now_s() - td;
+  std::memcpy(out_tokens, out.data(), out.size() * 4);
+  *out_len = out.size();
+}
+
+// ------------------------------------------------------------------------------------------------
+// Quantizer (src/quant.rs:158-251): the group quantization runs on the GPU, the file layout on the host
+// ------------------------------------------------------------------------------------------------
+
+static double quantize_model(const char* src_dir, const char* out_path, WeightFormat fmt, WeightFormat efmt, int clip, int dev) {
+  if (!fmt.quant()) LS_THROW(LS_ERR_ARG, "quantize needs a quantized target format");
+  if (!efmt.quant()) LS_THROW(LS_ERR_ARG, "the embedding table needs a quantized format too");
+  LS_CUDA(cudaSetDevice(dev));
+  SafetensorsModel src = SafetensorsModel::open(src_dir);
+  if (src.cfg.format.quant()) LS_THROW(LS_ERR_ARG, "the source model is already quantized");
+  const std::string qtext = inject_quant(src.config_text, fmt, efmt);
+  const Config q = parse_config(qtext);
+  const LayerLayout dst = layer_layout_for(q);
+  const size_t rb_out = q.embed_row_bytes(), rb_in = src.cfg.hidden * 2;
+  int ofd = ::open(out_path, O_WRONLY | O_CREAT | O_EXCL, 0644);
+  if (ofd < 0) LS_THROW(LS_ERR_IO, std::string(out_path) + ": cannot create (it must not exist already)");
+  int ifd = ::open(src.file.c_str(), O_RDONLY);
+  if (ifd < 0) {
+    ::close(ofd);
+    LS_THROW(LS_ERR_IO, src.file + ": cannot open");
+  }
+  cudaStream_t s;
+  LS_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  const size_t erows = std::min<size_t>(kHeadRows, q.vocab);
+  const size_t in_max = std::max(src.layout.total, erows * rb_in), out_max = std::max(dst.total, erows * rb_out);
+  uint8_t *din = nullptr, *dout = nullptr;
+  double* den = nullptr;
+  std::vector<uint8_t> hin(in_max), hout(out_max);
+  double result = 0;
+  try {
+    LS_CUDA(cudaMalloc(&din, in_max));
+    LS_CUDA(cudaMalloc(&dout, out_max));
+    LS_CUDA(cudaMalloc(&den, 16));
+    LS_CUDA(cudaMemsetAsync(den, 0, 16, s));
+    auto wr = [&](const void* p, size_t n) {
+      const char* b = (const char*)p;
+      while (n) {
+        ssize_t w = ::write(ofd, b, n);
+        if (w <= 0) LS_THROW(LS_ERR_IO, "write failed");
+        b += w;
+        n -= (size_t)w;
+      }
+    };
+    const std::string hb = lsq_header_bytes(qtext, dst.total, q.vocab * rb_out, q.hidden * 2);
+    wr(hb.data(), hb.size());
+    for (size_t l = 0; l < q.layers; l++) {
+      pread_all(ifd, hin.data(), src.layout.total, src.layer_start[l]);
+      LS_CUDA(cudaMemcpyAsync(din, hin.data(), src.layout.total, cudaMemcpyHostToDevice, s));
+      for (int sl = 0; sl < N_SLOTS; sl++) {
+        size_t rows, cols;
+        if (matrix_shape(sl, q, &rows, &cols))
+          launch_quantize_rows(reinterpret_cast<const uint16_t*>(din + src.layout.off[sl]), (int)rows, (int)cols, fmt.bits,
+                               fmt.group, clip, dout + dst.off[sl], den, s);
+      }
+      LS_CUDA(cudaMemcpyAsync(hout.data(), dout, dst.total, cudaMemcpyDeviceToHost, s));
+      LS_CUDA(cudaStreamSynchronize(s));
+      for (int sl = 0; sl < N_SLOTS; sl++) {
+        size_t rows, cols;
+        if (!matrix_shape(sl, q, &rows, &cols)) std::memcpy(hout.data() + dst.off[sl], hin.data() + src.layout.off[sl], dst.len[sl]);
+      }
+      wr(hout.data(), dst.total);
+    }
+    for (size_t first = 0; first < q.vocab; first += erows) {
+      const size_t n = std::min(erows, q.vocab - first);
+      pread_all(ifd, hin.data(), n * rb_in, src.embed_start + first * rb_in);
+      LS_CUDA(cudaMemcpyAsync(din, hin.data(), n * rb_in, cudaMemcpyHostToDevice, s));
+      launch_quantize_rows(reinterpret_cast<const uint16_t*>(din), (int)n, (int)q.hidden, efmt.bits, efmt.group, clip, dout, den, s);
+      LS_CUDA(cudaMemcpyAsync(hout.data(), dout, n * rb_out, cudaMemcpyDeviceToHost, s));
+      LS_CUDA(cudaStreamSynchronize(s));
+      wr(hout.data(), n * rb_out);
+    }
+    std::vector<uint8_t> nb(src.norm_len);
+    pread_all(ifd, nb.data(), nb.size(), src.norm_start);
+    wr(nb.data(), nb.size());
+    double en[2];
+    LS_CUDA(cudaMemcpy(en, den, 16, cudaMemcpyDeviceToHost));
+    result = en[1] > 0 ? std::sqrt(en[0] / en[1]) : 0.0;
+  } catch (...) {
+    cudaFree(din);
+    cudaFree(dout);
+    cudaFree(den);
+    cudaStreamDestroy(s);
+    ::close(ifd);
+    ::close(ofd);
+    ::unlink(out_path);
+    throw;
+  }
+  cudaFree(din);
+  cudaFree(dout);
+  cudaFree(den);
+  cudaStreamDestroy(s);
+  ::close(ifd);
+  if (::close(ofd) != 0) LS_THROW(LS_ERR_IO, "close failed");
+  return result;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Kernel-level GEMV entry points
+// ------------------------------------------------------------------------------------------------
+
+struct LsQWeights {
+  int device = 0;
+  QMat w;
+  void* mem = nullptr;
+  float* partial = nullptr;
+  unsigned* tickets = nullptr;
+  int num_sms = 148;
+  ~LsQWeights() {
+    cudaFree(mem);
+    cudaFree(partial);
+    cudaFree(tickets);
+  }
+};
+
+static void qweights_upload(LsQWeights* q, int dev, int bits, int group, const uint8_t* raw, uint64_t rows, uint64_t cols) {
+  WeightFormat f;
+  f.bits = bits;
+  f.group = group;
+  if ((bits != 8 && bits != 4) || group < 16 || group > 256 || (group & (group - 1)) || cols % (uint64_t)group || cols % 32)
+    LS_THROW(LS_ERR_ARG, "unsupported GEMV format or shape");
+  q->device = dev;
+  LS_CUDA(cudaSetDevice(dev));
+  LS_CUDA(cudaDeviceGetAttribute(&q->num_sms, cudaDevAttrMultiProcessorCount, dev));
+  const size_t bytes = qmat_bytes((int)rows, (int)cols, f);
+  LS_CUDA(cudaMalloc(&q->mem, bytes));
+  uint8_t* p = reinterpret_cast<uint8_t*>(q->mem);
+  q->w = carve(p, (int)rows, (int)cols, f);
+  const size_t rb = f.row_bytes(cols);
+  uint8_t* draw = nullptr;
+  LS_CUDA(cudaMalloc(&draw, rows * rb));
+  LS_CUDA(cudaMemcpy(draw, raw, rows * rb, cudaMemcpyHostToDevice));
+  RepackSrc s;
+  s.seg[0] = draw;
+  s.seg_rows[0] = (int)rows;
+  launch_repack(s, bits, group, (int)cols, const_cast<uint8_t*>(q->w.data), const_cast<uint16_t*>(q->w.scales), q->w.rows_pad, 0);
+  LS_CUDA(cudaDeviceSynchronize());
+  cudaFree(draw);
+  const size_t tiles = q->w.rows_pad / 32;
+  LS_CUDA(cudaMalloc(&q->partial, tiles * 32 * 16 * 32 * 4 * 3));
+  LS_CUDA(cudaMalloc(&q->tickets, tiles * 4 * 3));
+  LS_CUDA(cudaMemset(q->tickets, 0, tiles * 4 * 3));
+}
+
+static void qgemv_device(const LsQWeights* q, const float* x, uint64_t M, float* y, cudaStream_t s) {
+  if (M == 0 || M > 48) LS_THROW(LS_ERR_ARG, "the GEMV takes 1..48 token rows");
+  GemvLaunch g;
+  g.w = q->w;
+  g.x = x;
+  g.x_stride = q->w.cols;
+  g.M = (int)M;
+  g.epi = EPI_STORE;
+  g.y = y;
+  g.y_stride = q->w.rows;
+  const int tiles = q->w.rows_pad / 32, nz = ((int)M + 15) / 16;
+  const int U = (q->w.bits == 4 && q->w.group >= 32) ? q->w.group / 32 : 1;
+  const int units = q->w.chunks() / U;
+  g.ksplit = std::max(1, std::min({(2 * q->num_sms) / std::max(1, tiles * nz), std::max(1, units * U / 16), units, 32}));
+  g.partial = q->partial;
+  g.tickets = q->tickets;
+  launch_gemv(g, s);
+}
+
+// ------------------------------------------------------------------------------------------------
+// C ABI
+// ------------------------------------------------------------------------------------------------
+
+template <class F>
+static int guard(F&& f) {
+  try {
+    f();
+    return LS_OK;
+  } catch (const ls::Error& e) {
+    g_err = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return LS_ERR_ARG;
+  }
+}
+
+#define NEED(p)                                                  \
+  do {                                                           \
+    if (!(p)) LS_THROW(LS_ERR_ARG, #p " must not be NULL");      \
+  } while (0)
+
+extern "C" {
+
+int ls_last_error(char* buf, size_t cap) {
+  if (buf && cap) std::snprintf(buf, cap, "%s", g_err.c_str());
+  return (int)g_err.size();
+}
+
+int ls_model_open(const char* path, int device, uint64_t max_ctx, int mode, int slots, LsModel** out) {
+  return guard([&] {
+    NEED(path);
+    NEED(out);
+    *out = nullptr;
+    std::unique_ptr<LsModel> m(new LsModel);
+    m->open(path, device, max_ctx, mode, slots);
+    *out = m.release();
+  });
+}
+
+int ls_model_free(LsModel* m) {
+  return guard([&] { delete m; });
+}
+
+int ls_model_info(const LsModel* m, LsModelInfo* o) {
+  return guard([&] {
+    NEED(m);
+    NEED(o);
+    const Config& c = m->cfg;
+    o->hidden = c.hidden;
+    o->inter = c.inter;
+    o->layers = c.layers;
+    o->heads = c.heads;
+    o->kv_heads = c.kv_heads;
+    o->head_dim = c.head_dim;
+    o->vocab = c.vocab;
+    o->max_ctx = m->max_ctx;
+    o->bits = c.format.bits;
+    o->group = c.format.group;
+    o->embed_bits = c.embed_format.bits;
+    o->embed_group = c.embed_format.group;
+    o->eps = c.eps;
+    o->rope_theta = c.rope_theta;
+    o->layer_bytes = m->file.layout.total;
+    o->embed_row_bytes = c.embed_row_bytes();
+    o->weight_bytes = c.layers * m->file.layout.total + c.vocab * c.embed_row_bytes();
+  });
+}
+
+int ls_model_report(const LsModel* m, LsReport* o) {
+  return guard([&] {
+    NEED(m);
+    NEED(o);
+    o->resident_weight_bytes = m->resident_weight_bytes;
+    o->bytes_read = m->bytes_read;
+    o->wait_ns = m->wait_ns;
+    o->passes = m->passes;
+  });
+}
+
+int ls_pos(const LsModel* m, uint64_t* pos) {
+  return guard([&] {
+    NEED(m);
+    NEED(pos);
+    *pos = m->pos;
+  });
+}
+
+int ls_reset(LsModel* m) {
+  return guard([&] {
+    NEED(m);
+    m->pos = 0;
+  });
+}
+
+int ls_truncate(LsModel* m, uint64_t pos) {
+  return guard([&] {
+    NEED(m);
+    m->truncate(pos);
+  });
+}
+
+int ls_forward(LsModel* m, const uint32_t* ids, uint64_t n, float* logits, uint32_t* argmax) {
+  return guard([&] {
+    NEED(m);
+    if (n) NEED(ids);
+    LS_CUDA(cudaSetDevice(m->device));
+    uint32_t t = m->forward(ids, n, logits);
+    if (argmax) *argmax = t;
+  });
+}
+
+int ls_forward_multi(LsModel* m, const uint32_t* ids, uint64_t t, uint64_t n, float* logits) {
+  return guard([&] {
+    NEED(m);
+    if (t) NEED(ids);
+    LS_CUDA(cudaSetDevice(m->device));
+    m->forward_multi(ids, t, n, logits);
+  });
+}
+
+int ls_verify(LsModel* m, const uint32_t* block, uint64_t n, uint32_t* accepted_m, uint32_t* next) {
+  return guard([&] {
+    NEED(m);
+    NEED(accepted_m);
+    NEED(next);
+    if (n) NEED(block);
+    LS_CUDA(cudaSetDevice(m->device));
+    m->verify(block, n, accepted_m, next);
+  });
+}
+
+int ls_speculative_greedy(LsModel* target, LsModel* draft, const uint32_t* prompt, uint64_t plen, uint64_t max_new, uint64_t k,
+                          const uint32_t* eos, uint64_t neos, uint32_t* out_tokens, uint64_t* out_len, LsSpecStats* stats) {
+  return guard([&] {
+    NEED(target);
+    NEED(out_tokens);
+    NEED(out_len);
+    NEED(stats);
+    if (plen) NEED(prompt);
+    if (neos) NEED(eos);
+    LS_CUDA(cudaSetDevice(target->device));
+    speculative_greedy(*target, draft, prompt, plen, max_new, k, eos, neos, out_tokens, out_len, stats);
+  });
+}
+
+int ls_quantize_model(const char* src_dir, const char* out_path, int bits, int group, int embed_bits, int embed_group,
+                      int clip_search, int device, double* rel_rmse) {
+  return guard([&] {
+    NEED(src_dir);
+    NEED(out_path);
+    WeightFormat f, e;
+    f.bits = bits;
+    f.group = group;
+    e.bits = embed_bits;
+    e.group = embed_group;
+    double r = quantize_model(src_dir, out_path, f, e, clip_search, device);
+    if (rel_rmse) *rel_rmse = r;
+  });
+}
+
+int ls_qweights_upload(int device, int bits, int group, const uint8_t* rows_raw, uint64_t rows, uint64_t cols, LsQWeights** out) {
+  return guard([&] {
+    NEED(rows_raw);
+    NEED(out);
+    std::unique_ptr<LsQWeights> q(new LsQWeights);
+    qweights_upload(q.get(), device, bits, group, rows_raw, rows, cols);
+    *out = q.release();
+  });
+}
+
+int ls_qweights_free(LsQWeights* w) {
+  return guard([&] { delete w; });
+}
+
+int ls_qgemv_device(const LsQWeights* w, const float* x_dev, uint64_t M, float* y_dev, void* stream) {
+  return guard([&] {
+    NEED(w);
+    NEED(x_dev);
+    NEED(y_dev);
+    LS_CUDA(cudaSetDevice(w->device));
+    qgemv_device(w, x_dev, M, y_dev, reinterpret_cast<cudaStream_t>(stream));
+  });
+}
+
+int ls_qgemv_host(int bits, int group, const uint8_t* rows_raw, uint64_t rows, uint64_t cols, const float* x, uint64_t M, float* y,
+                  int iters, double* ms) {
+  return guard([&] {
+    NEED(rows_raw);
+    NEED(x);
+    NEED(y);
+    int dev = 0;
+    LS_CUDA(cudaGetDevice(&dev));
+    std::unique_ptr<LsQWeights> q(new LsQWeights);
+    qweights_upload(q.get(), dev, bits, group, rows_raw, rows, cols);
+    float *dx = nullptr, *dy = nullptr;
+    LS_CUDA(cudaMalloc(&dx, M * cols * 4));
+    LS_CUDA(cudaMalloc(&dy, M * rows * 4));
+    std::unique_ptr<float, decltype(&cudaFree)> gx(dx, &cudaFree), gy(dy, &cudaFree);
+    LS_CUDA(cudaMemcpy(dx, x, M * cols * 4, cudaMemcpyHostToDevice));
+    qgemv_device(q.get(), dx, M, dy, 0);
+    LS_CUDA(cudaDeviceSynchronize());
+    if (iters > 1 && ms) {
+      cudaEvent_t a, b;
+      LS_CUDA(cudaEventCreate(&a));
+      LS_CUDA(cudaEventCreate(&b));
+      LS_CUDA(cudaEventRecord(a, 0));
+      for (int i = 0; i < iters; i++) qgemv_device(q.get(), dx, M, dy, 0);
+      LS_CUDA(cudaEventRecord(b, 0));
+      LS_CUDA(cudaEventSynchronize(b));
+      float t = 0;
+      LS_CUDA(cudaEventElapsedTime(&t, a, b));
+      *ms = t / iters;
+      cudaEventDestroy(a);
+      cudaEventDestroy(b);
+    }
+    LS_CUDA(cudaMemcpy(y, dy, M * rows * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+int ls_dequant_rows_host(int bits, int group, const uint8_t* rows_raw, uint64_t rows, uint64_t cols, const uint32_t* ids,
+                         uint64_t n, float* out) {
+  return guard([&] {
+    NEED(rows_raw);
+    NEED(ids);
+    NEED(out);
+    if (n == 0 || n > 128) LS_THROW(LS_ERR_ARG, "1..128 rows per call");
+    for (uint64_t i = 0; i < n; i++)
+      if (ids[i] >= rows) LS_THROW(LS_ERR_ARG, "row id out of range");
+    int dev = 0;
+    LS_CUDA(cudaGetDevice(&dev));
+    std::unique_ptr<LsQWeights> q(new LsQWeights);
+    qweights_upload(q.get(), dev, bits, group, rows_raw, rows, cols);
+    Ctl* ctl = nullptr;
+    float* dx = nullptr;
+    LS_CUDA(cudaMalloc(&ctl, sizeof(Ctl)));
+    std::unique_ptr<Ctl, decltype(&cudaFree)> gc(ctl, &cudaFree);
+    LS_CUDA(cudaMalloc(&dx, n * cols * 4));
+    std::unique_ptr<float, decltype(&cudaFree)> gx(dx, &cudaFree);
+    LS_CUDA(cudaMemset(ctl, 0, sizeof(Ctl)));
+    LS_CUDA(cudaMemcpy(ctl->tokens, ids, n * 4, cudaMemcpyHostToDevice));
+    launch_embed(q->w, ctl, dx, (int)cols, (int)n, 0);
+    LS_CUDA(cudaMemcpy(out, dx, n * cols * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+uint64_t ls_qgemv_bytes(int bits, int group, uint64_t rows, uint64_t cols, uint64_t M) {
+  return rows * (cols * (uint64_t)bits / 8 + cols / (uint64_t)group * 2) + M * cols * 4 + M * rows * 4;
+}
+
+}  // extern "C"
