@@ -1,0 +1,414 @@
+#!/usr/bin/env python
+"""Benchmark of the speculative-decode verify path: accepted tokens/s on BASELINE.json's configs.
+
+Default workload (N=1): config 2 of BASELINE.json -- a Qwen2.5-0.5B-architecture random-init model
+(seeded N(0, 0.02) weights, BF16 then int4 group-32 with the clip search), batch 1 per GPU, a
+512-token prompt of random ids built from repeated 32-token spans, greedy decode of 256 tokens with
+k = 8 guesses per verify pass (prompt-lookup drafter by default; --drafter model uses a second,
+int4 model through the reference's draft-Model API).
+
+A step is the decode loop of one sequence (src/spec.rs:94-149): from the prefilled prompt, draft,
+verify (one (k+1)-row pass over all weights with the device-side argmax + acceptance), roll back,
+until 256 tokens. `value` = tokens emitted after the first / decode seconds (the reference's
+definition, src/main.rs:358-359), whole job over all ranks, device-timed with CUDA events on the
+model's stream. `e2e` = the same metric through ls_speculative_greedy with host buffers (prefill,
+token uploads and result reads inside the timed region). Each rank decodes its own sequence (weak
+scaling, no collective on the data path). Inputs: the weights (278 MB per verify pass) exceed L2,
+so every pass streams them from HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2]
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import re
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    1: dict(shape="0.5b", body=(8, 64), embed=(8, 64), prompt=128, span=16, repeats=3, max_new=32, k=4, drafter="model",
+            draft=(4, 32)),
+    2: dict(shape="0.5b", body=(4, 32), embed=(4, 32), prompt=512, span=32, repeats=0, max_new=256, k=8, drafter="lookup",
+            draft=(4, 32)),
+}
+METRIC = "spec-decode accepted tokens/s"
+UNIT = "tok/s"
+
+
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
+    ap.add_argument("--drafter", choices=["lookup", "model"], default=None)
+    ap.add_argument("--root", default=os.environ.get("LS_BENCH_ROOT", "/tmp/ls_b200_bench"))
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-sample-tokens", type=int, default=0, help="decode tokens per CPU sample (0: auto)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="print the per-kernel profile to stderr")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(kernel_class: str):
+    """DRAM bytes per launch from the committed ncu summary (profiles/*.md lines `traffic <class>: <bytes>`)."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for f in sorted(os.listdir(d)):
+        if not f.endswith(".md"):
+            continue
+        for line in open(os.path.join(d, f)):
+            m = re.match(rf"\s*[-*]?\s*traffic {re.escape(kernel_class)}:\s*([0-9.eE+]+)", line)
+            if m:
+                return float(m.group(1))
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in csv.reader(io.StringIO(out)):
+            if len(row) < 9:
+                continue
+            try:
+                sm.append(float(row[1]))
+                mx.append(float(row[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, row[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def setup_dist(args):
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        backend = "nccl" if args.impl == "ours" else "gloo"
+        if backend == "nccl":
+            import torch
+
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=900))
+    return rank, world, local, dist
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def prompt_for(cfg, vocab, rank):
+    from layerstream_b200 import synth
+
+    if cfg["repeats"]:
+        return synth.make_prompt(cfg["prompt"], vocab, cfg["span"], cfg["repeats"], seed=1000 + rank)
+    return synth.make_prompt_spans(cfg["prompt"], vocab, cfg["span"], seed=1000 + rank)
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU path (oracle): the reference's algorithm restated in C++, timed on the host cores
+# ------------------------------------------------------------------------------------------------
+
+
+def cpu_files(args, cfg, rank, dist):
+    """Model files made with the CPU quantizer (bytes identical to the GPU quantizer's)."""
+    from layerstream_b200 import synth
+    from oracle import oracle as O
+
+    os.makedirs(args.root, exist_ok=True)
+    d = synth.ensure_model(args.root, cfg["shape"], 0)
+
+    def lsq(body, embed):
+        p = os.path.join(args.root, f"{cfg['shape']}-s0-q{body[0]}g{body[1]}-e{embed[0]}g{embed[1]}-clip.lsq")
+        if not os.path.exists(p):
+            tmp = p + f".{os.getpid()}.partial"
+            O.quantize_model(d, tmp, body, embed, clip=True, threads=os.cpu_count() or 1)
+            os.replace(tmp, p)
+        return p
+
+    t = lsq(cfg["body"], cfg["embed"])
+    dr = lsq(cfg["draft"], cfg["draft"]) if cfg["drafter"] == "model" else None
+    return t, dr
+
+
+def cpu_sample(args, cfg, target_path, draft_path, steps, warmup):
+    """Times the oracle's decode loop on a bounded sample: prefill once, then `steps` decodes of
+    n_tok tokens from the prefilled state. Returns (tokens/s, per-step list, sample text, cores)."""
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    plen, k = cfg["prompt"], cfg["k"]
+    n_tok = args.cpu_sample_tokens or (2 * (k + 1) + 1)
+    max_ctx = plen + cfg["max_new"] + k + 16
+    T = O.Model(target_path, quantized=True, threads=threads, max_ctx=max_ctx)
+    D = O.Model(draft_path, quantized=True, threads=threads, max_ctx=max_ctx) if draft_path else None
+    prompt = prompt_for(cfg, T.vocab, 0)
+    first = O.forward_argmax(T, prompt)
+    if D is not None:
+        O.forward_argmax(D, prompt)
+    rates = []
+    for i in range(warmup + steps):
+        T.truncate(plen)
+        if D is not None:
+            D.truncate(plen)
+        toks, st = O.spec_continue(T, D, prompt, first, n_tok, k)
+        if i >= warmup:
+            rates.append((len(toks) - 1) / max(st["decode_secs"], 1e-9))
+    sample = (f"decode of {n_tok} tokens (of {cfg['max_new']}) from the prefilled {plen}-token prompt, "
+              f"{cfg['drafter']} drafter, k={k}, {steps} timed samples")
+    return float(np.mean(rates)), rates, sample, threads
+
+
+# ------------------------------------------------------------------------------------------------
+# CUDA path
+# ------------------------------------------------------------------------------------------------
+
+
+def main():
+    args = parse()
+    cfg = dict(CONFIGS[args.config])
+    if args.drafter:
+        cfg["drafter"] = args.drafter
+    rank, world, local, dist = setup_dist(args)
+    workload = (f"config{args.config}: {cfg['shape']} Qwen2 random-init int{cfg['body'][0]} g{cfg['body'][1]}, "
+                f"{cfg['prompt']}-token prompt, {cfg['max_new']} new tokens, k={cfg['k']}, batch 1 per GPU, "
+                f"{cfg['drafter']} drafter")
+    base_cfg = {"workload": workload, "config": args.config, "model": f"qwen2-{cfg['shape']}-arch random-init",
+                "weights": f"int{cfg['body'][0]}-g{cfg['body'][1]}", "embed": f"int{cfg['embed'][0]}-g{cfg['embed'][1]}",
+                "prompt_tokens": cfg["prompt"], "max_new": cfg["max_new"], "k": cfg["k"], "drafter": cfg["drafter"],
+                "global_batch": world, "parallelism": f"dp{world} (independent sequences, no collective)",
+                "l2": "inputs larger than L2 (weights streamed from HBM every pass)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            barrier(dist)
+            return
+        t_path, d_path = cpu_files(args, cfg, rank, None)
+        v, rates, sample, cores = cpu_sample(args, cfg, t_path, d_path, args.steps, args.warmup)
+        line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 activations, int4/int8 weights", "data": "synthetic", "config": base_cfg,
+                "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+                "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        barrier(dist)
+        return
+
+    import torch
+
+    import layerstream_b200 as ls
+    from layerstream_b200 import synth
+
+    torch.cuda.set_device(local)
+    os.makedirs(args.root, exist_ok=True)
+    if rank == 0:
+        t_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local)
+        d_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["draft"], cfg["draft"], clip=True,
+                                  device=local) if cfg["drafter"] == "model" else None
+    barrier(dist)
+    if rank != 0:
+        t_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local)
+        d_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["draft"], cfg["draft"], clip=True,
+                                  device=local) if cfg["drafter"] == "model" else None
+
+    plen, k, max_new = cfg["prompt"], cfg["k"], cfg["max_new"]
+    max_ctx = plen + max_new + k + 16
+    target = ls.Model(t_path, device=local, max_ctx=max_ctx)
+    draft = ls.Model(d_path, device=local, max_ctx=max_ctx) if d_path else None
+    V = target.vocab
+    info = target.info
+    prompt = prompt_for(cfg, V, rank)
+    stream = torch.cuda.ExternalStream(target.stream, device=torch.device("cuda", local))
+
+    first = target.forward(prompt, want_logits=False)
+    if draft is not None:
+        draft.forward(prompt, want_logits=False)
+
+    def step():
+        target.truncate(plen)
+        if draft is not None:
+            draft.truncate(plen)
+        toks, st = ls.spec_continue(target, draft, prompt, first, max_new, k)
+        return len(toks) - 1, st
+
+    for _ in range(args.warmup):
+        step()
+
+    passes0 = target.report()["passes"] + (draft.report()["passes"] if draft else 0)
+    target.profile_enable(True)
+    clocks = Clocks(local)
+    barrier(dist)
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    tokens, stats = 0, []
+    for _ in range(args.steps):
+        n, st = step()
+        tokens += n
+        stats.append(st)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier(dist)
+    ms = e0.elapsed_time(e1)
+    prof = target.profile()
+    target.profile_enable(False)
+    passes = target.report()["passes"] + (draft.report()["passes"] if draft else 0) - passes0
+    t_ms = torch.tensor([ms], device="cuda")
+    t_tok = torch.tensor([float(tokens)], device="cuda")
+    if dist is not None:
+        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t_tok, op=dist.ReduceOp.SUM)
+    ms_max, tok_all = float(t_ms.item()), float(t_tok.item())
+    value = tok_all / (ms_max / 1e3)
+
+    # e2e: the whole public call (prefill + decode) from host buffers
+    e2e_ms, e2e_tok = 0.0, 0
+    r0 = target.report()
+    for _ in range(args.e2e_steps):
+        target.reset()
+        if draft is not None:
+            draft.reset()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        toks, _ = ls.speculative_greedy(target, draft, prompt, max_new, k)
+        e2e_ms += (time.perf_counter() - t0) * 1e3
+        e2e_tok += len(toks) - 1
+    r1 = target.report()
+    t2 = torch.tensor([e2e_ms, float(e2e_tok)], device="cuda")
+    if dist is not None:
+        mx = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t2, op=dist.ReduceOp.SUM)
+        e2e_ms = float(mx.item())
+    e2e_val = float(t2[1].item()) / (e2e_ms / 1e3) if e2e_ms > 0 else None
+    h2d = (r1["h2d_bytes"] - r0["h2d_bytes"]) // max(args.e2e_steps, 1)
+    d2h = (r1["d2h_bytes"] - r0["d2h_bytes"]) // max(args.e2e_steps, 1)
+
+    # roofline of the dominant kernel class (live CUDA-event timing inside the passes)
+    peak, peak_kind = peaks()
+    L = info.layers
+    share = {}
+    for c, p in prof.items():
+        if c == "pass" or not p["launches"]:
+            continue
+        share[c] = p["ms"] * (L if c not in ("head",) else 1)
+    dom = max(share, key=share.get) if share else None
+    roof = None
+    if dom:
+        p = prof[dom]
+        achieved = p["bytes"] / (p["ms"] / 1e3) / 1e9
+        traffic = profile_traffic(dom)
+        roof = {"bound": "hbm", "kernel": f"gemv ({dom})" if dom != "attention" else "attention", "achieved": achieved,
+                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": traffic, "algorithmic_bytes_per_launch": p["bytes"] / p["launches"],
+                "avg_launch_us": p["ms"] * 1e3 / p["launches"]}
+    vstep = None
+    pp = prof["pass"]
+    if pp["launches"]:
+        avg_ctx = plen + max_new / 2
+        wbytes = info.weight_bytes
+        kvbytes = avg_ctx * L * info.kv_heads * info.head_dim * 2 * 2
+        pass_s = pp["ms"] / pp["launches"] / 1e3
+        vstep = {"bytes_per_pass": wbytes + kvbytes, "avg_pass_us": pass_s * 1e6, "achieved_gbs": (wbytes + kvbytes) / pass_s / 1e9,
+                 "frac": (wbytes + kvbytes) / pass_s / 1e9 / peak,
+                 "kernel_share_est": {c: share[c] / (pp["ms"]) for c in share}}
+    acc = sum(s["accepted"] for s in stats)
+    dr = sum(s["drafted"] for s in stats)
+    tp = sum(s["target_passes"] for s in stats)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            tpc, dpc = cpu_files(args, cfg, rank, None)
+            v, _, sample, cores = cpu_sample(args, cfg, tpc, dpc, steps=2, warmup=0)
+            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        except Exception as e:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
+
+    kernels_per_pass = 2 + 5 * L
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": f"f32 activations, int{cfg['body'][0]} weights (bf16 scales), f16 KV", "data": "synthetic",
+        "config": base_cfg, "clocks": clk,
+        "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "steps": args.e2e_steps, "includes": "prefill + decode through ls_speculative_greedy, host buffers"},
+        "gpu_launches": int(passes * kernels_per_pass),
+        "roofline": roof, "verify_step": vstep,
+        "spec": {"tokens_per_pass": tokens / max(tp, 1), "accepted_over_drafted": acc / max(dr, 1), "target_passes": tp},
+        "cpu_baseline": cpu,
+    }
+    if args.profile and rank == 0:
+        print(json.dumps(prof, indent=1), file=sys.stderr)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    target.close()
+    if draft is not None:
+        draft.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -68,7 +68,21 @@ typedef struct LsReport {
   uint64_t bytes_read;            /* bytes moved host->device for weights since open */
   uint64_t wait_ns;               /* host time blocked on streamed data */
   uint64_t passes;                /* forward passes run */
+  uint64_t h2d_bytes;             /* token blocks and control data copied host->device since open */
+  uint64_t d2h_bytes;             /* results (tokens, counts, logits) copied device->host since open */
 } LsReport;
+
+/* Live kernel timing (CUDA events recorded inside the pass, on the model's stream), enabled by
+ * ls_model_profile_enable. Classes: 0 QKV GEMV, 1 attention, 2 O GEMV, 3 gate/up GEMV, 4 down GEMV
+ * (all sampled on one middle layer per pass), 5 LM head GEMV + argmax, 6 the whole pass.
+ * bytes = algorithmic bytes of the timed launches (weights + scales + activations in and out; for
+ * attention the K/V cache rows read plus the new rows written). */
+#define LS_PROF_CLASSES 7
+typedef struct LsProfile {
+  uint64_t launches[LS_PROF_CLASSES];
+  double ms[LS_PROF_CLASSES];
+  double bytes[LS_PROF_CLASSES];
+} LsProfile;
 
 /* src/spec.rs:16-39 */
 typedef struct LsSpecStats {
@@ -86,6 +100,13 @@ int ls_model_open(const char *lsq_path, int device, uint64_t max_ctx, int mode, 
 int ls_model_free(LsModel *m);
 int ls_model_info(const LsModel *m, LsModelInfo *out);
 int ls_model_report(const LsModel *m, LsReport *out);
+
+/* The CUDA stream (cudaStream_t) every kernel of this model is launched on, for callers that time
+ * the model's work with their own CUDA events. */
+int ls_model_stream(const LsModel *m, void **stream);
+
+int ls_model_profile_enable(LsModel *m, int on);   /* also clears the counters */
+int ls_model_profile(const LsModel *m, LsProfile *out);
 
 int ls_pos(const LsModel *m, uint64_t *pos);
 int ls_reset(LsModel *m);
@@ -111,6 +132,14 @@ int ls_verify(LsModel *m, const uint32_t *block, uint64_t n, uint32_t *accepted_
 int ls_speculative_greedy(LsModel *target, LsModel *draft, const uint32_t *prompt, uint64_t plen, uint64_t max_new,
                           uint64_t k, const uint32_t *eos, uint64_t neos, uint32_t *out_tokens, uint64_t *out_len,
                           LsSpecStats *stats);
+
+/* The decode loop of spec::speculative_greedy (src/spec.rs:94-149) from an already prefilled state:
+ * target (and draft, if any) hold exactly the hlen tokens of `hist`, and `first` is the target's
+ * greedy token after them (ls_forward's argmax). out_tokens[0] = first. speculative_greedy is
+ * ls_forward(prompt) on both models followed by this call. */
+int ls_spec_continue(LsModel *target, LsModel *draft, const uint32_t *hist, uint64_t hlen, uint32_t first,
+                     uint64_t max_new, uint64_t k, const uint32_t *eos, uint64_t neos, uint32_t *out_tokens,
+                     uint64_t *out_len, LsSpecStats *stats);
 
 /* quant::quantize_model: reads a BF16 safetensors model directory (config.json +
  * model.safetensors) and writes a new `.lsq` file (must not exist). The group quantization with

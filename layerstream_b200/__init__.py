@@ -34,7 +34,14 @@ class ModelInfo(C.Structure):
 
 
 class Report(C.Structure):
-    _fields_ = [(n, C.c_uint64) for n in ("resident_weight_bytes", "bytes_read", "wait_ns", "passes")]
+    _fields_ = [(n, C.c_uint64) for n in ("resident_weight_bytes", "bytes_read", "wait_ns", "passes", "h2d_bytes", "d2h_bytes")]
+
+
+PROF_CLASSES = ("qkv", "attention", "o", "gate_up", "down", "head", "pass")
+
+
+class Profile(C.Structure):
+    _fields_ = [("launches", C.c_uint64 * 7), ("ms", C.c_double * 7), ("bytes", C.c_double * 7)]
 
 
 class SpecStats(C.Structure):
@@ -55,6 +62,9 @@ _SIGS = {
     "ls_model_free": (C.c_int, [C.c_void_p]),
     "ls_model_info": (C.c_int, [C.c_void_p, C.POINTER(ModelInfo)]),
     "ls_model_report": (C.c_int, [C.c_void_p, C.POINTER(Report)]),
+    "ls_model_stream": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "ls_model_profile_enable": (C.c_int, [C.c_void_p, C.c_int]),
+    "ls_model_profile": (C.c_int, [C.c_void_p, C.POINTER(Profile)]),
     "ls_pos": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64)]),
     "ls_reset": (C.c_int, [C.c_void_p]),
     "ls_truncate": (C.c_int, [C.c_void_p, C.c_uint64]),
@@ -63,6 +73,8 @@ _SIGS = {
     "ls_verify": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
     "ls_speculative_greedy": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_void_p,
                                         C.c_uint64, C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(SpecStats)]),
+    "ls_spec_continue": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint64,
+                                   C.c_void_p, C.c_uint64, C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(SpecStats)]),
     "ls_quantize_model": (C.c_int, [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                     C.POINTER(C.c_double)]),
     "ls_qgemv_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p,
@@ -166,6 +178,22 @@ class Model:
         _check(lib().ls_verify(self._h, _p(b), b.size, C.byref(m), C.byref(nxt)))
         return m.value, nxt.value
 
+    @property
+    def stream(self) -> int:
+        """cudaStream_t (as an int) of this model's kernels."""
+        p = C.c_void_p()
+        _check(lib().ls_model_stream(self._h, C.byref(p)))
+        return p.value or 0
+
+    def profile_enable(self, on: bool = True):
+        """Live CUDA-event timing of one sampled layer's kernels, the LM head and the whole pass."""
+        _check(lib().ls_model_profile_enable(self._h, int(on)))
+
+    def profile(self) -> dict:
+        p = Profile()
+        _check(lib().ls_model_profile(self._h, C.byref(p)))
+        return {c: {"launches": p.launches[i], "ms": p.ms[i], "bytes": p.bytes[i]} for i, c in enumerate(PROF_CLASSES)}
+
     def report(self) -> dict:
         r = Report()
         _check(lib().ls_model_report(self._h, C.byref(r)))
@@ -181,6 +209,18 @@ def speculative_greedy(target: Model, draft: Model | None, prompt, max_new: int,
     st = SpecStats()
     _check(lib().ls_speculative_greedy(target._h, draft._h if draft is not None else None, _p(p), p.size, max_new, k, _p(e),
                                        len(eos), _p(out), C.byref(n), C.byref(st)))
+    return out[: n.value].tolist(), st.as_dict()
+
+
+def spec_continue(target: Model, draft: Model | None, hist, first: int, max_new: int, k: int, eos=()):
+    """The decode loop of ``speculative_greedy`` from a prefilled state (both models hold ``hist``)."""
+    h = _u32(hist)
+    e = _u32(list(eos) if len(eos) else [0])
+    out = np.zeros(max(max_new, 1), np.uint32)
+    n = C.c_uint64()
+    st = SpecStats()
+    _check(lib().ls_spec_continue(target._h, draft._h if draft is not None else None, _p(h), h.size, first, max_new, k,
+                                  _p(e), len(eos), _p(out), C.byref(n), C.byref(st)))
     return out[: n.value].tolist(), st.as_dict()
 
 

@@ -117,14 +117,26 @@ struct LsModel {
   Ctl* ctl = nullptr;
   Ctl* ctl_host = nullptr;
 
-  std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;
+  std::map<std::tuple<int, int, int, int>, cudaGraphExec_t> graphs;
   size_t pos = 0;
-  uint64_t bytes_read = 0, wait_ns = 0, passes = 0, resident_weight_bytes = 0;
+  uint64_t bytes_read = 0, wait_ns = 0, passes = 0, resident_weight_bytes = 0, h2d_bytes = 0, d2h_bytes = 0;
+
+  // live profile: event pairs around the launches of one sampled layer, the head and the pass
+  bool prof_on = false;
+  std::vector<cudaEvent_t> prof_ev;
+  struct ProfRec { int cls; double bytes; };
+  std::vector<ProfRec> prof_rec;  // filled at enqueue (capture) time, one per event pair
+  std::map<std::tuple<int, int, int, int>, std::vector<ProfRec>> prof_recs;  // per graph
+  const std::vector<ProfRec>* prof_cur = nullptr;
+  bool prof_pending = false;
+  LsProfile prof{};
+  int prof_layer() const { return (int)cfg.layers / 2; }
 
   ~LsModel() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    for (auto e : prof_ev) cudaEventDestroy(e);
     for (auto e : ev_loaded) cudaEventDestroy(e);
     for (auto e : ev_free) cudaEventDestroy(e);
     for (void* p : dev_allocs) cudaFree(p);
@@ -364,6 +376,39 @@ struct LsModel {
 
   // ---- the pass --------------------------------------------------------------------------------
 
+  // Opens an event pair around the next launch when profiling (returns the pair index or -1).
+  int prof_begin(int cls, double bytes, cudaStream_t s) {
+    if (!prof_on) return -1;
+    const size_t i = prof_rec.size();
+    while (prof_ev.size() < 2 * (i + 1)) {
+      cudaEvent_t e;
+      LS_CUDA(cudaEventCreate(&e));
+      prof_ev.push_back(e);
+    }
+    prof_rec.push_back({cls, bytes});
+    LS_CUDA(cudaEventRecord(prof_ev[2 * i], s));
+    return (int)i;
+  }
+  void prof_end(int i, cudaStream_t s) {
+    if (i >= 0) LS_CUDA(cudaEventRecord(prof_ev[2 * i + 1], s));
+  }
+  double gemv_bytes(const QMat& w, int M, int out_rows) const {
+    const double rb = (double)w.cols * w.bits / 8 + (double)w.cols / w.group * 2;
+    return (double)w.rows * rb + (double)M * w.cols * 4 + (double)M * out_rows * 4;
+  }
+  void prof_collect() {
+    if (!prof_pending || !prof_cur) return;
+    prof_pending = false;
+    for (size_t i = 0; i < prof_cur->size(); i++) {
+      float ms = 0;
+      LS_CUDA(cudaEventElapsedTime(&ms, prof_ev[2 * i], prof_ev[2 * i + 1]));
+      const ProfRec& r = (*prof_cur)[i];
+      prof.launches[r.cls]++;
+      prof.ms[r.cls] += ms;
+      prof.bytes[r.cls] += r.bytes;
+    }
+  }
+
   int pick_ksplit(const QMat& w, int M) const {
     const int tiles = w.rows_pad / 32;
     const int nz = (M + 15) / 16;
@@ -419,7 +464,11 @@ struct LsModel {
 
   void layer_compute(const LayerW& W, size_t l, int T, cudaStream_t s) {
     const int h = (int)cfg.hidden, kv = (int)cfg.kv_dim(), I = (int)cfg.inter;
+    const bool sample = prof_on && (int)l == prof_layer();
+    auto pb = [&](int cls, double b) { return sample ? prof_begin(cls, b, s) : -1; };
+    int pi = pb(0, gemv_bytes(W.qkv, T, h + 2 * kv));
     gemv(W.qkv, x, h, T, EPI_BIAS_STORE, qkv, h + 2 * kv, W.in_norm, nullptr, W.qkv_bias, s);
+    prof_end(pi, s);
     AttnLaunch a;
     a.qkv = qkv;
     a.qkv_stride = h + 2 * kv;
@@ -436,10 +485,21 @@ struct LsModel {
     a.max_ctx = (int)max_ctx;
     a.M = T;
     a.max_splits = att_slots;
+    // attention bytes: cached K/V rows read (f16) + new rows written + q and out (f32); the cached
+    // length is the host's view of pos0 when the pass is enqueued (exact outside graph replays,
+    // which re-time the same shape)
+    pi = pb(1, (double)pos * kv * 2 * 2 + (double)T * kv * 2 * 2 + (double)T * (h + 2 * kv) * 4 + (double)T * h * 4);
     launch_attention(a, s);
+    prof_end(pi, s);
+    pi = pb(2, gemv_bytes(W.o, T, h) + (double)T * h * 4);
     gemv(W.o, attn, h, T, EPI_RESID, x, h, nullptr, nullptr, nullptr, s);
+    prof_end(pi, s);
+    pi = pb(3, gemv_bytes(W.gu, T, I));
     gemv(W.gu, x, h, T, EPI_SWIGLU, hbuf, I, W.post_norm, nullptr, nullptr, s);
+    prof_end(pi, s);
+    pi = pb(4, gemv_bytes(W.down, T, h) + (double)T * h * 4);
     gemv(W.down, hbuf, I, T, EPI_RESID, x, h, nullptr, nullptr, nullptr, s);
+    prof_end(pi, s);
   }
 
   // Enqueues one pass over T tokens already in ctl->tokens (pos0 in ctl). n_logits > 0 runs the
@@ -449,13 +509,17 @@ struct LsModel {
     const int h = (int)cfg.hidden;
     const size_t V = cfg.vocab;
     if (mode == LS_MODE_RESIDENT) {
+      const int pp = prof_begin(6, 0, stream);
       launch_embed(embed, ctl, x, h, T, stream);
       for (size_t l = 0; l < cfg.layers; l++) layer_compute(layers[l], l, T, stream);
       if (n_logits > 0) {
+        const int ph = prof_begin(5, gemv_bytes(embed, n_logits, 0), stream);
         head(embed, x + (size_t)(T - n_logits) * h, n_logits, want_logits, 0, (int)V, 0, 1, 0, stream);
+        prof_end(ph, stream);
       } else {
         launch_advance(ctl, stream);
       }
+      prof_end(pp, stream);
       return;
     }
     // streaming: items are layers 0..L-1 then head chunks; each slot is refilled by a copy on the
@@ -515,13 +579,15 @@ struct LsModel {
   void run_pass(int T, int n_logits, bool want_logits) {
     passes++;
     if (mode != LS_MODE_RESIDENT) {
+      prof_rec.clear();
       enqueue_pass(T, n_logits, want_logits);
       return;
     }
-    auto key = std::make_tuple(T, n_logits, (int)want_logits);
+    auto key = std::make_tuple(T, n_logits, (int)want_logits, (int)prof_on);
     auto it = graphs.find(key);
     if (it == graphs.end()) {
       cudaGraph_t graph;
+      prof_rec.clear();
       LS_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
       try {
         enqueue_pass(T, n_logits, want_logits);
@@ -534,8 +600,13 @@ struct LsModel {
       LS_CUDA(cudaGraphInstantiate(&exec, graph, 0));
       cudaGraphDestroy(graph);
       it = graphs.emplace(key, exec).first;
+      prof_recs[key] = prof_rec;
     }
     LS_CUDA(cudaGraphLaunch(it->second, stream));
+    if (prof_on) {
+      prof_cur = &prof_recs[key];
+      prof_pending = true;
+    }
   }
 
   // ---- host API --------------------------------------------------------------------------------
@@ -557,11 +628,14 @@ struct LsModel {
     std::memcpy(ctl_host->tokens, ids, (size_t)T * 4);
     ctl_host->err = 0;
     LS_CUDA(cudaMemcpyAsync(ctl, ctl_host, sizeof(Ctl), cudaMemcpyHostToDevice, stream));
+    h2d_bytes += sizeof(Ctl);
   }
 
   void fetch_result() {
     LS_CUDA(cudaMemcpyAsync(&ctl_host->argmax, &ctl->argmax, sizeof(Ctl) - offsetof(Ctl, argmax), cudaMemcpyDeviceToHost, stream));
+    d2h_bytes += sizeof(Ctl) - offsetof(Ctl, argmax);
     LS_CUDA(cudaStreamSynchronize(stream));
+    prof_collect();
     if (ctl_host->err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
   }
 
@@ -575,8 +649,10 @@ struct LsModel {
       const bool last = c + 1 == nchunks;
       push_ctl((int)(b - a), last ? 1 : 0, 0, ids + a);
       run_pass((int)(b - a), last ? 1 : 0, last && logits_out != nullptr);
-      if (last && logits_out)
+      if (last && logits_out) {
         LS_CUDA(cudaMemcpyAsync(logits_out, logits, cfg.vocab * 4, cudaMemcpyDeviceToHost, stream));
+        d2h_bytes += cfg.vocab * 4;
+      }
       fetch_result();
       pos += b - a;
       tok = ctl_host->next;
@@ -592,7 +668,10 @@ struct LsModel {
     if (n > (uint64_t)kMaxDraft + 1) LS_THROW(LS_ERR_ARG, "forward_multi returns logits for at most 33 positions");
     push_ctl((int)t, (int)n, 0, ids);
     run_pass((int)t, (int)n, logits_out != nullptr);
-    if (logits_out) LS_CUDA(cudaMemcpyAsync(logits_out, logits, n * cfg.vocab * 4, cudaMemcpyDeviceToHost, stream));
+    if (logits_out) {
+      LS_CUDA(cudaMemcpyAsync(logits_out, logits, n * cfg.vocab * 4, cudaMemcpyDeviceToHost, stream));
+      d2h_bytes += n * cfg.vocab * 4;
+    }
     fetch_result();
     pos += t;
   }
@@ -641,32 +720,31 @@ std::vector<uint32_t> lookup_draft(const std::vector<uint32_t>& hist, size_t kk)
 
 }  // namespace
 
-static void speculative_greedy(LsModel& target, LsModel* draft, const uint32_t* prompt, uint64_t plen, uint64_t max_new,
-                               uint64_t k, const uint32_t* eos, uint64_t neos, uint32_t* out_tokens, uint64_t* out_len,
-                               LsSpecStats* st) {
+static bool contains(const uint32_t* v, uint64_t n, uint32_t t) {
+  for (uint64_t i = 0; i < n; i++)
+    if (v[i] == t) return true;
+  return false;
+}
+
+// The decode loop of src/spec.rs:94-149, from a state where both models hold `hist` and `a` is the
+// target's greedy token after it. out_tokens[0] = a.
+static void spec_continue(LsModel& target, LsModel* draft, const uint32_t* hist0, uint64_t hlen, uint32_t a,
+                          uint64_t max_new, uint64_t k, const uint32_t* eos, uint64_t neos, uint32_t* out_tokens,
+                          uint64_t* out_len, LsSpecStats* st) {
   if (k == 0 || k > (uint64_t)kMaxDraft) LS_THROW(LS_ERR_ARG, "k must be between 1 and 32, not " + std::to_string(k));
-  if (plen == 0 || max_new == 0) LS_THROW(LS_ERR_ARG, "need a prompt and at least one token to generate");
-  if (target.pos != 0 || (draft && draft->pos != 0)) LS_THROW(LS_ERR_ARG, "both models must start with an empty cache");
+  if (max_new == 0) LS_THROW(LS_ERR_ARG, "need at least one token to generate");
+  if (target.pos != hlen || (draft && draft->pos != hlen)) LS_THROW(LS_ERR_ARG, "the models must hold exactly the history");
   if (draft && draft->cfg.vocab != target.cfg.vocab) LS_THROW(LS_ERR_ARG, "the draft and the target must share a vocabulary");
-  const uint64_t need = plen + max_new + k;
+  const uint64_t need = hlen + max_new + k;
   if (need > target.max_ctx || (draft && need > draft->max_ctx))
     LS_THROW(LS_ERR_ARG, "prompt + max_new + k = " + std::to_string(need) + " tokens exceed the context limit");
-  auto is_eos = [&](uint32_t t) {
-    for (uint64_t i = 0; i < neos; i++)
-      if (eos[i] == t) return true;
-    return false;
-  };
-  std::memset(st, 0, sizeof *st);
-  const double t0 = now_s();
-  uint32_t a = target.forward(prompt, plen, nullptr);
-  if (draft) draft->forward(prompt, plen, nullptr);
-  st->first_secs = now_s() - t0;
   std::vector<uint32_t> out{a};
-  std::vector<uint32_t> hist(prompt, prompt + plen);
+  std::vector<uint32_t> hist(hist0, hist0 + hlen);
   hist.push_back(a);
-  bool stop = is_eos(a);
+  bool stop = contains(eos, neos, a);
   const double td = now_s();
   while (!stop && out.size() < max_new) {
+    // never ask for more than is still needed: a pass yields at most kk + 1 tokens
     const uint64_t kk = std::min<uint64_t>(k, max_new - out.size() - 1);
     double ts = now_s();
     std::vector<uint32_t> drafts;
@@ -695,11 +773,12 @@ static void speculative_greedy(LsModel& target, LsModel* draft, const uint32_t* 
       const uint32_t tok = i < m ? drafts[i] : next;
       out.push_back(tok);
       hist.push_back(tok);
-      if (is_eos(tok) || out.size() == max_new) {
+      if (contains(eos, neos, tok) || out.size() == max_new) {
         stop = true;
         break;
       }
     }
+    // both models now hold exactly [.., a, d_1 .. d_m]
     if (draft) {
       const size_t want = p + m + 1;
       if (draft->pos > want) {
@@ -714,9 +793,27 @@ static void speculative_greedy(LsModel& target, LsModel* draft, const uint32_t* 
     }
     a = next;
   }
-  st->decode_secs = now_s() - td;
+  st->decode_secs += now_s() - td;
   std::memcpy(out_tokens, out.data(), out.size() * 4);
   *out_len = out.size();
+}
+
+static void speculative_greedy(LsModel& target, LsModel* draft, const uint32_t* prompt, uint64_t plen, uint64_t max_new,
+                               uint64_t k, const uint32_t* eos, uint64_t neos, uint32_t* out_tokens, uint64_t* out_len,
+                               LsSpecStats* st) {
+  if (k == 0 || k > (uint64_t)kMaxDraft) LS_THROW(LS_ERR_ARG, "k must be between 1 and 32, not " + std::to_string(k));
+  if (plen == 0 || max_new == 0) LS_THROW(LS_ERR_ARG, "need a prompt and at least one token to generate");
+  if (target.pos != 0 || (draft && draft->pos != 0)) LS_THROW(LS_ERR_ARG, "both models must start with an empty cache");
+  if (draft && draft->cfg.vocab != target.cfg.vocab) LS_THROW(LS_ERR_ARG, "the draft and the target must share a vocabulary");
+  const uint64_t need = plen + max_new + k;
+  if (need > target.max_ctx || (draft && need > draft->max_ctx))
+    LS_THROW(LS_ERR_ARG, "prompt + max_new + k = " + std::to_string(need) + " tokens exceed the context limit");
+  std::memset(st, 0, sizeof *st);
+  const double t0 = now_s();
+  const uint32_t a = target.forward(prompt, plen, nullptr);
+  if (draft) draft->forward(prompt, plen, nullptr);
+  st->first_secs = now_s() - t0;
+  spec_continue(target, draft, prompt, plen, a, max_new, k, eos, neos, out_tokens, out_len, st);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -959,6 +1056,33 @@ int ls_model_report(const LsModel* m, LsReport* o) {
     o->bytes_read = m->bytes_read;
     o->wait_ns = m->wait_ns;
     o->passes = m->passes;
+    o->h2d_bytes = m->h2d_bytes;
+    o->d2h_bytes = m->d2h_bytes;
+  });
+}
+
+int ls_model_stream(const LsModel* m, void** stream) {
+  return guard([&] {
+    NEED(m);
+    NEED(stream);
+    *stream = reinterpret_cast<void*>(m->stream);
+  });
+}
+
+int ls_model_profile_enable(LsModel* m, int on) {
+  return guard([&] {
+    NEED(m);
+    m->prof_on = on != 0;
+    m->prof = LsProfile{};
+    m->prof_pending = false;
+  });
+}
+
+int ls_model_profile(const LsModel* m, LsProfile* out) {
+  return guard([&] {
+    NEED(m);
+    NEED(out);
+    *out = m->prof;
   });
 }
 
@@ -1025,6 +1149,21 @@ int ls_speculative_greedy(LsModel* target, LsModel* draft, const uint32_t* promp
     if (neos) NEED(eos);
     LS_CUDA(cudaSetDevice(target->device));
     speculative_greedy(*target, draft, prompt, plen, max_new, k, eos, neos, out_tokens, out_len, stats);
+  });
+}
+
+int ls_spec_continue(LsModel* target, LsModel* draft, const uint32_t* hist, uint64_t hlen, uint32_t first, uint64_t max_new,
+                     uint64_t k, const uint32_t* eos, uint64_t neos, uint32_t* out_tokens, uint64_t* out_len, LsSpecStats* stats) {
+  return guard([&] {
+    NEED(target);
+    NEED(out_tokens);
+    NEED(out_len);
+    NEED(stats);
+    if (hlen) NEED(hist);
+    if (neos) NEED(eos);
+    LS_CUDA(cudaSetDevice(target->device));
+    std::memset(stats, 0, sizeof *stats);
+    spec_continue(*target, draft, hist, hlen, first, max_new, k, eos, neos, out_tokens, out_len, stats);
   });
 }
 

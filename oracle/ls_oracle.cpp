@@ -1255,42 +1255,62 @@ static double now_s() {
     return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
 }
 
-std::vector<uint32_t> speculative_greedy(Model& target, Model& draft, const uint32_t* prompt, size_t plen, size_t max_new, size_t k,
-                                         const uint32_t* eos, size_t neos, SpecStats* st) {
+// Prompt-lookup drafter (an addition to the reference, restated here so that the CPU baseline runs
+// the same algorithm as the CUDA path): the tokens that followed the most recent earlier
+// occurrence of the longest suffix n-gram (n = 3, 2, 1) of the history.
+std::vector<uint32_t> lookup_draft(const std::vector<uint32_t>& hist, size_t kk) {
+    std::vector<uint32_t> out;
+    if (kk == 0 || hist.size() < 2) return out;
+    for (size_t n = std::min<size_t>(3, hist.size() - 1); n >= 1; n--) {
+        size_t tail = hist.size() - n;
+        for (size_t s = tail; s-- > 0;) {
+            bool ok = true;
+            for (size_t j = 0; j < n && ok; j++) ok = hist[s + j] == hist[tail + j];
+            if (!ok) continue;
+            for (size_t j = s + n; j < hist.size() && out.size() < kk; j++) out.push_back(hist[j]);
+            return out;
+        }
+    }
+    return out;
+}
+
+// src/spec.rs:94-149: the decode loop from a state where both models hold `hist0` and `a` is the
+// target's greedy token after it. draft == nullptr selects the lookup drafter.
+std::vector<uint32_t> spec_continue(Model& target, Model* draft, const uint32_t* hist0, size_t hlen, uint32_t a, size_t max_new,
+                                    size_t k, const uint32_t* eos, size_t neos, SpecStats* st) {
     if (k == 0 || k > MAX_DRAFT) throw Err("k must be between 1 and 32, not " + std::to_string(k));
-    if (plen == 0 || max_new == 0) throw Err("need a prompt and at least one token to generate");
-    if (target.pos != 0 || draft.pos != 0) throw Err("both models must start with an empty cache");
-    if (target.cfg.vocab != draft.cfg.vocab) throw Err("the draft and the target must share a vocabulary");
-    size_t need = plen + max_new + k;
-    if (need > target.max_ctx || need > draft.max_ctx) throw Err("prompt + max_new + k exceed the context limit");
+    if (max_new == 0) throw Err("need at least one token to generate");
+    if (target.pos != hlen || (draft && draft->pos != hlen)) throw Err("the models must hold exactly the history");
+    if (draft && target.cfg.vocab != draft->cfg.vocab) throw Err("the draft and the target must share a vocabulary");
+    size_t need = hlen + max_new + k;
+    if (need > target.max_ctx || (draft && need > draft->max_ctx)) throw Err("prompt + max_new + k exceed the context limit");
     size_t V = target.cfg.vocab;
     auto is_eos = [&](uint32_t t) {
         for (size_t i = 0; i < neos; i++)
             if (eos[i] == t) return true;
         return false;
     };
-    double t0 = now_s();
-    std::vector<float> tl(V), dl(V);
-    target.forward(prompt, plen, tl.data());
-    draft.forward(prompt, plen, dl.data());
-    st->first_secs = now_s() - t0;
-    std::vector<uint32_t> out;
-    uint32_t a = argmax(tl.data(), V);
-    out.push_back(a);
+    std::vector<uint32_t> out{a};
+    std::vector<uint32_t> hist(hist0, hist0 + hlen);
+    hist.push_back(a);
     bool stop = is_eos(a);
     double td = now_s();
-    std::vector<float> logits;
+    std::vector<float> logits, dl(V);
     while (!stop && out.size() < max_new) {
         size_t kk = std::min(k, max_new - out.size() - 1);
         double ts = now_s();
         std::vector<uint32_t> drafts;
-        uint32_t cur = a;
-        for (size_t i = 0; i < kk; i++) {
-            draft.forward(&cur, 1, dl.data());
-            uint32_t d = argmax(dl.data(), V);
-            st->draft_forwards++;
-            drafts.push_back(d);
-            cur = d;
+        if (draft) {
+            uint32_t cur = a;
+            for (size_t i = 0; i < kk; i++) {
+                draft->forward(&cur, 1, dl.data());
+                uint32_t d = argmax(dl.data(), V);
+                st->draft_forwards++;
+                drafts.push_back(d);
+                cur = d;
+            }
+        } else {
+            drafts = lookup_draft(hist, kk);
         }
         st->draft_secs += now_s() - ts;
         std::vector<uint32_t> block;
@@ -1303,13 +1323,14 @@ std::vector<uint32_t> speculative_greedy(Model& target, Model& draft, const uint
         st->target_secs += now_s() - ts;
         st->target_passes++;
         size_t m = 0;
-        while (m < kk && argmax(&logits[m * V], V) == drafts[m]) m++;
+        while (m < drafts.size() && argmax(&logits[m * V], V) == drafts[m]) m++;
         uint32_t next = argmax(&logits[m * V], V);
-        st->drafted += kk;
+        st->drafted += drafts.size();
         st->accepted += m;
         for (size_t i = 0; i <= m; i++) {
             uint32_t tok = i < m ? drafts[i] : next;
             out.push_back(tok);
+            hist.push_back(tok);
             if (is_eos(tok) || out.size() == max_new) {
                 stop = true;
                 break;
@@ -1317,18 +1338,36 @@ std::vector<uint32_t> speculative_greedy(Model& target, Model& draft, const uint
         }
         size_t want = p + m + 1;
         target.truncate(want);
-        if (draft.pos > want) {
-            draft.truncate(want);
-        } else if (draft.pos < want) {
-            ts = now_s();
-            draft.forward(&block[draft.pos - p], m + 1 - (draft.pos - p), dl.data());
-            st->draft_forwards++;
-            st->draft_secs += now_s() - ts;
+        if (draft) {
+            if (draft->pos > want) {
+                draft->truncate(want);
+            } else if (draft->pos < want) {
+                ts = now_s();
+                draft->forward(&block[draft->pos - p], m + 1 - (draft->pos - p), dl.data());
+                st->draft_forwards++;
+                st->draft_secs += now_s() - ts;
+            }
         }
         a = next;
     }
-    st->decode_secs = now_s() - td;
+    st->decode_secs += now_s() - td;
     return out;
+}
+
+std::vector<uint32_t> speculative_greedy(Model& target, Model* draft, const uint32_t* prompt, size_t plen, size_t max_new, size_t k,
+                                         const uint32_t* eos, size_t neos, SpecStats* st) {
+    if (k == 0 || k > MAX_DRAFT) throw Err("k must be between 1 and 32, not " + std::to_string(k));
+    if (plen == 0 || max_new == 0) throw Err("need a prompt and at least one token to generate");
+    if (target.pos != 0 || (draft && draft->pos != 0)) throw Err("both models must start with an empty cache");
+    if (draft && target.cfg.vocab != draft->cfg.vocab) throw Err("the draft and the target must share a vocabulary");
+    size_t need = plen + max_new + k;
+    if (need > target.max_ctx || (draft && need > draft->max_ctx)) throw Err("prompt + max_new + k exceed the context limit");
+    double t0 = now_s();
+    std::vector<float> tl(target.cfg.vocab), dl(target.cfg.vocab);
+    target.forward(prompt, plen, tl.data());
+    if (draft) draft->forward(prompt, plen, dl.data());
+    st->first_secs = now_s() - t0;
+    return spec_continue(target, draft, prompt, plen, argmax(tl.data(), target.cfg.vocab), max_new, k, eos, neos, st);
 }
 
 }  // namespace orc
@@ -1501,13 +1540,37 @@ int orc_speculative_greedy(void* target, void* draft, const uint32_t* prompt, ui
                            const uint32_t* eos, uint64_t neos, uint32_t* out, uint64_t* out_len, uint64_t* stats, double* times) {
     return guard([&] {
         SpecStats st;
-        auto toks = speculative_greedy(*(Model*)target, *(Model*)draft, prompt, plen, max_new, k, eos, neos, &st);
+        auto toks = speculative_greedy(*(Model*)target, (Model*)draft, prompt, plen, max_new, k, eos, neos, &st);
         std::memcpy(out, toks.data(), toks.size() * 4);
         *out_len = toks.size();
         uint64_t s[4] = {st.target_passes, st.drafted, st.accepted, st.draft_forwards};
         std::memcpy(stats, s, sizeof s);
         double t[4] = {st.target_secs, st.draft_secs, st.first_secs, st.decode_secs};
         std::memcpy(times, t, sizeof t);
+    });
+}
+
+int orc_spec_continue(void* target, void* draft, const uint32_t* hist, uint64_t hlen, uint32_t first, uint64_t max_new, uint64_t k,
+                      const uint32_t* eos, uint64_t neos, uint32_t* out, uint64_t* out_len, uint64_t* stats, double* times) {
+    return guard([&] {
+        SpecStats st;
+        auto toks = spec_continue(*(Model*)target, (Model*)draft, hist, hlen, first, max_new, k, eos, neos, &st);
+        std::memcpy(out, toks.data(), toks.size() * 4);
+        *out_len = toks.size();
+        uint64_t s4[4] = {st.target_passes, st.drafted, st.accepted, st.draft_forwards};
+        std::memcpy(stats, s4, sizeof s4);
+        double t[4] = {st.target_secs, st.draft_secs, st.first_secs, st.decode_secs};
+        std::memcpy(times, t, sizeof t);
+    });
+}
+
+// Greedy token after a forward of n tokens (prefill helper for the CPU baseline).
+int orc_forward_argmax(void* m, const uint32_t* toks, uint64_t n, uint32_t* tok) {
+    return guard([&] {
+        Model* M = (Model*)m;
+        std::vector<float> l(M->cfg.vocab);
+        M->forward(toks, n, l.data());
+        *tok = argmax(l.data(), M->cfg.vocab);
     });
 }
 

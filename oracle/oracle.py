@@ -68,6 +68,8 @@ def lib():
         "orc_forward_multi": (i32, [vp, vp, u64, u64, vp]),
         "orc_forward_hidden": (i32, [vp, vp, u64, u64, vp]),
         "orc_speculative_greedy": (i32, [vp, vp, vp, u64, u64, u64, vp, u64, vp, P(u64), P(u64), P(f64)]),
+        "orc_spec_continue": (i32, [vp, vp, vp, u64, C.c_uint32, u64, u64, vp, u64, vp, P(u64), P(u64), P(f64)]),
+        "orc_forward_argmax": (i32, [vp, vp, u64, P(C.c_uint32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -244,14 +246,38 @@ class Model:
         return out
 
 
-def speculative_greedy(target: Model, draft: Model, prompt, max_new: int, k: int, eos=()):
+def speculative_greedy(target: Model, draft: Model | None, prompt, max_new: int, k: int, eos=()):
+    """src/spec.rs:57-152; draft=None selects the prompt-lookup drafter."""
     p = np.ascontiguousarray(prompt, dtype=np.uint32)
     e = np.ascontiguousarray(list(eos) if len(eos) else [0], dtype=np.uint32)
     out = np.zeros(max(max_new, 1), dtype=np.uint32)
     n = C.c_uint64()
     stats = (C.c_uint64 * 4)()
     times = (C.c_double * 4)()
-    _check(lib().orc_speculative_greedy(target._h, draft._h, _ptr(p), p.size, max_new, k, _ptr(e), len(eos), _ptr(out), C.byref(n), stats, times))
+    _check(lib().orc_speculative_greedy(target._h, draft._h if draft is not None else None, _ptr(p), p.size, max_new, k, _ptr(e),
+                                        len(eos), _ptr(out), C.byref(n), stats, times))
     st = dict(zip(["target_passes", "drafted", "accepted", "draft_forwards"], list(stats)))
     st.update(zip(["target_secs", "draft_secs", "first_secs", "decode_secs"], list(times)))
     return out[: n.value].tolist(), st
+
+
+def spec_continue(target: Model, draft: Model | None, hist, first: int, max_new: int, k: int, eos=()):
+    """The decode loop from a prefilled state (both models hold ``hist``)."""
+    h = np.ascontiguousarray(hist, dtype=np.uint32)
+    e = np.ascontiguousarray(list(eos) if len(eos) else [0], dtype=np.uint32)
+    out = np.zeros(max(max_new, 1), dtype=np.uint32)
+    n = C.c_uint64()
+    stats = (C.c_uint64 * 4)()
+    times = (C.c_double * 4)()
+    _check(lib().orc_spec_continue(target._h, draft._h if draft is not None else None, _ptr(h), h.size, first, max_new, k,
+                                   _ptr(e), len(eos), _ptr(out), C.byref(n), stats, times))
+    st = dict(zip(["target_passes", "drafted", "accepted", "draft_forwards"], list(stats)))
+    st.update(zip(["target_secs", "draft_secs", "first_secs", "decode_secs"], list(times)))
+    return out[: n.value].tolist(), st
+
+
+def forward_argmax(m: Model, tokens) -> int:
+    t = np.ascontiguousarray(tokens, dtype=np.uint32)
+    r = C.c_uint32()
+    _check(lib().orc_forward_argmax(m._h, _ptr(t), t.size, C.byref(r)))
+    return r.value

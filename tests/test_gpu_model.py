@@ -25,7 +25,7 @@ def tiny():
     d = F.TempDir("gpu-model").path
     F.write_tiny_model(d, 13)
     paths = {}
-    for body, embed in [((8, 32), (8, 32)), ((4, 32), (4, 32)), ((8, 64), (8, 64)), ((4, 16), (8, 32))]:
+    for body, embed in [((8, 32), (8, 32)), ((4, 32), (4, 32)), ((8, 64), (8, 64)), ((4, 16), (8, 32)), ((4, 32), (8, 32))]:
         p = os.path.join(d, f"q{body[0]}g{body[1]}e{embed[0]}g{embed[1]}.lsq")
         O.quantize_model(d, p, body, embed, clip=True)
         paths[(body, embed)] = p
