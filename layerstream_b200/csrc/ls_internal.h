@@ -176,6 +176,8 @@ struct GemvLaunch {
 };
 
 void launch_gemv(const GemvLaunch& g, cudaStream_t s);
+// Smallest K-split whose staged activations fit in shared memory.
+int gemv_min_ksplit(const QMat& w, int M);
 void launch_repack(const RepackSrc& src, int bits, int group, int cols, uint8_t* data, uint16_t* scales, int rows_pad,
                    cudaStream_t s);
 void launch_embed(const QMat& e, const Ctl* ctl, float* x, int hidden, int M, cudaStream_t s);

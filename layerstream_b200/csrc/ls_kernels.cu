@@ -444,8 +444,27 @@ static void launch_gemv_b(const GemvLaunch& g, cudaStream_t s) {
   return launch_gemv_t<BITS, G16, 16>(g, s);
 }
 
+int gemv_mt(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16; }
+
+int gemv_min_ksplit(const QMat& w, int M) {
+  const int MT = gemv_mt(M);
+  const size_t budget = 200 * 1024 - (size_t)GEMV_WARPS * MT * 32 * 4;
+  const int wpc = 128 / w.bits;
+  for (int ks = 1; ks <= 64; ks++) {
+    int maxcol = 0;
+    for (int k = 0; k < ks; k++) {
+      int c0, c1;
+      gemv_split(w.chunks(), w.bits, w.group, ks, k, &c0, &c1);
+      maxcol = max(maxcol, (c1 - c0) * wpc);
+    }
+    if ((size_t)MT * maxcol * 4 <= budget) return ks;
+  }
+  LS_THROW(-1, "matrix too wide for the GEMV kernel");
+}
+
 void launch_gemv(const GemvLaunch& g, cudaStream_t s) {
   if (g.M <= 0) return;
+  if (g.ksplit < gemv_min_ksplit(g.w, g.M)) LS_THROW(-1, "GEMV split too small for shared memory");
   if (g.w.bits == 8) return launch_gemv_b<8, false>(g, s);
   if (g.w.group == 16) return launch_gemv_b<4, true>(g, s);
   return launch_gemv_b<4, false>(g, s);

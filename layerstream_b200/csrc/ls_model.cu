@@ -317,13 +317,13 @@ struct LsModel {
       host_embed_dev = reinterpret_cast<const uint8_t*>(dp);
       const size_t chunk_rows = std::min<size_t>(kHeadRows, V);
       raw_slot_bytes = std::max(lt, chunk_rows * rb);
-      const size_t per = layer_plane_bytes();
-      const size_t head_per = qmat_bytes((int)chunk_rows, (int)h, cfg.embed_format);
+      // a slot holds either a layer or a head chunk, so their planes share one region
+      const size_t per = std::max(layer_plane_bytes(), qmat_bytes((int)chunk_rows, (int)h, cfg.embed_format));
       for (int s = 0; s < slots; s++) {
         raw_slot.push_back(dalloc<uint8_t>(raw_slot_bytes));
         uint8_t* p = dalloc<uint8_t>(per);
+        uint8_t* hp = p;
         layers.push_back(carve_layer(p));
-        uint8_t* hp = dalloc<uint8_t>(head_per);
         head_slot.push_back(carve(hp, (int)chunk_rows, (int)h, cfg.embed_format));
         cudaEvent_t a, b;
         LS_CUDA(cudaEventCreateWithFlags(&a, cudaEventDisableTiming));
@@ -331,7 +331,7 @@ struct LsModel {
         ev_loaded.push_back(a);
         ev_free.push_back(b);
       }
-      resident_weight_bytes = (size_t)slots * (raw_slot_bytes + per + head_per);
+      resident_weight_bytes = (size_t)slots * (raw_slot_bytes + per);
     }
 
     // KV cache [L][kv_heads][max_ctx][hd] f16 and the RoPE table, computed here with the same float
@@ -386,11 +386,13 @@ struct LsModel {
       prof_ev.push_back(e);
     }
     prof_rec.push_back({cls, bytes});
-    LS_CUDA(cudaEventRecord(prof_ev[2 * i], s));
+    // External: inside a stream capture this becomes an event-record node that timestamps every
+    // replay of the graph (a plain record would only be a capture dependency)
+    LS_CUDA(cudaEventRecordWithFlags(prof_ev[2 * i], s, cudaEventRecordExternal));
     return (int)i;
   }
   void prof_end(int i, cudaStream_t s) {
-    if (i >= 0) LS_CUDA(cudaEventRecord(prof_ev[2 * i + 1], s));
+    if (i >= 0) LS_CUDA(cudaEventRecordWithFlags(prof_ev[2 * i + 1], s, cudaEventRecordExternal));
   }
   double gemv_bytes(const QMat& w, int M, int out_rows) const {
     const double rb = (double)w.cols * w.bits / 8 + (double)w.cols / w.group * 2;
@@ -405,7 +407,8 @@ struct LsModel {
       const ProfRec& r = (*prof_cur)[i];
       prof.launches[r.cls]++;
       prof.ms[r.cls] += ms;
-      prof.bytes[r.cls] += r.bytes;
+      // attention also reads the cached K/V rows of this pass (pos0 of the pass, f16 K and V)
+      prof.bytes[r.cls] += r.bytes + (r.cls == 1 ? (double)ctl_host->pos0 * cfg.kv_dim() * 2 * 2 : 0.0);
     }
   }
 
@@ -416,7 +419,7 @@ struct LsModel {
     const int units = w.chunks() / U;
     const int by_work = std::max(1, units * U / 16);  // keep >= 16 chunks per CTA
     const int want = std::max(1, (2 * num_sms) / std::max(1, tiles * nz));
-    return std::max(1, std::min({want, by_work, units, 32}));
+    return std::max(gemv_min_ksplit(w, M), std::min({want, by_work, units, 32}));
   }
 
   void gemv(const QMat& w, const float* xin, int x_stride, int M, int epi, float* y, int y_stride, const uint16_t* norm_bf16,
@@ -485,10 +488,9 @@ struct LsModel {
     a.max_ctx = (int)max_ctx;
     a.M = T;
     a.max_splits = att_slots;
-    // attention bytes: cached K/V rows read (f16) + new rows written + q and out (f32); the cached
-    // length is the host's view of pos0 when the pass is enqueued (exact outside graph replays,
-    // which re-time the same shape)
-    pi = pb(1, (double)pos * kv * 2 * 2 + (double)T * kv * 2 * 2 + (double)T * (h + 2 * kv) * 4 + (double)T * h * 4);
+    // attention bytes: new K/V rows written (f16) + q|k|v in and out (f32); the cached rows read are
+    // added per replay from that pass's pos0 (prof_collect)
+    pi = pb(1, (double)T * kv * 2 * 2 + (double)T * (h + 2 * kv) * 4 + (double)T * h * 4);
     launch_attention(a, s);
     prof_end(pi, s);
     pi = pb(2, gemv_bytes(W.o, T, h) + (double)T * h * 4);
@@ -972,7 +974,8 @@ static void qgemv_device(const LsQWeights* q, const float* x, uint64_t M, float*
   const int tiles = q->w.rows_pad / 32, nz = ((int)M + 15) / 16;
   const int U = (q->w.bits == 4 && q->w.group >= 32) ? q->w.group / 32 : 1;
   const int units = q->w.chunks() / U;
-  g.ksplit = std::max(1, std::min({(2 * q->num_sms) / std::max(1, tiles * nz), std::max(1, units * U / 16), units, 32}));
+  g.ksplit = std::max(gemv_min_ksplit(q->w, (int)M),
+                      std::min({(2 * q->num_sms) / std::max(1, tiles * nz), std::max(1, units * U / 16), units, 32}));
   g.partial = q->partial;
   g.tickets = q->tickets;
   launch_gemv(g, s);

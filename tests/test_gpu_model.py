@@ -212,7 +212,10 @@ def test_streaming_gives_bit_identical_logits_and_reads_the_expected_bytes(tiny,
     info = s.info
     per_pass = info.layers * info.layer_bytes + info.vocab * info.embed_row_bytes
     assert s.report()["bytes_read"] == 4 * per_pass + 9 * info.embed_row_bytes
-    assert s.report()["resident_weight_bytes"] < r.report()["resident_weight_bytes"]
+    # HBM holds `slots` slots of one layer or head chunk (raw bytes + repacked planes), never the model
+    chunk = min(4096, info.vocab) * info.embed_row_bytes
+    slot_max = 2 * max(info.layer_bytes, chunk) + 64 * 1024
+    assert s.report()["resident_weight_bytes"] <= slots * slot_max
 
 
 def test_bad_requests_are_errors_not_crashes(tiny):
