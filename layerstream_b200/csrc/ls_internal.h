@@ -169,6 +169,9 @@ struct GemvLaunch {
   int n_part_tiles = 0;          // tiles over all launches of this pass (finalize)
   float* logits = nullptr;       // optional full logits [M][logits_stride]
   int logits_stride = 0;
+  // grid: CTAs along the row tiles (0 = one warp per tile)
+  int grid_x = 0;
+  int* err = nullptr;  // set to nonzero by a kernel whose bounded wait gave up
   // split-K
   int ksplit = 1;
   float* partial = nullptr;  // [row_ctas][ksplit][M][32]
@@ -178,6 +181,12 @@ struct GemvLaunch {
 void launch_gemv(const GemvLaunch& g, cudaStream_t s);
 // Smallest K-split whose staged activations fit in shared memory.
 int gemv_min_ksplit(const QMat& w, int M);
+int gemv_grid_x(const QMat& w, int ksplit, int M, int num_sms);
+int gemv_mt(int M);
+// tensor-core (tcgen05) GEMV
+bool gemv_tc_supported(const QMat& w);
+int gemv_tc_min_ksplit(const QMat& w, int M);
+void launch_gemv_tc(const GemvLaunch& g, cudaStream_t s);
 void launch_repack(const RepackSrc& src, int bits, int group, int cols, uint8_t* data, uint16_t* scales, int rows_pad,
                    cudaStream_t s);
 void launch_embed(const QMat& e, const Ctl* ctl, float* x, int hidden, int M, cudaStream_t s);

@@ -70,6 +70,49 @@ struct LayerW {
   uint16_t* qkv_bias = nullptr;  // q_b | k_b | v_b
 };
 
+// GEMV path: tensor cores (tcgen05) wherever the format allows, unless LS_GEMV=fma asks for the
+// CUDA-core kernel (kept as a cross-check).
+bool use_tc(const QMat& w) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char* e = getenv("LS_GEMV");
+    forced = (e && std::string(e) == "fma") ? 1 : 0;
+  }
+  return forced == 0 && gemv_tc_supported(w);
+}
+
+// Tensor-core GEMV: K-split and grid. Aim for ~4 CTAs per SM over (tiles x slices x token groups),
+// keep at least two 64-wide K blocks per slice, never fewer slices than shared memory needs.
+void choose_tc(const QMat& w, int M, int num_sms, bool argmax, int* ksplit, int* grid_x) {
+  const int tiles128 = (w.rows_pad / 32 + 3) / 4;
+  const int nz = (M + ((M <= 16) ? 16 : (M <= 32) ? 32 : (M <= 48) ? 48 : 64) - 1) /
+                 ((M <= 16) ? 16 : (M <= 32) ? 32 : (M <= 48) ? 48 : 64);
+  const int kb = (w.bits == 4 && w.group > 64) ? w.group : 64;
+  const int nblk = w.cols / kb;
+  const int target = 4 * num_sms;
+  int ks = 1;
+  if (!argmax) {
+    ks = (target + tiles128 * nz - 1) / (tiles128 * nz);
+    ks = std::min(ks, std::max(1, nblk / 2));
+    ks = std::min(ks, 32);
+  }
+  ks = std::max(ks, gemv_tc_min_ksplit(w, M));
+  ks = std::min(ks, nblk);
+  *ksplit = ks;
+  *grid_x = std::max(1, std::min(tiles128, (target + ks * nz - 1) / (ks * nz)));
+}
+
+// K-split of a GEMV launch: aim for ~8 warp-tiles per SM, keep at least 8 chunks (one unrolled
+// round of loads) per slice, and never less than the staged activations need.
+int choose_ksplit(const QMat& w, int M, int num_sms) {
+  const int tiles = w.rows_pad / 32, nz = (M + 15) / 16;
+  const int U = (w.bits == 4 && w.group >= 32) ? w.group / 32 : 1;
+  const int units = w.chunks() / U;
+  const int by_work = std::max(1, w.chunks() / 8 / U);
+  const int want = std::max(1, (8 * num_sms + tiles * nz - 1) / (tiles * nz));
+  return std::max(gemv_min_ksplit(w, M), std::min({want, by_work, units, 32}));
+}
+
 void check_gpu_format(const Config& c) {
   for (const WeightFormat* f : {&c.format, &c.embed_format}) {
     if (!f->quant()) LS_THROW(LS_ERR_ARG, "the CUDA path reads quantized (.lsq) models; bf16 weights are not supported yet");
@@ -412,15 +455,7 @@ struct LsModel {
     }
   }
 
-  int pick_ksplit(const QMat& w, int M) const {
-    const int tiles = w.rows_pad / 32;
-    const int nz = (M + 15) / 16;
-    const int U = (w.bits == 4 && w.group >= 32) ? w.group / 32 : 1;
-    const int units = w.chunks() / U;
-    const int by_work = std::max(1, units * U / 16);  // keep >= 16 chunks per CTA
-    const int want = std::max(1, (2 * num_sms) / std::max(1, tiles * nz));
-    return std::max(gemv_min_ksplit(w, M), std::min({want, by_work, units, 32}));
-  }
+  int pick_ksplit(const QMat& w, int M) const { return choose_ksplit(w, M, num_sms); }
 
   void gemv(const QMat& w, const float* xin, int x_stride, int M, int epi, float* y, int y_stride, const uint16_t* norm_bf16,
             const float* norm_f32, const uint16_t* bias, cudaStream_t s) {
@@ -436,14 +471,22 @@ struct LsModel {
     g.y = y;
     g.y_stride = y_stride;
     g.bias = bias;
-    g.ksplit = (epi == EPI_ARGMAX) ? 1 : pick_ksplit(w, M);
     g.partial = partial;
     g.tickets = tickets;
+    g.err = &ctl->err;
+    if (use_tc(w)) {
+      choose_tc(w, M, num_sms, epi == EPI_ARGMAX, &g.ksplit, &g.grid_x);
+      launch_gemv_tc(g, s);
+      return;
+    }
+    g.ksplit = (epi == EPI_ARGMAX) ? 1 : pick_ksplit(w, M);
+    g.grid_x = gemv_grid_x(w, g.ksplit, M, num_sms);
     launch_gemv(g, s);
   }
 
-  void head(const QMat& w, const float* xin, int n, bool want_logits, int row_offset, int n_valid, int part_tile_offset,
-            int finalize, int n_part_tiles, cudaStream_t s) {
+  // Returns the number of argmax parts (CTAs) the launch writes.
+  int head(const QMat& w, const float* xin, int n, bool want_logits, int row_offset, int n_valid, int part_tile_offset,
+           int finalize, int n_part_tiles, cudaStream_t s) {
     GemvLaunch g;
     g.w = w;
     g.x = xin;
@@ -462,7 +505,15 @@ struct LsModel {
     g.n_part_tiles = n_part_tiles;
     g.logits = want_logits ? logits : nullptr;
     g.logits_stride = (int)cfg.vocab;
+    g.err = &ctl->err;
+    if (use_tc(w)) {
+      choose_tc(w, n, num_sms, true, &g.ksplit, &g.grid_x);
+      launch_gemv_tc(g, s);
+      return g.grid_x;
+    }
+    g.grid_x = gemv_grid_x(w, 1, n, num_sms);
     launch_gemv(g, s);
+    return g.grid_x;
   }
 
   void layer_compute(const LayerW& W, size_t l, int T, cudaStream_t s) {
@@ -570,8 +621,8 @@ struct LsModel {
         hq.rows_pad = pad32((int)rows);
         repack_embed_rows(raw_slot[s], 0, (int)rows, hq, stream);
         LS_CUDA(cudaEventRecord(ev_free[s], stream));
-        head(hq, x + (size_t)(T - n_logits) * h, n_logits, want_logits, (int)first, (int)rows, part_tiles, 0, 0, stream);
-        part_tiles += hq.rows_pad / 32;
+        part_tiles += head(hq, x + (size_t)(T - n_logits) * h, n_logits, want_logits, (int)first, (int)rows, part_tiles, 0, 0,
+                           stream);
       }
     }
     if (n_logits > 0) launch_argmax_finalize(arg_parts, part_tiles, n_logits, ctl, stream);
@@ -638,6 +689,7 @@ struct LsModel {
     d2h_bytes += sizeof(Ctl) - offsetof(Ctl, argmax);
     LS_CUDA(cudaStreamSynchronize(stream));
     prof_collect();
+    if (ctl_host->err == 1) LS_THROW(LS_ERR_DEVICE, "a tensor-core kernel gave up waiting on an mbarrier (bounded wait)");
     if (ctl_host->err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
   }
 
@@ -924,11 +976,13 @@ struct LsQWeights {
   void* mem = nullptr;
   float* partial = nullptr;
   unsigned* tickets = nullptr;
+  int* err = nullptr;
   int num_sms = 148;
   ~LsQWeights() {
     cudaFree(mem);
     cudaFree(partial);
     cudaFree(tickets);
+    cudaFree(err);
   }
 };
 
@@ -959,6 +1013,8 @@ static void qweights_upload(LsQWeights* q, int dev, int bits, int group, const u
   LS_CUDA(cudaMalloc(&q->partial, tiles * 32 * 16 * 32 * 4 * 3));
   LS_CUDA(cudaMalloc(&q->tickets, tiles * 4 * 3));
   LS_CUDA(cudaMemset(q->tickets, 0, tiles * 4 * 3));
+  LS_CUDA(cudaMalloc(&q->err, sizeof(int)));
+  LS_CUDA(cudaMemset(q->err, 0, sizeof(int)));
 }
 
 static void qgemv_device(const LsQWeights* q, const float* x, uint64_t M, float* y, cudaStream_t s) {
@@ -971,14 +1027,23 @@ static void qgemv_device(const LsQWeights* q, const float* x, uint64_t M, float*
   g.epi = EPI_STORE;
   g.y = y;
   g.y_stride = q->w.rows;
-  const int tiles = q->w.rows_pad / 32, nz = ((int)M + 15) / 16;
-  const int U = (q->w.bits == 4 && q->w.group >= 32) ? q->w.group / 32 : 1;
-  const int units = q->w.chunks() / U;
-  g.ksplit = std::max(gemv_min_ksplit(q->w, (int)M),
-                      std::min({(2 * q->num_sms) / std::max(1, tiles * nz), std::max(1, units * U / 16), units, 32}));
   g.partial = q->partial;
   g.tickets = q->tickets;
+  g.err = q->err;
+  if (use_tc(q->w)) {
+    choose_tc(q->w, (int)M, q->num_sms, false, &g.ksplit, &g.grid_x);
+    launch_gemv_tc(g, s);
+    return;
+  }
+  g.ksplit = choose_ksplit(q->w, (int)M, q->num_sms);
+  g.grid_x = gemv_grid_x(q->w, g.ksplit, (int)M, q->num_sms);
   launch_gemv(g, s);
+}
+
+static void qweights_check(const LsQWeights* q) {
+  int e = 0;
+  LS_CUDA(cudaMemcpy(&e, q->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e) LS_THROW(LS_ERR_DEVICE, "a tensor-core kernel gave up waiting on an mbarrier (bounded wait)");
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -1241,6 +1306,7 @@ int ls_qgemv_host(int bits, int group, const uint8_t* rows_raw, uint64_t rows, u
       cudaEventDestroy(b);
     }
     LS_CUDA(cudaMemcpy(y, dy, M * rows * 4, cudaMemcpyDeviceToHost));
+    qweights_check(q.get());
   });
 }
 
