@@ -67,7 +67,49 @@ def parse():
     ap.add_argument("--cpu-sample-tokens", type=int, default=0, help="decode tokens per CPU sample (0: auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="print the per-kernel profile to stderr")
+    ap.add_argument("--ncu-case", choices=["pass", "gemv"], default=None,
+                    help="short fixed workloads for ncu: 'pass' = prefill + 3 verify passes of the bench model, "
+                         "'gemv' = 3 launches of the LM-head GEMV (151936 x 896, int4 g32, M = 9)")
     return ap.parse_args()
+
+
+def ncu_case(args, cfg):
+    """Small deterministic workloads to capture under ncu (see profiles/)."""
+    import torch
+
+    import layerstream_b200 as ls
+    from layerstream_b200 import synth
+
+    torch.cuda.set_device(0)
+    os.makedirs(args.root, exist_ok=True)
+    t_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True)
+    if args.ncu_case == "pass":
+        plen, k = cfg["prompt"], cfg["k"]
+        m = ls.Model(t_path, max_ctx=plen + cfg["max_new"] + k + 16)
+        prompt = prompt_for(cfg, m.vocab, 0)
+        first = m.forward(prompt, want_logits=False)
+        block = [first] + prompt[-k:]
+        for _ in range(3):
+            m.truncate(plen)
+            m.verify(block)
+        print(json.dumps({"ncu_case": "pass", "verify_passes": 3, "block": len(block)}))
+        return
+    # gemv: the LM head matrix of the bench model as a standalone GEMV, M = k + 1 rows
+    info_m = ls.Model(t_path, max_ctx=64)
+    V, h = info_m.vocab, info_m.info.hidden
+    rb = info_m.info.embed_row_bytes
+    start = os.path.getsize(t_path) - h * 2 - V * rb
+    info_m.close()
+    raw = np.fromfile(t_path, dtype=np.uint8, count=V * rb, offset=start)
+    w = ls.QWeights(cfg["embed"][0], cfg["embed"][1], raw, V, h)
+    M = cfg["k"] + 1
+    x = torch.randn(M, h, device="cuda")
+    y = torch.empty(M, V, device="cuda")
+    for _ in range(3):
+        w.gemv(x.data_ptr(), M, y.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_case": "gemv", "rows": V, "cols": h, "M": M, "bytes_per_launch": w.bytes(M)}))
+
 
 
 def peaks():
@@ -228,6 +270,9 @@ def main():
     cfg = dict(CONFIGS[args.config])
     if args.drafter:
         cfg["drafter"] = args.drafter
+    if args.ncu_case:
+        ncu_case(args, cfg)
+        return
     rank, world, local, dist = setup_dist(args)
     workload = (f"config{args.config}: {cfg['shape']} Qwen2 random-init int{cfg['body'][0]} g{cfg['body'][1]}, "
                 f"{cfg['prompt']}-token prompt, {cfg['max_new']} new tokens, k={cfg['k']}, batch 1 per GPU, "

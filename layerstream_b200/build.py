@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "liblayerstream_b200.so")
-SOURCES = ["ls_kernels.cu", "ls_model.cu", "ls_format.cpp"]
+SOURCES = ["ls_gemv_tc.cu", "ls_kernels.cu", "ls_model.cu", "ls_format.cpp"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
@@ -33,16 +33,19 @@ def needs_build() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not needs_build():
         return OUT
-    objs = []
+    objs, procs = [], []
     build_dir = os.path.join(HERE, "_build")
     os.makedirs(build_dir, exist_ok=True)
-    for src in SOURCES:
+    for src in SOURCES:  # translation units compile in parallel
         obj = os.path.join(build_dir, src + ".o")
         cmd = ["nvcc", *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
         if verbose:
             print(" ".join(cmd))
-        subprocess.run(cmd, check=True)
+        procs.append((src, subprocess.Popen(cmd)))
         objs.append(obj)
+    for src, p in procs:
+        if p.wait() != 0:
+            raise RuntimeError(f"nvcc failed on {src}")
     cmd = ["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", OUT, *objs]
     if verbose:
         print(" ".join(cmd))

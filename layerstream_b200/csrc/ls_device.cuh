@@ -4,6 +4,10 @@
 #include <math_constants.h>
 #include <stdint.h>
 
+#include <map>
+#include <mutex>
+#include <string>
+
 #include "ls_internal.h"
 
 namespace ls {
@@ -81,5 +85,102 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   if (bytes >= 16) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes & ~15u) : "memory");
 }
 
+
+constexpr int GEMV_WARPS = 8;
+constexpr int GEMV_THREADS = GEMV_WARPS * 32;
+
+// Reduces the per-CTA argmax parts of every token (first-maximum rule), then applies the
+// acceptance rule of src/spec.rs:121-125 (verify) or records the next token (forward).
+// Run by one whole CTA of at most GEMV_THREADS threads.
+__device__ __noinline__ static void argmax_finalize_block(const ArgPart* parts, int nparts, int M, Ctl* ctl) {
+  __shared__ float s_v[GEMV_THREADS];
+  __shared__ uint32_t s_i[GEMV_THREADS];
+  const int per = (int)blockDim.x / M;  // threads per token (M <= blockDim.x)
+  const int t = threadIdx.x % M, j = threadIdx.x / M;
+  float v = -CUDART_INF_F;
+  uint32_t idx = 0xffffffffu;
+  if (j < per) {
+#pragma unroll 8
+    for (int k = j; k < nparts; k += per) {
+      const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(parts + (size_t)k * M + t));
+      const float pv = __uint_as_float(raw.x);
+      if (arg_better(pv, raw.y, v, idx)) {
+        v = pv;
+        idx = raw.y;
+      }
+    }
+  }
+  s_v[threadIdx.x] = v;
+  s_i[threadIdx.x] = idx;
+  __syncthreads();
+  if (threadIdx.x < M) {
+    for (int jj = 1; jj < per; jj++) {
+      const int q = jj * M + threadIdx.x;
+      if (arg_better(s_v[q], s_i[q], v, idx)) {
+        v = s_v[q];
+        idx = s_i[q];
+      }
+    }
+    ctl->argmax[threadIdx.x] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (ctl->mode == 1) {
+      // longest prefix of guesses the target agrees with, then the correction (or bonus) token;
+      // the cache keeps [a, d_1 .. d_m]
+      int m = 0;
+      while (m < M - 1 && ctl->argmax[m] == ctl->tokens[m + 1]) m++;
+      ctl->m = m;
+      ctl->next = ctl->argmax[m];
+      ctl->pos0 += m + 1;
+    } else {
+      ctl->m = 0;
+      ctl->next = ctl->argmax[M - 1];
+      ctl->pos0 += ctl->M;
+      if (ctl->mode == 2) ctl->tokens[0] = ctl->next;
+    }
+  }
+}
+
+// Raises a kernel's dynamic shared-memory limit (per device) before a launch that needs it. The
+// default 48 KB limit covers static plus dynamic shared memory, so the static part is counted.
+template <class K>
+static void ensure_smem(K kernel, size_t dyn) {
+  struct Entry {
+    size_t configured;
+    size_t static_bytes;
+  };
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, Entry> seen;  // (kernel, device)
+  int dev = 0;
+  LS_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  auto it = seen.find(key);
+  if (it == seen.end()) {
+    cudaFuncAttributes fa;
+    LS_CUDA(cudaFuncGetAttributes(&fa, kernel));
+    it = seen.emplace(key, Entry{0, fa.sharedSizeBytes}).first;
+  }
+  if (dyn + it->second.static_bytes > 48 * 1024 && dyn > it->second.configured) {
+    LS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
+    it->second.configured = dyn;
+  }
+}
+
+template <class K, class... Args>
+static void launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  LS_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...));
+}
 
 }  // namespace ls

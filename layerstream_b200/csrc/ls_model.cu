@@ -407,7 +407,7 @@ struct LsModel {
     partial_floats = (size_t)max_tiles * 32 * 16 * 32 * (kMaxT / 16 + 1);
     partial = dalloc<float>(partial_floats);
     arg_ticket = dalloc<unsigned>(1);
-    att_slots = (int)std::max<size_t>(1, std::min<size_t>(16, (max_ctx + 63) / 64));
+    att_slots = (int)std::max<size_t>(1, std::min<size_t>(16, (max_ctx + 63) / 64));  // <= ATT_MAX_SLOTS
     att_part_floats = cfg.heads * (size_t)att_slots * kMaxT * (cfg.head_dim + 2);
     att_part = dalloc<float>(att_part_floats);
     att_tickets = dalloc<unsigned>(cfg.heads);
