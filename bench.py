@@ -390,24 +390,32 @@ def main():
     h2d = (r1["h2d_bytes"] - r0["h2d_bytes"]) // max(args.e2e_steps, 1)
     d2h = (r1["d2h_bytes"] - r0["d2h_bytes"]) // max(args.e2e_steps, 1)
 
-    # roofline of the dominant kernel class (live CUDA-event timing inside the passes)
+    # roofline of the dominant kernel (live CUDA-event timing inside the passes). The launch list
+    # (profiles/verify_pass_launches_config2.md) shows the tensor-core GEMV is ~80 % of a pass:
+    # its launches per pass are QKV, O, gate/up and down on every layer (timed on one sampled
+    # layer, times L) plus the LM head.
     peak, peak_kind = peaks()
     L = info.layers
-    share = {}
+    per_pass = {}
     for c, p in prof.items():
         if c == "pass" or not p["launches"]:
             continue
-        share[c] = p["ms"] * (L if c not in ("head",) else 1)
-    dom = max(share, key=share.get) if share else None
+        mult = 1 if c == "head" else L
+        per_pass[c] = (p["bytes"] / p["launches"] * mult, p["ms"] / p["launches"] * mult, mult)
     roof = None
-    if dom:
-        p = prof[dom]
-        achieved = p["bytes"] / (p["ms"] / 1e3) / 1e9
-        traffic = profile_traffic(dom)
-        roof = {"bound": "hbm", "kernel": f"gemv ({dom})" if dom != "attention" else "attention", "achieved": achieved,
+    gemv_c = [c for c in ("qkv", "o", "gate_up", "down", "head") if c in per_pass]
+    if gemv_c:
+        b = sum(per_pass[c][0] for c in gemv_c)
+        t_ms = sum(per_pass[c][1] for c in gemv_c)
+        n = sum(per_pass[c][2] for c in gemv_c)
+        achieved = b / (t_ms / 1e3) / 1e9
+        traffic = profile_traffic("gemv-pass")
+        roof = {"bound": "hbm", "kernel": "gemv_tc_kernel (all launches of a verify pass)", "achieved": achieved,
                 "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                "traffic": traffic, "algorithmic_bytes_per_launch": p["bytes"] / p["launches"],
-                "avg_launch_us": p["ms"] * 1e3 / p["launches"]}
+                "traffic": traffic, "algorithmic_bytes_per_launch": b / n, "avg_launch_us": t_ms * 1e3 / n,
+                "launches_per_pass": n,
+                "per_class": {c: {"gbs": per_pass[c][0] / (per_pass[c][1] / 1e3) / 1e9,
+                                  "us_per_launch": per_pass[c][1] * 1e3 / per_pass[c][2]} for c in per_pass}}
     vstep = None
     pp = prof["pass"]
     if pp["launches"]:
@@ -417,7 +425,7 @@ def main():
         pass_s = pp["ms"] / pp["launches"] / 1e3
         vstep = {"bytes_per_pass": wbytes + kvbytes, "avg_pass_us": pass_s * 1e6, "achieved_gbs": (wbytes + kvbytes) / pass_s / 1e9,
                  "frac": (wbytes + kvbytes) / pass_s / 1e9 / peak,
-                 "kernel_share_est": {c: share[c] / (pp["ms"]) for c in share}}
+                 "kernel_share_est": {c: per_pass[c][1] / (pp["ms"] / pp["launches"]) for c in per_pass}}
     acc = sum(s["accepted"] for s in stats)
     dr = sum(s["drafted"] for s in stats)
     tp = sum(s["target_passes"] for s in stats)

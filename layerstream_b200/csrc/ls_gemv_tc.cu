@@ -109,7 +109,7 @@ __device__ __forceinline__ uint32_t h2_splat(float s) {
 }  // namespace tc
 
 constexpr int TC_THREADS = 128;
-constexpr int TC_STAGES = 4;
+constexpr int TC_STAGES = 6;
 
 // K elements per A block: one group for int4 groups of 128, else 64.
 __host__ __device__ constexpr int tc_kb(int bits, int group) { return (bits == 4 && group > 64) ? group : 64; }
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
   constexpr int TCOLS = (2 * ACOLS + NT <= 128) ? 128 : 256;
   constexpr int NW = TC_THREADS / 32;
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  __shared__ uint64_t bar_a[2], bar_d;
+  __shared__ uint64_t bar_a[2], bar_full[2], bar_d;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ float s_inv[NT];
@@ -156,6 +156,8 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
   if (threadIdx.x == 0) {
     tc::mbar_init(&bar_a[0], 1);
     tc::mbar_init(&bar_a[1], 1);
+    tc::mbar_init(&bar_full[0], TC_THREADS);
+    tc::mbar_init(&bar_full[1], TC_THREADS);
     tc::mbar_init(&bar_d, 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -251,15 +253,17 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
     const bool row_valid = t32 < tiles32;
     const uint8_t* db = g.w.data + ((size_t)(row_valid ? t32 : 0) * nch) * 512 + lane * 16;
     const uint16_t* sb = g.w.scales + (size_t)(row_valid ? t32 : 0) * ngr * 32 + lane;
-    auto load_scales = [&](int kb, uint32_t (&sc)[NS]) {
+    // raw bf16 scales, loaded two blocks ahead and converted only when used
+    auto load_scales = [&](int kb, uint16_t (&sc)[NS]) {
 #pragma unroll
       for (int s = 0; s < NS; s++) {
         const int gi = (kb * KB) / G + s;
-        sc[s] = tc::h2_splat(row_valid && kb < kb1 ? bf16f(sb[(size_t)gi * 32]) : 0.f);
+        sc[s] = (row_valid && kb < kb1) ? sb[(size_t)gi * 32] : (uint16_t)0;
       }
     };
-    uint32_t scur[NS], snext[NS];
-    load_scales(kb0, scur);
+    uint16_t sraw0[NS], sraw1[NS], sraw2[NS];
+    load_scales(kb0, sraw0);
+    load_scales(kb0 + 1, sraw1);
     if (t128 != first) issue_prologue(t128);
     for (int kb = kb0; kb < kb1; kb++) {
       const int it = kb - kb0;
@@ -272,7 +276,10 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
         }
         tc::cp_commit();
       }
-      load_scales(kb + 1, snext);
+      load_scales(kb + 2, sraw2);
+      uint32_t scur[NS];
+#pragma unroll
+      for (int q = 0; q < NS; q++) scur[q] = tc::h2_splat(bf16f(sraw0[q]));
       tc::cp_wait<TC_STAGES - 1>();
       uint4 wv[CPB];
       const uint8_t* rs = ring + (size_t)(it % TC_STAGES) * kStageStride + (size_t)threadIdx.x * CPB * 16;
@@ -325,42 +332,54 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
         }
       }
 #pragma unroll
-      for (int s = 0; s < NS; s++) scur[s] = snext[s];
+      for (int q = 0; q < NS; q++) {
+        sraw0[q] = sraw1[q];
+        sraw1[q] = sraw2[q];
+      }
 
       // ---- A buffer reuse: the MMAs that read it two blocks ago must have completed ----
       const int b = it & 1;
-      bool fail = false;
-      if (uses[b] > 0) fail = !tc::mbar_wait(&bar_a[b], (uses[b] - 1) & 1, &s_abort);
-      if (!fail) {
-        tc::fence_after();
-#pragma unroll
-        for (int q = 0; q < ACOLS / 16; q++) tc::st16(tmem + lane_base + b * ACOLS + q * 16, a + q * 16);
-        tc::wait_st();
-      }
-      tc::fence_before();
-      if (__syncthreads_or(fail)) {
+      if (uses[b] > 0 && !tc::mbar_wait(&bar_a[b], (uses[b] - 1) & 1, &s_abort)) failed = true;
+      if (__any_sync(0xffffffffu, failed)) {  // warp-uniform before the warp-collective stores
         failed = true;
         break;
       }
-      if (threadIdx.x == 0) {
-        tc::fence_after();
+      tc::fence_after();
+      __syncwarp();
 #pragma unroll
-        for (int j = 0; j < KB / 16; j++) {
-          const uint32_t kpos = (uint32_t)(it * KB + j * 16);  // K offset inside the staged slice
-          const uint64_t bd = tc::sdesc(xb_addr + (kpos / 8) * 128u, 128u, sbo);
-          tc::mma_f16_ts(d_col, tmem + b * ACOLS + j * 8, bd, idesc, (it > 0 || j > 0) ? 1u : 0u);
+      for (int q = 0; q < ACOLS / 16; q++) tc::st16(tmem + lane_base + b * ACOLS + q * 16, a + q * 16);
+      tc::wait_st();
+      tc::fence_before();
+      // block written: one arrival per thread; only the MMA issuer waits for all 128
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_full[b])) : "memory");
+      if (threadIdx.x == 0) {
+        if (!tc::mbar_wait(&bar_full[b], uses[b] & 1, &s_abort)) {
+          failed = true;
+        } else {
+          tc::fence_after();
+#pragma unroll
+          for (int j = 0; j < KB / 16; j++) {
+            const uint32_t kpos = (uint32_t)(it * KB + j * 16);  // K offset inside the staged slice
+            const uint64_t bd = tc::sdesc(xb_addr + (kpos / 8) * 128u, 128u, sbo);
+            tc::mma_f16_ts(d_col, tmem + b * ACOLS + j * 8, bd, idesc, (it > 0 || j > 0) ? 1u : 0u);
+          }
+          tc::commit(&bar_a[b]);
         }
-        tc::commit(&bar_a[b]);
       }
+      __syncwarp();
       uses[b]++;
+      if (__any_sync(0xffffffffu, failed)) {
+        failed = true;
+        break;
+      }
     }
     tc::cp_wait<0>();
     if (failed) break;
 
     // ---- accumulators of this tile ----
     if (threadIdx.x == 0) tc::commit(&bar_d);
-    const bool dfail = !tc::mbar_wait(&bar_d, tiles_done & 1, &s_abort);
-    if (__syncthreads_or(dfail)) {
+    if (!tc::mbar_wait(&bar_d, tiles_done & 1, &s_abort)) failed = true;
+    if (__any_sync(0xffffffffu, failed)) {
       failed = true;
       break;
     }
@@ -451,7 +470,7 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
   // ---- release tensor memory (also on the error path) ----
   tc::cp_wait<0>();
   tc::fence_before();
-  __syncthreads();
+  failed = __syncthreads_or(failed || s_abort);
   if (warp == 0) {
     tc::fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
