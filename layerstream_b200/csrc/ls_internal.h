@@ -214,4 +214,39 @@ void launch_set_ctl(Ctl* ctl, int pos0, int M, int n_logits, int mode, const uin
 void launch_quantize_rows(const uint16_t* src_bf16, int rows, int cols, int bits, int group, int clip, uint8_t* dst,
                           double* err_norm, cudaStream_t s);
 
+// ---- persistent pass kernel (ls_pass.cu) ----
+
+struct PassLayer {
+  QMat qkv, o, gu, down;
+  const uint16_t* in_norm;
+  const uint16_t* post_norm;
+  const uint16_t* qkv_bias;
+};
+
+struct PassArgs {
+  const PassLayer* layers;
+  QMat embed;
+  const float* final_norm;
+  Ctl* ctl;
+  long long* x;     // [T][h] residual stream, fixed point
+  long long* qkv;   // [T][h + 2 kv] q|k|v sums (bias included), fixed point
+  long long* gu;    // [T][2 I] gate/up sums in the interleaved row order, fixed point
+  float* att_part;  // [heads][slots][T][hd + 2]
+  uint16_t* kc;     // [L][kv_heads][max_ctx][hd] f16
+  uint16_t* vc;
+  const float2* rope;
+  ArgPart* arg_parts;  // [gridDim][T]
+  float* logits;       // optional [n_logits][vocab]
+  unsigned* bar;
+  int L, hidden, inter, heads, kv_heads, hd, vocab, max_ctx, T, n_logits, slots;
+  int ks_qkv, ks_o, ks_gu, ks_down;
+  float eps;
+};
+
+bool pass_kernel_supported(const WeightFormat& body, const WeightFormat& embed, int T, int hd);
+size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int heads, int slots, int ks_down,
+                        int ks_o);
+void launch_pass(const PassArgs& a, const WeightFormat& f, size_t smem, int grid, cudaStream_t s);
+int pass_kernel_max_grid(const WeightFormat& f, int T, size_t smem, int num_sms);
+
 }  // namespace ls

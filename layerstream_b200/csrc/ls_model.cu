@@ -160,6 +160,16 @@ struct LsModel {
   Ctl* ctl = nullptr;
   Ctl* ctl_host = nullptr;
 
+  // persistent pass kernel state (resident mode, passes of <= 48 tokens)
+  PassLayer* d_pass_layers = nullptr;
+  long long *x_fix = nullptr, *qkv_fix = nullptr, *gu_fix = nullptr;
+  float* pk_att = nullptr;
+  unsigned* pk_bar = nullptr;
+  ArgPart* pk_parts = nullptr;
+  int pk_slots = 1, pk_grid = 0;
+  int ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_down = 1;
+  cudaEvent_t pk_ev[2] = {nullptr, nullptr};
+
   std::map<std::tuple<int, int, int, int>, cudaGraphExec_t> graphs;
   size_t pos = 0;
   uint64_t bytes_read = 0, wait_ns = 0, passes = 0, resident_weight_bytes = 0, h2d_bytes = 0, d2h_bytes = 0;
@@ -180,6 +190,8 @@ struct LsModel {
     if (stream) cudaStreamSynchronize(stream);
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
     for (auto e : prof_ev) cudaEventDestroy(e);
+    for (auto e : pk_ev)
+      if (e) cudaEventDestroy(e);
     for (auto e : ev_loaded) cudaEventDestroy(e);
     for (auto e : ev_free) cudaEventDestroy(e);
     for (void* p : dev_allocs) cudaFree(p);
@@ -414,8 +426,97 @@ struct LsModel {
     ctl = dalloc<Ctl>(1);
     ctl_host = halloc<Ctl>(1);
     std::memset(ctl_host, 0, sizeof(Ctl));
+    if (mode == LS_MODE_RESIDENT) setup_pass_kernel();
     LS_CUDA(cudaStreamSynchronize(stream));
   }
+
+  // Device table of layer planes, fixed-point accumulators and the K-split plan of the pass kernel.
+  void setup_pass_kernel() {
+    const char* e = getenv("LS_PASS");
+    if (e && std::string(e) == "0") return;
+    if (!pass_kernel_supported(cfg.format, cfg.embed_format, 1, (int)cfg.head_dim)) return;
+    const int h = (int)cfg.hidden, kv = (int)cfg.kv_dim(), I = (int)cfg.inter, QS = h + 2 * kv;
+    std::vector<PassLayer> pl(cfg.layers);
+    for (size_t l = 0; l < cfg.layers; l++) {
+      pl[l].qkv = layers[l].qkv;
+      pl[l].o = layers[l].o;
+      pl[l].gu = layers[l].gu;
+      pl[l].down = layers[l].down;
+      pl[l].in_norm = layers[l].in_norm;
+      pl[l].post_norm = layers[l].post_norm;
+      pl[l].qkv_bias = layers[l].qkv_bias;
+    }
+    d_pass_layers = dalloc<PassLayer>(cfg.layers);
+    LS_CUDA(cudaMemcpyAsync(d_pass_layers, pl.data(), pl.size() * sizeof(PassLayer), cudaMemcpyHostToDevice, stream));
+    const int kb = (cfg.format.bits == 4 && cfg.format.group > 64) ? cfg.format.group : 64;
+    auto plan = [&](const QMat& w) {
+      const int tiles128 = (w.rows_pad / 32 + 3) / 4, nblk = w.cols / kb;
+      return std::max(1, std::min(nblk, num_sms / tiles128));
+    };
+    ks_qkv = plan(layers[0].qkv);
+    ks_o = plan(layers[0].o);
+    ks_gu = plan(layers[0].gu);
+    ks_down = plan(layers[0].down);
+    pk_slots = std::max(1, std::min(16, num_sms / (int)cfg.heads));
+    constexpr int kMaxPassT = 48;
+    const size_t smem = pass_kernel_smem(cfg.format, kMaxPassT, h, I, (int)cfg.head_dim, (int)cfg.heads, pk_slots, ks_down, ks_o);
+    if (smem > 220 * 1024) return;
+    pk_grid = pass_kernel_max_grid(cfg.format, kMaxPassT, smem, num_sms);
+    if (pk_grid <= 0) return;
+    x_fix = dalloc<long long>((size_t)kMaxPassT * h);
+    qkv_fix = dalloc<long long>((size_t)kMaxPassT * QS);
+    gu_fix = dalloc<long long>((size_t)kMaxPassT * 2 * I);
+    pk_att = dalloc<float>(cfg.heads * (size_t)pk_slots * kMaxPassT * (cfg.head_dim + 2));
+    pk_bar = dalloc<unsigned>(1);
+    pk_parts = dalloc<ArgPart>((size_t)pk_grid * kMaxPassT);
+    LS_CUDA(cudaEventCreate(&pk_ev[0]));
+    LS_CUDA(cudaEventCreate(&pk_ev[1]));
+  }
+
+  bool use_pass_kernel(int T) const { return pk_grid > 0 && T >= 1 && T <= 48; }
+
+  void launch_pass_kernel(int T, int n_logits, bool want_logits) {
+    PassArgs a{};
+    a.layers = d_pass_layers;
+    a.embed = embed;
+    a.final_norm = final_norm;
+    a.ctl = ctl;
+    a.x = x_fix;
+    a.qkv = qkv_fix;
+    a.gu = gu_fix;
+    a.att_part = pk_att;
+    a.kc = kc;
+    a.vc = vc;
+    a.rope = rope;
+    a.arg_parts = pk_parts;
+    a.logits = want_logits ? logits : nullptr;
+    a.bar = pk_bar;
+    a.L = (int)cfg.layers;
+    a.hidden = (int)cfg.hidden;
+    a.inter = (int)cfg.inter;
+    a.heads = (int)cfg.heads;
+    a.kv_heads = (int)cfg.kv_heads;
+    a.hd = (int)cfg.head_dim;
+    a.vocab = (int)cfg.vocab;
+    a.max_ctx = (int)max_ctx;
+    a.T = T;
+    a.n_logits = n_logits;
+    a.slots = pk_slots;
+    a.ks_qkv = ks_qkv;
+    a.ks_o = ks_o;
+    a.ks_gu = ks_gu;
+    a.ks_down = ks_down;
+    a.eps = cfg.eps;
+    const size_t smem = pass_kernel_smem(cfg.format, T, a.hidden, a.inter, a.hd, a.heads, pk_slots, ks_down, ks_o);
+    LS_CUDA(cudaMemsetAsync(pk_bar, 0, sizeof(unsigned), stream));
+    if (prof_on) LS_CUDA(cudaEventRecord(pk_ev[0], stream));
+    launch_pass(a, cfg.format, smem, pk_grid, stream);
+    if (prof_on) {
+      LS_CUDA(cudaEventRecord(pk_ev[1], stream));
+      pk_pending = true;
+    }
+  }
+  bool pk_pending = false;
 
   // ---- the pass --------------------------------------------------------------------------------
 
@@ -442,6 +543,18 @@ struct LsModel {
     return (double)w.rows * rb + (double)M * w.cols * 4 + (double)M * out_rows * 4;
   }
   void prof_collect() {
+    if (pk_pending) {
+      pk_pending = false;
+      float ms = 0;
+      LS_CUDA(cudaEventElapsedTime(&ms, pk_ev[0], pk_ev[1]));
+      // one launch covers the whole pass: weights once + the cached K/V rows read + new rows
+      const double wb = (double)cfg.layers * file.layout.total + (double)cfg.vocab * cfg.embed_row_bytes();
+      const double kvb = (double)cfg.layers * ((double)ctl_host->pos0 + ctl_host->M) * cfg.kv_dim() * 2 * 2;
+      prof.launches[7 - 1]++;
+      prof.ms[7 - 1] += ms;
+      prof.bytes[7 - 1] += wb + kvb;
+      return;
+    }
     if (!prof_pending || !prof_cur) return;
     prof_pending = false;
     for (size_t i = 0; i < prof_cur->size(); i++) {
@@ -631,6 +744,10 @@ struct LsModel {
 
   void run_pass(int T, int n_logits, bool want_logits) {
     passes++;
+    if (mode == LS_MODE_RESIDENT && use_pass_kernel(T)) {
+      launch_pass_kernel(T, n_logits, want_logits);
+      return;
+    }
     if (mode != LS_MODE_RESIDENT) {
       prof_rec.clear();
       enqueue_pass(T, n_logits, want_logits);
@@ -690,6 +807,7 @@ struct LsModel {
     LS_CUDA(cudaStreamSynchronize(stream));
     prof_collect();
     if (ctl_host->err == 1) LS_THROW(LS_ERR_DEVICE, "a tensor-core kernel gave up waiting on an mbarrier (bounded wait)");
+    if (ctl_host->err == 3) LS_THROW(LS_ERR_DEVICE, "the pass kernel gave up waiting at a grid barrier (bounded wait)");
     if (ctl_host->err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
   }
 
