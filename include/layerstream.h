@@ -72,16 +72,22 @@ typedef struct LsReport {
   uint64_t d2h_bytes;             /* results (tokens, counts, logits) copied device->host since open */
 } LsReport;
 
-/* Live kernel timing (CUDA events recorded inside the pass, on the model's stream), enabled by
- * ls_model_profile_enable. Classes: 0 QKV GEMV, 1 attention, 2 O GEMV, 3 gate/up GEMV, 4 down GEMV
- * (all sampled on one middle layer per pass), 5 LM head GEMV + argmax, 6 the whole pass.
- * bytes = algorithmic bytes of the timed launches (weights + scales + activations in and out; for
+/* Live kernel timing (on the model's stream), enabled by ls_model_profile_enable. Classes: 0 QKV
+ * GEMV, 1 attention, 2 O GEMV, 3 gate/up GEMV, 4 down GEMV (one layer per pass), 5 LM head GEMV +
+ * argmax, 6 the whole pass.
+ * Separate kernels: CUDA events around each launch; classes 0-4 sample one middle layer.
+ * Persistent pass kernel: class 6 from CUDA events around the launch; classes 0-5 from device
+ * timestamps taken at its grid barriers, ms = phase span (departure of the last CTA from the
+ * previous barrier to departure of the last CTA from this one) averaged over the layers, busy_ms =
+ * the part of it the average CTA spends working rather than waiting at the barrier.
+ * bytes = algorithmic bytes of the timed work (weights + scales + activations in and out; for
  * attention the K/V cache rows read plus the new rows written). */
 #define LS_PROF_CLASSES 7
 typedef struct LsProfile {
   uint64_t launches[LS_PROF_CLASSES];
   double ms[LS_PROF_CLASSES];
   double bytes[LS_PROF_CLASSES];
+  double busy_ms[LS_PROF_CLASSES];
 } LsProfile;
 
 /* src/spec.rs:16-39 */

@@ -189,11 +189,12 @@ constexpr int GEMV_THREADS = GEMV_WARPS * 32;
 
 // Reduces the per-CTA argmax parts of every token (first-maximum rule), then applies the
 // acceptance rule of src/spec.rs:121-125 (verify) or records the next token (forward).
-// Run by one whole CTA of at most GEMV_THREADS threads.
+// Run by one whole CTA (its first GEMV_THREADS threads do the reduction).
 __device__ __noinline__ static void argmax_finalize_block(const ArgPart* parts, int nparts, int M, Ctl* ctl) {
   __shared__ float s_v[GEMV_THREADS];
   __shared__ uint32_t s_i[GEMV_THREADS];
-  const int per = (int)blockDim.x / M;  // threads per token (M <= blockDim.x)
+  const int nth = (int)blockDim.x < GEMV_THREADS ? (int)blockDim.x : GEMV_THREADS;
+  const int per = nth / M;  // threads per token (M <= nth)
   const int t = threadIdx.x % M, j = threadIdx.x / M;
   float v = -CUDART_INF_F;
   uint32_t idx = 0xffffffffu;
@@ -208,8 +209,10 @@ __device__ __noinline__ static void argmax_finalize_block(const ArgPart* parts, 
       }
     }
   }
-  s_v[threadIdx.x] = v;
-  s_i[threadIdx.x] = idx;
+  if ((int)threadIdx.x < nth) {
+    s_v[threadIdx.x] = v;
+    s_i[threadIdx.x] = idx;
+  }
   __syncthreads();
   if (threadIdx.x < M) {
     for (int jj = 1; jj < per; jj++) {

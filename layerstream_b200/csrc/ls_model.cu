@@ -166,8 +166,7 @@ struct LsModel {
   float* pk_att = nullptr;
   unsigned* pk_bar = nullptr;
   ArgPart* pk_parts = nullptr;
-  int pk_slots = 1, pk_grid = 0;
-  int ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_down = 1;
+  int pk_max_grid = 0;
   cudaEvent_t pk_ev[2] = {nullptr, nullptr};
 
   std::map<std::tuple<int, int, int, int>, cudaGraphExec_t> graphs;
@@ -430,12 +429,62 @@ struct LsModel {
     LS_CUDA(cudaStreamSynchronize(stream));
   }
 
-  // Device table of layer planes, fixed-point accumulators and the K-split plan of the pass kernel.
+  // Launch plan of the pass kernel for one token tile (16, 32 or 48 tokens): CTAs, attention slots
+  // per head, K slices per GEMV phase and dynamic shared memory.
+  struct PassPlan {
+    int grid = 0, slots = 1, ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_down = 1;
+    size_t smem = 0;
+  };
+  PassPlan pk_plan[3];
+  static int pk_class(int T) { return T <= 16 ? 0 : T <= 32 ? 1 : 2; }
+
+  // Device table of layer planes, fixed-point accumulators and the launch plans of the pass kernel.
   void setup_pass_kernel() {
     const char* e = getenv("LS_PASS");
     if (e && std::string(e) == "0") return;
     if (!pass_kernel_supported(cfg.format, cfg.embed_format, 1, (int)cfg.head_dim)) return;
+    int max_per_sm = 4;
+    if (const char* c = getenv("LS_PASS_CTAS")) max_per_sm = std::max(1, std::min(4, atoi(c)));
     const int h = (int)cfg.hidden, kv = (int)cfg.kv_dim(), I = (int)cfg.inter, QS = h + 2 * kv;
+    const int kb = (cfg.format.bits == 4 && cfg.format.group > 64) ? cfg.format.group : 64;
+    int max_grid = 0;
+    for (int c = 0; c < 3; c++) {
+      PassPlan& P = pk_plan[c];
+      const int T = 16 * (c + 1);
+      // items are 256-row tiles x K slices; enough slices to give every CTA about one item
+      auto plan = [&](const QMat& w, int grid) {
+        const int tiles = (w.rows_pad / 32 + 7) / 8, nblk = w.cols / kb;
+        return std::max(1, std::min(nblk, grid / tiles));
+      };
+      // the down slice width sets the shared memory, which sets the CTAs per SM: settle both
+      P.ks_down = plan(layers[0].down, num_sms);
+      size_t smem = pass_kernel_smem(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down);
+      if (smem > 220 * 1024) continue;
+      int per_sm = pass_kernel_blocks_per_sm(cfg.format, T, smem, max_per_sm);
+      if (per_sm < 1) continue;
+      for (int iter = 0; iter < 3; iter++) {
+        const int ks = plan(layers[0].down, per_sm * num_sms);
+        const size_t sm2 = pass_kernel_smem(cfg.format, T, h, I, (int)cfg.head_dim, ks);
+        const int ps2 = pass_kernel_blocks_per_sm(cfg.format, T, sm2, max_per_sm);
+        if (ps2 < per_sm) break;
+        P.ks_down = ks;
+        smem = sm2;
+      }
+      P.grid = per_sm * num_sms;
+      P.smem = smem;
+      P.ks_qkv = plan(layers[0].qkv, P.grid);
+      P.ks_o = plan(layers[0].o, P.grid);
+      P.ks_gu = plan(layers[0].gu, P.grid);
+      P.slots = std::max(1, std::min(kMaxAttSlots, P.grid / (int)cfg.heads));
+      max_grid = std::max(max_grid, P.grid);
+    }
+    if (getenv("LS_PASS_VERBOSE"))
+      for (int c = 0; c < 3; c++)
+        fprintf(stderr, "pass plan T<=%d: grid %d slots %d ks qkv %d o %d gu %d down %d smem %zu\n", 16 * (c + 1),
+                pk_plan[c].grid, pk_plan[c].slots, pk_plan[c].ks_qkv, pk_plan[c].ks_o, pk_plan[c].ks_gu, pk_plan[c].ks_down,
+                pk_plan[c].smem);
+    if (pk_plan[0].grid == 0) return;
+    pk_max_grid = max_grid;
     std::vector<PassLayer> pl(cfg.layers);
     for (size_t l = 0; l < cfg.layers; l++) {
       pl[l].qkv = layers[l].qkv;
@@ -448,34 +497,24 @@ struct LsModel {
     }
     d_pass_layers = dalloc<PassLayer>(cfg.layers);
     LS_CUDA(cudaMemcpyAsync(d_pass_layers, pl.data(), pl.size() * sizeof(PassLayer), cudaMemcpyHostToDevice, stream));
-    const int kb = (cfg.format.bits == 4 && cfg.format.group > 64) ? cfg.format.group : 64;
-    auto plan = [&](const QMat& w) {
-      const int tiles128 = (w.rows_pad / 32 + 3) / 4, nblk = w.cols / kb;
-      return std::max(1, std::min(nblk, num_sms / tiles128));
-    };
-    ks_qkv = plan(layers[0].qkv);
-    ks_o = plan(layers[0].o);
-    ks_gu = plan(layers[0].gu);
-    ks_down = plan(layers[0].down);
-    pk_slots = std::max(1, std::min(16, num_sms / (int)cfg.heads));
     constexpr int kMaxPassT = 48;
-    const size_t smem = pass_kernel_smem(cfg.format, kMaxPassT, h, I, (int)cfg.head_dim, (int)cfg.heads, pk_slots, ks_down, ks_o);
-    if (smem > 220 * 1024) return;
-    pk_grid = pass_kernel_max_grid(cfg.format, kMaxPassT, smem, num_sms);
-    if (pk_grid <= 0) return;
     x_fix = dalloc<long long>((size_t)kMaxPassT * h);
     qkv_fix = dalloc<long long>((size_t)kMaxPassT * QS);
     gu_fix = dalloc<long long>((size_t)kMaxPassT * 2 * I);
-    pk_att = dalloc<float>(cfg.heads * (size_t)pk_slots * kMaxPassT * (cfg.head_dim + 2));
-    pk_bar = dalloc<unsigned>(1);
-    pk_parts = dalloc<ArgPart>((size_t)pk_grid * kMaxPassT);
+    pk_att = dalloc<float>(cfg.heads * (size_t)kMaxAttSlots * kMaxPassT * (cfg.head_dim + 2));
+    pk_attn = dalloc<float>((size_t)kMaxPassT * h);
+    pk_bar = dalloc<unsigned>(1 + cfg.heads);
+    pk_parts = dalloc<ArgPart>((size_t)max_grid * kMaxPassT);
     LS_CUDA(cudaEventCreate(&pk_ev[0]));
     LS_CUDA(cudaEventCreate(&pk_ev[1]));
   }
+  static constexpr int kMaxAttSlots = 16;  // equals the kernel's slot bound
+  float* pk_attn = nullptr;
 
-  bool use_pass_kernel(int T) const { return pk_grid > 0 && T >= 1 && T <= 48; }
+  bool use_pass_kernel(int T) const { return T >= 1 && T <= 48 && pk_plan[pk_class(T)].grid > 0; }
 
   void launch_pass_kernel(int T, int n_logits, bool want_logits) {
+    const PassPlan& P = pk_plan[pk_class(T)];
     PassArgs a{};
     a.layers = d_pass_layers;
     a.embed = embed;
@@ -485,12 +524,19 @@ struct LsModel {
     a.qkv = qkv_fix;
     a.gu = gu_fix;
     a.att_part = pk_att;
+    a.attn = pk_attn;
+    a.att_cnt = pk_bar + 1;
     a.kc = kc;
     a.vc = vc;
     a.rope = rope;
     a.arg_parts = pk_parts;
     a.logits = want_logits ? logits : nullptr;
     a.bar = pk_bar;
+    if (prof_on && !pk_trace) pk_trace = dalloc<unsigned>(pk_trace_slots() * (size_t)pk_max_grid);
+    a.trace = prof_on ? pk_trace : nullptr;
+    pk_T = T;
+    pk_n_logits = n_logits;
+    pk_grid_last = P.grid;
     a.L = (int)cfg.layers;
     a.hidden = (int)cfg.hidden;
     a.inter = (int)cfg.inter;
@@ -501,22 +547,77 @@ struct LsModel {
     a.max_ctx = (int)max_ctx;
     a.T = T;
     a.n_logits = n_logits;
-    a.slots = pk_slots;
-    a.ks_qkv = ks_qkv;
-    a.ks_o = ks_o;
-    a.ks_gu = ks_gu;
-    a.ks_down = ks_down;
+    a.slots = P.slots;
+    a.ks_qkv = P.ks_qkv;
+    a.ks_o = P.ks_o;
+    a.ks_gu = P.ks_gu;
+    a.ks_down = P.ks_down;
     a.eps = cfg.eps;
-    const size_t smem = pass_kernel_smem(cfg.format, T, a.hidden, a.inter, a.hd, a.heads, pk_slots, ks_down, ks_o);
-    LS_CUDA(cudaMemsetAsync(pk_bar, 0, sizeof(unsigned), stream));
+    // barrier counter and per-head attention counters start at zero
+    LS_CUDA(cudaMemsetAsync(pk_bar, 0, sizeof(unsigned) * (1 + cfg.heads), stream));
     if (prof_on) LS_CUDA(cudaEventRecord(pk_ev[0], stream));
-    launch_pass(a, cfg.format, smem, pk_grid, stream);
+    launch_pass(a, cfg.format, P.smem, P.grid, stream);
     if (prof_on) {
       LS_CUDA(cudaEventRecord(pk_ev[1], stream));
       pk_pending = true;
     }
   }
+  int pk_grid_last = 0;
   bool pk_pending = false;
+  unsigned* pk_trace = nullptr;
+  int pk_T = 0, pk_n_logits = 0;
+  // timeline slots of one pass: start, (arrive, leave) per grid barrier, end
+  size_t pk_trace_slots() const { return 2 * (2 + 5 * cfg.layers) + 2; }
+
+  // Turns the pass kernel's barrier timestamps into per-class phase spans (averaged over layers).
+  void collect_pass_trace() {
+    const int G = pk_grid_last, L = (int)cfg.layers, T = pk_T;
+    const int nb = 1 + 5 * L + (pk_n_logits > 0 ? 1 : 0);
+    std::vector<uint32_t> tr((size_t)(2 * nb + 2) * G);
+    LS_CUDA(cudaMemcpy(tr.data(), pk_trace, tr.size() * 4, cudaMemcpyDeviceToHost));
+    auto at = [&](int slot, int c) { return tr[(size_t)slot * G + c]; };
+    uint32_t t0 = at(0, 0);
+    for (int c = 1; c < G; c++)
+      if ((int32_t)(at(0, c) - t0) < 0) t0 = at(0, c);
+    auto rel = [&](int slot, int c) { return (double)(int32_t)(at(slot, c) - t0) * 1e-6; };  // ms
+    double prev_leave = 0;
+    const int h = (int)cfg.hidden, kv = (int)cfg.kv_dim(), I = (int)cfg.inter;
+    const LayerW& W = layers[cfg.layers / 2];
+    for (int b = 1; b <= nb; b++) {
+      double leave = -1e30, busy = 0;
+      for (int c = 0; c < G; c++) {
+        leave = std::max(leave, rel(2 * b, c));
+        busy += rel(2 * b - 1, c) - rel(2 * b - 2, c);
+      }
+      busy /= G;
+      double span = leave - prev_leave;
+      prev_leave = leave;
+      if (b == 1) continue;  // embedding rows: part of the whole-pass class only
+      int cls = 5;
+      double scale = 1.0;
+      if (b <= 1 + 5 * L) {
+        cls = (b - 2) % 5;
+        scale = 1.0 / L;
+      } else {
+        span += rel(2 * nb + 1, 0) - rel(2 * nb, 0);  // argmax merge + acceptance in CTA 0
+      }
+      prof.ms[cls] += span * scale;
+      prof.busy_ms[cls] += busy * scale;
+    }
+    const double pos0 = ctl_host->pos0;
+    const double b_cls[5] = {gemv_bytes(W.qkv, T, h + 2 * kv),
+                             (double)T * kv * 2 * 2 + (double)T * (h + 2 * kv) * 4 + (double)T * h * 4 + pos0 * kv * 2 * 2,
+                             gemv_bytes(W.o, T, h) + (double)T * h * 4, gemv_bytes(W.gu, T, I),
+                             gemv_bytes(W.down, T, h) + (double)T * h * 4};
+    for (int c = 0; c < 5; c++) {
+      prof.launches[c]++;
+      prof.bytes[c] += b_cls[c];
+    }
+    if (pk_n_logits > 0) {
+      prof.launches[5]++;
+      prof.bytes[5] += gemv_bytes(embed, pk_n_logits, 0);
+    }
+  }
 
   // ---- the pass --------------------------------------------------------------------------------
 
@@ -552,7 +653,9 @@ struct LsModel {
       const double kvb = (double)cfg.layers * ((double)ctl_host->pos0 + ctl_host->M) * cfg.kv_dim() * 2 * 2;
       prof.launches[7 - 1]++;
       prof.ms[7 - 1] += ms;
+      prof.busy_ms[7 - 1] += ms;
       prof.bytes[7 - 1] += wb + kvb;
+      if (pk_trace) collect_pass_trace();
       return;
     }
     if (!prof_pending || !prof_cur) return;
@@ -563,6 +666,7 @@ struct LsModel {
       const ProfRec& r = (*prof_cur)[i];
       prof.launches[r.cls]++;
       prof.ms[r.cls] += ms;
+      prof.busy_ms[r.cls] += ms;
       // attention also reads the cached K/V rows of this pass (pos0 of the pass, f16 K and V)
       prof.bytes[r.cls] += r.bytes + (r.cls == 1 ? (double)ctl_host->pos0 * cfg.kv_dim() * 2 * 2 : 0.0);
     }

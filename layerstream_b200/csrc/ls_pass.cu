@@ -12,20 +12,36 @@
 // finish — the pass stays deterministic and every token's result is independent of how many
 // tokens share the pass.
 //
+// GEMV phases: a CTA has PK_NWG dequantizing warpgroups, each owning one 128-row tile of the
+// current 256-row item, and one issuer warp. Every K block of 64 columns, each warpgroup turns its
+// int4/int8 rows into f16 (scale applied) and stores them to its A buffer in tensor memory; the
+// issuer warp runs the tcgen05 MMAs of all warpgroups against the activations staged in shared
+// memory. A and the f32 accumulators are double-buffered in tensor memory, so dequantization, MMA
+// issue and the accumulator read-back of the previous item overlap.
+//
 // Every wait is bounded (grid barrier spins, mbarrier polls); on a timeout the CTA records an
 // error in the control block, the other CTAs see it at their next wait, tensor memory is released
 // and the kernel returns.
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 
 #include "ls_device.cuh"
 #include "ls_internal.h"
 
 namespace ls {
 
-constexpr int PK_THREADS = 128;
+constexpr int PK_NWG = 2;                    // dequantizing warpgroups per CTA
+constexpr int PK_CT = PK_NWG * 128;           // their threads
+constexpr int PK_THREADS = PK_CT + 32;        // + the MMA issuer warp
 constexpr int PK_NW = PK_THREADS / 32;
-constexpr int PK_STAGES = 6;
+constexpr int PK_ISSUER = PK_CT / 32;         // warp index of the issuer
 constexpr int PK_ATT_TILE = 64;
+constexpr int kMaxSlots = 16;  // attention slots per head (context tiles split across CTAs)
+// Bytes of weights one CTA keeps in flight (the load ring): ~64 KB per SM covers HBM latency at
+// full bandwidth.
+constexpr int PK_RING_BYTES = 65536;
+constexpr int PK_TMEM_COLS = 512;  // one CTA per SM: the whole tensor memory
 
 __device__ __forceinline__ long long to_fix(float v) {
   v = fminf(fmaxf(v, -1.0e9f), 1.0e9f);
@@ -36,6 +52,12 @@ __device__ __forceinline__ void fix_add(long long* p, float v) {
   atomicAdd(reinterpret_cast<unsigned long long*>(p), (unsigned long long)to_fix(v));
 }
 __device__ __forceinline__ long long ldcg_ll(const long long* p) { return __ldcg(p); }
+
+__device__ __forceinline__ unsigned gtimer() {
+  unsigned t;
+  asm volatile("mov.u32 %0, %%globaltimer_lo;" : "=r"(t));
+  return t;
+}
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
@@ -73,26 +95,34 @@ __device__ bool grid_barrier(unsigned* bar, unsigned target, int* err) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// The tensor-core GEMV of one 128-row tile over K blocks [kb0, kb1), as in gemv_tc_kernel, with
-// state kept across items: each thread owns one weight row and leaves its NT accumulators in tot.
+// The tensor-core GEMV of one item: rows [256 t256, 256 t256 + 256) over K blocks [kb0, kb1).
+// State is kept across items and phases; both roles advance the same block / item counters.
+// Tensor memory columns: A buffer (b, g) at (b PK_NWG + g) ACOLS, accumulator (d, g) at
+// 2 PK_NWG ACOLS + (d PK_NWG + g) NT.
 // ---------------------------------------------------------------------------------------------
 template <int BITS, int G, int NT>
 struct TcGemv {
   static constexpr int KB = tc_kb(BITS, G), NS = tc_ns(BITS, G), WPC = 128 / BITS, CPB = KB / WPC, ACOLS = KB / 2;
-  static constexpr uint32_t kStage = PK_THREADS * CPB * 16;
+  static constexpr uint32_t kStage = PK_CT * CPB * 16;
+  static constexpr int STAGES = (int)(PK_RING_BYTES / kStage) < 4 ? 4 : (int)(PK_RING_BYTES / kStage);
+  static_assert(2 * PK_NWG * ACOLS + 2 * PK_NWG * NT <= PK_TMEM_COLS, "tensor memory");
   uint32_t tmem, ring_addr;
   uint8_t* ring;
-  uint64_t *bar_a, *bar_full, *bar_d;
+  uint64_t *bar_a, *bar_full, *bar_d, *bar_dfree;  // [2] each
   int* abort;
-  uint32_t uses0, uses1, dphase;
+  uint32_t blk, itc;  // K blocks and items run so far (identical in both roles)
 
-  __device__ void prologue(const QMat& w, int t128, int kb0, int kb1) const {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t32 = t128 * 4 + warp;
+  __device__ uint32_t a_col(int b, int g) const { return tmem + (uint32_t)((b * PK_NWG + g) * ACOLS); }
+  __device__ uint32_t d_col(int d, int g) const { return tmem + (uint32_t)(2 * PK_NWG * ACOLS + (d * PK_NWG + g) * NT); }
+
+  // Starts the weight stream of an item (compute threads only).
+  __device__ void prologue(const QMat& w, int t256, int kb0, int kb1) const {
+    const int g = threadIdx.x >> 7, warp = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
+    const int t32 = (t256 * PK_NWG + g) * 4 + warp;
     const bool valid = t32 < w.rows_pad / 32;
     const uint8_t* db = w.data + ((size_t)(valid ? t32 : 0) * w.chunks()) * 512 + lane * 16;
 #pragma unroll
-    for (int s = 0; s < PK_STAGES - 1; s++) {
+    for (int s = 0; s < STAGES - 1; s++) {
       const int kb = kb0 + s;
       if (kb < kb1 && valid) {
 #pragma unroll
@@ -102,17 +132,16 @@ struct TcGemv {
     }
   }
 
-  // Runs the K loop (prologue already issued) and reads the accumulators. false on a timeout.
-  __device__ bool run(const QMat& w, int t128, int kb0, int kb1, uint32_t xb_addr, uint32_t sbo, float (&tot)[NT]) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Compute threads: the K loop of an item (prologue already issued), then the next item's
+  // prologue (nx, when not null), then the accumulators. false on a timeout.
+  __device__ bool run(const QMat& w, int t256, int kb0, int kb1, float (&tot)[NT], const int* nx) {
+    const int g = threadIdx.x >> 7, warp = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
     const int tiles32 = w.rows_pad / 32, nch = w.chunks(), ngr = w.groups();
-    const int t32 = t128 * 4 + warp;
+    const int t32 = (t256 * PK_NWG + g) * 4 + warp;
     const bool row_valid = t32 < tiles32;
     const uint8_t* db = w.data + ((size_t)(row_valid ? t32 : 0) * nch) * 512 + lane * 16;
     const uint16_t* sb = w.scales + (size_t)(row_valid ? t32 : 0) * ngr * 32 + lane;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t d_col = tmem + 2 * ACOLS;
-    const uint32_t idesc = tc::idesc_f16(NT);
     const uint32_t sub8 = BITS == 8 ? 0x64806480u : 0x64086408u;
     auto load_scales = [&](int kb, uint16_t (&sc)[NS]) {
 #pragma unroll
@@ -121,11 +150,10 @@ struct TcGemv {
     uint16_t sr0[NS], sr1[NS], sr2[NS];
     load_scales(kb0, sr0);
     load_scales(kb0 + 1, sr1);
-    bool failed = false;
     for (int kb = kb0; kb < kb1; kb++) {
       const int it = kb - kb0;
       {
-        const int kn = kb + PK_STAGES - 1, sn = (it + PK_STAGES - 1) % PK_STAGES;
+        const int kn = kb + STAGES - 1, sn = (it + STAGES - 1) % STAGES;
         if (kn < kb1 && row_valid) {
 #pragma unroll
           for (int q = 0; q < CPB; q++) tc::cp_async16(ring_addr + sn * kStage + q * 16, db + (size_t)(kn * CPB + q) * 512);
@@ -136,9 +164,9 @@ struct TcGemv {
       uint32_t sc[NS];
 #pragma unroll
       for (int q = 0; q < NS; q++) sc[q] = tc::h2_splat(bf16f(sr0[q]));
-      tc::cp_wait<PK_STAGES - 1>();
+      tc::cp_wait<STAGES - 1>();
       uint4 wv[CPB];
-      const uint8_t* rs = ring + (size_t)(it % PK_STAGES) * kStage + (size_t)threadIdx.x * CPB * 16;
+      const uint8_t* rs = ring + (size_t)(it % STAGES) * kStage + (size_t)threadIdx.x * CPB * 16;
 #pragma unroll
       for (int q = 0; q < CPB; q++) wv[q] = row_valid ? *reinterpret_cast<const uint4*>(rs + q * 16) : make_uint4(0, 0, 0, 0);
       uint32_t a[ACOLS];
@@ -185,69 +213,92 @@ struct TcGemv {
         sr0[q] = sr1[q];
         sr1[q] = sr2[q];
       }
-      const int b = it & 1;
-      const uint32_t ub = b ? uses1 : uses0;
-      if (ub > 0 && !tc::mbar_wait(&bar_a[b], (ub - 1) & 1, abort)) failed = true;
-      if (__any_sync(0xffffffffu, failed)) {
-        failed = true;
-        break;
+      // A buffer b is free once the MMAs of block blk - 2 have completed
+      const int b = blk & 1;
+      const uint32_t u = blk >> 1;
+      bool fail = u > 0 && !tc::mbar_wait(&bar_a[b], (u - 1) & 1, abort);
+      if (__any_sync(0xffffffffu, fail)) {
+        tc::cp_wait<0>();
+        return false;
       }
       tc::fence_after();
-      __syncwarp();
 #pragma unroll
-      for (int q = 0; q < ACOLS / 16; q++) tc::st16(tmem + lane_base + b * ACOLS + q * 16, a + q * 16);
+      for (int q = 0; q < ACOLS / 16; q++) tc::st16(a_col(b, g) + lane_base + q * 16, a + q * 16);
       tc::wait_st();
       tc::fence_before();
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_full[b])) : "memory");
-      if (threadIdx.x == 0) {
-        if (!tc::mbar_wait(&bar_full[b], ub & 1, abort)) {
-          failed = true;
-        } else {
-          tc::fence_after();
-#pragma unroll
-          for (int j = 0; j < KB / 16; j++) {
-            const uint32_t kpos = (uint32_t)(it * KB + j * 16);
-            const uint64_t bd = tc::sdesc(xb_addr + (kpos / 8) * 128u, 128u, sbo);
-            tc::mma_f16_ts(d_col, tmem + b * ACOLS + j * 8, bd, idesc, (it > 0 || j > 0) ? 1u : 0u);
-          }
-          tc::commit(&bar_a[b]);
-        }
-      }
       __syncwarp();
-      if (b) uses1++;
-      else uses0++;
-      if (__any_sync(0xffffffffu, failed)) {
-        failed = true;
-        break;
-      }
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_full[b])) : "memory");
+      blk++;
     }
-    tc::cp_wait<0>();
-    if (failed) return false;
-    if (threadIdx.x == 0) tc::commit(bar_d);
-    if (!tc::mbar_wait(bar_d, dphase & 1, abort)) failed = true;
-    if (__any_sync(0xffffffffu, failed)) return false;
-    dphase++;
+    // the ring slots are free (every thread has read its own): stream the next item meanwhile
+    if (nx) prologue(w, nx[0], nx[1], nx[2]);
+    const int d = itc & 1;
+    const uint32_t v = itc >> 1;
+    itc++;
+    bool fail = !tc::mbar_wait(&bar_d[d], v & 1, abort);
+    if (__any_sync(0xffffffffu, fail)) return false;
     tc::fence_after();
 #pragma unroll
     for (int q = 0; q < NT / 16; q++) {
-      uint32_t v[16];
-      tc::ld16(d_col + lane_base + q * 16, v);
+      uint32_t r[16];
+      tc::ld16(d_col(d, g) + lane_base + q * 16, r);
       tc::wait_ld();
 #pragma unroll
-      for (int e = 0; e < 16; e++) tot[q * 16 + e] = __uint_as_float(v[e]);
+      for (int e = 0; e < 16; e++) tot[q * 16 + e] = __uint_as_float(r[e]);
     }
     tc::fence_before();
+    __syncwarp();
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_dfree[d])) : "memory");
     return true;
+  }
+
+  // Issuer warp (lane 0 issues): the MMAs of an item, B = the staged activations. false on a timeout.
+  __device__ bool issue(int kb0, int kb1, uint32_t xb_addr, uint32_t sbo) {
+    const int lane = threadIdx.x & 31;
+    const int d = itc & 1;
+    const uint32_t v = itc >> 1;
+    itc++;
+    const uint32_t idesc = tc::idesc_f16(NT);
+    bool fail = false;
+    if (lane == 0) {
+      // accumulator d is free once the compute threads have read item itc - 2
+      if (v > 0 && !tc::mbar_wait(&bar_dfree[d], (v - 1) & 1, abort)) fail = true;
+      for (int kb = kb0; kb < kb1 && !fail; kb++) {
+        const int b = blk & 1;
+        const uint32_t u = blk >> 1;
+        blk++;
+        if (!tc::mbar_wait(&bar_full[b], u & 1, abort)) {
+          fail = true;
+          break;
+        }
+        tc::fence_after();
+#pragma unroll
+        for (int g = 0; g < PK_NWG; g++) {
+#pragma unroll
+          for (int j = 0; j < KB / 16; j++) {
+            const uint32_t kpos = (uint32_t)((kb - kb0) * KB + j * 16);
+            const uint64_t bd = tc::sdesc(xb_addr + (kpos / 8) * 128u, 128u, sbo);
+            tc::mma_f16_ts(d_col(d, g), a_col(b, g) + j * 8, bd, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+          }
+        }
+        tc::commit(&bar_a[b]);
+      }
+      if (!fail) tc::commit(&bar_d[d]);
+    } else {
+      blk += kb1 - kb0;
+    }
+    blk = __shfl_sync(0xffffffffu, blk, 0);
+    return !__any_sync(0xffffffffu, fail);
   }
 };
 
-// Item split of a GEMV phase: item i -> (K slice, 128-row tile), slices outermost.
+// Item split of a GEMV phase: item i -> (K slice, 256-row tile), slices outermost.
 struct Split {
-  int tiles128, ks, nblk;
-  __device__ int items() const { return tiles128 * ks; }
-  __device__ void item(int i, int* t128, int* kb0, int* kb1) const {
-    const int k = i / tiles128;
-    *t128 = i - k * tiles128;
+  int tiles, ks, nblk;
+  __device__ int items() const { return tiles * ks; }
+  __device__ void item(int i, int* t256, int* kb0, int* kb1) const {
+    const int k = i / tiles;
+    *t256 = i - k * tiles;
     *kb0 = (int)((long long)k * nblk / ks);
     *kb1 = (int)((long long)(k + 1) * nblk / ks);
   }
@@ -256,7 +307,7 @@ struct Split {
 template <int BITS, int G>
 __device__ __forceinline__ Split make_split(const QMat& w, int ks) {
   Split s;
-  s.tiles128 = (w.rows_pad / 32 + 3) / 4;
+  s.tiles = (w.rows_pad / 32 + 4 * PK_NWG - 1) / (4 * PK_NWG);
   s.ks = ks;
   s.nblk = w.cols / tc_kb(BITS, G);
   return s;
@@ -283,30 +334,74 @@ __device__ __forceinline__ void stage_b(uint8_t* xb, uint32_t sbo, int T, int co
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// 1 / rms of the first T rows of x (fixed point, n columns) into s_inv (one warp per token).
-__device__ __forceinline__ void rms_stats(const long long* x, int T, int n, float eps, float* s_inv) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = warp; t < T; t += PK_NW) {
-    float ss = 0.f;
-#pragma unroll 8
-    for (int c = lane; c < n; c += 32) {
-      const float v = from_fix(ldcg_ll(x + (size_t)t * n + c));
-      ss = fmaf(v, v, ss);
+// 1 / rms of the first T rows of x (fixed point, n columns, n even) into s_inv. Every thread reads
+// 16-byte pairs of columns (all loads of a batch in flight at once) and sums its own columns of
+// each token in a fixed order; red (T x PK_THREADS floats of shared memory) then holds the per-thread
+// partial sums, which one warp per token adds in a fixed order: the result is deterministic.
+__device__ __forceinline__ void rms_stats(const long long* x, int T, int n, float eps, float* s_inv, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int np = n >> 1, total = T * np;
+  for (int t = 0; t < T; t++) red[t * PK_THREADS + tid] = 0.f;
+  int cur = -1;
+  float ss = 0.f;
+  for (int j0 = 0; j0 < total; j0 += 4 * PK_THREADS) {
+    longlong2 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int j = j0 + u * PK_THREADS + tid;
+      if (j < total) {
+        const int t = j / np;
+        v[u] = __ldcg(reinterpret_cast<const longlong2*>(x + (size_t)t * n) + (j - t * np));
+      }
     }
-    ss = warp_sum(ss);
-    if (lane == 0) s_inv[t] = 1.0f / sqrtf(ss / (float)n + eps);
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int j = j0 + u * PK_THREADS + tid;
+      if (j < total) {
+        const int t = j / np;
+        if (t != cur) {
+          if (cur >= 0) red[cur * PK_THREADS + tid] = ss;
+          ss = 0.f;
+          cur = t;
+        }
+        const float f0 = from_fix(v[u].x), f1 = from_fix(v[u].y);
+        ss = fmaf(f0, f0, ss);
+        ss = fmaf(f1, f1, ss);
+      }
+    }
   }
+  if (cur >= 0) red[cur * PK_THREADS + tid] = ss;
+  __syncthreads();
+  for (int t = warp; t < T; t += PK_NW) {
+    float v = 0.f;
+#pragma unroll
+    for (int k = 0; k < PK_THREADS / 32; k++) v += red[t * PK_THREADS + k * 32 + lane];
+    v = warp_sum(v);
+    if (lane == 0) s_inv[t] = 1.0f / sqrtf(v / (float)n + eps);
+  }
+  __syncthreads();
 }
 
 __device__ __forceinline__ void zero_ll(long long* p, size_t n) {
   for (size_t i = (size_t)blockIdx.x * PK_THREADS + threadIdx.x; i < n; i += (size_t)gridDim.x * PK_THREADS) p[i] = 0;
 }
 
+// Shared memory of one attention item: q [T][HD] f32, K and V tiles [64][HD + 2] f16 (the odd word
+// stride keeps the per-position reads free of bank conflicts), running state [T][HD + 2] f32.
+// The state region is reused by the slot merge ([T][S][3] floats).
+__host__ __device__ constexpr size_t pk_att_smem(int T, int hd) {
+  return (size_t)T * hd * 4 + 2 * (size_t)PK_ATT_TILE * (hd + 2) * 2 +
+         (size_t)T * ((hd + 2) > 3 * kMaxSlots ? (hd + 2) : 3 * kMaxSlots) * 4;
+}
+
 // ---------------------------------------------------------------------------------------------
-// Attention item: query head hh over context tiles {slot, slot + S, ...}; writes (m, l, acc).
+// Attention item: query head hh over context tiles {slot, slot + S, ...}; writes (m, l, acc) of
+// the slot. The last CTA to finish a head (per-head arrival counter) merges the S slot states into
+// the attention output of that head.
 // ---------------------------------------------------------------------------------------------
-__device__ void attention_item(const PassArgs& a, int l, int hh, int slot, float* sm) {
-  const int HD = a.hd, HALF = HD / 2, HP = HD + 1, T = a.T, S = a.slots;
+__device__ void attention_item(const PassArgs& a, int l, int hh, int slot, uint8_t* sm) {
+  __shared__ int s_last;
+  const int HD = a.hd, HALF = HD / 2, HP = HD + 2, T = a.T, S = a.slots;
   const int group = a.heads / a.kv_heads, g = hh / group;
   const int pos0 = a.ctl->pos0, total = pos0 + T;
   const int ntiles = (total + PK_ATT_TILE - 1) / PK_ATT_TILE;
@@ -315,10 +410,10 @@ __device__ void attention_item(const PassArgs& a, int l, int hh, int slot, float
   const size_t lstride = (size_t)a.kv_heads * a.max_ctx * HD;
   uint16_t* kc = a.kc + (size_t)l * lstride;
   uint16_t* vc = a.vc + (size_t)l * lstride;
-  float* qs = sm;                    // [T][HD]
-  float* Ks = qs + T * HD;           // [64][HP]
-  float* Vs = Ks + PK_ATT_TILE * HP;
-  float* st = Vs + PK_ATT_TILE * HP;  // [T][HD + 2]
+  float* qs = reinterpret_cast<float*>(sm);                         // [T][HD]
+  __half* Ks = reinterpret_cast<__half*>(qs + T * HD);              // [64][HP]
+  __half* Vs = Ks + PK_ATT_TILE * HP;                               // [64][HP]
+  float* st = reinterpret_cast<float*>(Vs + PK_ATT_TILE * HP);      // [T][HP]
   const float scale = 1.0f / sqrtf((float)HD);
   for (int i = threadIdx.x; i < T * HALF; i += PK_THREADS) {
     const int t = i / HALF, d = i - t * HALF;
@@ -328,36 +423,46 @@ __device__ void attention_item(const PassArgs& a, int l, int hh, int slot, float
     qs[t * HD + d] = x1 * cs.x - x2 * cs.y;
     qs[t * HD + d + HALF] = x2 * cs.x + x1 * cs.y;
   }
-  for (int i = threadIdx.x; i < T * (HD + 2); i += PK_THREADS) st[i] = (i % (HD + 2) == 0) ? -CUDART_INF_F : 0.f;
+  for (int i = threadIdx.x; i < T * HP; i += PK_THREADS) st[i] = (i % HP == 0) ? -CUDART_INF_F : 0.f;
   const bool writer = (hh % group) == 0;
+  const int c8 = HD / 8;  // 16-byte chunks per cached row
   for (int tile = slot; tile < ntiles; tile += S) {
     const int p0 = tile * PK_ATT_TILE;
     __syncthreads();
+    // cached rows: 16-byte loads, all of a thread's chunks in flight together
+    for (int i = threadIdx.x; i < PK_ATT_TILE * c8; i += PK_THREADS) {
+      const int pl = i / c8, ch = i - pl * c8, p = p0 + pl;
+      if (p < pos0) {
+        const size_t base = ((size_t)g * a.max_ctx + p) * HD + ch * 8;
+        const uint4 kv4 = __ldcg(reinterpret_cast<const uint4*>(kc + base));
+        const uint4 vv4 = __ldcg(reinterpret_cast<const uint4*>(vc + base));
+        uint32_t* kd = reinterpret_cast<uint32_t*>(Ks + pl * HP + ch * 8);
+        uint32_t* vd = reinterpret_cast<uint32_t*>(Vs + pl * HP + ch * 8);
+        kd[0] = kv4.x, kd[1] = kv4.y, kd[2] = kv4.z, kd[3] = kv4.w;
+        vd[0] = vv4.x, vd[1] = vv4.y, vd[2] = vv4.z, vd[3] = vv4.w;
+      }
+    }
+    // rows of this block (rotated, rounded to f16, appended to the cache) and zero padding
     for (int i = threadIdx.x; i < PK_ATT_TILE * HALF; i += PK_THREADS) {
       const int pl = i / HALF, d = i - pl * HALF, p = p0 + pl;
-      float k1 = 0.f, k2 = 0.f, v1 = 0.f, v2 = 0.f;
-      if (p < pos0) {
-        const size_t base = ((size_t)g * a.max_ctx + p) * HD;
-        k1 = __half2float(__ushort_as_half(kc[base + d]));
-        k2 = __half2float(__ushort_as_half(kc[base + d + HALF]));
-        v1 = __half2float(__ushort_as_half(vc[base + d]));
-        v2 = __half2float(__ushort_as_half(vc[base + d + HALF]));
-      } else if (p < total) {
+      if (p < pos0) continue;
+      __half k1 = __float2half_rn(0.f), k2 = k1, v1 = k1, v2 = k1;
+      if (p < total) {
         const int t = p - pos0;
         const long long* kr = a.qkv + (size_t)t * QS + H + g * HD;
         const long long* vr = a.qkv + (size_t)t * QS + H + KV + g * HD;
         const float2 cs = a.rope[(size_t)p * HALF + d];
         const float x1 = from_fix(ldcg_ll(kr + d)), x2 = from_fix(ldcg_ll(kr + d + HALF));
-        k1 = __half2float(__float2half_rn(x1 * cs.x - x2 * cs.y));
-        k2 = __half2float(__float2half_rn(x2 * cs.x + x1 * cs.y));
-        v1 = __half2float(__float2half_rn(from_fix(ldcg_ll(vr + d))));
-        v2 = __half2float(__float2half_rn(from_fix(ldcg_ll(vr + d + HALF))));
+        k1 = __float2half_rn(x1 * cs.x - x2 * cs.y);
+        k2 = __float2half_rn(x2 * cs.x + x1 * cs.y);
+        v1 = __float2half_rn(from_fix(ldcg_ll(vr + d)));
+        v2 = __float2half_rn(from_fix(ldcg_ll(vr + d + HALF)));
         if (writer) {
           const size_t base = ((size_t)g * a.max_ctx + p) * HD;
-          kc[base + d] = __half_as_ushort(__float2half_rn(k1));
-          kc[base + d + HALF] = __half_as_ushort(__float2half_rn(k2));
-          vc[base + d] = __half_as_ushort(__float2half_rn(v1));
-          vc[base + d + HALF] = __half_as_ushort(__float2half_rn(v2));
+          kc[base + d] = __half_as_ushort(k1);
+          kc[base + d + HALF] = __half_as_ushort(k2);
+          vc[base + d] = __half_as_ushort(v1);
+          vc[base + d + HALF] = __half_as_ushort(v2);
         }
       }
       Ks[pl * HP + d] = k1;
@@ -370,19 +475,26 @@ __device__ void attention_item(const PassArgs& a, int l, int hh, int slot, float
       const int ctx = pos0 + t + 1;
       if (p0 >= ctx) continue;
       const float* q = qs + t * HD;
-      float s0 = -CUDART_INF_F, s1 = -CUDART_INF_F;
-      if (p0 + lane < ctx) {
-        float acc = 0.f;
-        for (int d = 0; d < HD; d++) acc = fmaf(q[d], Ks[lane * HP + d], acc);
-        s0 = acc * scale;
+      // scores of positions p0 + lane and p0 + 32 + lane: four independent FMA chains
+      const __half2* kr0 = reinterpret_cast<const __half2*>(Ks + lane * HP);
+      const __half2* kr1 = reinterpret_cast<const __half2*>(Ks + (lane + 32) * HP);
+      float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+      for (int d = 0; d < HD; d += 4) {
+        const float2 ka = __half22float2(kr0[d / 2]), kb = __half22float2(kr0[d / 2 + 1]);
+        const float2 kc2 = __half22float2(kr1[d / 2]), kd = __half22float2(kr1[d / 2 + 1]);
+        a0 = fmaf(q[d], ka.x, a0);
+        a0 = fmaf(q[d + 1], ka.y, a0);
+        a1 = fmaf(q[d + 2], kb.x, a1);
+        a1 = fmaf(q[d + 3], kb.y, a1);
+        b0 = fmaf(q[d], kc2.x, b0);
+        b0 = fmaf(q[d + 1], kc2.y, b0);
+        b1 = fmaf(q[d + 2], kd.x, b1);
+        b1 = fmaf(q[d + 3], kd.y, b1);
       }
-      if (p0 + 32 + lane < ctx) {
-        float acc = 0.f;
-        for (int d = 0; d < HD; d++) acc = fmaf(q[d], Ks[(lane + 32) * HP + d], acc);
-        s1 = acc * scale;
-      }
+      const float s0 = (p0 + lane < ctx) ? (a0 + a1) * scale : -CUDART_INF_F;
+      const float s1 = (p0 + 32 + lane < ctx) ? (b0 + b1) * scale : -CUDART_INF_F;
       const float tmax = warp_max(fmaxf(s0, s1));
-      float* Sx = st + t * (HD + 2);
+      float* Sx = st + t * HP;
       const float m_old = Sx[0], m_new = fmaxf(m_old, tmax);
       const float corr = (m_old == -CUDART_INF_F) ? 0.f : expf(m_old - m_new);
       const float e0 = (s0 == -CUDART_INF_F) ? 0.f : expf(s0 - m_new);
@@ -390,16 +502,14 @@ __device__ void attention_item(const PassArgs& a, int l, int hh, int slot, float
       const float lsum = warp_sum(e0 + e1);
       for (int d0 = 0; d0 < HD; d0 += 32) {
         const int d = d0 + lane;
-        float acc = (d < HD) ? Sx[2 + d] * corr : 0.f;
+        const int dc = d < HD ? d : 0;
+        float acc = (d < HD) ? Sx[2 + d] * corr : 0.f, acc2 = 0.f;
         for (int pl = 0; pl < 32; pl++) {
-          const float e = __shfl_sync(0xffffffffu, e0, pl);
-          if (d < HD) acc = fmaf(e, Vs[pl * HP + d], acc);
+          const float ea = __shfl_sync(0xffffffffu, e0, pl), eb = __shfl_sync(0xffffffffu, e1, pl);
+          acc = fmaf(ea, __half2float(Vs[pl * HP + dc]), acc);
+          acc2 = fmaf(eb, __half2float(Vs[(pl + 32) * HP + dc]), acc2);
         }
-        for (int pl = 0; pl < 32; pl++) {
-          const float e = __shfl_sync(0xffffffffu, e1, pl);
-          if (d < HD) acc = fmaf(e, Vs[(pl + 32) * HP + d], acc);
-        }
-        if (d < HD) Sx[2 + d] = acc;
+        if (d < HD) Sx[2 + d] = acc + acc2;
       }
       __syncwarp();
       if (lane == 0) {
@@ -410,8 +520,49 @@ __device__ void attention_item(const PassArgs& a, int l, int hh, int slot, float
     }
   }
   __syncthreads();
-  float* part = a.att_part + ((size_t)hh * S + slot) * T * (HD + 2);
-  for (int i = threadIdx.x; i < T * (HD + 2); i += PK_THREADS) part[i] = st[i];
+  float* part = a.att_part + ((size_t)hh * S + slot) * T * HP;
+  for (int i = threadIdx.x; i < T * HP; i += PK_THREADS) part[i] = st[i];
+  // publish the slot state; the last of the S slots merges them
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&a.att_cnt[hh], 1u) == (unsigned)(S - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // merge: slot weights e^(m_s - m*) / L per token (T x S, into shared memory), then every output
+  // element is a weighted sum over the slots with all S loads in flight
+  const float* hp = a.att_part + (size_t)hh * S * T * HP;
+  float* ml = st;           // [T][S][2] (m, l) — st is free once the part is written
+  float* wts = ml + T * S * 2;  // [T][S]
+  for (int i = threadIdx.x; i < T * S; i += PK_THREADS) {
+    const int t = i / S, s2 = i - t * S;
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(hp + ((size_t)s2 * T + t) * HP));
+    ml[2 * i] = v.x;
+    ml[2 * i + 1] = v.y;
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < T; t += PK_THREADS) {
+    const float* r = ml + t * S * 2;
+    float mx = -CUDART_INF_F;
+    for (int s2 = 0; s2 < S; s2++) mx = fmaxf(mx, r[2 * s2]);
+    float L = 0.f;
+    for (int s2 = 0; s2 < S; s2++) L += (r[2 * s2] == -CUDART_INF_F) ? 0.f : r[2 * s2 + 1] * expf(r[2 * s2] - mx);
+    for (int s2 = 0; s2 < S; s2++) wts[t * S + s2] = (r[2 * s2] == -CUDART_INF_F) ? 0.f : expf(r[2 * s2] - mx) / L;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < T * HD; i += PK_THREADS) {
+    const int t = i / HD, d = i - t * HD;
+    const float* base = hp + (size_t)t * HP + 2 + d;
+    float v[kMaxSlots];
+#pragma unroll
+    for (int s2 = 0; s2 < kMaxSlots; s2++) v[s2] = s2 < S ? __ldcg(base + (size_t)s2 * T * HP) : 0.f;
+    float o = 0.f;
+#pragma unroll
+    for (int s2 = 0; s2 < kMaxSlots; s2++)
+      if (s2 < S) o = fmaf(v[s2], wts[t * S + s2], o);
+    a.attn[(size_t)t * a.hidden + hh * HD + d] = o;
+  }
+  if (threadIdx.x == 0) a.att_cnt[hh] = 0;  // the counter is reused by the next layer
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -421,7 +572,7 @@ template <int BITS, int G, int NT>
 __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   using Gemv = TcGemv<BITS, G, NT>;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bar_a[2], bar_full[2], bar_d;
+  __shared__ uint64_t bar_a[2], bar_full[2], bar_d[2], bar_dfree[2], bar_fin;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ float s_inv[NT];
@@ -429,25 +580,30 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   __shared__ uint32_t s_bi[PK_NW][NT];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool compute = threadIdx.x < PK_CT;
   const int T = a.T, h = a.hidden, I = a.inter;
   const int kvd = a.kv_heads * a.hd, QS = h + 2 * kvd;
   int* err = &a.ctl->err;
-  // shared memory: [load ring][B operand or attention scratch]
+  // shared memory: [load ring][B operand, or attention scratch, or rms partial sums]
   uint8_t* ring = smem;
-  uint8_t* xb = smem + (size_t)PK_STAGES * Gemv::kStage;
+  uint8_t* xb = smem + (size_t)Gemv::STAGES * Gemv::kStage;
+  float* red = reinterpret_cast<float*>(xb);
   const uint32_t xb_addr = tc::su32(xb);
 
   if (threadIdx.x == 0) {
-    tc::mbar_init(&bar_a[0], 1);
-    tc::mbar_init(&bar_a[1], 1);
-    tc::mbar_init(&bar_full[0], PK_THREADS);
-    tc::mbar_init(&bar_full[1], PK_THREADS);
-    tc::mbar_init(&bar_d, 1);
+    for (int i = 0; i < 2; i++) {
+      tc::mbar_init(&bar_a[i], 1);
+      tc::mbar_init(&bar_full[i], PK_NWG * 4);  // one arrival per compute warp
+      tc::mbar_init(&bar_d[i], 1);
+      tc::mbar_init(&bar_dfree[i], PK_NWG * 4);
+    }
+    tc::mbar_init(&bar_fin, 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::su32(&s_tmem)), "r"(128)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::su32(&s_tmem)),
+                 "r"(PK_TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -456,61 +612,80 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   Gemv gm;
   gm.tmem = s_tmem;
   gm.ring = ring;
-  gm.ring_addr = tc::su32(ring) + (uint32_t)threadIdx.x * Gemv::CPB * 16;
+  gm.ring_addr = tc::su32(ring) + (uint32_t)(compute ? threadIdx.x : 0) * Gemv::CPB * 16;
   gm.bar_a = bar_a;
   gm.bar_full = bar_full;
-  gm.bar_d = &bar_d;
+  gm.bar_d = bar_d;
+  gm.bar_dfree = bar_dfree;
   gm.abort = &s_abort;
-  gm.uses0 = gm.uses1 = gm.dphase = 0;
+  gm.blk = gm.itc = 0;
 
+  // Profiling timeline: slot 0 = start, 2b - 1 / 2b = arrival at / departure from barrier b.
+  auto stamp = [&](unsigned slot) {
+    if (a.trace && threadIdx.x == 0) a.trace[(size_t)slot * gridDim.x + blockIdx.x] = gtimer();
+  };
+  stamp(0);
   unsigned nbar = 0;
   bool ok = true;
   auto barrier = [&]() {
     nbar++;
+    if (a.trace) {
+      __syncthreads();
+      stamp(2 * nbar - 1);
+    }
     if (ok && !grid_barrier(a.bar, nbar * gridDim.x, err)) ok = false;
     if (s_abort) ok = false;
+    stamp(2 * nbar);
     return ok;
   };
   // Starts the weight stream of this CTA's first item of a GEMV phase (before the barrier).
   auto prefetch = [&](const QMat& w, int ks) {
     const Split sp = make_split<BITS, G>(w, ks);
-    if ((int)blockIdx.x < sp.items()) {
-      int t128, kb0, kb1;
-      sp.item(blockIdx.x, &t128, &kb0, &kb1);
-      gm.prologue(w, t128, kb0, kb1);
+    if (compute && (int)blockIdx.x < sp.items()) {
+      int t256, kb0, kb1;
+      sp.item(blockIdx.x, &t256, &kb0, &kb1);
+      gm.prologue(w, t256, kb0, kb1);
     }
   };
-  // Runs the items of a GEMV phase: stage(kb0, kb1) fills the B operand of a K slice,
-  // epi(t128, ks_index, tot) consumes the accumulators.
+  // Runs the items of a GEMV phase (the first one's weights already streaming): stage(col0, ncol,
+  // sbo) fills the B operand of a K slice, epi(row, ks_index, tot) consumes the accumulators.
+  // Every thread walks the same item sequence (so the staging barriers match even after a failure,
+  // when the work is skipped and every bounded wait returns at once).
   auto gemv_phase = [&](const QMat& w, int ks, auto stage, auto epi) {
     const Split sp = make_split<BITS, G>(w, ks);
     int staged = -1;
-    bool first = true;
-    for (int i = blockIdx.x; i < sp.items() && ok; i += gridDim.x) {
-      int t128, kb0, kb1;
-      sp.item(i, &t128, &kb0, &kb1);
-      const int kslice = i / sp.tiles128;
+    for (int i = blockIdx.x; i < sp.items(); i += gridDim.x) {
+      int t256, kb0, kb1;
+      sp.item(i, &t256, &kb0, &kb1);
+      const int kslice = i / sp.tiles;
       const int col0 = kb0 * Gemv::KB, ncol = (kb1 - kb0) * Gemv::KB;
       const uint32_t sbo = (uint32_t)(ncol / 8) * 128u;
       if (kslice != staged) {
         __syncthreads();
-        stage(col0, ncol, sbo);
+        if (ok) stage(col0, ncol, sbo);
         __syncthreads();
         staged = kslice;
       }
-      if (!first) gm.prologue(w, t128, kb0, kb1);
-      first = false;
-      float tot[NT];
-      if (!gm.run(w, t128, kb0, kb1, xb_addr, sbo, tot)) {
+      if (!ok) continue;
+      if (compute) {
+        int nx[3];
+        const bool has_next = i + (int)gridDim.x < sp.items();
+        if (has_next) sp.item(i + gridDim.x, &nx[0], &nx[1], &nx[2]);
+        float tot[NT];
+        if (!gm.run(w, t256, kb0, kb1, tot, has_next ? nx : nullptr)) {
+          ok = false;
+        } else {
+          const int t32 = (t256 * PK_NWG + (warp >> 2)) * 4 + (warp & 3);
+          if (t32 < w.rows_pad / 32) epi(t32 * 32 + lane, kslice, tot);
+        }
+      } else if (!gm.issue(kb0, kb1, xb_addr, sbo)) {
         ok = false;
-        s_abort = 1;
-        if (threadIdx.x == 0) atomicCAS(err, 0, 1);  // the other CTAs stop at their next wait
-        break;
       }
-      const int t32 = t128 * 4 + warp;
-      if (t32 < w.rows_pad / 32) epi(t32 * 32 + lane, kslice, tot);
+      if (!ok) {
+        s_abort = 1;
+        if (lane == 0) atomicCAS(err, 0, 1);  // the other CTAs stop at their next wait
+      }
     }
-    // drain an unused prologue (a CTA without items never issued one)
     tc::cp_wait<0>();
   };
 
@@ -548,8 +723,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   for (int l = 0; l < a.L && ok; l++) {
     const PassLayer& W = a.layers[l];
     // ---- QKV: RMSNorm(x) -> q|k|v sums (+ bias once) ----
-    rms_stats(a.x, T, h, a.eps, s_inv);
-    __syncthreads();
+    rms_stats(a.x, T, h, a.eps, s_inv, red);
     gemv_phase(
         W.qkv, a.ks_qkv,
         [&](int col0, int ncol, uint32_t sbo) {
@@ -569,44 +743,17 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     // ---- attention (the block's K/V appended to the cache); zero the gate/up accumulators ----
     for (int it = blockIdx.x; it < a.heads * a.slots; it += gridDim.x) {
       __syncthreads();
-      attention_item(a, l, it / a.slots, it % a.slots, reinterpret_cast<float*>(xb));
+      attention_item(a, l, it / a.slots, it % a.slots, xb);
     }
     zero_ll(a.gu, (size_t)T * 2 * I);
     prefetch(W.o, a.ks_o);
     if (!barrier()) break;
 
-    // ---- O: combine the attention slots while staging, residual add into x ----
+    // ---- O: residual add into x ----
     gemv_phase(
         W.o, a.ks_o,
         [&](int col0, int ncol, uint32_t sbo) {
-          // per (head, token) slot weights e^(m_s - m*) / L, then the weighted sum of acc_s
-          const int HD = a.hd, S = a.slots;
-          const int h0 = col0 / HD, nh = (ncol + HD - 1) / HD;
-          float* wts = reinterpret_cast<float*>(xb + (size_t)NT * ncol * 2);  // [nh][T][S]
-          for (int i = threadIdx.x; i < nh * T; i += PK_THREADS) {
-            const int hi = i / T, t = i - hi * T;
-            const float* base = a.att_part + (size_t)(h0 + hi) * S * T * (HD + 2) + (size_t)t * (HD + 2);
-            float mx = -CUDART_INF_F;
-            for (int s = 0; s < S; s++) mx = fmaxf(mx, __ldcg(base + (size_t)s * T * (HD + 2)));
-            float L = 0.f;
-            for (int s = 0; s < S; s++) {
-              const float ms = __ldcg(base + (size_t)s * T * (HD + 2));
-              L += (ms == -CUDART_INF_F) ? 0.f : __ldcg(base + (size_t)s * T * (HD + 2) + 1) * expf(ms - mx);
-            }
-            for (int s = 0; s < S; s++) {
-              const float ms = __ldcg(base + (size_t)s * T * (HD + 2));
-              wts[(size_t)i * S + s] = (ms == -CUDART_INF_F) ? 0.f : expf(ms - mx) / L;
-            }
-          }
-          __syncthreads();
-          stage_b<NT>(xb, sbo, T, col0, ncol, [&](int t, int c) {
-            const int hh = c / HD, d = c - hh * HD;
-            const float* base = a.att_part + (size_t)hh * S * T * (HD + 2) + (size_t)t * (HD + 2) + 2 + d;
-            const float* w = wts + ((size_t)(hh - h0) * T + t) * S;
-            float o = 0.f;
-            for (int s = 0; s < S; s++) o = fmaf(__ldcg(base + (size_t)s * T * (HD + 2)), w[s], o);
-            return o;
-          });
+          stage_b<NT>(xb, sbo, T, col0, ncol, [&](int t, int c) { return __ldcg(a.attn + (size_t)t * h + c); });
         },
         [&](int r, int, float (&tot)[NT]) {
           if (r >= h) return;
@@ -619,8 +766,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     if (!barrier()) break;
 
     // ---- gate/up: RMSNorm(x) -> gate/up sums ----
-    rms_stats(a.x, T, h, a.eps, s_inv);
-    __syncthreads();
+    rms_stats(a.x, T, h, a.eps, s_inv, red);
     gemv_phase(
         W.gu, a.ks_gu,
         [&](int col0, int ncol, uint32_t sbo) {
@@ -629,6 +775,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
           });
         },
         [&](int r, int, float (&tot)[NT]) {
+          if (r >= 2 * I) return;
 #pragma unroll
           for (int t = 0; t < NT; t++)
             if (t < T) fix_add(a.gu + (size_t)t * 2 * I + r, tot[t]);
@@ -653,7 +800,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
             if (t < T) fix_add(a.x + (size_t)t * h + r, tot[t]);
         });
     if (l + 1 < a.L) prefetch(a.layers[l + 1].qkv, a.ks_qkv);
-    else prefetch(a.embed, 1);
+    else if (a.n_logits > 0) prefetch(a.embed, 1);
     if (!barrier()) break;
   }
 
@@ -664,8 +811,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
       (&s_bv[0][0])[i] = -CUDART_INF_F;
       (&s_bi[0][0])[i] = 0xffffffffu;
     }
-    rms_stats(a.x + (size_t)r0 * h, n, h, a.eps, s_inv);
-    __syncthreads();
+    rms_stats(a.x + (size_t)r0 * h, n, h, a.eps, s_inv, red);
     gemv_phase(
         a.embed, 1,
         [&](int col0, int ncol, uint32_t sbo) {
@@ -704,14 +850,21 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   } else if (ok && blockIdx.x == 0 && threadIdx.x == 0) {
     a.ctl->pos0 += a.ctl->M;
   }
+  __syncthreads();
+  stamp(2 * nbar + 1);
 
-  // ---- release tensor memory ----
+  // ---- release tensor memory (after the issuer's MMAs have all completed, also after an abort) ----
   tc::cp_wait<0>();
+  if (warp == PK_ISSUER && lane == 0) {
+    volatile int no_abort = 0;
+    tc::commit(&bar_fin);
+    tc::mbar_wait(&bar_fin, 0, &no_abort);
+  }
   tc::fence_before();
   __syncthreads();
   if (warp == 0) {
     tc::fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(s_tmem), "r"(128) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(s_tmem), "r"(PK_TMEM_COLS) : "memory");
   }
   if (s_abort && threadIdx.x == 0) atomicCAS(err, 0, 1);
 }
@@ -720,28 +873,25 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
 // Host side
 // ---------------------------------------------------------------------------------------------
 
-static int pk_nt(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : 48; }
+int pass_kernel_nt(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : 48; }
 
 bool pass_kernel_supported(const WeightFormat& body, const WeightFormat& embed, int T, int hd) {
-  if (!(body == embed) || T < 1 || T > 48 || hd % 2 || hd > 128) return false;
+  if (!(body == embed) || T < 1 || T > 48 || hd % 8 || hd > 128) return false;
   return (body.bits == 8 && (body.group == 32 || body.group == 64)) || (body.bits == 4 && (body.group == 16 || body.group == 32));
 }
 
-size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int heads, int slots, int ks_down,
-                        int ks_o) {
-  const int NT = pk_nt(T);
+size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down) {
+  const int NT = pass_kernel_nt(T);
   const int kb = tc_kb(f.bits, f.group), cpb = kb / (128 / f.bits);
-  const size_t ring = (size_t)PK_STAGES * PK_THREADS * cpb * 16;
-  // largest B operand: a K slice of down (inter / ks_down), the full hidden (QKV, gate/up, head),
-  // or an O slice plus its slot weights
+  const size_t stage = (size_t)PK_CT * cpb * 16;
+  const size_t stages = std::max<size_t>(4, PK_RING_BYTES / stage);
+  // largest B operand: the full hidden width (QKV, O, gate/up, head) or a K slice of down
   const int nblk_down = inter / kb;
   const int down_cols = ((nblk_down + ks_down - 1) / ks_down) * kb;
-  const int nblk_o = hidden / kb;
-  const int o_cols = ((nblk_o + ks_o - 1) / ks_o) * kb;
-  size_t b = (size_t)NT * std::max(hidden, std::max(down_cols, o_cols)) * 2;
-  b = std::max(b, (size_t)NT * o_cols * 2 + (size_t)((o_cols + hd - 1) / hd + 1) * T * slots * 4);
-  const size_t att = ((size_t)T * hd + 2 * PK_ATT_TILE * (hd + 1) + (size_t)T * (hd + 2)) * 4;
-  return ring + std::max(b, att);
+  size_t b = (size_t)NT * std::max(hidden, down_cols) * 2;
+  b = std::max(b, (size_t)T * PK_THREADS * 4);  // rms partial sums
+  b = std::max(b, pk_att_smem(T, hd));
+  return stages * stage + b;
 }
 
 template <int BITS, int G, int NT>
@@ -761,7 +911,7 @@ static void launch_pass_t(const PassArgs& a, size_t smem, int grid, cudaStream_t
 }
 
 void launch_pass(const PassArgs& a, const WeightFormat& f, size_t smem, int grid, cudaStream_t s) {
-  const int NT = pk_nt(a.T);
+  const int NT = pass_kernel_nt(a.T);
 #define LS_PK(B, GG)                                                   \
   if (f.bits == B && f.group == GG) {                                  \
     if (NT == 16) return launch_pass_t<B, GG, 16>(a, smem, grid, s);  \
@@ -776,9 +926,10 @@ void launch_pass(const PassArgs& a, const WeightFormat& f, size_t smem, int grid
   LS_THROW(-1, "format not supported by the pass kernel");
 }
 
-// Occupancy check: the cooperative launch needs every CTA resident at once.
-int pass_kernel_max_grid(const WeightFormat& f, int T, size_t smem, int num_sms) {
-  const int NT = pk_nt(T);
+// CTAs of the token tile of T that are resident per SM at once (the cooperative launch needs the
+// whole grid resident), capped at max_per_sm and at one (each CTA allocates all tensor memory).
+int pass_kernel_blocks_per_sm(const WeightFormat& f, int T, size_t smem, int max_per_sm) {
+  const int NT = pass_kernel_nt(T);
   int per_sm = 0;
   auto q = [&](auto kern) {
     ensure_smem(kern, smem);
@@ -795,7 +946,9 @@ int pass_kernel_max_grid(const WeightFormat& f, int T, size_t smem, int num_sms)
   LS_PKO(4, 16)
   LS_PKO(4, 32)
 #undef LS_PKO
-  return per_sm >= 1 ? num_sms : 0;
+  if (getenv("LS_PASS_VERBOSE")) fprintf(stderr, "pass kernel T=%d smem %zu: %d CTAs/SM resident\n", T, smem, per_sm);
+  // the CTA takes the whole tensor memory of its SM
+  return std::min(std::min(per_sm, max_per_sm), 1);
 }
 
 }  // namespace ls
