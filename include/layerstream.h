@@ -171,6 +171,21 @@ int ls_qweights_free(LsQWeights *w);
 /* x_dev: M x cols f32, y_dev: M x rows f32, both device pointers; stream: a cudaStream_t or NULL. */
 int ls_qgemv_device(const LsQWeights *w, const float *x_dev, uint64_t M, float *y_dev, void *stream);
 
+/* No counterpart in the reference. The GEMV above for hosts that cannot let this library allocate
+ * device memory (their device memory belongs to another allocator, or to a fixed budget, so a
+ * cudaMalloc here could fail, escape their accounting or synchronize the device mid-pipeline):
+ * y_dev[t][r] = dot(stored row r, x_dev[t]) for t < M, the `rows` stored rows (.lsq row format,
+ * rows x row_bytes) already in device memory the caller owns; x_dev M x cols f32, y_dev M x rows
+ * f32 (rows_dev 2-byte, x_dev and y_dev 4-byte aligned), all on the current device; stream: a
+ * cudaStream_t or NULL. The K-split partial sums go to a fixed 4 MiB array in the library's device
+ * memory that every GPU loading the library holds until exit; requests beyond it (M > 16 or
+ * M x rows > 262144) fail with LS_ERR_ARG. The first call on a device looks up that array's
+ * address, so make it before any stream capture. All calls on a GPU share the array, and every
+ * call overwrites what it reads: calls that overlap on the GPU (other streams, other threads)
+ * race and must be serialized by the caller. */
+int ls_qgemv_rows_noalloc(int bits, int group, const uint8_t *rows_dev, uint64_t rows, uint64_t cols, const float *x_dev,
+                          uint64_t M, float *y_dev, void *stream);
+
 /* Embedding gather + dequantisation of n stored rows (ids index `rows` stored rows in the .lsq row
  * format) into out (n x cols floats), through the same repack and gather kernels the model uses.
  * Mirrors kernels::dequant_row (src/kernels.rs:95-121); the result is bit-exact. */

@@ -84,6 +84,8 @@ _SIGS = {
     "ls_qweights_free": (C.c_int, [C.c_void_p]),
     "ls_qgemv_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p]),
     "ls_qgemv_bytes": (C.c_uint64, [C.c_int, C.c_int, C.c_uint64, C.c_uint64, C.c_uint64]),
+    "ls_qgemv_rows_noalloc": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64,
+                                        C.c_void_p, C.c_void_p]),
     "ls_dequant_rows_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p]),
 }
 
@@ -273,6 +275,14 @@ class QWeights:
         if getattr(self, "_h", None):
             lib().ls_qweights_free(self._h)
             self._h = None
+
+
+def qgemv_rows_noalloc(bits: int, group: int, rows_ptr: int, rows: int, cols: int, x_ptr: int, M: int, y_ptr: int,
+                       stream: int = 0):
+    """y = W x on device buffers the caller owns (W in the stored row format); the library allocates
+    nothing (its K-split scratch is a fixed per-GPU array shared by all calls)."""
+    _check(lib().ls_qgemv_rows_noalloc(bits, group, C.c_void_p(rows_ptr), rows, cols, C.c_void_p(x_ptr), M,
+                                       C.c_void_p(y_ptr), C.c_void_p(stream)))
 
 
 SYMBOLS = tuple(_SIGS)

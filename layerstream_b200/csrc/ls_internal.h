@@ -246,6 +246,10 @@ struct PassArgs {
   float eps;
 };
 
+// ---- allocation-free GEMV (ls_noalloc.cu) ----
+void qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t rows, uint64_t cols, const float* x_dev,
+                        uint64_t M, float* y_dev, cudaStream_t s);
+
 int pass_kernel_nt(int T);
 bool pass_kernel_supported(const WeightFormat& body, const WeightFormat& embed, int T, int hd);
 size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down);

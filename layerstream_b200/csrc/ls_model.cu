@@ -1496,6 +1496,11 @@ int ls_qgemv_device(const LsQWeights* w, const float* x_dev, uint64_t M, float* 
   });
 }
 
+int ls_qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t rows, uint64_t cols, const float* x_dev,
+                          uint64_t M, float* y_dev, void* stream) {
+  return guard([&] { qgemv_rows_noalloc(bits, group, rows_dev, rows, cols, x_dev, M, y_dev, reinterpret_cast<cudaStream_t>(stream)); });
+}
+
 int ls_qgemv_host(int bits, int group, const uint8_t* rows_raw, uint64_t rows, uint64_t cols, const float* x, uint64_t M, float* y,
                   int iters, double* ms) {
   return guard([&] {
