@@ -339,7 +339,6 @@ def main():
         step()
 
     passes0 = target.report()["passes"] + (draft.report()["passes"] if draft else 0)
-    target.profile_enable(True)
     clocks = Clocks(local)
     barrier(dist)
     torch.cuda.synchronize()
@@ -356,9 +355,18 @@ def main():
     clk = clocks.stop()
     barrier(dist)
     ms = e0.elapsed_time(e1)
-    prof = target.profile()
-    target.profile_enable(False)
     passes = target.report()["passes"] + (draft.report()["passes"] if draft else 0) - passes0
+    # profiled samples after the timed region: CUDA events around every launch (roofline), then
+    # the persistent pass kernel's barrier timeline (per-phase split; it slows the pass a little)
+    target.profile_enable(1)
+    step()
+    prof = target.profile()
+    prof_tl = None
+    if info.persistent_pass:
+        target.profile_enable(2)
+        step()
+        prof_tl = target.profile()
+    target.profile_enable(0)
     t_ms = torch.tensor([ms], device="cuda")
     t_tok = torch.tensor([float(tokens)], device="cuda")
     if dist is not None:
@@ -390,10 +398,11 @@ def main():
     h2d = (r1["h2d_bytes"] - r0["h2d_bytes"]) // max(args.e2e_steps, 1)
     d2h = (r1["d2h_bytes"] - r0["d2h_bytes"]) // max(args.e2e_steps, 1)
 
-    # roofline of the dominant kernel (live CUDA-event timing inside the passes). The launch list
-    # (profiles/verify_pass_launches_config2.md) shows the tensor-core GEMV is ~80 % of a pass:
-    # its launches per pass are QKV, O, gate/up and down on every layer (timed on one sampled
-    # layer, times L) plus the LM head.
+    # roofline of the dominant kernel (live CUDA-event timing of its launches). With the persistent
+    # pass kernel a verify pass is one launch (profiles/pass_kernel_config2.md): algorithmic bytes =
+    # weights + the K/V rows read and written at that pass's context. Otherwise the tensor-core GEMV
+    # launches dominate (profiles/verify_pass_launches_config2.md): QKV, O, gate/up and down on
+    # every layer (timed on one sampled layer, times L) plus the LM head.
     peak, peak_kind = peaks()
     L = info.layers
     per_pass = {}
@@ -404,6 +413,23 @@ def main():
         per_pass[c] = (p["bytes"] / p["launches"] * mult, p["ms"] / p["launches"] * mult, mult)
     roof = None
     gemv_c = [c for c in ("qkv", "o", "gate_up", "down", "head") if c in per_pass]
+    if info.persistent_pass and prof["pass"]["launches"]:
+        pp = prof["pass"]
+        b, t_ms = pp["bytes"] / pp["launches"], pp["ms"] / pp["launches"]
+        achieved = b / (t_ms / 1e3) / 1e9
+        phases = {}
+        if prof_tl is not None:
+            for c in ("qkv", "attention", "o", "gate_up", "down", "head"):
+                q = prof_tl[c]
+                if q["launches"]:
+                    phases[c] = {"us": q["ms"] * 1e3 / q["launches"], "busy_us": q["busy_ms"] * 1e3 / q["launches"],
+                                 "gbs": q["bytes"] / q["ms"] * 1e3 / 1e9 if q["ms"] > 0 else None,
+                                 "per": "layer" if c != "head" else "pass"}
+        roof = {"bound": "hbm", "kernel": "pass_kernel (one persistent launch per verify pass)", "achieved": achieved,
+                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": profile_traffic("pass_kernel"), "algorithmic_bytes_per_launch": b, "avg_launch_us": t_ms * 1e3,
+                "launches_per_pass": 1, "phases": phases}
+        gemv_c = []
     if gemv_c:
         b = sum(per_pass[c][0] for c in gemv_c)
         t_ms = sum(per_pass[c][1] for c in gemv_c)
@@ -425,7 +451,8 @@ def main():
         pass_s = pp["ms"] / pp["launches"] / 1e3
         vstep = {"bytes_per_pass": wbytes + kvbytes, "avg_pass_us": pass_s * 1e6, "achieved_gbs": (wbytes + kvbytes) / pass_s / 1e9,
                  "frac": (wbytes + kvbytes) / pass_s / 1e9 / peak,
-                 "kernel_share_est": {c: per_pass[c][1] / (pp["ms"] / pp["launches"]) for c in per_pass}}
+                 "kernel_share_est": ({c: per_pass[c][1] / (pp["ms"] / pp["launches"]) for c in per_pass}
+                                      if not info.persistent_pass else None)}
     acc = sum(s["accepted"] for s in stats)
     dr = sum(s["drafted"] for s in stats)
     tp = sum(s["target_passes"] for s in stats)
@@ -447,7 +474,7 @@ def main():
         "config": base_cfg, "clocks": clk,
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "steps": args.e2e_steps, "includes": "prefill + decode through ls_speculative_greedy, host buffers"},
-        "gpu_launches": int(passes * kernels_per_pass),
+        "gpu_launches": int(passes * (1 if info.persistent_pass else kernels_per_pass)),
         "roofline": roof, "verify_step": vstep,
         "spec": {"tokens_per_pass": tokens / max(tp, 1), "accepted_over_drafted": acc / max(dr, 1), "target_passes": tp},
         "cpu_baseline": cpu,

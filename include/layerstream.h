@@ -60,6 +60,7 @@ typedef struct LsModelInfo {
   uint64_t layer_bytes;        /* bytes of one stored layer block */
   uint64_t embed_row_bytes;    /* bytes of one stored embedding row */
   uint64_t weight_bytes;       /* layers * layer_bytes + vocab * embed_row_bytes */
+  int32_t persistent_pass;     /* 1: passes of 1..48 tokens run as one persistent kernel launch */
 } LsModelInfo;
 
 /* src/provider.rs:29-37, src/source.rs:13-21 */
@@ -111,7 +112,9 @@ int ls_model_report(const LsModel *m, LsReport *out);
  * the model's work with their own CUDA events. */
 int ls_model_stream(const LsModel *m, void **stream);
 
-int ls_model_profile_enable(LsModel *m, int on);   /* also clears the counters */
+/* on: 0 off, 1 CUDA-event timing, 2 also the persistent pass kernel's barrier timeline (which
+ * adds a few % to the pass); also clears the counters */
+int ls_model_profile_enable(LsModel *m, int on);
 int ls_model_profile(const LsModel *m, LsProfile *out);
 
 int ls_pos(const LsModel *m, uint64_t *pos);

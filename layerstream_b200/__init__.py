@@ -30,7 +30,7 @@ class ModelInfo(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("hidden", "inter", "layers", "heads", "kv_heads", "head_dim", "vocab", "max_ctx")] + [
         (n, C.c_int32) for n in ("bits", "group", "embed_bits", "embed_group")
     ] + [("eps", C.c_float), ("rope_theta", C.c_float), ("layer_bytes", C.c_uint64), ("embed_row_bytes", C.c_uint64),
-         ("weight_bytes", C.c_uint64)]
+         ("weight_bytes", C.c_uint64), ("persistent_pass", C.c_int32)]
 
 
 class Report(C.Structure):
@@ -188,8 +188,9 @@ class Model:
         _check(lib().ls_model_stream(self._h, C.byref(p)))
         return p.value or 0
 
-    def profile_enable(self, on: bool = True):
-        """Live CUDA-event timing of one sampled layer's kernels, the LM head and the whole pass."""
+    def profile_enable(self, on=True):
+        """Live timing: 1/True = CUDA events (per-kernel classes, or the whole persistent pass);
+        2 = also the persistent pass kernel's barrier timeline (per-phase split, a few % slower)."""
         _check(lib().ls_model_profile_enable(self._h, int(on)))
 
     def profile(self) -> dict:

@@ -175,6 +175,7 @@ struct LsModel {
 
   // live profile: event pairs around the launches of one sampled layer, the head and the pass
   bool prof_on = false;
+  bool prof_timeline = false;  // barrier timestamps of the persistent pass kernel
   std::vector<cudaEvent_t> prof_ev;
   struct ProfRec { int cls; double bytes; };
   std::vector<ProfRec> prof_rec;  // filled at enqueue (capture) time, one per event pair
@@ -532,10 +533,11 @@ struct LsModel {
     a.arg_parts = pk_parts;
     a.logits = want_logits ? logits : nullptr;
     a.bar = pk_bar;
-    if (prof_on && !pk_trace) pk_trace = dalloc<unsigned>(pk_trace_slots() * (size_t)pk_max_grid);
-    a.trace = prof_on ? pk_trace : nullptr;
+    if (prof_timeline && !pk_trace) pk_trace = dalloc<unsigned>(pk_trace_slots() * (size_t)pk_max_grid);
+    a.trace = prof_timeline ? pk_trace : nullptr;
     pk_T = T;
     pk_n_logits = n_logits;
+    pk_traced = a.trace != nullptr;
     pk_grid_last = P.grid;
     a.L = (int)cfg.layers;
     a.hidden = (int)cfg.hidden;
@@ -566,6 +568,7 @@ struct LsModel {
   bool pk_pending = false;
   unsigned* pk_trace = nullptr;
   int pk_T = 0, pk_n_logits = 0;
+  bool pk_traced = false;
   // timeline slots of one pass: start, (arrive, leave) per grid barrier, end
   size_t pk_trace_slots() const { return 2 * (2 + 5 * cfg.layers) + 2; }
 
@@ -655,7 +658,7 @@ struct LsModel {
       prof.ms[7 - 1] += ms;
       prof.busy_ms[7 - 1] += ms;
       prof.bytes[7 - 1] += wb + kvb;
-      if (pk_trace) collect_pass_trace();
+      if (pk_trace && pk_traced) collect_pass_trace();
       return;
     }
     if (!prof_pending || !prof_cur) return;
@@ -1335,6 +1338,7 @@ int ls_model_info(const LsModel* m, LsModelInfo* o) {
     o->layer_bytes = m->file.layout.total;
     o->embed_row_bytes = c.embed_row_bytes();
     o->weight_bytes = c.layers * m->file.layout.total + c.vocab * c.embed_row_bytes();
+    o->persistent_pass = m->pk_max_grid > 0 ? 1 : 0;
   });
 }
 
@@ -1363,6 +1367,7 @@ int ls_model_profile_enable(LsModel* m, int on) {
   return guard([&] {
     NEED(m);
     m->prof_on = on != 0;
+    m->prof_timeline = on >= 2;
     m->prof = LsProfile{};
     m->prof_pending = false;
   });
