@@ -16,7 +16,7 @@ token uploads and result reads inside the timed region). Each rank decodes its o
 scaling, no collective on the data path). Inputs: the weights (278 MB per verify pass) exceed L2,
 so every pass streams them from HBM.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3]
 """
 
 from __future__ import annotations
@@ -37,12 +37,16 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+MICRO_SHAPES = {"qkv": (1152, 896), "o": (896, 896), "gate_up": (9728, 896), "down": (896, 4864), "head": (151936, 896)}
+
 CONFIGS = {
     1: dict(shape="0.5b", body=(8, 64), embed=(8, 64), prompt=128, span=16, repeats=3, max_new=32, k=4, drafter="model",
             draft=(4, 32)),
     2: dict(shape="0.5b", body=(4, 32), embed=(4, 32), prompt=512, span=32, repeats=0, max_new=256, k=8, drafter="lookup",
             draft=(4, 32)),
 }
+CONFIGS[3] = dict(shape="0.5b", body=(8, 64), embed=(8, 64), prompt=0, span=0, repeats=0, max_new=0, k=0, drafter="none",
+                  draft=(4, 32), micro=True)
 METRIC = "spec-decode accepted tokens/s"
 UNIT = "tok/s"
 
@@ -198,6 +202,19 @@ def barrier(dist):
         dist.barrier()
 
 
+def reduce_over_ranks(dist, ms: float, tokens: float, device="cpu"):
+    """Whole-job figures of a data-parallel run: the slowest rank's device time and the tokens of
+    all ranks (every rank takes the same two collectives, in the same order)."""
+    import torch
+
+    t_ms = torch.tensor([float(ms)], device=device)
+    t_tok = torch.tensor([float(tokens)], device=device)
+    if dist is not None:
+        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t_tok, op=dist.ReduceOp.SUM)
+    return float(t_ms.item()), float(t_tok.item())
+
+
 def prompt_for(cfg, vocab, rank):
     from layerstream_b200 import synth
 
@@ -265,9 +282,90 @@ def cpu_sample(args, cfg, target_path, draft_path, steps, warmup):
 # ------------------------------------------------------------------------------------------------
 
 
+def stored_rows(bits, group, rows, cols, seed):
+    """Random stored rows (.lsq row format) with bf16 group scales near 1e-2."""
+    rb = cols * bits // 8 + cols // group * 2
+    rng = np.random.default_rng(seed)
+    raw = rng.integers(0, 256, size=(rows, rb), dtype=np.uint8)
+    sc = raw[:, cols * bits // 8:].view(np.uint16)
+    sc[:] = (0x3C23 + rng.integers(-64, 64, size=sc.shape)).astype(np.uint16)
+    return np.ascontiguousarray(raw.reshape(-1))
+
+
+def microbench(args):
+    """Config 3: the verify-path kernels one at a time on one 0.5B layer's shapes. GEMV: every
+    launch timed alone with CUDA events after a 256 MB write that evicts L2 (so weights come from
+    HBM). Attention: KV length sweep, back-to-back launches (K/V up to 16.8 MB stay in L2)."""
+    import torch
+
+    import layerstream_b200 as ls
+
+    rank, world, local, dist = setup_dist(args)
+    torch.cuda.set_device(local)
+    peak, peak_kind = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.current_stream()
+    gemv = []
+    reps = max(args.steps, 3)
+    for bits, group in ((8, 64), (4, 32)):
+        for name, (rows, cols) in MICRO_SHAPES.items():
+            w = ls.QWeights(bits, group, stored_rows(bits, group, rows, cols, seed=rows), rows, cols, device=local)
+            for M in (1, 2, 4, 8, 16):
+                x = torch.randn(M, cols, device="cuda")
+                y = torch.empty(M, rows, device="cuda")
+                for _ in range(args.warmup):
+                    w.gemv(x.data_ptr(), M, y.data_ptr(), s.cuda_stream)
+                ts = []
+                for _ in range(reps):
+                    flush.fill_(1)
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(s)
+                    w.gemv(x.data_ptr(), M, y.data_ptr(), s.cuda_stream)
+                    e1.record(s)
+                    torch.cuda.synchronize()
+                    ts.append(e0.elapsed_time(e1))
+                us = float(np.median(ts)) * 1e3
+                b = w.bytes(M)
+                gemv.append({"fmt": f"int{bits}-g{group}", "shape": name, "rows": rows, "cols": cols, "M": M, "us": us,
+                             "bytes": b, "gbs": b / us / 1e3, "frac": b / us / 1e3 / peak})
+            del w
+    att = []
+    heads, kvh, hd, M = 14, 2, 64, 9
+    rng = np.random.default_rng(5)
+    for L in [512 << i for i in range(7)]:
+        pos0 = L - M
+        qkv = rng.standard_normal((M, (heads + 2 * kvh) * hd)).astype(np.float32)
+        kc = rng.standard_normal((kvh, pos0, hd)).astype(np.float16)
+        vc = rng.standard_normal((kvh, pos0, hd)).astype(np.float16)
+        _, ms = ls.attention(heads, kvh, hd, pos0, qkv, kc, vc, iters=max(20, reps))
+        b = L * kvh * hd * 2 * 2 + M * (heads + 2 * kvh) * hd * 4 + M * heads * hd * 4
+        att.append({"kv_len": L, "M": M, "us": ms * 1e3, "bytes": b, "gbs": b / (ms * 1e3) / 1e3})
+    head8 = [g for g in gemv if g["shape"] == "head" and g["fmt"] == "int8-g64" and g["M"] == 8][0]
+    line = {"metric": "verify-kernel microbench: LM-head GEMV HBM GB/s (int8 g64, M = 8)", "value": head8["gbs"],
+            "unit": "GB/s", "n_gpus": 1, "steps": reps, "warmup": args.warmup, "ms_per_step": head8["us"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int4 weights, f32 x, f16 KV",
+            "data": "synthetic",
+            "config": {"workload": "config3: one 0.5B layer's GEMV shapes x M in 1..16, int8 g64 and int4 g32; GQA "
+                                   "attention 14/2 heads, hd 64, M = 9, KV 512..32768",
+                       "l2": "GEMV: 256 MB write before every timed launch; attention: back-to-back, K/V in L2"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_tc_kernel (LM head, int8 g64, M = 8)", "achieved": head8["gbs"],
+                         "peak": peak, "unit": "GB/s", "frac": head8["gbs"] / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                         "traffic": None},
+            "gemv": gemv, "attention": att, "gpu_launches": len(gemv) * (reps + args.warmup)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     cfg = dict(CONFIGS[args.config])
+    if cfg.get("micro"):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 3 is a GPU kernel microbenchmark; the reference's "
+                                                                  "CPU kernels are timed through configs 1 and 2"}))
+            return
+        microbench(args)
+        return
     if args.drafter:
         cfg["drafter"] = args.drafter
     if args.ncu_case:
@@ -367,12 +465,7 @@ def main():
         step()
         prof_tl = target.profile()
     target.profile_enable(0)
-    t_ms = torch.tensor([ms], device="cuda")
-    t_tok = torch.tensor([float(tokens)], device="cuda")
-    if dist is not None:
-        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
-        dist.all_reduce(t_tok, op=dist.ReduceOp.SUM)
-    ms_max, tok_all = float(t_ms.item()), float(t_tok.item())
+    ms_max, tok_all = reduce_over_ranks(dist, ms, tokens, device="cuda")
     value = tok_all / (ms_max / 1e3)
 
     # e2e: the whole public call (prefill + decode) from host buffers
@@ -427,7 +520,8 @@ def main():
                                  "per": "layer" if c != "head" else "pass"}
         roof = {"bound": "hbm", "kernel": "pass_kernel (one persistent launch per verify pass)", "achieved": achieved,
                 "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                "traffic": profile_traffic("pass_kernel"), "algorithmic_bytes_per_launch": b, "avg_launch_us": t_ms * 1e3,
+                "traffic": profile_traffic(f"pass_kernel-config{args.config}"), "algorithmic_bytes_per_launch": b,
+                "avg_launch_us": t_ms * 1e3,
                 "launches_per_pass": 1, "phases": phases}
         gemv_c = []
     if gemv_c:

@@ -166,6 +166,16 @@ int ls_quantize_model(const char *src_dir, const char *out_path, int bits, int g
 int ls_qgemv_host(int bits, int group, const uint8_t *rows_raw, uint64_t rows, uint64_t cols, const float *x, uint64_t M,
                   float *y, int iters, double *ms);
 
+/* One layer's causal GQA attention (src/model.rs:261-282, src/kernels.rs:242-265) through the
+ * CUDA attention kernel of the verify path: the block's M rows at positions pos0..pos0+M-1
+ * (qkv: M x (heads + 2 kv_heads) * hd f32, q | k | v before RoPE, bias added) attend over the pos0
+ * cached rows (k_cache, v_cache: kv_heads x pos0 x hd, f16 bits, keys already rotated) and their
+ * own rows; row i sees pos0 + i + 1 positions. The block's K/V rows are rotated (theta =
+ * rope_theta) and rounded to f16 as the cache stores them. out: M x heads * hd f32. Host buffers;
+ * iters > 1 repeats the kernel and returns its mean time in *ms (may be NULL). */
+int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
+                      const float *qkv, const uint16_t *k_cache, const uint16_t *v_cache, float *out, int iters, double *ms);
+
 /* The same GEMV on device buffers prepared once by ls_qweights_upload (for timing loops). */
 typedef struct LsQWeights LsQWeights;
 int ls_qweights_upload(int device, int bits, int group, const uint8_t *rows_raw, uint64_t rows, uint64_t cols,

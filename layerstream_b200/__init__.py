@@ -84,6 +84,8 @@ _SIGS = {
     "ls_qweights_free": (C.c_int, [C.c_void_p]),
     "ls_qgemv_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p]),
     "ls_qgemv_bytes": (C.c_uint64, [C.c_int, C.c_int, C.c_uint64, C.c_uint64, C.c_uint64]),
+    "ls_attention_host": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p,
+                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
     "ls_qgemv_rows_noalloc": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64,
                                         C.c_void_p, C.c_void_p]),
     "ls_dequant_rows_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p]),
@@ -276,6 +278,21 @@ class QWeights:
         if getattr(self, "_h", None):
             lib().ls_qweights_free(self._h)
             self._h = None
+
+
+def attention(heads: int, kv_heads: int, hd: int, pos0: int, qkv: np.ndarray, k_cache=None, v_cache=None,
+              rope_theta: float = 1e6, iters: int = 1):
+    """One layer's causal GQA attention of an M-row block (qkv: M x (heads + 2 kv_heads) * hd f32,
+    pre-RoPE) over pos0 cached rows (kv_heads x pos0 x hd f16 arrays). Returns (out M x heads*hd, ms)."""
+    q = np.ascontiguousarray(qkv, np.float32)
+    M = q.shape[0]
+    out = np.empty((M, heads * hd), np.float32)
+    kc = np.ascontiguousarray(k_cache, np.float16).view(np.uint16) if pos0 else None
+    vc = np.ascontiguousarray(v_cache, np.float16).view(np.uint16) if pos0 else None
+    ms = C.c_double()
+    _check(lib().ls_attention_host(heads, kv_heads, hd, rope_theta, pos0, M, _p(q), _p(kc) if kc is not None else None,
+                                   _p(vc) if vc is not None else None, _p(out), iters, C.byref(ms)))
+    return out, ms.value
 
 
 def qgemv_rows_noalloc(bits: int, group: int, rows_ptr: int, rows: int, cols: int, x_ptr: int, M: int, y_ptr: int,

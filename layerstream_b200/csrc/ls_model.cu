@@ -38,6 +38,21 @@ double now_s() {
 
 size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
+// RoPE (cos, sin) table [n_pos][hd/2] with the float steps of src/model.rs:62-65 and
+// src/kernels.rs:242-252: inv_freq in f64 then f32, angle = pos as f32 * inv_freq, libm cosf/sinf.
+std::vector<float2> rope_table(float theta, size_t hd, size_t n_pos) {
+  const size_t half = hd / 2;
+  std::vector<float> inv(half);
+  for (size_t i = 0; i < half; i++) inv[i] = (float)(1.0 / std::pow((double)theta, (double)(2 * i) / (double)hd));
+  std::vector<float2> tab(n_pos * half);
+  for (size_t p = 0; p < n_pos; p++)
+    for (size_t i = 0; i < half; i++) {
+      const float ang = (float)p * inv[i];
+      tab[p * half + i] = make_float2(cosf(ang), sinf(ang));
+    }
+  return tab;
+}
+
 // Device planes of one quantized matrix carved out of a larger allocation.
 QMat carve(uint8_t*& p, int rows, int cols, const WeightFormat& f) {
   QMat m;
@@ -394,15 +409,7 @@ struct LsModel {
     kc = dalloc<uint16_t>(L * kv * max_ctx);
     vc = dalloc<uint16_t>(L * kv * max_ctx);
     const size_t half = cfg.head_dim / 2;
-    std::vector<float> inv(half);
-    for (size_t i = 0; i < half; i++)
-      inv[i] = (float)(1.0 / std::pow((double)cfg.rope_theta, (double)(2 * i) / (double)cfg.head_dim));
-    std::vector<float2> tab(max_ctx * half);
-    for (size_t p = 0; p < max_ctx; p++)
-      for (size_t i = 0; i < half; i++) {
-        float ang = (float)p * inv[i];
-        tab[p * half + i] = make_float2(cosf(ang), sinf(ang));
-      }
+    const std::vector<float2> tab = rope_table(cfg.rope_theta, cfg.head_dim, max_ctx);
     rope = dalloc<float2>(max_ctx * half);
     LS_CUDA(cudaMemcpyAsync(rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, stream));
 
@@ -1504,6 +1511,94 @@ int ls_qgemv_device(const LsQWeights* w, const float* x_dev, uint64_t M, float* 
 int ls_qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t rows, uint64_t cols, const float* x_dev,
                           uint64_t M, float* y_dev, void* stream) {
   return guard([&] { qgemv_rows_noalloc(bits, group, rows_dev, rows, cols, x_dev, M, y_dev, reinterpret_cast<cudaStream_t>(stream)); });
+}
+
+int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
+                      const float* qkv, const uint16_t* k_cache, const uint16_t* v_cache, float* out, int iters, double* ms) {
+  return guard([&] {
+    NEED(qkv);
+    NEED(out);
+    if (pos0 && (!k_cache || !v_cache)) LS_THROW(LS_ERR_ARG, "k_cache and v_cache must not be NULL when pos0 > 0");
+    if (heads == 0 || kv_heads == 0 || heads % kv_heads || heads > 256) LS_THROW(LS_ERR_ARG, "heads must be a multiple of kv_heads");
+    if (hd != 16 && hd != 32 && hd != 64 && hd != 128) LS_THROW(LS_ERR_ARG, "head_dim must be 16, 32, 64 or 128");
+    if (M == 0 || M > 64) LS_THROW(LS_ERR_ARG, "the attention block takes 1..64 rows");
+    if (pos0 + M > (1u << 20)) LS_THROW(LS_ERR_ARG, "context beyond 2^20 positions");
+    const size_t ctx = pos0 + M, KV = kv_heads * hd, H = heads * hd, QS = H + 2 * KV;
+    int dev = 0;
+    LS_CUDA(cudaGetDevice(&dev));
+    cudaStream_t st;
+    LS_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    std::vector<void*> owned;
+    auto dmalloc = [&](size_t bytes) {
+      void* p = nullptr;
+      LS_CUDA(cudaMalloc(&p, std::max<size_t>(bytes, 16)));
+      owned.push_back(p);
+      return p;
+    };
+    struct Cleanup {
+      std::vector<void*>& o;
+      cudaStream_t s;
+      ~Cleanup() {
+        cudaStreamSynchronize(s);
+        for (void* p : o) cudaFree(p);
+        cudaStreamDestroy(s);
+      }
+    } cleanup{owned, st};
+    auto* dq = static_cast<float*>(dmalloc(M * QS * 4));
+    auto* dk = static_cast<uint16_t*>(dmalloc(kv_heads * ctx * hd * 2));
+    auto* dv = static_cast<uint16_t*>(dmalloc(kv_heads * ctx * hd * 2));
+    auto* dout = static_cast<float*>(dmalloc(M * H * 4));
+    auto* drope = static_cast<float2*>(dmalloc(ctx * (hd / 2) * sizeof(float2)));
+    const int slots = (int)std::max<size_t>(1, std::min<size_t>(16, (ctx + 63) / 64));
+    auto* dpart = static_cast<float*>(dmalloc(heads * (size_t)slots * M * (hd + 2) * 4));
+    auto* dtick = static_cast<unsigned*>(dmalloc(heads * 4));
+    auto* dctl = static_cast<Ctl*>(dmalloc(sizeof(Ctl)));
+    LS_CUDA(cudaMemsetAsync(dtick, 0, heads * 4, st));
+    LS_CUDA(cudaMemcpyAsync(dq, qkv, M * QS * 4, cudaMemcpyHostToDevice, st));
+    if (pos0) {
+      LS_CUDA(cudaMemcpy2DAsync(dk, ctx * hd * 2, k_cache, pos0 * hd * 2, pos0 * hd * 2, kv_heads, cudaMemcpyHostToDevice, st));
+      LS_CUDA(cudaMemcpy2DAsync(dv, ctx * hd * 2, v_cache, pos0 * hd * 2, pos0 * hd * 2, kv_heads, cudaMemcpyHostToDevice, st));
+    }
+    const std::vector<float2> tab = rope_table(rope_theta, hd, ctx);
+    LS_CUDA(cudaMemcpyAsync(drope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, st));
+    launch_set_ctl(dctl, (int)pos0, (int)M, 0, 0, nullptr, st);
+    AttnLaunch a;
+    a.qkv = dq;
+    a.qkv_stride = (int)QS;
+    a.k_cache = dk;
+    a.v_cache = dv;
+    a.rope = drope;
+    a.ctl = dctl;
+    a.out = dout;
+    a.part = dpart;
+    a.tickets = dtick;
+    a.heads = (int)heads;
+    a.kv_heads = (int)kv_heads;
+    a.hd = (int)hd;
+    a.max_ctx = (int)ctx;
+    a.M = (int)M;
+    a.max_splits = slots;
+    launch_attention(a, st);
+    if (iters > 1) {
+      cudaEvent_t e0, e1;
+      LS_CUDA(cudaEventCreate(&e0));
+      LS_CUDA(cudaEventCreate(&e1));
+      LS_CUDA(cudaEventRecord(e0, st));
+      for (int i = 0; i < iters; i++) launch_attention(a, st);
+      LS_CUDA(cudaEventRecord(e1, st));
+      LS_CUDA(cudaEventSynchronize(e1));
+      float t = 0;
+      LS_CUDA(cudaEventElapsedTime(&t, e0, e1));
+      if (ms) *ms = t / iters;
+      cudaEventDestroy(e0);
+      cudaEventDestroy(e1);
+    } else if (ms) {
+      *ms = 0;
+    }
+    LS_CUDA(cudaMemcpyAsync(out, dout, M * H * 4, cudaMemcpyDeviceToHost, st));
+    LS_CUDA(cudaStreamSynchronize(st));
+    (void)dev;
+  });
 }
 
 int ls_qgemv_host(int bits, int group, const uint8_t* rows_raw, uint64_t rows, uint64_t cols, const float* x, uint64_t M, float* y,
