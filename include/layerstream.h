@@ -156,6 +156,28 @@ int ls_spec_continue(LsModel *target, LsModel *draft, const uint32_t *hist, uint
 int ls_quantize_model(const char *src_dir, const char *out_path, int bits, int group, int embed_bits, int embed_group,
                       int clip_search, int device, double *rel_rmse);
 
+/* ---- batches of independent sequences (configs 4 and 5) -------------------------------------- */
+
+/* B sequences sharing one resident model's weights, each with its own K/V cache of max_ctx
+ * positions; a verify pass takes one block of M <= max_block tokens per sequence ([B][M] blocks)
+ * and runs all B*M rows through the model at once. */
+typedef struct LsBatch LsBatch;
+int ls_batch_open(LsModel *m, uint64_t batch, uint64_t max_ctx, uint64_t max_block, LsBatch **out);
+int ls_batch_free(LsBatch *b);
+int ls_batch_pos(const LsBatch *b, uint64_t seq, uint64_t *pos);
+int ls_batch_truncate(LsBatch *b, uint64_t seq, uint64_t pos);
+/* src/model.rs:111-119 for sequence `seq`: pushes n tokens, returns the greedy token after them. */
+int ls_batch_prefill(LsBatch *b, uint64_t seq, const uint32_t *ids, uint64_t n, uint32_t *argmax);
+/* ls_verify for sequences 0..nseq-1 in one pass: blocks [nseq][M]; per sequence the accepted
+ * count m (src/spec.rs:121-125) and the next token; each sequence's position advances by m + 1. */
+int ls_batch_verify(LsBatch *b, const uint32_t *blocks, uint64_t nseq, uint64_t M, uint32_t *accepted_m, uint32_t *next);
+/* spec::speculative_greedy (src/spec.rs:57-152) for all B sequences with the prompt-lookup drafter:
+ * prompts [B][plen] (caches must be empty or are reset), out_tokens [B][max_new], out_len [B];
+ * every sequence's tokens equal its own greedy decode. stats sums over sequences. */
+int ls_batch_spec(LsBatch *b, const uint32_t *prompts, uint64_t plen, uint64_t max_new, uint64_t k, const uint32_t *eos,
+                  uint64_t neos, uint32_t *out_tokens, uint64_t *out_len, LsSpecStats *stats);
+int ls_batch_report(const LsBatch *b, uint64_t *passes, uint64_t *h2d_bytes, uint64_t *d2h_bytes);
+
 /* ---- kernel-level entry points (microbenchmarks and parity tests) ---------------------------- */
 
 /* y[t][r] = dot(stored row r, x[t]) for t < M, with W given as `rows` stored rows in the .lsq

@@ -84,6 +84,15 @@ _SIGS = {
     "ls_qweights_free": (C.c_int, [C.c_void_p]),
     "ls_qgemv_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p]),
     "ls_qgemv_bytes": (C.c_uint64, [C.c_int, C.c_int, C.c_uint64, C.c_uint64, C.c_uint64]),
+    "ls_batch_open": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64, C.POINTER(C.c_void_p)]),
+    "ls_batch_free": (C.c_int, [C.c_void_p]),
+    "ls_batch_pos": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "ls_batch_truncate": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64]),
+    "ls_batch_prefill": (C.c_int, [C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64, C.POINTER(C.c_uint32)]),
+    "ls_batch_verify": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p]),
+    "ls_batch_spec": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64,
+                                C.c_void_p, C.c_void_p, C.POINTER(SpecStats)]),
+    "ls_batch_report": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "ls_attention_host": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
     "ls_qgemv_rows_noalloc": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64,
@@ -229,6 +238,61 @@ def spec_continue(target: Model, draft: Model | None, hist, first: int, max_new:
     _check(lib().ls_spec_continue(target._h, draft._h if draft is not None else None, _p(h), h.size, first, max_new, k,
                                   _p(e), len(eos), _p(out), C.byref(n), C.byref(st)))
     return out[: n.value].tolist(), st.as_dict()
+
+
+class Batch:
+    """B independent sequences sharing one resident model's weights (configs 4 and 5): per-sequence
+    K/V caches, one verify pass for all sequences' [B][M] blocks."""
+
+    def __init__(self, model: Model, batch: int, max_ctx: int, max_block: int):
+        h = C.c_void_p()
+        _check(lib().ls_batch_open(model._h, batch, max_ctx, max_block, C.byref(h)))
+        self._h, self.model, self.batch, self.max_ctx, self.max_block = h, model, batch, max_ctx, max_block
+
+    def pos(self, seq: int) -> int:
+        v = C.c_uint64()
+        _check(lib().ls_batch_pos(self._h, seq, C.byref(v)))
+        return v.value
+
+    def truncate(self, seq: int, pos: int):
+        _check(lib().ls_batch_truncate(self._h, seq, pos))
+
+    def prefill(self, seq: int, ids) -> int:
+        a = _u32(ids)
+        out = C.c_uint32()
+        _check(lib().ls_batch_prefill(self._h, seq, _p(a), a.size, C.byref(out)))
+        return out.value
+
+    def verify(self, blocks) -> tuple[list[int], list[int]]:
+        b = np.ascontiguousarray(blocks, np.uint32)
+        nseq, M = b.shape
+        m = np.zeros(nseq, np.uint32)
+        nxt = np.zeros(nseq, np.uint32)
+        _check(lib().ls_batch_verify(self._h, _p(b), nseq, M, _p(m), _p(nxt)))
+        return m.tolist(), nxt.tolist()
+
+    def spec(self, prompts, max_new: int, k: int, eos=()):
+        p = np.ascontiguousarray(prompts, np.uint32)
+        B, plen = p.shape
+        e = _u32(list(eos) if len(eos) else [0])
+        out = np.zeros((B, max(max_new, 1)), np.uint32)
+        n = np.zeros(B, np.uint64)
+        st = SpecStats()
+        _check(lib().ls_batch_spec(self._h, _p(p), plen, max_new, k, _p(e), len(eos), _p(out), _p(n), C.byref(st)))
+        return [out[i, : int(n[i])].tolist() for i in range(B)], st.as_dict()
+
+    def report(self) -> dict:
+        a, b, c = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        _check(lib().ls_batch_report(self._h, C.byref(a), C.byref(b), C.byref(c)))
+        return {"passes": a.value, "h2d_bytes": b.value, "d2h_bytes": c.value}
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().ls_batch_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
 
 
 def quantize_model(src_dir: str, out_path: str, body=(8, 64), embed=None, clip: bool = True, device: int = 0) -> float:

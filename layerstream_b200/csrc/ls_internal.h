@@ -207,6 +207,13 @@ struct AttnLaunch {
   float* part = nullptr; // split partials
   unsigned* tickets = nullptr;
   int heads = 0, kv_heads = 0, hd = 0, max_ctx = 0, M = 0, split = 64, max_splits = 0;
+  // batches: grid.z = nseq sequences of M rows each (rows s*M .. s*M+M-1 of qkv and out); sequence
+  // s has its cache at k_cache/v_cache + s * seq_stride, its position pos0[s], its partials and
+  // tickets after those of sequences < s. pos0 == nullptr: one sequence at ctl->pos0.
+  int nseq = 1;
+  const int* pos0 = nullptr;
+  size_t seq_stride = 0;
+  bool pdl = true;  // false: plain launch (positions written by the previous kernel are read early)
 };
 void launch_attention(const AttnLaunch& a, cudaStream_t s);
 
@@ -245,6 +252,16 @@ struct PassArgs {
   int ks_qkv, ks_o, ks_gu, ks_down;
   float eps;
 };
+
+// ---- batched verify (ls_batch.cu): B sequences x M rows per pass ----
+// Embedding rows of T tokens (err = 2 on an id >= vocab), bit-exact with embed_kernel.
+void launch_embed_tokens(const QMat& e, const uint32_t* tokens, int T, float* x, int hidden, int vocab, int* err,
+                         cudaStream_t s);
+// argmax[t] over the nparts per-CTA parts of every row t (first-maximum rule); then for every
+// sequence of M rows the acceptance rule of src/spec.rs:121-125: m = longest prefix with
+// argmax[i] == tokens[i+1], next = argmax[m].
+void launch_batch_accept(const ArgPart* parts, int nparts, int T, int M, const uint32_t* tokens, uint32_t* argmax,
+                         uint32_t* m_out, uint32_t* next_out, cudaStream_t s);
 
 // ---- allocation-free GEMV (ls_noalloc.cu) ----
 void qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t rows, uint64_t cols, const float* x_dev,

@@ -406,7 +406,8 @@ __device__ __forceinline__ float f16_round(float v) { return __half2float(__floa
 
 // Cached K/V rows [p0, p0+64) below pos0 of kv head g into the f32 tiles (16-byte loads).
 template <int HD>
-__device__ __forceinline__ void att_load_cached(const AttnLaunch& a, int g, int p0, int pos0, float* Ks, float* Vs) {
+__device__ __forceinline__ void att_load_cached(const AttnLaunch& a, const uint16_t* kcache, const uint16_t* vcache, int g,
+                                                int p0, int pos0, float* Ks, float* Vs) {
   constexpr int HP = HD + 1, V8 = HD / 8;
   for (int i = threadIdx.x; i < ATT_TILE * V8; i += ATT_THREADS) {
     const int pl = i / V8, d8 = (i - pl * V8) * 8;
@@ -420,8 +421,8 @@ __device__ __forceinline__ void att_load_cached(const AttnLaunch& a, int g, int 
       continue;
     }
     const size_t base = ((size_t)g * a.max_ctx + p) * HD + d8;
-    const uint4 kr = __ldg(reinterpret_cast<const uint4*>(a.k_cache + base));
-    const uint4 vr = __ldg(reinterpret_cast<const uint4*>(a.v_cache + base));
+    const uint4 kr = __ldg(reinterpret_cast<const uint4*>(kcache + base));
+    const uint4 vr = __ldg(reinterpret_cast<const uint4*>(vcache + base));
     const __half* kh = reinterpret_cast<const __half*>(&kr);
     const __half* vh = reinterpret_cast<const __half*>(&vr);
 #pragma unroll
@@ -437,14 +438,19 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
   extern __shared__ __align__(16) float sm[];
   constexpr int HP = HD + 1;  // padded row: conflict-free column access
   constexpr int HALF = HD / 2;
-  const int hh = blockIdx.x, slot = blockIdx.y, nslot = gridDim.y;
+  const int hh = blockIdx.x, slot = blockIdx.y, nslot = gridDim.y, sq = blockIdx.z;
   const int group = a.heads / a.kv_heads;
   const int g = hh / group;
   const int M = a.M;
-  const int pos0 = a.ctl->pos0;  // written by the host before the pass: safe before the wait
+  // written by the host before the pass (or, for batches launched without PDL, by an earlier kernel)
+  const int pos0 = a.pos0 ? a.pos0[sq] : a.ctl->pos0;
   const int total = pos0 + M;
   const int ntiles = (total + ATT_TILE - 1) / ATT_TILE;
   const int H = a.heads * HD, KV = a.kv_heads * HD;
+  const float* qkv = a.qkv + (size_t)sq * M * a.qkv_stride;
+  float* out = a.out + (size_t)sq * M * H;
+  uint16_t* kcache = a.k_cache + (size_t)sq * a.seq_stride;
+  uint16_t* vcache = a.v_cache + (size_t)sq * a.seq_stride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* qs = sm;                       // [M][HD]
   float* Ks = qs + M * HD;              // [64][HP]
@@ -454,14 +460,14 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
 
   pdl_trigger();
   // the cached part of the first tile does not depend on the previous kernel
-  if (slot < ntiles) att_load_cached<HD>(a, g, slot * ATT_TILE, pos0, Ks, Vs);
+  if (slot < ntiles) att_load_cached<HD>(a, kcache, vcache, g, slot * ATT_TILE, pos0, Ks, Vs);
   for (int i = threadIdx.x; i < M * (HD + 2); i += ATT_THREADS) st[i] = (i % (HD + 2) == 0) ? -CUDART_INF_F : 0.f;
   pdl_wait();
 
   for (int i = threadIdx.x; i < M * HALF; i += ATT_THREADS) {
     const int t = i / HALF, d = i - t * HALF;
     const float2 cs = a.rope[(size_t)(pos0 + t) * HALF + d];
-    const float* q = a.qkv + (size_t)t * a.qkv_stride + hh * HD;
+    const float* q = qkv + (size_t)t * a.qkv_stride + hh * HD;
     const float x1 = q[d], x2 = q[d + HALF];
     qs[t * HD + d] = x1 * cs.x - x2 * cs.y;
     qs[t * HD + d + HALF] = x2 * cs.x + x1 * cs.y;
@@ -473,7 +479,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
     const int p0 = tile * ATT_TILE;
     if (!first) {
       __syncthreads();
-      att_load_cached<HD>(a, g, p0, pos0, Ks, Vs);
+      att_load_cached<HD>(a, kcache, vcache, g, p0, pos0, Ks, Vs);
     }
     first = false;
     __syncthreads();
@@ -482,8 +488,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
     for (int i = threadIdx.x; i < nb * HALF; i += ATT_THREADS) {
       const int j = i / HALF, d = i - j * HALF;
       const int p = max(p0, pos0) + j, pl = p - p0, t = p - pos0;
-      const float* kr = a.qkv + (size_t)t * a.qkv_stride + H + g * HD;
-      const float* vr = a.qkv + (size_t)t * a.qkv_stride + H + KV + g * HD;
+      const float* kr = qkv + (size_t)t * a.qkv_stride + H + g * HD;
+      const float* vr = qkv + (size_t)t * a.qkv_stride + H + KV + g * HD;
       const float2 cs = a.rope[(size_t)p * HALF + d];
       const float x1 = kr[d], x2 = kr[d + HALF];
       const float k1 = f16_round(x1 * cs.x - x2 * cs.y), k2 = f16_round(x2 * cs.x + x1 * cs.y);
@@ -494,10 +500,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
       Vs[pl * HP + d + HALF] = v2;
       if (writer) {
         const size_t base = ((size_t)g * a.max_ctx + p) * HD;
-        a.k_cache[base + d] = __half_as_ushort(__float2half_rn(k1));
-        a.k_cache[base + d + HALF] = __half_as_ushort(__float2half_rn(k2));
-        a.v_cache[base + d] = __half_as_ushort(__float2half_rn(v1));
-        a.v_cache[base + d + HALF] = __half_as_ushort(__float2half_rn(v2));
+        kcache[base + d] = __half_as_ushort(__float2half_rn(k1));
+        kcache[base + d + HALF] = __half_as_ushort(__float2half_rn(k2));
+        vcache[base + d] = __half_as_ushort(__float2half_rn(v1));
+        vcache[base + d + HALF] = __half_as_ushort(__float2half_rn(v2));
       }
     }
     __syncthreads();
@@ -564,15 +570,15 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
     for (int i = threadIdx.x; i < M * HD; i += ATT_THREADS) {
       const int t = i / HD, d = i - t * HD;
       const float* S = st + t * (HD + 2);
-      a.out[(size_t)t * H + hh * HD + d] = S[2 + d] / S[1];
+      out[(size_t)t * H + hh * HD + d] = S[2 + d] / S[1];
     }
     return;
   }
   // partial (m, l, acc) of this CTA for every token, then the combine in the last CTA of the head
-  float* part = a.part + ((size_t)hh * nslot + slot) * M * (HD + 2);
+  float* part = a.part + (((size_t)sq * a.heads + hh) * nslot + slot) * M * (HD + 2);
   for (int i = threadIdx.x; i < M * (HD + 2); i += ATT_THREADS) part[i] = st[i];
-  if (!last_cta(a.tickets + hh, (unsigned)nslot)) return;
-  const float* all = a.part + (size_t)hh * nslot * M * (HD + 2);
+  if (!last_cta(a.tickets + (size_t)sq * a.heads + hh, (unsigned)nslot)) return;
+  const float* all = a.part + ((size_t)sq * a.heads + hh) * nslot * M * (HD + 2);
   for (int i = threadIdx.x; i < M * HD; i += ATT_THREADS) {
     const int t = i / HD, d = i - t * HD;
     float ms[ATT_MAX_SLOTS], ls[ATT_MAX_SLOTS], as[ATT_MAX_SLOTS];
@@ -598,14 +604,20 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
         acc += as[s] * w;
       }
     }
-    a.out[(size_t)t * H + hh * HD + d] = acc / L;
+    out[(size_t)t * H + hh * HD + d] = acc / L;
   }
 }
 
 template <int HD>
 static void launch_attention_t(const AttnLaunch& a, size_t smem, cudaStream_t s) {
   ensure_smem(attention_kernel<HD>, smem);
-  launch_pdl(attention_kernel<HD>, dim3(a.heads, a.max_splits), dim3(ATT_THREADS), smem, s, a);
+  const dim3 grid(a.heads, a.max_splits, a.nseq);
+  if (a.pdl) {
+    launch_pdl(attention_kernel<HD>, grid, dim3(ATT_THREADS), smem, s, a);
+  } else {
+    attention_kernel<HD><<<grid, ATT_THREADS, smem, s>>>(a);
+    LS_CUDA(cudaGetLastError());
+  }
 }
 
 void launch_attention(const AttnLaunch& a, cudaStream_t s) {
@@ -624,15 +636,8 @@ void launch_attention(const AttnLaunch& a, cudaStream_t s) {
 // Embedding gather + dequantisation (bit-exact with src/kernels.rs:95-121)
 // ------------------------------------------------------------------------------------------------
 
-__global__ void embed_kernel(const QMat e, const Ctl* ctl, float* x, int hidden, int vocab) {
-  const int t = blockIdx.x;
-  const uint32_t tok = ctl->tokens[t];
-  float* xr = x + (size_t)t * hidden;
-  if (tok >= (uint32_t)vocab) {
-    for (int c = threadIdx.x; c < hidden; c += blockDim.x) xr[c] = 0.f;
-    if (threadIdx.x == 0) const_cast<Ctl*>(ctl)->err = 2;
-    return;
-  }
+// Dequantised embedding row of token tok into xr (the CTA's threads share the columns).
+__device__ __forceinline__ void embed_row(const QMat& e, uint32_t tok, float* xr, int hidden) {
   const int nch = e.chunks();
   const uint8_t* row = e.data + ((size_t)(tok / 32) * nch) * 512 + (tok % 32) * 16;
   const uint16_t* sc = e.scales + (size_t)(tok / 32) * e.groups() * 32 + (tok % 32);
@@ -651,6 +656,77 @@ __global__ void embed_kernel(const QMat e, const Ctl* ctl, float* x, int hidden,
     }
     xr[c] = q * bf16f(sc[(size_t)g * 32]);
   }
+}
+
+__global__ void embed_kernel(const QMat e, const Ctl* ctl, float* x, int hidden, int vocab) {
+  const int t = blockIdx.x;
+  const uint32_t tok = ctl->tokens[t];
+  float* xr = x + (size_t)t * hidden;
+  if (tok >= (uint32_t)vocab) {
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x) xr[c] = 0.f;
+    if (threadIdx.x == 0) const_cast<Ctl*>(ctl)->err = 2;
+    return;
+  }
+  embed_row(e, tok, xr, hidden);
+}
+
+__global__ void embed_tokens_kernel(const QMat e, const uint32_t* tokens, float* x, int hidden, int vocab, int* err) {
+  const int t = blockIdx.x;
+  const uint32_t tok = tokens[t];
+  float* xr = x + (size_t)t * hidden;
+  if (tok >= (uint32_t)vocab) {
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x) xr[c] = 0.f;
+    if (threadIdx.x == 0) atomicExch(err, 2);
+    return;
+  }
+  embed_row(e, tok, xr, hidden);
+}
+
+void launch_embed_tokens(const QMat& e, const uint32_t* tokens, int T, float* x, int hidden, int vocab, int* err,
+                         cudaStream_t s) {
+  embed_tokens_kernel<<<T, 256, 0, s>>>(e, tokens, x, hidden, vocab, err);
+  LS_CUDA(cudaGetLastError());
+}
+
+// One warp per row: the first maximum over the per-CTA parts (value, then lower index).
+__global__ void batch_argmax_kernel(const ArgPart* parts, int nparts, int T, uint32_t* argmax) {
+  const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= T) return;
+  float v = -CUDART_INF_F;
+  uint32_t idx = 0xffffffffu;
+  for (int k = lane; k < nparts; k += 32) {
+    const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(parts + (size_t)k * T + t));
+    const float pv = __uint_as_float(raw.x);
+    if (arg_better(pv, raw.y, v, idx)) {
+      v = pv;
+      idx = raw.y;
+    }
+  }
+  warp_argmax(v, idx);
+  if (lane == 0) argmax[t] = idx;
+}
+
+// src/spec.rs:121-125 per sequence: m = longest prefix of guesses the target agrees with, next =
+// the target's token after it (correction or bonus).
+__global__ void batch_accept_kernel(const uint32_t* argmax, const uint32_t* tokens, int nseq, int M, uint32_t* m_out,
+                                    uint32_t* next_out) {
+  const int sq = blockIdx.x * blockDim.x + threadIdx.x;
+  if (sq >= nseq) return;
+  const uint32_t* am = argmax + (size_t)sq * M;
+  const uint32_t* tk = tokens + (size_t)sq * M;
+  int m = 0;
+  while (m < M - 1 && am[m] == tk[m + 1]) m++;
+  m_out[sq] = (uint32_t)m;
+  next_out[sq] = am[m];
+}
+
+void launch_batch_accept(const ArgPart* parts, int nparts, int T, int M, const uint32_t* tokens, uint32_t* argmax,
+                         uint32_t* m_out, uint32_t* next_out, cudaStream_t s) {
+  batch_argmax_kernel<<<(T + 7) / 8, 256, 0, s>>>(parts, nparts, T, argmax);
+  LS_CUDA(cudaGetLastError());
+  const int nseq = T / M;
+  batch_accept_kernel<<<(nseq + 127) / 128, 128, 0, s>>>(argmax, tokens, nseq, M, m_out, next_out);
+  LS_CUDA(cudaGetLastError());
 }
 
 void launch_embed(const QMat& e, const Ctl* ctl, float* x, int hidden, int M, cudaStream_t s) {

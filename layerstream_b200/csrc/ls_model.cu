@@ -1103,6 +1103,312 @@ static void speculative_greedy(LsModel& target, LsModel* draft, const uint32_t* 
 }
 
 // ------------------------------------------------------------------------------------------------
+// Batched verify (configs 4 and 5): B independent sequences sharing one resident model's weights.
+// A pass runs ns sequences x M rows as one set of GEMV launches (token groups of 64 on the grid's
+// z axis, so each weight tile is read once per pass), one attention launch over all sequences and
+// a per-sequence acceptance on the device. src/spec.rs:94-149 per sequence; the sequences share
+// nothing but the weights, so every sequence's tokens equal its own single-sequence decode.
+// ------------------------------------------------------------------------------------------------
+
+struct LsBatch {
+  LsModel* m = nullptr;
+  size_t B = 0, max_ctx = 0, max_rows = 0, max_block = 0;
+  size_t layer_stride = 0, seq_stride = 0;  // elements: one layer's cache, one sequence's cache
+  cudaStream_t stream = nullptr;
+  std::vector<void*> dev_allocs, host_allocs;
+  uint16_t *kc = nullptr, *vc = nullptr;
+  float2* rope = nullptr;
+  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *hbuf = nullptr, *partial = nullptr, *att_part = nullptr;
+  unsigned *tickets = nullptr, *att_tickets = nullptr;
+  ArgPart* parts = nullptr;
+  uint32_t *d_tok = nullptr, *d_argmax = nullptr, *d_m = nullptr, *d_next = nullptr;
+  int *d_pos0 = nullptr, *d_err = nullptr;
+  uint32_t *h_tok = nullptr, *h_m = nullptr, *h_next = nullptr;
+  int *h_pos0 = nullptr, *h_err = nullptr;
+  std::vector<uint64_t> pos;
+  uint64_t passes = 0, h2d_bytes = 0, d2h_bytes = 0;
+
+  template <class T>
+  T* dalloc(size_t n) {
+    void* p = nullptr;
+    LS_CUDA(cudaMalloc(&p, std::max<size_t>(n * sizeof(T), 16)));
+    dev_allocs.push_back(p);
+    LS_CUDA(cudaMemsetAsync(p, 0, std::max<size_t>(n * sizeof(T), 16), stream));
+    return reinterpret_cast<T*>(p);
+  }
+  template <class T>
+  T* halloc(size_t n) {
+    void* p = nullptr;
+    LS_CUDA(cudaHostAlloc(&p, std::max<size_t>(n * sizeof(T), 16), cudaHostAllocDefault));
+    host_allocs.push_back(p);
+    return reinterpret_cast<T*>(p);
+  }
+
+  // Split-K scratch of the tensor-core GEMV for one launch of M token rows.
+  void tc_scratch(const QMat& w, int M, size_t* floats, size_t* tks) const {
+    int ks = 1, gx = 1;
+    choose_tc(w, M, m->num_sms, false, &ks, &gx);
+    const int NT = M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64;
+    const size_t nz = (M + NT - 1) / NT, tiles32 = w.rows_pad / 32;
+    *floats = std::max(*floats, nz * tiles32 * ks * NT * 32);
+    *tks = std::max(*tks, nz * tiles32);
+  }
+
+  LsBatch(LsModel* model, size_t batch, size_t ctx, size_t block) : m(model), B(batch), max_ctx(ctx), max_block(block) {
+    if (m->mode != LS_MODE_RESIDENT) LS_THROW(LS_ERR_ARG, "batches need a resident model");
+    if (B == 0 || B > 4096) LS_THROW(LS_ERR_ARG, "batch must be in 1..4096");
+    if (max_block == 0 || max_block > (size_t)kMaxDraft + 1) LS_THROW(LS_ERR_ARG, "the verify block holds 1..33 tokens");
+    if (max_ctx < 2 || max_ctx > (1u << 20)) LS_THROW(LS_ERR_ARG, "max_ctx must be in 2..2^20");
+    const Config& c = m->cfg;
+    const size_t L = c.layers, kv = c.kv_dim(), h = c.hidden, I = c.inter, QS = h + 2 * kv;
+    max_rows = std::max<size_t>(kMaxT, B * max_block);
+    if (max_rows > 8192) LS_THROW(LS_ERR_ARG, "batch x block exceeds 8192 rows per pass");
+    LS_CUDA(cudaSetDevice(m->device));
+    LS_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    layer_stride = kv * max_ctx;
+    seq_stride = L * layer_stride;
+    kc = dalloc<uint16_t>(B * seq_stride);
+    vc = dalloc<uint16_t>(B * seq_stride);
+    const std::vector<float2> tab = rope_table(c.rope_theta, c.head_dim, max_ctx);
+    rope = dalloc<float2>(tab.size());
+    LS_CUDA(cudaMemcpyAsync(rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, stream));
+    x = dalloc<float>(max_rows * h);
+    qkv = dalloc<float>(max_rows * QS);
+    attn = dalloc<float>(max_rows * h);
+    hbuf = dalloc<float>(max_rows * I);
+    size_t pf = 0, tk = 0;
+    const LayerW& W = m->layers[0];
+    for (int rows = 1; rows <= (int)max_rows; rows++)
+      for (const QMat* w : {&W.qkv, &W.o, &W.gu, &W.down}) tc_scratch(*w, rows, &pf, &tk);
+    partial = dalloc<float>(pf);
+    tickets = dalloc<unsigned>(tk);
+    parts = dalloc<ArgPart>((size_t)(m->embed.rows_pad / 128 + 1) * max_rows);
+    att_part = dalloc<float>(c.heads * (size_t)16 * max_rows * (c.head_dim + 2));
+    att_tickets = dalloc<unsigned>(B * c.heads);
+    d_tok = dalloc<uint32_t>(max_rows);
+    d_argmax = dalloc<uint32_t>(max_rows);
+    d_m = dalloc<uint32_t>(B);
+    d_next = dalloc<uint32_t>(B);
+    d_pos0 = dalloc<int>(B);
+    d_err = dalloc<int>(1);
+    h_tok = halloc<uint32_t>(max_rows);
+    h_m = halloc<uint32_t>(B);
+    h_next = halloc<uint32_t>(B);
+    h_pos0 = halloc<int>(B);
+    h_err = halloc<int>(1);
+    pos.assign(B, 0);
+    LS_CUDA(cudaStreamSynchronize(stream));
+  }
+  ~LsBatch() {
+    cudaSetDevice(m->device);
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : dev_allocs) cudaFree(p);
+    for (void* p : host_allocs) cudaFreeHost(p);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  void gemv(const QMat& w, const float* xin, int x_stride, int M, int epi, float* y, int y_stride, const uint16_t* norm_bf16,
+            const uint16_t* bias) {
+    GemvLaunch g;
+    g.w = w;
+    g.x = xin;
+    g.x_stride = x_stride;
+    g.M = M;
+    g.norm_bf16 = norm_bf16;
+    g.eps = m->cfg.eps;
+    g.epi = epi;
+    g.y = y;
+    g.y_stride = y_stride;
+    g.bias = bias;
+    g.partial = partial;
+    g.tickets = tickets;
+    g.err = d_err;
+    if (use_tc(w)) {
+      choose_tc(w, M, m->num_sms, false, &g.ksplit, &g.grid_x);
+      launch_gemv_tc(g, stream);
+      return;
+    }
+    LS_THROW(LS_ERR_ARG, "batches need a weight format the tensor-core GEMV supports");
+  }
+
+  // Argmax parts of the LM head over M rows of x (final RMSNorm folded in); returns the CTA count.
+  int head(const float* xin, int M) {
+    GemvLaunch g;
+    g.w = m->embed;
+    g.x = xin;
+    g.x_stride = (int)m->cfg.hidden;
+    g.M = M;
+    g.norm_f32 = m->final_norm;
+    g.eps = m->cfg.eps;
+    g.epi = EPI_ARGMAX;
+    g.arg_parts = parts;
+    g.n_valid_rows = (int)m->cfg.vocab;
+    g.finalize = 0;
+    g.err = d_err;
+    if (!use_tc(m->embed)) LS_THROW(LS_ERR_ARG, "batches need a weight format the tensor-core GEMV supports");
+    choose_tc(m->embed, M, m->num_sms, true, &g.ksplit, &g.grid_x);
+    launch_gemv_tc(g, stream);
+    return g.grid_x;
+  }
+
+  // One pass over sequences [s0, s0 + ns), M rows each. head_mode 0: advance only; 1: argmax of
+  // every row and the acceptance rule per sequence (pos += m + 1); 2: argmax of the last row
+  // (prefill of one sequence), pos += M.
+  void pass(size_t s0, size_t ns, int M, const uint32_t* tokens, int head_mode) {
+    const Config& c = m->cfg;
+    const int h = (int)c.hidden, kv = (int)c.kv_dim(), I = (int)c.inter, QS = h + 2 * kv;
+    const size_t T = ns * (size_t)M;
+    if (T == 0 || T > max_rows) LS_THROW(LS_ERR_ARG, "pass of " + std::to_string(T) + " rows exceeds the batch's " + std::to_string(max_rows));
+    if (s0 + ns > B) LS_THROW(LS_ERR_ARG, "sequence index out of range");
+    size_t maxpos = 0;
+    for (size_t i = 0; i < ns; i++) {
+      if (pos[s0 + i] + M > max_ctx)
+        LS_THROW(LS_ERR_ARG, "sequence " + std::to_string(s0 + i) + ": context is full (" + std::to_string(pos[s0 + i]) + " + " +
+                                 std::to_string(M) + " > " + std::to_string(max_ctx) + ")");
+      maxpos = std::max<size_t>(maxpos, pos[s0 + i]);
+      h_pos0[i] = (int)pos[s0 + i];
+    }
+    for (size_t i = 0; i < T; i++)
+      if (tokens[i] >= c.vocab) LS_THROW(LS_ERR_ARG, "token id " + std::to_string(tokens[i]) + " is outside the vocabulary");
+    std::memcpy(h_tok, tokens, T * 4);
+    LS_CUDA(cudaMemcpyAsync(d_tok, h_tok, T * 4, cudaMemcpyHostToDevice, stream));
+    LS_CUDA(cudaMemcpyAsync(d_pos0, h_pos0, ns * 4, cudaMemcpyHostToDevice, stream));
+    LS_CUDA(cudaMemsetAsync(d_err, 0, 4, stream));
+    h2d_bytes += T * 4 + ns * 4;
+    launch_embed_tokens(m->embed, d_tok, (int)T, x, h, (int)c.vocab, d_err, stream);
+    const int slots = (int)std::max<size_t>(1, std::min<size_t>(16, (maxpos + M + 63) / 64));
+    for (size_t l = 0; l < c.layers; l++) {
+      const LayerW& W = m->layers[l];
+      gemv(W.qkv, x, h, (int)T, EPI_BIAS_STORE, qkv, QS, W.in_norm, W.qkv_bias);
+      AttnLaunch a;
+      a.qkv = qkv;
+      a.qkv_stride = QS;
+      a.k_cache = kc + s0 * seq_stride + l * layer_stride;
+      a.v_cache = vc + s0 * seq_stride + l * layer_stride;
+      a.rope = rope;
+      a.out = attn;
+      a.part = att_part;
+      a.tickets = att_tickets;
+      a.heads = (int)c.heads;
+      a.kv_heads = (int)c.kv_heads;
+      a.hd = (int)c.head_dim;
+      a.max_ctx = (int)max_ctx;
+      a.M = M;
+      a.max_splits = slots;
+      a.nseq = (int)ns;
+      a.pos0 = d_pos0;
+      a.seq_stride = seq_stride;
+      a.pdl = false;
+      launch_attention(a, stream);
+      gemv(W.o, attn, h, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+      gemv(W.gu, x, h, (int)T, EPI_SWIGLU, hbuf, I, W.post_norm, nullptr);
+      gemv(W.down, hbuf, I, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+    }
+    if (head_mode == 1) {
+      const int np = head(x, (int)T);
+      launch_batch_accept(parts, np, (int)T, M, d_tok, d_argmax, d_m, d_next, stream);
+    } else if (head_mode == 2) {
+      const int np = head(x + (T - 1) * h, 1);
+      launch_batch_accept(parts, np, 1, 1, d_tok, d_argmax, d_m, d_next, stream);
+    }
+    if (head_mode) {
+      const size_t nres = head_mode == 1 ? ns : 1;
+      LS_CUDA(cudaMemcpyAsync(h_m, d_m, nres * 4, cudaMemcpyDeviceToHost, stream));
+      LS_CUDA(cudaMemcpyAsync(h_next, d_next, nres * 4, cudaMemcpyDeviceToHost, stream));
+      d2h_bytes += 2 * nres * 4;
+    }
+    LS_CUDA(cudaMemcpyAsync(h_err, d_err, 4, cudaMemcpyDeviceToHost, stream));
+    LS_CUDA(cudaStreamSynchronize(stream));
+    passes++;
+    if (*h_err == 1) LS_THROW(LS_ERR_DEVICE, "a tensor-core kernel gave up waiting on an mbarrier (bounded wait)");
+    if (*h_err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
+    for (size_t i = 0; i < ns; i++) pos[s0 + i] += head_mode == 1 ? h_m[i] + 1 : (uint64_t)M;
+  }
+
+  // src/model.rs:111-119 for one sequence: 128-token chunks; returns the greedy token after them.
+  uint32_t prefill(size_t sq, const uint32_t* ids, uint64_t n) {
+    if (sq >= B) LS_THROW(LS_ERR_ARG, "sequence index out of range");
+    if (n == 0) LS_THROW(LS_ERR_ARG, "no tokens to process");
+    if (pos[sq] + n > max_ctx) LS_THROW(LS_ERR_ARG, "context is full");
+    for (uint64_t off = 0; off < n; off += kPrefillChunk) {
+      const uint64_t len = std::min<uint64_t>(kPrefillChunk, n - off);
+      pass(sq, 1, (int)len, ids + off, off + len == n ? 2 : 0);
+    }
+    return h_next[0];
+  }
+
+  // The decode loop of src/spec.rs:94-149 for every sequence, with the prompt-lookup drafter; all
+  // sequences verify one k+1 block per pass (a sequence that has finished stays in the pass at a
+  // frozen position, its results ignored).
+  void spec(const uint32_t* prompts, uint64_t plen, uint64_t max_new, uint64_t k, const uint32_t* eos, uint64_t neos,
+            uint32_t* out, uint64_t* out_len, LsSpecStats* st) {
+    if (k == 0 || k + 1 > max_block) LS_THROW(LS_ERR_ARG, "k must be between 1 and the batch's block length - 1");
+    if (plen == 0 || max_new == 0) LS_THROW(LS_ERR_ARG, "need a prompt and at least one token to generate");
+    if (plen + max_new + k + 1 > max_ctx) LS_THROW(LS_ERR_ARG, "prompt + max_new + k exceeds the batch's context");
+    std::memset(st, 0, sizeof *st);
+    std::fill(pos.begin(), pos.end(), 0);
+    const double t0 = now_s();
+    std::vector<std::vector<uint32_t>> outs(B), hist(B);
+    std::vector<char> active(B, 1);
+    for (size_t sq = 0; sq < B; sq++) {
+      const uint32_t* p = prompts + sq * plen;
+      const uint32_t a = prefill(sq, p, plen);
+      outs[sq].push_back(a);
+      hist[sq].assign(p, p + plen);
+      hist[sq].push_back(a);
+      if (contains(eos, neos, a) || max_new == 1) active[sq] = 0;
+    }
+    st->first_secs = now_s() - t0;
+    const double td = now_s();
+    const int M = (int)k + 1;
+    std::vector<uint32_t> blocks(B * M);
+    std::vector<std::vector<uint32_t>> drafts(B);
+    std::vector<uint64_t> frozen(B);
+    while (std::find(active.begin(), active.end(), 1) != active.end()) {
+      const double ts = now_s();
+      for (size_t sq = 0; sq < B; sq++) {
+        const uint32_t a = outs[sq].back();
+        drafts[sq] = active[sq] ? lookup_draft(hist[sq], k) : std::vector<uint32_t>();
+        uint32_t* blk = blocks.data() + sq * M;
+        blk[0] = a;
+        for (int i = 1; i < M; i++) blk[i] = (size_t)(i - 1) < drafts[sq].size() ? drafts[sq][i - 1] : (i > 1 ? blk[i - 1] : a);
+        frozen[sq] = pos[sq];
+      }
+      st->draft_secs += now_s() - ts;
+      const double tv = now_s();
+      pass(0, B, M, blocks.data(), 1);
+      st->target_secs += now_s() - tv;
+      st->target_passes++;
+      for (size_t sq = 0; sq < B; sq++) {
+        if (!active[sq]) {
+          pos[sq] = frozen[sq];
+          continue;
+        }
+        const uint32_t mm = h_m[sq], next = h_next[sq];
+        const uint32_t* blk = blocks.data() + sq * M;
+        st->drafted += drafts[sq].size();
+        st->accepted += std::min<uint64_t>(mm, drafts[sq].size());
+        for (uint32_t i = 0; i <= mm; i++) {
+          const uint32_t tok = i < mm ? blk[i + 1] : next;
+          outs[sq].push_back(tok);
+          hist[sq].push_back(tok);
+          if (contains(eos, neos, tok) || outs[sq].size() == max_new) {
+            active[sq] = 0;
+            break;
+          }
+        }
+      }
+    }
+    st->decode_secs = now_s() - td;
+    for (size_t sq = 0; sq < B; sq++) {
+      out_len[sq] = outs[sq].size();
+      std::memset(out + sq * max_new, 0, max_new * 4);
+      std::memcpy(out + sq * max_new, outs[sq].data(), outs[sq].size() * 4);
+    }
+  }
+};
+
+// ------------------------------------------------------------------------------------------------
 // Quantizer (src/quant.rs:158-251): the group quantization runs on the GPU, the file layout on the host
 // ------------------------------------------------------------------------------------------------
 
@@ -1511,6 +1817,87 @@ int ls_qgemv_device(const LsQWeights* w, const float* x_dev, uint64_t M, float* 
 int ls_qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t rows, uint64_t cols, const float* x_dev,
                           uint64_t M, float* y_dev, void* stream) {
   return guard([&] { qgemv_rows_noalloc(bits, group, rows_dev, rows, cols, x_dev, M, y_dev, reinterpret_cast<cudaStream_t>(stream)); });
+}
+
+int ls_batch_open(LsModel* m, uint64_t batch, uint64_t max_ctx, uint64_t max_block, LsBatch** out) {
+  return guard([&] {
+    NEED(m);
+    NEED(out);
+    *out = nullptr;
+    LS_CUDA(cudaSetDevice(m->device));
+    *out = new LsBatch(m, batch, max_ctx, max_block);
+  });
+}
+
+int ls_batch_free(LsBatch* b) {
+  delete b;
+  return LS_OK;
+}
+
+int ls_batch_pos(const LsBatch* b, uint64_t seq, uint64_t* pos) {
+  return guard([&] {
+    NEED(b);
+    NEED(pos);
+    if (seq >= b->B) LS_THROW(LS_ERR_ARG, "sequence index out of range");
+    *pos = b->pos[seq];
+  });
+}
+
+int ls_batch_truncate(LsBatch* b, uint64_t seq, uint64_t pos) {
+  return guard([&] {
+    NEED(b);
+    if (seq >= b->B) LS_THROW(LS_ERR_ARG, "sequence index out of range");
+    if (pos > b->pos[seq]) LS_THROW(LS_ERR_ARG, "cannot truncate to a position beyond the cache");
+    b->pos[seq] = pos;
+  });
+}
+
+int ls_batch_prefill(LsBatch* b, uint64_t seq, const uint32_t* ids, uint64_t n, uint32_t* argmax) {
+  return guard([&] {
+    NEED(b);
+    NEED(ids);
+    LS_CUDA(cudaSetDevice(b->m->device));
+    const uint32_t a = b->prefill(seq, ids, n);
+    if (argmax) *argmax = a;
+  });
+}
+
+int ls_batch_verify(LsBatch* b, const uint32_t* blocks, uint64_t nseq, uint64_t M, uint32_t* accepted_m, uint32_t* next) {
+  return guard([&] {
+    NEED(b);
+    NEED(blocks);
+    NEED(accepted_m);
+    NEED(next);
+    if (M == 0 || M > b->max_block) LS_THROW(LS_ERR_ARG, "verify blocks hold 1..max_block tokens");
+    if (nseq == 0 || nseq > b->B) LS_THROW(LS_ERR_ARG, "nseq must be in 1..batch");
+    LS_CUDA(cudaSetDevice(b->m->device));
+    b->pass(0, nseq, (int)M, blocks, 1);
+    std::memcpy(accepted_m, b->h_m, nseq * 4);
+    std::memcpy(next, b->h_next, nseq * 4);
+  });
+}
+
+int ls_batch_spec(LsBatch* b, const uint32_t* prompts, uint64_t plen, uint64_t max_new, uint64_t k, const uint32_t* eos,
+                  uint64_t neos, uint32_t* out_tokens, uint64_t* out_len, LsSpecStats* stats) {
+  return guard([&] {
+    NEED(b);
+    NEED(prompts);
+    NEED(out_tokens);
+    NEED(out_len);
+    if (neos) NEED(eos);
+    LsSpecStats local;
+    LS_CUDA(cudaSetDevice(b->m->device));
+    b->spec(prompts, plen, max_new, k, eos, neos, out_tokens, out_len, stats ? stats : &local);
+  });
+}
+
+int ls_batch_report(const LsBatch* b, uint64_t* passes, uint64_t* h2d_bytes, uint64_t* d2h_bytes) {
+  return guard([&] {
+    NEED(b);
+    if (passes) *passes = b->passes;
+    if (h2d_bytes) *h2d_bytes = b->h2d_bytes;
+    if (d2h_bytes) *d2h_bytes = b->d2h_bytes;
+  });
 }
 
 int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
