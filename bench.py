@@ -16,7 +16,7 @@ token uploads and result reads inside the timed region). Each rank decodes its o
 scaling, no collective on the data path). Inputs: the weights (278 MB per verify pass) exceed L2,
 so every pass streams them from HBM.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4]
 """
 
 from __future__ import annotations
@@ -45,6 +45,8 @@ CONFIGS = {
     2: dict(shape="0.5b", body=(4, 32), embed=(4, 32), prompt=512, span=32, repeats=0, max_new=256, k=8, drafter="lookup",
             draft=(4, 32)),
 }
+CONFIGS[4] = dict(shape="0.5b", body=(8, 64), embed=(8, 64), prompt=2048, span=32, repeats=0, max_new=512, k=4,
+                  drafter="lookup", draft=(4, 32), batch=64)
 CONFIGS[3] = dict(shape="0.5b", body=(8, 64), embed=(8, 64), prompt=0, span=0, repeats=0, max_new=0, k=0, drafter="none",
                   draft=(4, 32), micro=True)
 METRIC = "spec-decode accepted tokens/s"
@@ -292,6 +294,28 @@ def stored_rows(bits, group, rows, cols, seed):
     return np.ascontiguousarray(raw.reshape(-1))
 
 
+def ref_batch(args, cfg):
+    """Config 4 on the CPU restatement: a reduced sample (one sequence's prefill and a short
+    decode), extrapolated to the batch as per-sequence throughput x 1 (the reference runs sequences
+    one after another)."""
+    rank, world, local, dist = setup_dist(args)
+    if rank != 0:
+        barrier(dist)
+        return
+    c2 = dict(cfg)
+    c2["max_new"] = 16
+    t_path, _ = cpu_files(args, c2, rank, None)
+    v, rates, sample, cores = cpu_sample(args, c2, t_path, None, max(args.steps, 1), 0)
+    sample = "reduced sample: one sequence of the batch, " + sample
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 activations, int8 weights", "data": "synthetic", "config": {"workload": "config4", "config": 4},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    barrier(dist)
+
+
 def microbench(args):
     """Config 3: the verify-path kernels one at a time on one 0.5B layer's shapes. GEMV: every
     launch timed alone with CUDA events after a 256 MB write that evicts L2 (so weights come from
@@ -356,9 +380,86 @@ def microbench(args):
         print(json.dumps(line), flush=True)
 
 
+def batch_bench(args, cfg):
+    """Config 4: B independent sequences per GPU through one batched verify pass per decode step
+    (ls_batch_spec, prompt-lookup drafter). value = tokens generated after the first, all
+    sequences, all ranks, / the slowest rank's decode-loop time; prefill is reported apart."""
+    import torch
+
+    import layerstream_b200 as ls
+    from layerstream_b200 import synth
+
+    rank, world, local, dist = setup_dist(args)
+    torch.cuda.set_device(local)
+    os.makedirs(args.root, exist_ok=True)
+    if rank == 0:
+        path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local)
+    barrier(dist)
+    if rank != 0:
+        path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local)
+    B, plen, max_new, k = cfg["batch"], cfg["prompt"], cfg["max_new"], cfg["k"]
+    model = ls.Model(path, device=local, max_ctx=plen + 64)
+    V = model.vocab
+    prompts = np.array([prompt_for(cfg, V, rank * B + i) for i in range(B)], np.uint32)
+    batch = ls.Batch(model, B, max_ctx=plen + max_new + k + 16, max_block=k + 1)
+    for _ in range(max(args.warmup, 1)):
+        batch.spec(prompts, 8, k)
+    clocks = Clocks(local)
+    barrier(dist)
+    clocks.start()
+    tokens, decode_s, first_s, passes, acc, dr = 0, 0.0, 0.0, 0, 0, 0
+    for _ in range(max(args.steps, 1)):
+        outs, st = batch.spec(prompts, max_new, k)
+        tokens += sum(len(o) - 1 for o in outs)
+        decode_s += st["decode_secs"]
+        first_s += st["first_secs"]
+        passes += st["target_passes"]
+        acc += st["accepted"]
+        dr += st["drafted"]
+    clk = clocks.stop()
+    barrier(dist)
+    ms_max, tok_all = reduce_over_ranks(dist, decode_s * 1e3, tokens, device="cuda")
+    value = tok_all / (ms_max / 1e3)
+    info = model.info
+    avg_ctx = plen + max_new / 2
+    kv = avg_ctx * info.layers * info.kv_heads * info.head_dim * 2 * 2 * B
+    pass_s = decode_s / max(passes, 1)
+    peak, peak_kind = peaks()
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / max(args.steps, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": f"f32 activations, int{cfg['body'][0]} weights (bf16 scales), f16 KV", "data": "synthetic",
+            "config": {"workload": f"config4: 0.5b Qwen2 random-init int8 g64, {B} sequences per GPU, {plen}-token prompts, "
+                                   f"{max_new} new tokens each, k={k}, lookup drafter, batched verify",
+                       "config": 4, "batch_per_gpu": B, "global_batch": B * world,
+                       "parallelism": f"dp{world} (independent sequences, no collective)",
+                       "timing": "host wall time of the decode loop (all sequences), prefill excluded"},
+            "clocks": clk,
+            "e2e": {"value": tok_all / ((ms_max / 1e3) + first_s / max(args.steps, 1)), "unit": UNIT,
+                    "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+                    "includes": "prefill of all sequences + decode through ls_batch_spec, host buffers"},
+            "gpu_launches": int(passes * (2 + 5 * info.layers + 2)),
+            "roofline": {"bound": "hbm", "kernel": "batched verify pass (separate kernels, KV-bound attention)",
+                         "achieved": (info.weight_bytes + kv) / pass_s / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": (info.weight_bytes + kv) / pass_s / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                         "traffic": None, "algorithmic_bytes_per_launch": info.weight_bytes + kv,
+                         "avg_launch_us": pass_s * 1e6, "launches_per_pass": 2 + 5 * info.layers + 2},
+            "spec": {"tokens_per_pass": tokens / max(passes, 1) / B, "accepted_over_drafted": acc / max(dr, 1),
+                     "target_passes": passes, "prefill_s": first_s / max(args.steps, 1)}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    batch.close()
+    model.close()
+
+
 def main():
     args = parse()
     cfg = dict(CONFIGS[args.config])
+    if cfg.get("batch"):
+        if args.impl == "reference":
+            ref_batch(args, cfg)
+            return
+        batch_bench(args, cfg)
+        return
     if cfg.get("micro"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "config 3 is a GPU kernel microbenchmark; the reference's "

@@ -1,6 +1,7 @@
 // Internal declarations shared by the host code and the CUDA kernels of layerstream_b200.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -223,8 +224,15 @@ void launch_quantize_rows(const uint16_t* src_bf16, int rows, int cols, int bits
 
 // ---- persistent pass kernel (ls_pass.cu) ----
 
+// TMA descriptors of one matrix's planes for the pass kernel's weight stream: data as
+// [row group][16-byte chunk][128 x u32], scales as [row group][group][32 x bf16].
+struct QMaps {
+  CUtensorMap data, scales;
+};
+
 struct PassLayer {
   QMat qkv, o, gu, down;
+  const QMaps* maps;  // device [4]: qkv, o, gate/up, down
   const uint16_t* in_norm;
   const uint16_t* post_norm;
   const uint16_t* qkv_bias;
@@ -233,6 +241,7 @@ struct PassLayer {
 struct PassArgs {
   const PassLayer* layers;
   QMat embed;
+  const QMaps* embed_maps;  // device
   const float* final_norm;
   Ctl* ctl;
   long long* x;     // [T][h] residual stream, fixed point
@@ -272,5 +281,8 @@ bool pass_kernel_supported(const WeightFormat& body, const WeightFormat& embed, 
 size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down);
 void launch_pass(const PassArgs& a, const WeightFormat& f, size_t smem, int grid, cudaStream_t s);
 int pass_kernel_blocks_per_sm(const WeightFormat& f, int T, size_t smem, int max_per_sm);
+// K blocks of 64 columns per weight-stream stage of the pass kernel, and the descriptors.
+int pass_kernel_stage_blocks(const WeightFormat& f);
+void pass_encode_maps(const QMat& w, QMaps* out);
 
 }  // namespace ls

@@ -177,6 +177,7 @@ struct LsModel {
 
   // persistent pass kernel state (resident mode, passes of <= 48 tokens)
   PassLayer* d_pass_layers = nullptr;
+  QMaps* d_pass_maps = nullptr;
   long long *x_fix = nullptr, *qkv_fix = nullptr, *gu_fix = nullptr;
   float* pk_att = nullptr;
   unsigned* pk_bar = nullptr;
@@ -459,10 +460,12 @@ struct LsModel {
     for (int c = 0; c < 3; c++) {
       PassPlan& P = pk_plan[c];
       const int T = 16 * (c + 1);
-      // items are 256-row tiles x K slices; enough slices to give every CTA about one item
+      // items are 256-row tiles x K slices; enough slices to give every CTA about one item, but
+      // at least one whole weight-stream stage (nbs K blocks) per item
+      const int nbs = pass_kernel_stage_blocks(cfg.format);
       auto plan = [&](const QMat& w, int grid) {
         const int tiles = (w.rows_pad / 32 + 7) / 8, nblk = w.cols / kb;
-        return std::max(1, std::min(nblk, grid / tiles));
+        return std::max(1, std::min(std::max(1, nblk / nbs), grid / tiles));
       };
       // the down slice width sets the shared memory, which sets the CTAs per SM: settle both
       P.ks_down = plan(layers[0].down, num_sms);
@@ -493,12 +496,24 @@ struct LsModel {
                 pk_plan[c].smem);
     if (pk_plan[0].grid == 0) return;
     pk_max_grid = max_grid;
+    // TMA descriptors of every matrix: [layer][qkv, o, gate/up, down], then the embedding/head
+    std::vector<QMaps> maps(4 * cfg.layers + 1);
+    for (size_t l = 0; l < cfg.layers; l++) {
+      pass_encode_maps(layers[l].qkv, &maps[4 * l + 0]);
+      pass_encode_maps(layers[l].o, &maps[4 * l + 1]);
+      pass_encode_maps(layers[l].gu, &maps[4 * l + 2]);
+      pass_encode_maps(layers[l].down, &maps[4 * l + 3]);
+    }
+    pass_encode_maps(embed, &maps[4 * cfg.layers]);
+    d_pass_maps = dalloc<QMaps>(maps.size());
+    LS_CUDA(cudaMemcpyAsync(d_pass_maps, maps.data(), maps.size() * sizeof(QMaps), cudaMemcpyHostToDevice, stream));
     std::vector<PassLayer> pl(cfg.layers);
     for (size_t l = 0; l < cfg.layers; l++) {
       pl[l].qkv = layers[l].qkv;
       pl[l].o = layers[l].o;
       pl[l].gu = layers[l].gu;
       pl[l].down = layers[l].down;
+      pl[l].maps = d_pass_maps + 4 * l;
       pl[l].in_norm = layers[l].in_norm;
       pl[l].post_norm = layers[l].post_norm;
       pl[l].qkv_bias = layers[l].qkv_bias;
@@ -526,6 +541,7 @@ struct LsModel {
     PassArgs a{};
     a.layers = d_pass_layers;
     a.embed = embed;
+    a.embed_maps = d_pass_maps + 4 * cfg.layers;
     a.final_norm = final_norm;
     a.ctl = ctl;
     a.x = x_fix;

@@ -33,15 +33,24 @@ namespace ls {
 
 constexpr int PK_NWG = 2;                    // dequantizing warpgroups per CTA
 constexpr int PK_CT = PK_NWG * 128;           // their threads
-constexpr int PK_THREADS = PK_CT + 32;        // + the MMA issuer warp
+constexpr int PK_ISSUER = PK_CT / 32;         // warp index of the MMA issuer
+constexpr int PK_PRODUCER = PK_ISSUER + 1;    // warp index of the weight-stream (TMA) producer
+constexpr int PK_STAGERS = PK_CT + 32;        // compute warps + issuer: the B-operand staging group
+constexpr int PK_THREADS = PK_CT + 64;
 constexpr int PK_NW = PK_THREADS / 32;
-constexpr int PK_ISSUER = PK_CT / 32;         // warp index of the issuer
 constexpr int PK_ATT_TILE = 64;
 constexpr int kMaxSlots = 16;  // attention slots per head (context tiles split across CTAs)
-// Bytes of weights one CTA keeps in flight (the load ring): ~64 KB per SM covers HBM latency at
-// full bandwidth.
-constexpr int PK_RING_BYTES = 65536;
+// Weight stream: STAGES stages of one 256-row box of ~16 KB of packed weights (+ its scales),
+// filled by TMA. Bulk copies of >= 16 KB per stage stream at HBM bandwidth with one CTA per SM
+// (per-thread 16-byte copies top out near a third of it).
+constexpr int PK_STAGES = 4;
+constexpr int PK_STAGE_DATA = 16384;
 constexpr int PK_TMEM_COLS = 512;  // one CTA per SM: the whole tensor memory
+constexpr int PK_ABUF = 4;         // A buffers per warpgroup (dequantizers run ahead of the MMAs)
+
+// Named barrier over the compute warps and the issuer (the producer never joins it, so it can
+// wait on the ring while the others stage activations).
+__device__ __forceinline__ void stagers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(PK_STAGERS) : "memory"); }
 
 __device__ __forceinline__ long long to_fix(float v) {
   v = fminf(fmaxf(v, -1.0e9f), 1.0e9f);
@@ -96,142 +105,136 @@ __device__ bool grid_barrier(unsigned* bar, unsigned target, int* err) {
 
 // ---------------------------------------------------------------------------------------------
 // The tensor-core GEMV of one item: rows [256 t256, 256 t256 + 256) over K blocks [kb0, kb1).
-// State is kept across items and phases; both roles advance the same block / item counters.
+// The producer warp streams the item's weights (and group scales) as 256-row TMA boxes of NB K
+// blocks into a PK_STAGES ring (full / empty mbarriers); each compute warpgroup dequantizes its
+// 128 rows block by block into its A buffer in tensor memory; the issuer warp runs the MMAs.
+// State is kept across items and phases; all roles walk the same item / block sequence.
 // Tensor memory columns: A buffer (b, g) at (b PK_NWG + g) ACOLS, accumulator (d, g) at
-// 2 PK_NWG ACOLS + (d PK_NWG + g) NT.
+// PK_ABUF PK_NWG ACOLS + (d PK_NWG + g) NT.
 // ---------------------------------------------------------------------------------------------
+template <int BITS, int G>
+struct Stream {
+  static constexpr int KB = tc_kb(BITS, G), NS = tc_ns(BITS, G), CPB = KB / (128 / BITS);
+  static constexpr int NB = (PK_STAGE_DATA / (8 * CPB * 512)) < 1 ? 1 : PK_STAGE_DATA / (8 * CPB * 512);
+  static constexpr uint32_t kData = 8 * CPB * NB * 512, kScales = 8 * NS * NB * 64, kStage = kData + kScales;
+};
+
+__device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(tc::su32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(tc::su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 template <int BITS, int G, int NT>
 struct TcGemv {
-  static constexpr int KB = tc_kb(BITS, G), NS = tc_ns(BITS, G), WPC = 128 / BITS, CPB = KB / WPC, ACOLS = KB / 2;
-  static constexpr uint32_t kStage = PK_CT * CPB * 16;
-  static constexpr int STAGES = (int)(PK_RING_BYTES / kStage) < 4 ? 4 : (int)(PK_RING_BYTES / kStage);
-  static_assert(2 * PK_NWG * ACOLS + 2 * PK_NWG * NT <= PK_TMEM_COLS, "tensor memory");
-  uint32_t tmem, ring_addr;
+  using S = Stream<BITS, G>;
+  static constexpr int KB = S::KB, NS = S::NS, CPB = S::CPB, NB = S::NB, ACOLS = KB / 2;
+  static_assert(PK_ABUF * PK_NWG * ACOLS + 2 * PK_NWG * NT <= PK_TMEM_COLS, "tensor memory");
+  uint32_t tmem;
   uint8_t* ring;
-  uint64_t *bar_a, *bar_full, *bar_d, *bar_dfree;  // [2] each
+  uint64_t *full, *empty;        // [PK_STAGES] weight stream
+  uint64_t *bar_a, *bar_full;    // [PK_ABUF] A buffers: MMAs done / A written
+  uint64_t *bar_d, *bar_dfree;   // [2] accumulators: ready / read
   int* abort;
-  uint32_t blk, itc;  // K blocks and items run so far (identical in both roles)
+  uint32_t blk, itc, rpos;  // K blocks, items and stream stages consumed so far
 
   __device__ uint32_t a_col(int b, int g) const { return tmem + (uint32_t)((b * PK_NWG + g) * ACOLS); }
-  __device__ uint32_t d_col(int d, int g) const { return tmem + (uint32_t)(2 * PK_NWG * ACOLS + (d * PK_NWG + g) * NT); }
-
-  // Starts the weight stream of an item (compute threads only).
-  __device__ void prologue(const QMat& w, int t256, int kb0, int kb1) const {
-    const int g = threadIdx.x >> 7, warp = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
-    const int t32 = (t256 * PK_NWG + g) * 4 + warp;
-    const bool valid = t32 < w.rows_pad / 32;
-    const uint8_t* db = w.data + ((size_t)(valid ? t32 : 0) * w.chunks()) * 512 + lane * 16;
-#pragma unroll
-    for (int s = 0; s < STAGES - 1; s++) {
-      const int kb = kb0 + s;
-      if (kb < kb1 && valid) {
-#pragma unroll
-        for (int q = 0; q < CPB; q++) tc::cp_async16(ring_addr + s * kStage + q * 16, db + (size_t)(kb * CPB + q) * 512);
-      }
-      tc::cp_commit();
-    }
+  __device__ uint32_t d_col(int d, int g) const {
+    return tmem + (uint32_t)(PK_ABUF * PK_NWG * ACOLS + (d * PK_NWG + g) * NT);
   }
 
-  // Compute threads: the K loop of an item (prologue already issued), then the next item's
-  // prologue (nx, when not null), then the accumulators. false on a timeout.
-  __device__ bool run(const QMat& w, int t256, int kb0, int kb1, float (&tot)[NT], const int* nx) {
-    const int g = threadIdx.x >> 7, warp = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
-    const int tiles32 = w.rows_pad / 32, nch = w.chunks(), ngr = w.groups();
-    const int t32 = (t256 * PK_NWG + g) * 4 + warp;
-    const bool row_valid = t32 < tiles32;
-    const uint8_t* db = w.data + ((size_t)(row_valid ? t32 : 0) * nch) * 512 + lane * 16;
-    const uint16_t* sb = w.scales + (size_t)(row_valid ? t32 : 0) * ngr * 32 + lane;
+  // Compute threads: the K loop of an item over the streamed stages, then the accumulators.
+  // false on a timeout.
+  __device__ bool run(int kb0, int kb1, float (&tot)[NT]) {
+    const int g = threadIdx.x >> 7, warp8 = threadIdx.x >> 5, warp = warp8 & 3, lane = threadIdx.x & 31;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     const uint32_t sub8 = BITS == 8 ? 0x64806480u : 0x64086408u;
-    auto load_scales = [&](int kb, uint16_t (&sc)[NS]) {
+    for (int kbs = kb0; kbs < kb1; kbs += NB) {
+      const int slot = rpos % PK_STAGES;
+      bool fail = !tc::mbar_wait(&full[slot], (rpos / PK_STAGES) & 1, abort);
+      if (__any_sync(0xffffffffu, fail)) return false;
+      rpos++;
+      const uint8_t* st = ring + (size_t)slot * S::kStage;
+      const int nb = min(NB, kb1 - kbs);
+      for (int bi = 0; bi < nb; bi++) {
+        // this warp's 32 rows (row group warp8 of the box): chunk (bi CPB + q), group (bi NS + s)
+        uint4 wv[CPB];
 #pragma unroll
-      for (int s = 0; s < NS; s++) sc[s] = (row_valid && kb < kb1) ? sb[(size_t)((kb * KB) / G + s) * 32] : (uint16_t)0;
-    };
-    uint16_t sr0[NS], sr1[NS], sr2[NS];
-    load_scales(kb0, sr0);
-    load_scales(kb0 + 1, sr1);
-    for (int kb = kb0; kb < kb1; kb++) {
-      const int it = kb - kb0;
-      {
-        const int kn = kb + STAGES - 1, sn = (it + STAGES - 1) % STAGES;
-        if (kn < kb1 && row_valid) {
+        for (int q = 0; q < CPB; q++)
+          wv[q] = *reinterpret_cast<const uint4*>(st + ((size_t)(warp8 * CPB * NB + bi * CPB + q)) * 512 + lane * 16);
+        uint32_t sc[NS];
 #pragma unroll
-          for (int q = 0; q < CPB; q++) tc::cp_async16(ring_addr + sn * kStage + q * 16, db + (size_t)(kn * CPB + q) * 512);
-        }
-        tc::cp_commit();
-      }
-      load_scales(kb + 2, sr2);
-      uint32_t sc[NS];
+        for (int q = 0; q < NS; q++)
+          sc[q] = tc::h2_splat(bf16f(reinterpret_cast<const uint16_t*>(st + S::kData + (size_t)(warp8 * NS * NB + bi * NS + q) * 64)[lane]));
+        uint32_t a[ACOLS];
 #pragma unroll
-      for (int q = 0; q < NS; q++) sc[q] = tc::h2_splat(bf16f(sr0[q]));
-      tc::cp_wait<STAGES - 1>();
-      uint4 wv[CPB];
-      const uint8_t* rs = ring + (size_t)(it % STAGES) * kStage + (size_t)threadIdx.x * CPB * 16;
+        for (int q = 0; q < CPB; q++) {
+          const uint32_t wd[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
+          if constexpr (BITS == 8) {
+            const uint32_t s2 = sc[(NS > 1) ? (q * 16) / G : 0];
 #pragma unroll
-      for (int q = 0; q < CPB; q++) wv[q] = row_valid ? *reinterpret_cast<const uint4*>(rs + q * 16) : make_uint4(0, 0, 0, 0);
-      uint32_t a[ACOLS];
+            for (int k = 0; k < 4; k++) {
+              const uint32_t p0 = (__byte_perm(wd[k], 0u, 0x4140u) ^ 0x00800080u) | 0x64006400u;
+              const uint32_t p1 = (__byte_perm(wd[k], 0u, 0x4342u) ^ 0x00800080u) | 0x64006400u;
+              a[q * 8 + 2 * k] = tc::h2_sub_mul(p0, sub8, s2);
+              a[q * 8 + 2 * k + 1] = tc::h2_sub_mul(p1, sub8, s2);
+            }
+          } else if constexpr (G == 16) {
 #pragma unroll
-      for (int q = 0; q < CPB; q++) {
-        const uint32_t wd[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
-        if constexpr (BITS == 8) {
-          const uint32_t s2 = sc[(NS > 1) ? (q * 16) / G : 0];
+            for (int k = 0; k < 4; k++) {
+              const uint32_t s2 = sc[2 * q + (k < 2 ? 0 : 1)];
+              const int base = q * 16 + (k < 2 ? 0 : 8), j = (k & 1) * 4;
+              const uint32_t p0 = __byte_perm(wd[k], 0u, 0x4140u), p1 = __byte_perm(wd[k], 0u, 0x4342u);
+              a[base + j / 2] = tc::h2_sub_mul((p0 & 0x000F000Fu) | 0x64006400u, sub8, s2);
+              a[base + j / 2 + 1] = tc::h2_sub_mul((p1 & 0x000F000Fu) | 0x64006400u, sub8, s2);
+              a[base + 4 + j / 2] = tc::h2_sub_mul(((p0 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, s2);
+              a[base + 4 + j / 2 + 1] = tc::h2_sub_mul(((p1 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, s2);
+            }
+          } else {
+            constexpr int HALF = G / 2;
+            const uint32_t s2 = sc[(NS > 1) ? (q * 32) / G : 0];
+            const int j0 = (q * 16) % HALF, gbase = ((q * 32) / G) * G;
 #pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const uint32_t p0 = (__byte_perm(wd[k], 0u, 0x4140u) ^ 0x00800080u) | 0x64006400u;
-            const uint32_t p1 = (__byte_perm(wd[k], 0u, 0x4342u) ^ 0x00800080u) | 0x64006400u;
-            a[q * 8 + 2 * k] = tc::h2_sub_mul(p0, sub8, s2);
-            a[q * 8 + 2 * k + 1] = tc::h2_sub_mul(p1, sub8, s2);
-          }
-        } else if constexpr (G == 16) {
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const uint32_t s2 = sc[2 * q + (k < 2 ? 0 : 1)];
-            const int base = q * 16 + (k < 2 ? 0 : 8), j = (k & 1) * 4;
-            const uint32_t p0 = __byte_perm(wd[k], 0u, 0x4140u), p1 = __byte_perm(wd[k], 0u, 0x4342u);
-            a[base + j / 2] = tc::h2_sub_mul((p0 & 0x000F000Fu) | 0x64006400u, sub8, s2);
-            a[base + j / 2 + 1] = tc::h2_sub_mul((p1 & 0x000F000Fu) | 0x64006400u, sub8, s2);
-            a[base + 4 + j / 2] = tc::h2_sub_mul(((p0 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, s2);
-            a[base + 4 + j / 2 + 1] = tc::h2_sub_mul(((p1 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, s2);
-          }
-        } else {
-          constexpr int HALF = G / 2;
-          const uint32_t s2 = sc[(NS > 1) ? (q * 32) / G : 0];
-          const int j0 = (q * 16) % HALF, gbase = ((q * 32) / G) * G;
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const uint32_t p0 = __byte_perm(wd[k], 0u, 0x4140u), p1 = __byte_perm(wd[k], 0u, 0x4342u);
-            const int lo = (gbase + j0 + 4 * k) / 2, hi = (gbase + j0 + HALF + 4 * k) / 2;
-            a[lo] = tc::h2_sub_mul((p0 & 0x000F000Fu) | 0x64006400u, sub8, s2);
-            a[lo + 1] = tc::h2_sub_mul((p1 & 0x000F000Fu) | 0x64006400u, sub8, s2);
-            a[hi] = tc::h2_sub_mul(((p0 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, s2);
-            a[hi + 1] = tc::h2_sub_mul(((p1 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, s2);
+            for (int k = 0; k < 4; k++) {
+              const uint32_t p0 = __byte_perm(wd[k], 0u, 0x4140u), p1 = __byte_perm(wd[k], 0u, 0x4342u);
+              const int lo = (gbase + j0 + 4 * k) / 2, hi = (gbase + j0 + HALF + 4 * k) / 2;
+              a[lo] = tc::h2_sub_mul((p0 & 0x000F000Fu) | 0x64006400u, sub8, s2);
+              a[lo + 1] = tc::h2_sub_mul((p1 & 0x000F000Fu) | 0x64006400u, sub8, s2);
+              a[hi] = tc::h2_sub_mul(((p0 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, s2);
+              a[hi + 1] = tc::h2_sub_mul(((p1 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, s2);
+            }
           }
         }
-      }
+        if (bi == nb - 1) {  // this warp is done with the stage: the producer may refill it
+          __syncwarp();
+          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&empty[slot])) : "memory");
+        }
+        // A buffer b is free once the MMAs of block blk - PK_ABUF have completed
+        const int b = blk % PK_ABUF;
+        const uint32_t u = blk / PK_ABUF;
+        fail = u > 0 && !tc::mbar_wait(&bar_a[b], (u - 1) & 1, abort);
+        if (__any_sync(0xffffffffu, fail)) return false;
+        tc::fence_after();
 #pragma unroll
-      for (int q = 0; q < NS; q++) {
-        sr0[q] = sr1[q];
-        sr1[q] = sr2[q];
+        for (int q = 0; q < ACOLS / 16; q++) tc::st16(a_col(b, g) + lane_base + q * 16, a + q * 16);
+        tc::wait_st();
+        tc::fence_before();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_full[b])) : "memory");
+        blk++;
       }
-      // A buffer b is free once the MMAs of block blk - 2 have completed
-      const int b = blk & 1;
-      const uint32_t u = blk >> 1;
-      bool fail = u > 0 && !tc::mbar_wait(&bar_a[b], (u - 1) & 1, abort);
-      if (__any_sync(0xffffffffu, fail)) {
-        tc::cp_wait<0>();
-        return false;
-      }
-      tc::fence_after();
-#pragma unroll
-      for (int q = 0; q < ACOLS / 16; q++) tc::st16(a_col(b, g) + lane_base + q * 16, a + q * 16);
-      tc::wait_st();
-      tc::fence_before();
-      __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_full[b])) : "memory");
-      blk++;
     }
-    // the ring slots are free (every thread has read its own): stream the next item meanwhile
-    if (nx) prologue(w, nx[0], nx[1], nx[2]);
     const int d = itc & 1;
     const uint32_t v = itc >> 1;
     itc++;
@@ -264,8 +267,8 @@ struct TcGemv {
       // accumulator d is free once the compute threads have read item itc - 2
       if (v > 0 && !tc::mbar_wait(&bar_dfree[d], (v - 1) & 1, abort)) fail = true;
       for (int kb = kb0; kb < kb1 && !fail; kb++) {
-        const int b = blk & 1;
-        const uint32_t u = blk >> 1;
+        const int b = blk % PK_ABUF;
+        const uint32_t u = blk / PK_ABUF;
         blk++;
         if (!tc::mbar_wait(&bar_full[b], u & 1, abort)) {
           fail = true;
@@ -313,13 +316,68 @@ __device__ __forceinline__ Split make_split(const QMat& w, int ks) {
   return s;
 }
 
+// Producer (lane 0 of warp PK_PRODUCER): issues the stages of the CTA's items of a GEMV phase, in
+// the order the compute warps consume them, each a 256-row box of NB K blocks plus its scales.
+template <int BITS, int G>
+struct Producer {
+  using S = Stream<BITS, G>;
+  uint8_t* ring;
+  uint64_t *full, *empty;
+  int* abort;
+  uint32_t lpos;  // stages issued so far
+  const QMaps* maps;
+  Split sp;
+  int i, kb, kb1, t256;
+
+  __device__ void begin(const QMaps* m, const Split& s) {
+    maps = m;
+    sp = s;
+    i = blockIdx.x;
+    if (i < sp.items()) {
+      int kb0;
+      sp.item(i, &t256, &kb0, &kb1);
+      kb = kb0;
+    }
+  }
+  __device__ bool done() const { return i >= sp.items(); }
+  // Issues the next stage. wait == false: returns false at once when its slot is still in use.
+  // A timeout also returns false (and raises *abort).
+  __device__ bool issue_one(bool wait) {
+    const int slot = lpos % PK_STAGES;
+    const uint32_t use = lpos / PK_STAGES;
+    if (use > 0) {
+      if (!wait) {
+        if (!mbar_test(&empty[slot], (use - 1) & 1)) return false;
+      } else if (!tc::mbar_wait(&empty[slot], (use - 1) & 1, abort)) {
+        return false;
+      }
+    }
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::su32(&full[slot])), "r"(S::kStage)
+                 : "memory");
+    const uint32_t dst = tc::su32(ring + (size_t)slot * S::kStage);
+    tma_load3(dst, &maps->data, 0, kb * S::CPB, t256 * 8, &full[slot]);
+    tma_load3(dst + S::kData, &maps->scales, 0, kb * S::NS, t256 * 8, &full[slot]);
+    lpos++;
+    kb += S::NB;
+    if (kb >= kb1) {
+      i += gridDim.x;
+      if (i < sp.items()) {
+        int kb0;
+        sp.item(i, &t256, &kb0, &kb1);
+        kb = kb0;
+      }
+    }
+    return true;
+  }
+};
+
 // Writes activations (already f32) for tokens t < T, K columns [col0, col0 + ncol) into the
 // canonical K-major f16 layout; value(t, col) is a callable.
 template <int NT, class F>
 __device__ __forceinline__ void stage_b(uint8_t* xb, uint32_t sbo, int T, int col0, int ncol, F value) {
   const int n8 = ncol / 8;
 #pragma unroll 4
-  for (int i = threadIdx.x; i < NT * n8; i += PK_THREADS) {
+  for (int i = threadIdx.x; i < NT * n8; i += PK_STAGERS) {
     const int t = i / n8, kc = i - t * n8;
     uint32_t w4[4] = {0u, 0u, 0u, 0u};
     if (t < T) {
@@ -571,8 +629,10 @@ __device__ void attention_item(const PassArgs& a, int l, int hh, int slot, uint8
 template <int BITS, int G, int NT>
 __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   using Gemv = TcGemv<BITS, G, NT>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bar_a[2], bar_full[2], bar_d[2], bar_dfree[2], bar_fin;
+  using Str = Stream<BITS, G>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t bar_a[PK_ABUF], bar_full[PK_ABUF], bar_d[2], bar_dfree[2], bar_fin;
+  __shared__ uint64_t s_full[PK_STAGES], s_empty[PK_STAGES];
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ float s_inv[NT];
@@ -584,18 +644,24 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   const int T = a.T, h = a.hidden, I = a.inter;
   const int kvd = a.kv_heads * a.hd, QS = h + 2 * kvd;
   int* err = &a.ctl->err;
-  // shared memory: [load ring][B operand, or attention scratch, or rms partial sums]
-  uint8_t* ring = smem;
-  uint8_t* xb = smem + (size_t)Gemv::STAGES * Gemv::kStage;
+  // shared memory: [weight-stream ring (1 KB aligned)][B operand, or attention scratch, or rms sums]
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* xb = ring + (size_t)PK_STAGES * Str::kStage;
   float* red = reinterpret_cast<float*>(xb);
   const uint32_t xb_addr = tc::su32(xb);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < PK_ABUF; i++) {
       tc::mbar_init(&bar_a[i], 1);
       tc::mbar_init(&bar_full[i], PK_NWG * 4);  // one arrival per compute warp
+    }
+    for (int i = 0; i < 2; i++) {
       tc::mbar_init(&bar_d[i], 1);
       tc::mbar_init(&bar_dfree[i], PK_NWG * 4);
+    }
+    for (int i = 0; i < PK_STAGES; i++) {
+      tc::mbar_init(&s_full[i], 1);
+      tc::mbar_init(&s_empty[i], PK_NWG * 4);
     }
     tc::mbar_init(&bar_fin, 1);
     s_abort = 0;
@@ -612,13 +678,23 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   Gemv gm;
   gm.tmem = s_tmem;
   gm.ring = ring;
-  gm.ring_addr = tc::su32(ring) + (uint32_t)(compute ? threadIdx.x : 0) * Gemv::CPB * 16;
+  gm.full = s_full;
+  gm.empty = s_empty;
   gm.bar_a = bar_a;
   gm.bar_full = bar_full;
   gm.bar_d = bar_d;
   gm.bar_dfree = bar_dfree;
   gm.abort = &s_abort;
-  gm.blk = gm.itc = 0;
+  gm.blk = gm.itc = gm.rpos = 0;
+  Producer<BITS, G> pr;
+  pr.ring = ring;
+  pr.full = s_full;
+  pr.empty = s_empty;
+  pr.abort = &s_abort;
+  pr.lpos = 0;
+  pr.i = 1 << 30;
+  pr.sp.tiles = pr.sp.ks = pr.sp.nblk = 0;
+  const bool producer = warp == PK_PRODUCER && lane == 0;
 
   // Profiling timeline: slot 0 = start, 2b - 1 / 2b = arrival at / departure from barrier b.
   auto stamp = [&](unsigned slot) {
@@ -638,21 +714,32 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     stamp(2 * nbar);
     return ok;
   };
-  // Starts the weight stream of this CTA's first item of a GEMV phase (before the barrier).
-  auto prefetch = [&](const QMat& w, int ks) {
-    const Split sp = make_split<BITS, G>(w, ks);
-    if (compute && (int)blockIdx.x < sp.items()) {
-      int t256, kb0, kb1;
-      sp.item(blockIdx.x, &t256, &kb0, &kb1);
-      gm.prologue(w, t256, kb0, kb1);
+  // Starts the weight stream of this CTA's items of the next GEMV phase (before the barrier):
+  // as many stages as the ring has free, without waiting.
+  auto prefetch = [&](const QMat& w, const QMaps* maps, int ks) {
+    if (!producer) return;
+    pr.begin(maps, make_split<BITS, G>(w, ks));
+    while (!pr.done() && pr.issue_one(false)) {
     }
   };
-  // Runs the items of a GEMV phase (the first one's weights already streaming): stage(col0, ncol,
-  // sbo) fills the B operand of a K slice, epi(row, ks_index, tot) consumes the accumulators.
-  // Every thread walks the same item sequence (so the staging barriers match even after a failure,
-  // when the work is skipped and every bounded wait returns at once).
+  // Runs the items of a GEMV phase (its weights streaming since the prefetch): stage(col0, ncol,
+  // sbo) fills the B operand of a K slice, epi(row, ks_index, tot) consumes the accumulators. The
+  // producer finishes the phase's stream; the others walk the same item sequence (so the staging
+  // barriers match even after a failure, when the work is skipped and bounded waits return).
   auto gemv_phase = [&](const QMat& w, int ks, auto stage, auto epi) {
     const Split sp = make_split<BITS, G>(w, ks);
+    if (warp == PK_PRODUCER) {
+      if (producer) {
+        while (ok && !pr.done()) {
+          if (!pr.issue_one(true)) {
+            ok = false;
+            s_abort = 1;
+            atomicCAS(err, 0, 1);
+          }
+        }
+      }
+      return;
+    }
     int staged = -1;
     for (int i = blockIdx.x; i < sp.items(); i += gridDim.x) {
       int t256, kb0, kb1;
@@ -661,21 +748,18 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
       const int col0 = kb0 * Gemv::KB, ncol = (kb1 - kb0) * Gemv::KB;
       const uint32_t sbo = (uint32_t)(ncol / 8) * 128u;
       if (kslice != staged) {
-        __syncthreads();
+        stagers_sync();
         if (ok) stage(col0, ncol, sbo);
-        __syncthreads();
+        stagers_sync();
         staged = kslice;
       }
       if (!ok) continue;
       if (compute) {
-        int nx[3];
-        const bool has_next = i + (int)gridDim.x < sp.items();
-        if (has_next) sp.item(i + gridDim.x, &nx[0], &nx[1], &nx[2]);
         float tot[NT];
-        if (!gm.run(w, t256, kb0, kb1, tot, has_next ? nx : nullptr)) {
+        if (!gm.run(kb0, kb1, tot)) {
           ok = false;
         } else {
-          const int t32 = (t256 * PK_NWG + (warp >> 2)) * 4 + (warp & 3);
+          const int t32 = t256 * 8 + warp;
           if (t32 < w.rows_pad / 32) epi(t32 * 32 + lane, kslice, tot);
         }
       } else if (!gm.issue(kb0, kb1, xb_addr, sbo)) {
@@ -686,7 +770,6 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
         if (lane == 0) atomicCAS(err, 0, 1);  // the other CTAs stop at their next wait
       }
     }
-    tc::cp_wait<0>();
   };
 
   // ---- embedding rows into the residual stream; zero the q|k|v accumulators ----
@@ -717,7 +800,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     }
     zero_ll(a.qkv, (size_t)T * QS);
   }
-  prefetch(a.layers[0].qkv, a.ks_qkv);
+  prefetch(a.layers[0].qkv, &a.layers[0].maps[0], a.ks_qkv);
   barrier();
 
   for (int l = 0; l < a.L && ok; l++) {
@@ -746,7 +829,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
       attention_item(a, l, it / a.slots, it % a.slots, xb);
     }
     zero_ll(a.gu, (size_t)T * 2 * I);
-    prefetch(W.o, a.ks_o);
+    prefetch(W.o, &W.maps[1], a.ks_o);
     if (!barrier()) break;
 
     // ---- O: residual add into x ----
@@ -762,7 +845,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
             if (t < T) fix_add(a.x + (size_t)t * h + r, tot[t]);
         });
     zero_ll(a.qkv, (size_t)T * QS);
-    prefetch(W.gu, a.ks_gu);
+    prefetch(W.gu, &W.maps[2], a.ks_gu);
     if (!barrier()) break;
 
     // ---- gate/up: RMSNorm(x) -> gate/up sums ----
@@ -780,7 +863,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
           for (int t = 0; t < NT; t++)
             if (t < T) fix_add(a.gu + (size_t)t * 2 * I + r, tot[t]);
         });
-    prefetch(W.down, a.ks_down);
+    prefetch(W.down, &W.maps[3], a.ks_down);
     if (!barrier()) break;
 
     // ---- down: SwiGLU while staging, residual add into x ----
@@ -799,8 +882,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
           for (int t = 0; t < NT; t++)
             if (t < T) fix_add(a.x + (size_t)t * h + r, tot[t]);
         });
-    if (l + 1 < a.L) prefetch(a.layers[l + 1].qkv, a.ks_qkv);
-    else if (a.n_logits > 0) prefetch(a.embed, 1);
+    if (l + 1 < a.L) prefetch(a.layers[l + 1].qkv, &a.layers[l + 1].maps[0], a.ks_qkv);
+    else if (a.n_logits > 0) prefetch(a.embed, a.embed_maps, 1);
     if (!barrier()) break;
   }
 
@@ -853,12 +936,17 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   __syncthreads();
   stamp(2 * nbar + 1);
 
-  // ---- release tensor memory (after the issuer's MMAs have all completed, also after an abort) ----
-  tc::cp_wait<0>();
+  // ---- release tensor memory (after the issuer's MMAs and the stream's copies have all
+  // completed, also after an abort) ----
   if (warp == PK_ISSUER && lane == 0) {
     volatile int no_abort = 0;
     tc::commit(&bar_fin);
     tc::mbar_wait(&bar_fin, 0, &no_abort);
+  }
+  if (producer) {
+    volatile int no_abort = 0;
+    for (uint32_t p = pr.lpos > PK_STAGES ? pr.lpos - PK_STAGES : 0; p < pr.lpos; p++)
+      tc::mbar_wait(&s_full[p % PK_STAGES], (p / PK_STAGES) & 1, &no_abort);
   }
   tc::fence_before();
   __syncthreads();
@@ -880,18 +968,67 @@ bool pass_kernel_supported(const WeightFormat& body, const WeightFormat& embed, 
   return (body.bits == 8 && (body.group == 32 || body.group == 64)) || (body.bits == 4 && (body.group == 16 || body.group == 32));
 }
 
+int pass_kernel_stage_blocks(const WeightFormat& f) {
+  const int cpb = tc_kb(f.bits, f.group) / (128 / f.bits);
+  return std::max(1, PK_STAGE_DATA / (8 * cpb * 512));
+}
+
+static size_t pass_stage_bytes(const WeightFormat& f) {
+  const int kb = tc_kb(f.bits, f.group), cpb = kb / (128 / f.bits), ns = kb >= f.group ? kb / f.group : 1;
+  const int nb = pass_kernel_stage_blocks(f);
+  return (size_t)8 * cpb * nb * 512 + (size_t)8 * ns * nb * 64;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
+void pass_encode_maps(const QMat& w, QMaps* out) {
+  using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                              const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Encode encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    LS_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !fn) LS_THROW(-3, "cuTensorMapEncodeTiled is not available from the driver");
+    encode = reinterpret_cast<Encode>(fn);
+  }
+  WeightFormat f;
+  f.bits = w.bits;
+  f.group = w.group;
+  const int kb = tc_kb(w.bits, w.group), cpb = kb / (128 / w.bits), ns = kb >= w.group ? kb / w.group : 1;
+  const int nb = pass_kernel_stage_blocks(f);
+  const cuuint64_t tiles32 = (cuuint64_t)w.rows_pad / 32, nch = (cuuint64_t)w.chunks(), ngr = (cuuint64_t)w.groups();
+  const cuuint32_t es[3] = {1, 1, 1};
+  {
+    const cuuint64_t dims[3] = {128, nch, tiles32};
+    const cuuint64_t strides[2] = {512, nch * 512};
+    const cuuint32_t box[3] = {128, (cuuint32_t)(cpb * nb), 8};
+    const CUresult r = encode(&out->data, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(w.data), dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) LS_THROW(-3, "cuTensorMapEncodeTiled (weights) failed: " + std::to_string((int)r));
+  }
+  {
+    const cuuint64_t dims[3] = {32, ngr, tiles32};
+    const cuuint64_t strides[2] = {64, ngr * 64};
+    const cuuint32_t box[3] = {32, (cuuint32_t)(ns * nb), 8};
+    const CUresult r = encode(&out->scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(w.scales), dims, strides, box,
+                              es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) LS_THROW(-3, "cuTensorMapEncodeTiled (scales) failed: " + std::to_string((int)r));
+  }
+}
+
 size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down) {
   const int NT = pass_kernel_nt(T);
-  const int kb = tc_kb(f.bits, f.group), cpb = kb / (128 / f.bits);
-  const size_t stage = (size_t)PK_CT * cpb * 16;
-  const size_t stages = std::max<size_t>(4, PK_RING_BYTES / stage);
+  const int kb = tc_kb(f.bits, f.group);
   // largest B operand: the full hidden width (QKV, O, gate/up, head) or a K slice of down
   const int nblk_down = inter / kb;
   const int down_cols = ((nblk_down + ks_down - 1) / ks_down) * kb;
   size_t b = (size_t)NT * std::max(hidden, down_cols) * 2;
   b = std::max(b, (size_t)T * PK_THREADS * 4);  // rms partial sums
   b = std::max(b, pk_att_smem(T, hd));
-  return stages * stage + b;
+  return 1024 + (size_t)PK_STAGES * pass_stage_bytes(f) + b;  // 1 KB for aligning the ring
 }
 
 template <int BITS, int G, int NT>
