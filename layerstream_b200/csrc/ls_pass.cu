@@ -33,10 +33,10 @@ namespace ls {
 
 constexpr int PK_NWG = 2;                    // dequantizing warpgroups per CTA
 constexpr int PK_CT = PK_NWG * 128;           // their threads
-constexpr int PK_ISSUER = PK_CT / 32;         // warp index of the MMA issuer
-constexpr int PK_PRODUCER = PK_ISSUER + 1;    // warp index of the weight-stream (TMA) producer
-constexpr int PK_STAGERS = PK_CT + 32;        // compute warps + issuer: the B-operand staging group
-constexpr int PK_THREADS = PK_CT + 64;
+constexpr int PK_ISSUER = PK_CT / 32;           // warp of warpgroup g's MMA issuer: PK_ISSUER + g
+constexpr int PK_PRODUCER = PK_ISSUER + PK_NWG;  // warp index of the weight-stream (TMA) producer
+constexpr int PK_STAGERS = PK_CT + 32 * PK_NWG;  // compute warps + issuers: the B-operand staging group
+constexpr int PK_THREADS = PK_STAGERS + 32;
 constexpr int PK_NW = PK_THREADS / 32;
 constexpr int PK_ATT_TILE = 64;
 constexpr int kMaxSlots = 16;  // attention slots per head (context tiles split across CTAs)
@@ -136,16 +136,23 @@ __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
   return ok != 0;
 }
 
-template <int BITS, int G, int NT>
+// Instrumentation policy of the GEMV core: mark(point, block) is called at fixed points of the
+// K loop; the product instance does nothing (microbenchmarks pass a recording one).
+struct NoMarks {
+  __device__ __forceinline__ void mark(int, uint32_t) const {}
+};
+
+template <int BITS, int G, int NT, class Marks = NoMarks>
 struct TcGemv {
   using S = Stream<BITS, G>;
+  Marks marks;
   static constexpr int KB = S::KB, NS = S::NS, CPB = S::CPB, NB = S::NB, ACOLS = KB / 2;
   static_assert(PK_ABUF * PK_NWG * ACOLS + 2 * PK_NWG * NT <= PK_TMEM_COLS, "tensor memory");
   uint32_t tmem;
   uint8_t* ring;
   uint64_t *full, *empty;        // [PK_STAGES] weight stream
-  uint64_t *bar_a, *bar_full;    // [PK_ABUF] A buffers: MMAs done / A written
-  uint64_t *bar_d, *bar_dfree;   // [2] accumulators: ready / read
+  uint64_t *bar_a, *bar_full;    // [PK_NWG][PK_ABUF] A buffers: MMAs done / A written
+  uint64_t *bar_d, *bar_dfree;   // [PK_NWG][2] accumulators: ready / read
   int* abort;
   uint32_t blk, itc, rpos;  // K blocks, items and stream stages consumed so far
 
@@ -164,6 +171,7 @@ struct TcGemv {
       const int slot = rpos % PK_STAGES;
       bool fail = !tc::mbar_wait(&full[slot], (rpos / PK_STAGES) & 1, abort);
       if (__any_sync(0xffffffffu, fail)) return false;
+      marks.mark(0, blk);
       rpos++;
       const uint8_t* st = ring + (size_t)slot * S::kStage;
       const int nb = min(NB, kb1 - kbs);
@@ -220,25 +228,29 @@ struct TcGemv {
           __syncwarp();
           if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&empty[slot])) : "memory");
         }
+        marks.mark(1, blk + (a[ACOLS - 1] == 0x7fffffffu ? 1u : 0u));
         // A buffer b is free once the MMAs of block blk - PK_ABUF have completed
         const int b = blk % PK_ABUF;
         const uint32_t u = blk / PK_ABUF;
-        fail = u > 0 && !tc::mbar_wait(&bar_a[b], (u - 1) & 1, abort);
+        fail = u > 0 && !tc::mbar_wait(&bar_a[g * PK_ABUF + b], (u - 1) & 1, abort);
         if (__any_sync(0xffffffffu, fail)) return false;
+        marks.mark(2, blk);
         tc::fence_after();
 #pragma unroll
         for (int q = 0; q < ACOLS / 16; q++) tc::st16(a_col(b, g) + lane_base + q * 16, a + q * 16);
         tc::wait_st();
         tc::fence_before();
         __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_full[b])) : "memory");
+        if (lane == 0)
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_full[g * PK_ABUF + b])) : "memory");
+        marks.mark(3, blk);
         blk++;
       }
     }
     const int d = itc & 1;
     const uint32_t v = itc >> 1;
     itc++;
-    bool fail = !tc::mbar_wait(&bar_d[d], v & 1, abort);
+    bool fail = !tc::mbar_wait(&bar_d[g * 2 + d], v & 1, abort);
     if (__any_sync(0xffffffffu, fail)) return false;
     tc::fence_after();
 #pragma unroll
@@ -251,12 +263,13 @@ struct TcGemv {
     }
     tc::fence_before();
     __syncwarp();
-    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_dfree[d])) : "memory");
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_dfree[g * 2 + d])) : "memory");
     return true;
   }
 
-  // Issuer warp (lane 0 issues): the MMAs of an item, B = the staged activations. false on a timeout.
-  __device__ bool issue(int kb0, int kb1, uint32_t xb_addr, uint32_t sbo) {
+  // Issuer warp of warpgroup g (lane 0 issues): the MMAs of an item, B = the staged activations.
+  // Descriptors are formed once per item and advanced by adds. false on a timeout.
+  __device__ bool issue(int g, int kb0, int kb1, uint32_t xb_addr, uint32_t sbo) {
     const int lane = threadIdx.x & 31;
     const int d = itc & 1;
     const uint32_t v = itc >> 1;
@@ -265,28 +278,28 @@ struct TcGemv {
     bool fail = false;
     if (lane == 0) {
       // accumulator d is free once the compute threads have read item itc - 2
-      if (v > 0 && !tc::mbar_wait(&bar_dfree[d], (v - 1) & 1, abort)) fail = true;
+      if (v > 0 && !tc::mbar_wait(&bar_dfree[g * 2 + d], (v - 1) & 1, abort)) fail = true;
+      const uint64_t bd0 = tc::sdesc(xb_addr, 128u, sbo);  // start address field: 16-byte units
+      const uint32_t dcol = d_col(d, g);
       for (int kb = kb0; kb < kb1 && !fail; kb++) {
         const int b = blk % PK_ABUF;
         const uint32_t u = blk / PK_ABUF;
         blk++;
-        if (!tc::mbar_wait(&bar_full[b], u & 1, abort)) {
+        if (!tc::mbar_wait(&bar_full[g * PK_ABUF + b], u & 1, abort)) {
           fail = true;
           break;
         }
+        marks.mark(4, blk - 1);
         tc::fence_after();
+        const uint32_t acol = a_col(b, g);
+        const uint64_t bdk = bd0 + (uint64_t)((kb - kb0) * KB);  // K column kpos sits kpos / 8 * 128 bytes in
 #pragma unroll
-        for (int g = 0; g < PK_NWG; g++) {
-#pragma unroll
-          for (int j = 0; j < KB / 16; j++) {
-            const uint32_t kpos = (uint32_t)((kb - kb0) * KB + j * 16);
-            const uint64_t bd = tc::sdesc(xb_addr + (kpos / 8) * 128u, 128u, sbo);
-            tc::mma_f16_ts(d_col(d, g), a_col(b, g) + j * 8, bd, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
-          }
-        }
-        tc::commit(&bar_a[b]);
+        for (int j = 0; j < KB / 16; j++)
+          tc::mma_f16_ts(dcol, acol + j * 8, bdk + (uint64_t)(j * 16), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+        tc::commit(&bar_a[g * PK_ABUF + b]);
+        marks.mark(5, blk - 1);
       }
-      if (!fail) tc::commit(&bar_d[d]);
+      if (!fail) tc::commit(&bar_d[g * 2 + d]);
     } else {
       blk += kb1 - kb0;
     }
@@ -631,7 +644,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   using Gemv = TcGemv<BITS, G, NT>;
   using Str = Stream<BITS, G>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ uint64_t bar_a[PK_ABUF], bar_full[PK_ABUF], bar_d[2], bar_dfree[2], bar_fin;
+  __shared__ uint64_t bar_a[PK_NWG * PK_ABUF], bar_full[PK_NWG * PK_ABUF], bar_d[PK_NWG * 2], bar_dfree[PK_NWG * 2],
+      bar_fin[PK_NWG];
   __shared__ uint64_t s_full[PK_STAGES], s_empty[PK_STAGES];
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
@@ -651,19 +665,19 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   const uint32_t xb_addr = tc::su32(xb);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < PK_ABUF; i++) {
+    for (int i = 0; i < PK_NWG * PK_ABUF; i++) {
       tc::mbar_init(&bar_a[i], 1);
-      tc::mbar_init(&bar_full[i], PK_NWG * 4);  // one arrival per compute warp
+      tc::mbar_init(&bar_full[i], 4);  // one arrival per compute warp of the warpgroup
     }
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < PK_NWG * 2; i++) {
       tc::mbar_init(&bar_d[i], 1);
-      tc::mbar_init(&bar_dfree[i], PK_NWG * 4);
+      tc::mbar_init(&bar_dfree[i], 4);
     }
     for (int i = 0; i < PK_STAGES; i++) {
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&s_empty[i], PK_NWG * 4);
     }
-    tc::mbar_init(&bar_fin, 1);
+    for (int i = 0; i < PK_NWG; i++) tc::mbar_init(&bar_fin[i], 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -762,7 +776,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
           const int t32 = t256 * 8 + warp;
           if (t32 < w.rows_pad / 32) epi(t32 * 32 + lane, kslice, tot);
         }
-      } else if (!gm.issue(kb0, kb1, xb_addr, sbo)) {
+      } else if (!gm.issue(warp - PK_ISSUER, kb0, kb1, xb_addr, sbo)) {
         ok = false;
       }
       if (!ok) {
@@ -938,10 +952,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
 
   // ---- release tensor memory (after the issuer's MMAs and the stream's copies have all
   // completed, also after an abort) ----
-  if (warp == PK_ISSUER && lane == 0) {
+  if (warp >= PK_ISSUER && warp < PK_ISSUER + PK_NWG && lane == 0) {
     volatile int no_abort = 0;
-    tc::commit(&bar_fin);
-    tc::mbar_wait(&bar_fin, 0, &no_abort);
+    tc::commit(&bar_fin[warp - PK_ISSUER]);
+    tc::mbar_wait(&bar_fin[warp - PK_ISSUER], 0, &no_abort);
   }
   if (producer) {
     volatile int no_abort = 0;
