@@ -195,7 +195,10 @@ def setup_dist(args):
             import torch
 
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=900))
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=900),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=900))
     return rank, world, local, dist
 
 
