@@ -16,7 +16,7 @@ token uploads and result reads inside the timed region). Each rank decodes its o
 scaling, no collective on the data path). Inputs: the weights (278 MB per verify pass) exceed L2,
 so every pass streams them from HBM.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4|5]
 """
 
 from __future__ import annotations
@@ -47,6 +47,8 @@ CONFIGS = {
 }
 CONFIGS[4] = dict(shape="0.5b", body=(8, 64), embed=(8, 64), prompt=2048, span=32, repeats=0, max_new=512, k=4,
                   drafter="lookup", draft=(4, 32), batch=64)
+CONFIGS[5] = dict(shape="3b", body=(4, 32), embed=(4, 32), prompt=1024, span=32, repeats=0, max_new=256, k=4,
+                  drafter="lookup", draft=(4, 32), batch=8, stream_slots=2)
 CONFIGS[3] = dict(shape="0.5b", body=(8, 64), embed=(8, 64), prompt=0, span=0, repeats=0, max_new=0, k=0, drafter="none",
                   draft=(4, 32), micro=True)
 METRIC = "spec-decode accepted tokens/s"
@@ -401,7 +403,11 @@ def batch_bench(args, cfg):
     if rank != 0:
         path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local)
     B, plen, max_new, k = cfg["batch"], cfg["prompt"], cfg["max_new"], cfg["k"]
-    model = ls.Model(path, device=local, max_ctx=plen + 64)
+    slots = cfg.get("stream_slots")
+    if slots:
+        model = ls.Model(path, device=local, max_ctx=plen + 64, mode="stream", slots=slots)
+    else:
+        model = ls.Model(path, device=local, max_ctx=plen + 64)
     V = model.vocab
     prompts = np.array([prompt_for(cfg, V, rank * B + i) for i in range(B)], np.uint32)
     batch = ls.Batch(model, B, max_ctx=plen + max_new + k + 16, max_block=k + 1)
@@ -411,6 +417,7 @@ def batch_bench(args, cfg):
     barrier(dist)
     clocks.start()
     tokens, decode_s, first_s, passes, acc, dr = 0, 0.0, 0.0, 0, 0, 0
+    r0 = model.report()
     for _ in range(max(args.steps, 1)):
         outs, st = batch.spec(prompts, max_new, k)
         tokens += sum(len(o) - 1 for o in outs)
@@ -420,6 +427,7 @@ def batch_bench(args, cfg):
         acc += st["accepted"]
         dr += st["drafted"]
     clk = clocks.stop()
+    r1 = model.report()
     barrier(dist)
     ms_max, tok_all = reduce_over_ranks(dist, decode_s * 1e3, tokens, device="cuda")
     value = tok_all / (ms_max / 1e3)
@@ -428,6 +436,13 @@ def batch_bench(args, cfg):
     kv = avg_ctx * info.layers * info.kv_heads * info.head_dim * 2 * 2 * B
     pass_s = decode_s / max(passes, 1)
     peak, peak_kind = peaks()
+    streamed = None
+    if slots:
+        # bytes moved host -> device for weights over the whole run (prefill chunks + verify passes)
+        run_s = decode_s + first_s
+        streamed = {"slots": slots, "h2d_weight_bytes": r1["bytes_read"] - r0["bytes_read"],
+                    "h2d_gbs": (r1["bytes_read"] - r0["bytes_read"]) / max(run_s, 1e-9) / 1e9,
+                    "bytes_per_pass": info.weight_bytes, "note": "every pass streams all layers and the head over PCIe"}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / max(args.steps, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": f"f32 activations, int{cfg['body'][0]} weights (bf16 scales), f16 KV", "data": "synthetic",
@@ -447,7 +462,19 @@ def batch_bench(args, cfg):
                          "traffic": None, "algorithmic_bytes_per_launch": info.weight_bytes + kv,
                          "avg_launch_us": pass_s * 1e6, "launches_per_pass": 2 + 5 * info.layers + 2},
             "spec": {"tokens_per_pass": tokens / max(passes, 1) / B, "accepted_over_drafted": acc / max(dr, 1),
-                     "target_passes": passes, "prefill_s": first_s / max(args.steps, 1)}}
+                     "target_passes": passes, "prefill_s": first_s / max(args.steps, 1)},
+            "streaming": streamed}
+    if slots:
+        # streamed weights: the bound is the host-to-device link, not HBM
+        pcie = 64.0  # GB/s, nominal PCIe 5.0 x16 per direction (no measured figure on this pool)
+        line["roofline"] = {"bound": "h2d", "kernel": "weight stream (cudaMemcpyAsync of layers and head chunks, 2 slots)",
+                            "achieved": streamed["h2d_gbs"], "peak": pcie, "unit": "GB/s", "frac": streamed["h2d_gbs"] / pcie,
+                            "peak_source": "nominal PCIe 5.0 x16", "traffic": None,
+                            "algorithmic_bytes_per_launch": info.weight_bytes, "avg_launch_us": pass_s * 1e6}
+        line["config"]["workload"] = (f"config5: 3b Qwen2 random-init int4 g32, {B} sequences, {plen}-token prompts, "
+                                      f"{max_new} new tokens, k={k}, lookup drafter, {slots}-slot layer streaming from pinned host")
+        line["config"]["config"] = 5
+        line["dtype"] = "f32 activations, int4 weights (bf16 scales), f16 KV"
     if rank == 0:
         print(json.dumps(line), flush=True)
     batch.close()

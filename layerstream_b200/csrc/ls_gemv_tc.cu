@@ -1,4 +1,6 @@
 // Tensor-core (tcgen05) GEMV of the verify path.
+#include <algorithm>
+
 #include "ls_device.cuh"
 #include "ls_internal.h"
 
@@ -418,8 +420,10 @@ static size_t gemv_tc_smem(const QMat& w, int ksplit, int NT) {
   return (size_t)NT * maxblk * kb * 2 + (size_t)TC_STAGES * TC_THREADS * cpb * 16;
 }
 
-int gemv_tc_min_ksplit(const QMat& w, int M) {
-  const int NT = tc_nt(M);
+int gemv_tc_nt(int M, int max_nt) { return tc_nt(std::min(M, max_nt)); }
+
+int gemv_tc_min_ksplit(const QMat& w, int M, int max_nt) {
+  const int NT = gemv_tc_nt(M, max_nt);
   for (int ks = 1; ks <= 64; ks++)
     if (gemv_tc_smem(w, ks, NT) <= 190 * 1024) return ks;
   LS_THROW(-1, "matrix too wide for the tensor-core GEMV");
@@ -437,7 +441,7 @@ static void launch_tc_t(const GemvLaunch& g, cudaStream_t s) {
 
 template <int BITS, int G>
 static void launch_tc_g(const GemvLaunch& g, cudaStream_t s) {
-  switch (tc_nt(g.M)) {
+  switch (gemv_tc_nt(g.M, g.max_nt)) {
     case 16: return launch_tc_t<BITS, G, 16>(g, s);
     case 32: return launch_tc_t<BITS, G, 32>(g, s);
     case 48: return launch_tc_t<BITS, G, 48>(g, s);
@@ -448,7 +452,8 @@ static void launch_tc_g(const GemvLaunch& g, cudaStream_t s) {
 void launch_gemv_tc(const GemvLaunch& g, cudaStream_t s) {
   if (g.M <= 0) return;
   if (!gemv_tc_supported(g.w)) LS_THROW(-1, "format not supported by the tensor-core GEMV");
-  if (g.ksplit < gemv_tc_min_ksplit(g.w, g.M)) LS_THROW(-1, "tensor-core GEMV split too small for shared memory");
+  if (g.ksplit < gemv_tc_min_ksplit(g.w, g.M, g.max_nt)) LS_THROW(-1, "tensor-core GEMV split too small for shared memory");
+  if (g.ksplit > 1 && (!g.partial || !g.tickets)) LS_THROW(-1, "a split tensor-core GEMV needs partial-sum scratch");
   if (g.w.bits == 8) {
     switch (g.w.group) {
       case 16: return launch_tc_g<8, 16>(g, s);

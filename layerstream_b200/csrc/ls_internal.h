@@ -175,6 +175,7 @@ struct GemvLaunch {
   int* err = nullptr;  // set to nonzero by a kernel whose bounded wait gave up
   // split-K
   int ksplit = 1;
+  int max_nt = 64;           // tensor-core GEMV: widest token group (16, 32, 48 or 64)
   float* partial = nullptr;  // [row_ctas][ksplit][M][32]
   unsigned* tickets = nullptr;
 };
@@ -186,7 +187,8 @@ int gemv_grid_x(const QMat& w, int ksplit, int M, int num_sms);
 int gemv_mt(int M);
 // tensor-core (tcgen05) GEMV
 bool gemv_tc_supported(const QMat& w);
-int gemv_tc_min_ksplit(const QMat& w, int M);
+int gemv_tc_min_ksplit(const QMat& w, int M, int max_nt = 64);
+int gemv_tc_nt(int M, int max_nt);
 void launch_gemv_tc(const GemvLaunch& g, cudaStream_t s);
 void launch_repack(const RepackSrc& src, int bits, int group, int cols, uint8_t* data, uint16_t* scales, int rows_pad,
                    cudaStream_t s);
@@ -269,6 +271,9 @@ void launch_embed_tokens(const QMat& e, const uint32_t* tokens, int T, float* x,
 // argmax[t] over the nparts per-CTA parts of every row t (first-maximum rule); then for every
 // sequence of M rows the acceptance rule of src/spec.rs:121-125: m = longest prefix with
 // argmax[i] == tokens[i+1], next = argmax[m].
+// The same from a host-mapped table of stored rows (streaming models).
+void launch_embed_raw_tokens(const uint8_t* table, size_t row_bytes, int bits, int group, const uint32_t* tokens, float* x,
+                             int hidden, int vocab, int T, int* err, cudaStream_t s);
 void launch_batch_accept(const ArgPart* parts, int nparts, int T, int M, const uint32_t* tokens, uint32_t* argmax,
                          uint32_t* m_out, uint32_t* next_out, cudaStream_t s);
 

@@ -736,16 +736,9 @@ void launch_embed(const QMat& e, const Ctl* ctl, float* x, int hidden, int M, cu
 
 // Streaming mode: the embedding table stays in pinned host memory in the file layout; the rows of
 // the block's tokens are read through the mapped pointer (one row per token crosses the link).
-__global__ void embed_raw_kernel(const uint8_t* table, size_t row_bytes, int bits, int group, const Ctl* ctl, float* x,
-                                 int hidden, int vocab) {
-  const int t = blockIdx.x;
-  const uint32_t tok = ctl->tokens[t];
-  float* xr = x + (size_t)t * hidden;
-  if (tok >= (uint32_t)vocab) {
-    for (int c = threadIdx.x; c < hidden; c += blockDim.x) xr[c] = 0.f;
-    if (threadIdx.x == 0) const_cast<Ctl*>(ctl)->err = 2;
-    return;
-  }
+// One stored embedding row (host-mapped .lsq row format) dequantised into xr.
+__device__ __forceinline__ void embed_raw_row(const uint8_t* table, size_t row_bytes, int bits, int group, uint32_t tok,
+                                              float* xr, int hidden) {
   const uint8_t* row = table + (size_t)tok * row_bytes;
   const uint8_t* sc = row + (size_t)hidden * bits / 8;
   for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
@@ -760,6 +753,38 @@ __global__ void embed_raw_kernel(const uint8_t* table, size_t row_bytes, int bit
     }
     xr[c] = q * __uint_as_float((uint32_t)(sc[2 * g] | (sc[2 * g + 1] << 8)) << 16);
   }
+}
+
+__global__ void embed_raw_kernel(const uint8_t* table, size_t row_bytes, int bits, int group, const Ctl* ctl, float* x,
+                                 int hidden, int vocab) {
+  const int t = blockIdx.x;
+  const uint32_t tok = ctl->tokens[t];
+  float* xr = x + (size_t)t * hidden;
+  if (tok >= (uint32_t)vocab) {
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x) xr[c] = 0.f;
+    if (threadIdx.x == 0) const_cast<Ctl*>(ctl)->err = 2;
+    return;
+  }
+  embed_raw_row(table, row_bytes, bits, group, tok, xr, hidden);
+}
+
+__global__ void embed_raw_tokens_kernel(const uint8_t* table, size_t row_bytes, int bits, int group, const uint32_t* tokens,
+                                        float* x, int hidden, int vocab, int* err) {
+  const int t = blockIdx.x;
+  const uint32_t tok = tokens[t];
+  float* xr = x + (size_t)t * hidden;
+  if (tok >= (uint32_t)vocab) {
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x) xr[c] = 0.f;
+    if (threadIdx.x == 0) atomicExch(err, 2);
+    return;
+  }
+  embed_raw_row(table, row_bytes, bits, group, tok, xr, hidden);
+}
+
+void launch_embed_raw_tokens(const uint8_t* table, size_t row_bytes, int bits, int group, const uint32_t* tokens, float* x,
+                             int hidden, int vocab, int T, int* err, cudaStream_t s) {
+  embed_raw_tokens_kernel<<<T, 256, 0, s>>>(table, row_bytes, bits, group, tokens, x, hidden, vocab, err);
+  LS_CUDA(cudaGetLastError());
 }
 
 void launch_embed_raw(const uint8_t* table, size_t row_bytes, int bits, int group, const Ctl* ctl, float* x, int hidden,

@@ -98,10 +98,18 @@ bool use_tc(const QMat& w) {
 
 // Tensor-core GEMV: K-split and grid. Aim for ~4 CTAs per SM over (tiles x slices x token groups),
 // keep at least two 64-wide K blocks per slice, never fewer slices than shared memory needs.
-void choose_tc(const QMat& w, int M, int num_sms, bool argmax, int* ksplit, int* grid_x) {
+// The argmax epilogue needs whole dot products (no K split): it narrows the token groups instead
+// until one K slice of staged activations fits (max_nt, when given, receives the width).
+void choose_tc(const QMat& w, int M, int num_sms, bool argmax, int* ksplit, int* grid_x, int* max_nt = nullptr) {
+  int cap = 64;
+  if (argmax) {
+    while (cap > 16 && gemv_tc_min_ksplit(w, M, cap) > 1) cap -= 16;
+    if (gemv_tc_min_ksplit(w, M, cap) > 1) LS_THROW(LS_ERR_ARG, "matrix too wide for the LM-head GEMV");
+  }
+  if (max_nt) *max_nt = cap;
+  const int NT = gemv_tc_nt(M, cap);
   const int tiles128 = (w.rows_pad / 32 + 3) / 4;
-  const int nz = (M + ((M <= 16) ? 16 : (M <= 32) ? 32 : (M <= 48) ? 48 : 64) - 1) /
-                 ((M <= 16) ? 16 : (M <= 32) ? 32 : (M <= 48) ? 48 : 64);
+  const int nz = (M + NT - 1) / NT;
   const int kb = (w.bits == 4 && w.group > 64) ? w.group : 64;
   const int nblk = w.cols / kb;
   const int target = 4 * num_sms;
@@ -111,7 +119,7 @@ void choose_tc(const QMat& w, int M, int num_sms, bool argmax, int* ksplit, int*
     ks = std::min(ks, std::max(1, nblk / 2));
     ks = std::min(ks, 32);
   }
-  ks = std::max(ks, gemv_tc_min_ksplit(w, M));
+  ks = std::max(ks, gemv_tc_min_ksplit(w, M, cap));
   ks = std::min(ks, nblk);
   *ksplit = ks;
   *grid_x = std::max(1, std::min(tiles128, (target + ks * nz - 1) / (ks * nz)));
@@ -718,7 +726,7 @@ struct LsModel {
     g.tickets = tickets;
     g.err = &ctl->err;
     if (use_tc(w)) {
-      choose_tc(w, M, num_sms, epi == EPI_ARGMAX, &g.ksplit, &g.grid_x);
+      choose_tc(w, M, num_sms, epi == EPI_ARGMAX, &g.ksplit, &g.grid_x, &g.max_nt);
       launch_gemv_tc(g, s);
       return;
     }
@@ -750,7 +758,7 @@ struct LsModel {
     g.logits_stride = (int)cfg.vocab;
     g.err = &ctl->err;
     if (use_tc(w)) {
-      choose_tc(w, n, num_sms, true, &g.ksplit, &g.grid_x);
+      choose_tc(w, n, num_sms, true, &g.ksplit, &g.grid_x, &g.max_nt);
       launch_gemv_tc(g, s);
       return g.grid_x;
     }
@@ -818,14 +826,29 @@ struct LsModel {
       prof_end(pp, stream);
       return;
     }
-    // streaming: items are layers 0..L-1 then head chunks; each slot is refilled by a copy on the
-    // side stream once the compute that used it has finished (src/provider.rs:234-268)
+    // streaming (src/provider.rs:234-268)
     launch_embed_raw(host_embed_dev, cfg.embed_row_bytes(), cfg.embed_format.bits, cfg.embed_format.group, ctl, x, h,
                      (int)V, T, stream);
     bytes_read += (uint64_t)T * cfg.embed_row_bytes();
-    const size_t L = cfg.layers;
+    int part_tiles = 0;
+    stream_weights(
+        n_logits > 0, stream, [&](const LayerW& W, size_t l) { layer_compute(W, l, T, stream); },
+        [&](const QMat& hq, int first, int rows) {
+          part_tiles += head(hq, x + (size_t)(T - n_logits) * h, n_logits, want_logits, first, rows, part_tiles, 0, 0, stream);
+        });
+    if (n_logits > 0) launch_argmax_finalize(arg_parts, part_tiles, n_logits, ctl, stream);
+    else launch_advance(ctl, stream);
+  }
+
+  // Streams the weights through the HBM slots: items are layers 0..L-1, then (with_head) the LM
+  // head in chunks of kHeadRows rows; each slot is refilled by a copy on the side stream once the
+  // compute that used it has finished (src/provider.rs:234-268). layer_fn(planes, l) and
+  // head_fn(planes, first_row, rows) enqueue the compute on stream cs.
+  template <class LF, class HF>
+  void stream_weights(bool with_head, cudaStream_t cs, LF layer_fn, HF head_fn) {
+    const size_t V = cfg.vocab, L = cfg.layers;
     const size_t chunk_rows = std::min<size_t>(kHeadRows, V);
-    const size_t nchunks = n_logits > 0 ? (V + chunk_rows - 1) / chunk_rows : 0;
+    const size_t nchunks = with_head ? (V + chunk_rows - 1) / chunk_rows : 0;
     const size_t items = L + nchunks;
     const size_t lt = file.layout.total, rb = cfg.embed_row_bytes();
     size_t issued = 0;
@@ -846,30 +869,24 @@ struct LsModel {
       LS_CUDA(cudaEventRecord(ev_loaded[s], copy_stream));
       bytes_read += n;
     };
-    const int vtiles_total = pad32((int)V) / 32;
-    (void)vtiles_total;
-    int part_tiles = 0;
     for (size_t it = 0; it < items; it++) {
       while (issued < items && issued < it + (size_t)slots) issue(issued++);
       const int s = (int)(it % slots);
-      LS_CUDA(cudaStreamWaitEvent(stream, ev_loaded[s], 0));
+      LS_CUDA(cudaStreamWaitEvent(cs, ev_loaded[s], 0));
       if (it < L) {
-        repack_layer(raw_slot[s], layers[s], stream);
-        LS_CUDA(cudaEventRecord(ev_free[s], stream));  // the raw slot may be refilled now
-        layer_compute(layers[s], it, T, stream);
+        repack_layer(raw_slot[s], layers[s], cs);
+        LS_CUDA(cudaEventRecord(ev_free[s], cs));  // the raw slot may be refilled now
+        layer_fn(layers[s], it);
       } else {
         const size_t c = it - L, first = c * chunk_rows, rows = std::min(chunk_rows, V - first);
         QMat hq = head_slot[s];
         hq.rows = (int)rows;
         hq.rows_pad = pad32((int)rows);
-        repack_embed_rows(raw_slot[s], 0, (int)rows, hq, stream);
-        LS_CUDA(cudaEventRecord(ev_free[s], stream));
-        part_tiles += head(hq, x + (size_t)(T - n_logits) * h, n_logits, want_logits, (int)first, (int)rows, part_tiles, 0, 0,
-                           stream);
+        repack_embed_rows(raw_slot[s], 0, (int)rows, hq, cs);
+        LS_CUDA(cudaEventRecord(ev_free[s], cs));
+        head_fn(hq, (int)first, (int)rows);
       }
     }
-    if (n_logits > 0) launch_argmax_finalize(arg_parts, part_tiles, n_logits, ctl, stream);
-    else launch_advance(ctl, stream);
   }
 
   void run_pass(int T, int n_logits, bool want_logits) {
@@ -1171,7 +1188,6 @@ struct LsBatch {
   }
 
   LsBatch(LsModel* model, size_t batch, size_t ctx, size_t block) : m(model), B(batch), max_ctx(ctx), max_block(block) {
-    if (m->mode != LS_MODE_RESIDENT) LS_THROW(LS_ERR_ARG, "batches need a resident model");
     if (B == 0 || B > 4096) LS_THROW(LS_ERR_ARG, "batch must be in 1..4096");
     if (max_block == 0 || max_block > (size_t)kMaxDraft + 1) LS_THROW(LS_ERR_ARG, "the verify block holds 1..33 tokens");
     if (max_ctx < 2 || max_ctx > (1u << 20)) LS_THROW(LS_ERR_ARG, "max_ctx must be in 2..2^20");
@@ -1198,7 +1214,7 @@ struct LsBatch {
       for (const QMat* w : {&W.qkv, &W.o, &W.gu, &W.down}) tc_scratch(*w, rows, &pf, &tk);
     partial = dalloc<float>(pf);
     tickets = dalloc<unsigned>(tk);
-    parts = dalloc<ArgPart>((size_t)(m->embed.rows_pad / 128 + 1) * max_rows);
+    parts = dalloc<ArgPart>((size_t)(pad32((int)c.vocab) / 128 + c.vocab / kHeadRows + 2) * max_rows);
     att_part = dalloc<float>(c.heads * (size_t)16 * max_rows * (c.head_dim + 2));
     att_tickets = dalloc<unsigned>(B * c.heads);
     d_tok = dalloc<uint32_t>(max_rows);
@@ -1247,10 +1263,11 @@ struct LsBatch {
     LS_THROW(LS_ERR_ARG, "batches need a weight format the tensor-core GEMV supports");
   }
 
-  // Argmax parts of the LM head over M rows of x (final RMSNorm folded in); returns the CTA count.
-  int head(const float* xin, int M) {
+  // Argmax parts of the LM head rows [first, first + rows) (planes w) over M rows of x (final
+  // RMSNorm folded in), written after part_off earlier parts; returns this launch's CTA count.
+  int head(const QMat& w, int first, int rows, const float* xin, int M, int part_off) {
     GemvLaunch g;
-    g.w = m->embed;
+    g.w = w;
     g.x = xin;
     g.x_stride = (int)m->cfg.hidden;
     g.M = M;
@@ -1258,11 +1275,13 @@ struct LsBatch {
     g.eps = m->cfg.eps;
     g.epi = EPI_ARGMAX;
     g.arg_parts = parts;
-    g.n_valid_rows = (int)m->cfg.vocab;
+    g.n_valid_rows = rows;
+    g.row_offset = first;
+    g.part_tile_offset = part_off;
     g.finalize = 0;
     g.err = d_err;
-    if (!use_tc(m->embed)) LS_THROW(LS_ERR_ARG, "batches need a weight format the tensor-core GEMV supports");
-    choose_tc(m->embed, M, m->num_sms, true, &g.ksplit, &g.grid_x);
+    if (!use_tc(w)) LS_THROW(LS_ERR_ARG, "batches need a weight format the tensor-core GEMV supports");
+    choose_tc(w, M, m->num_sms, true, &g.ksplit, &g.grid_x, &g.max_nt);
     launch_gemv_tc(g, stream);
     return g.grid_x;
   }
@@ -1291,10 +1310,16 @@ struct LsBatch {
     LS_CUDA(cudaMemcpyAsync(d_pos0, h_pos0, ns * 4, cudaMemcpyHostToDevice, stream));
     LS_CUDA(cudaMemsetAsync(d_err, 0, 4, stream));
     h2d_bytes += T * 4 + ns * 4;
-    launch_embed_tokens(m->embed, d_tok, (int)T, x, h, (int)c.vocab, d_err, stream);
+    const bool streamed = m->mode != LS_MODE_RESIDENT;
+    if (streamed) {
+      launch_embed_raw_tokens(m->host_embed_dev, c.embed_row_bytes(), c.embed_format.bits, c.embed_format.group, d_tok, x, h,
+                              (int)c.vocab, (int)T, d_err, stream);
+      m->bytes_read += T * c.embed_row_bytes();
+    } else {
+      launch_embed_tokens(m->embed, d_tok, (int)T, x, h, (int)c.vocab, d_err, stream);
+    }
     const int slots = (int)std::max<size_t>(1, std::min<size_t>(16, (maxpos + M + 63) / 64));
-    for (size_t l = 0; l < c.layers; l++) {
-      const LayerW& W = m->layers[l];
+    auto layer_fn = [&](const LayerW& W, size_t l) {
       gemv(W.qkv, x, h, (int)T, EPI_BIAS_STORE, qkv, QS, W.in_norm, W.qkv_bias);
       AttnLaunch a;
       a.qkv = qkv;
@@ -1319,14 +1344,20 @@ struct LsBatch {
       gemv(W.o, attn, h, (int)T, EPI_RESID, x, h, nullptr, nullptr);
       gemv(W.gu, x, h, (int)T, EPI_SWIGLU, hbuf, I, W.post_norm, nullptr);
       gemv(W.down, hbuf, I, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+    };
+    // head over all T rows (verify) or the last row (prefill end)
+    const float* hx = head_mode == 2 ? x + (T - 1) * h : x;
+    const int hM = head_mode == 2 ? 1 : (int)T;
+    int nparts = 0;
+    auto head_fn = [&](const QMat& w, int first, int rows) { nparts += head(w, first, rows, hx, hM, nparts); };
+    if (streamed) {
+      m->stream_weights(head_mode != 0, stream, layer_fn, head_fn);
+    } else {
+      for (size_t l = 0; l < c.layers; l++) layer_fn(m->layers[l], l);
+      if (head_mode) head_fn(m->embed, 0, (int)c.vocab);
     }
-    if (head_mode == 1) {
-      const int np = head(x, (int)T);
-      launch_batch_accept(parts, np, (int)T, M, d_tok, d_argmax, d_m, d_next, stream);
-    } else if (head_mode == 2) {
-      const int np = head(x + (T - 1) * h, 1);
-      launch_batch_accept(parts, np, 1, 1, d_tok, d_argmax, d_m, d_next, stream);
-    }
+    if (head_mode == 1) launch_batch_accept(parts, nparts, (int)T, M, d_tok, d_argmax, d_m, d_next, stream);
+    else if (head_mode == 2) launch_batch_accept(parts, nparts, 1, 1, d_tok, d_argmax, d_m, d_next, stream);
     if (head_mode) {
       const size_t nres = head_mode == 1 ? ns : 1;
       LS_CUDA(cudaMemcpyAsync(h_m, d_m, nres * 4, cudaMemcpyDeviceToHost, stream));

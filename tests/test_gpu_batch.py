@@ -122,5 +122,45 @@ def test_bad_batch_requests_are_errors(tiny):
         b.prefill(0, list(range(1, 18)))  # context overflow
     with pytest.raises(ls.LayerstreamError):
         b.verify(np.zeros((2, 4), np.uint32))  # block longer than max_block
-    with pytest.raises(ls.LayerstreamError):
-        ls.Batch(ls.Model(p, mode="stream", slots=2, max_ctx=64), 2, max_ctx=16, max_block=3)
+
+
+@pytest.mark.parametrize("slots", [1, 2])
+def test_a_batch_over_streamed_weights_decodes_like_the_resident_one(tiny, slots):
+    # config 5 (a): the layers and head chunks stream through HBM slots; the batch's tokens and the
+    # streamed bytes follow tests/quant.rs:232-248 per pass
+    p = tiny[(4, 32)]
+    prompts = np.array(PROMPTS, np.uint32)
+    want, _ = ls.Batch(ls.Model(p, max_ctx=128), len(PROMPTS), max_ctx=64, max_block=5).spec(prompts, 16, 4)
+    sm = ls.Model(p, mode="stream", slots=slots, max_ctx=128)
+    b = ls.Batch(sm, len(PROMPTS), max_ctx=64, max_block=5)
+    got, st = b.spec(prompts, 16, 4)
+    assert got == want
+    info = sm.info
+    per_pass = info.layers * info.layer_bytes
+    head = info.vocab * info.embed_row_bytes
+    passes = b.report()["passes"]
+    prefill_passes = len(PROMPTS)  # one chunk per prompt, each with the head on its last row
+    verify_passes = st["target_passes"]
+    rows = len(PROMPTS) * len(PROMPTS[0]) + verify_passes * len(PROMPTS) * 5
+    assert passes == prefill_passes + verify_passes
+    assert sm.report()["bytes_read"] == passes * (per_pass + head) + rows * info.embed_row_bytes
+
+
+def test_a_wide_model_verifies_a_large_batch_without_splitting_the_head():
+    # hidden 2048 (the 3B width): the staged activations of 40 verify rows outgrow one K slice of
+    # the LM-head GEMV, whose argmax epilogue needs whole dot products; the head narrows its token
+    # groups instead. Every sequence must still decode as it does alone.
+    from layerstream_b200 import synth
+
+    synth.SHAPES["wide-test"] = dict(hidden_size=2048, num_attention_heads=16, num_key_value_heads=2,
+                                     intermediate_size=256, num_hidden_layers=1, vocab_size=1000, rope_theta=1e6,
+                                     max_position_embeddings=4096)
+    d = F.TempDir("gpu-wide").path
+    synth.write_random_model(d, "wide-test", 3)
+    p = os.path.join(d, "w.lsq")
+    ls.quantize_model(d, p, body=(4, 32), embed=(4, 32))
+    prompts = [[(7 * i + 13 * s) % 1000 for i in range(12)] for s in range(8)]
+    want = [plain_greedy(ls.Model(p, max_ctx=64), pr, 10) for pr in prompts]
+    b = ls.Batch(ls.Model(p, max_ctx=64), 8, max_ctx=64, max_block=5)
+    got, _ = b.spec(np.array(prompts, np.uint32), 10, 4)
+    assert got == want
