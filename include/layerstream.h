@@ -163,6 +163,17 @@ int ls_quantize_model(const char *src_dir, const char *out_path, int bits, int g
  * and runs all B*M rows through the model at once. */
 typedef struct LsBatch LsBatch;
 int ls_batch_open(LsModel *m, uint64_t batch, uint64_t max_ctx, uint64_t max_block, LsBatch **out);
+/* Tensor parallelism (config 5b), one model split over `world` GPUs: rank `rank`
+ * (one process or thread per GPU, its model opened resident on its own device) keeps its q heads
+ * (and the kv heads they read), a 64-column-aligned slice of the intermediate dimension and a slice
+ * of the vocabulary; O and down are row-parallel with a sum all-reduce, the LM head is
+ * vocabulary-parallel with an all-gather of each rank's (max, first index) per row. Every rank
+ * makes the same calls with the same inputs and gets the same tokens. The ranks share one NCCL
+ * unique id (ls_tp_unique_id on one rank, passed to the others by the host); opening is
+ * collective. NCCL (libnccl.so.2) is loaded at the first tensor-parallel call. */
+int ls_tp_unique_id(uint8_t *out, size_t cap); /* cap >= 128 */
+int ls_batch_open_tp(LsModel *m, uint64_t batch, uint64_t max_ctx, uint64_t max_block, int rank, int world,
+                     const uint8_t *id, LsBatch **out);
 int ls_batch_free(LsBatch *b);
 int ls_batch_pos(const LsBatch *b, uint64_t seq, uint64_t *pos);
 int ls_batch_truncate(LsBatch *b, uint64_t seq, uint64_t pos);

@@ -86,6 +86,9 @@ _SIGS = {
     "ls_qgemv_bytes": (C.c_uint64, [C.c_int, C.c_int, C.c_uint64, C.c_uint64, C.c_uint64]),
     "ls_batch_open": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64, C.POINTER(C.c_void_p)]),
     "ls_batch_free": (C.c_int, [C.c_void_p]),
+    "ls_tp_unique_id": (C.c_int, [C.c_void_p, C.c_size_t]),
+    "ls_batch_open_tp": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_int, C.c_int, C.c_void_p,
+                                   C.POINTER(C.c_void_p)]),
     "ls_batch_pos": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_uint64)]),
     "ls_batch_truncate": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64]),
     "ls_batch_prefill": (C.c_int, [C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64, C.POINTER(C.c_uint32)]),
@@ -244,9 +247,16 @@ class Batch:
     """B independent sequences sharing one resident model's weights (configs 4 and 5): per-sequence
     K/V caches, one verify pass for all sequences' [B][M] blocks."""
 
-    def __init__(self, model: Model, batch: int, max_ctx: int, max_block: int):
+    def __init__(self, model: Model, batch: int, max_ctx: int, max_block: int, tp=None):
+        """tp = (rank, world, id): this rank's shard of a tensor-parallel split (id from tp_unique_id
+        on one rank, the same bytes on every rank; opening is collective)."""
         h = C.c_void_p()
-        _check(lib().ls_batch_open(model._h, batch, max_ctx, max_block, C.byref(h)))
+        if tp is None:
+            _check(lib().ls_batch_open(model._h, batch, max_ctx, max_block, C.byref(h)))
+        else:
+            rank, world, uid = tp
+            buf = (C.c_uint8 * len(uid)).from_buffer_copy(bytes(uid))
+            _check(lib().ls_batch_open_tp(model._h, batch, max_ctx, max_block, rank, world, buf, C.byref(h)))
         self._h, self.model, self.batch, self.max_ctx, self.max_block = h, model, batch, max_ctx, max_block
 
     def pos(self, seq: int) -> int:
@@ -293,6 +303,13 @@ class Batch:
 
     def __del__(self):
         self.close()
+
+
+def tp_unique_id() -> bytes:
+    """NCCL unique id for a tensor-parallel group (made on one rank, shared with the others)."""
+    buf = (C.c_uint8 * 128)()
+    _check(lib().ls_tp_unique_id(buf, 128))
+    return bytes(buf)
 
 
 def quantize_model(src_dir: str, out_path: str, body=(8, 64), embed=None, clip: bool = True, device: int = 0) -> float:

@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "liblayerstream_b200.so")
-SOURCES = ["ls_pass.cu", "ls_noalloc.cu", "ls_gemv_tc.cu", "ls_kernels.cu", "ls_model.cu", "ls_format.cpp"]
+SOURCES = ["ls_pass.cu", "ls_noalloc.cu", "ls_gemv_tc.cu", "ls_kernels.cu", "ls_model.cu", "ls_format.cpp", "ls_nccl.cpp"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
@@ -46,7 +46,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     for src, p in procs:
         if p.wait() != 0:
             raise RuntimeError(f"nvcc failed on {src}")
-    cmd = ["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", OUT, *objs]
+    cmd = ["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", OUT, *objs, "-ldl"]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <nccl.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -271,11 +272,26 @@ void launch_embed_tokens(const QMat& e, const uint32_t* tokens, int T, float* x,
 // argmax[t] over the nparts per-CTA parts of every row t (first-maximum rule); then for every
 // sequence of M rows the acceptance rule of src/spec.rs:121-125: m = longest prefix with
 // argmax[i] == tokens[i+1], next = argmax[m].
+// best[t] = first maximum of row t over nparts parts; x += y over n floats.
+void launch_row_best(const ArgPart* parts, int nparts, int T, ArgPart* best, cudaStream_t s);
+void launch_add(float* x, const float* y, size_t n, cudaStream_t s);
 // The same from a host-mapped table of stored rows (streaming models).
 void launch_embed_raw_tokens(const uint8_t* table, size_t row_bytes, int bits, int group, const uint32_t* tokens, float* x,
                              int hidden, int vocab, int T, int* err, cudaStream_t s);
 void launch_batch_accept(const ArgPart* parts, int nparts, int T, int M, const uint32_t* tokens, uint32_t* argmax,
                          uint32_t* m_out, uint32_t* next_out, cudaStream_t s);
+
+// ---- NCCL, loaded at run time (ls_nccl.cpp) ----
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+const NcclApi& nccl_api();  // throws when libnccl.so.2 cannot be loaded
+void nccl_check(ncclResult_t r, const char* what);
 
 // ---- allocation-free GEMV (ls_noalloc.cu) ----
 void qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t rows, uint64_t cols, const float* x_dev,

@@ -17,6 +17,7 @@
 #include <cuda_fp16.h>
 #include <math_constants.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 
@@ -704,6 +705,39 @@ __global__ void batch_argmax_kernel(const ArgPart* parts, int nparts, int T, uin
   }
   warp_argmax(v, idx);
   if (lane == 0) argmax[t] = idx;
+}
+
+// One warp per row: the first maximum over the per-CTA parts, kept as a (value, index) part
+// (tensor-parallel heads gather these across ranks).
+__global__ void row_best_kernel(const ArgPart* parts, int nparts, int T, ArgPart* best) {
+  const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= T) return;
+  float v = -CUDART_INF_F;
+  uint32_t idx = 0xffffffffu;
+  for (int k = lane; k < nparts; k += 32) {
+    const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(parts + (size_t)k * T + t));
+    const float pv = __uint_as_float(raw.x);
+    if (arg_better(pv, raw.y, v, idx)) {
+      v = pv;
+      idx = raw.y;
+    }
+  }
+  warp_argmax(v, idx);
+  if (lane == 0) best[t] = ArgPart{v, idx};
+}
+
+void launch_row_best(const ArgPart* parts, int nparts, int T, ArgPart* best, cudaStream_t s) {
+  row_best_kernel<<<(T + 7) / 8, 256, 0, s>>>(parts, nparts, T, best);
+  LS_CUDA(cudaGetLastError());
+}
+
+__global__ void add_rows_kernel(float* __restrict__ x, const float* __restrict__ y, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) x[i] += y[i];
+}
+
+void launch_add(float* x, const float* y, size_t n, cudaStream_t s) {
+  add_rows_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 2368), 256, 0, s>>>(x, y, n);
+  LS_CUDA(cudaGetLastError());
 }
 
 // src/spec.rs:121-125 per sequence: m = longest prefix of guesses the target agrees with, next =

@@ -1146,6 +1146,18 @@ static void speculative_greedy(LsModel& target, LsModel* draft, const uint32_t* 
 struct LsBatch {
   LsModel* m = nullptr;
   size_t B = 0, max_ctx = 0, max_rows = 0, max_block = 0;
+  // Per-rank compute dimensions: the whole model, or this rank's tensor-parallel shard (its q
+  // heads, the kv heads they read, a slice of the intermediate dimension).
+  struct Dims {
+    int heads, kv_heads, q_dim, kv_dim, inter;
+  } dm{};
+  int tp_rank = 0, tp_world = 1, tp_v0 = 0;
+  std::vector<LayerW> tp_layers;
+  QMat tp_head;  // this rank's vocabulary rows of the tied head (a view into the model's table)
+  ncclComm_t comm = nullptr;
+  float* ybuf = nullptr;                            // partial sums of row-parallel projections
+  ArgPart *tp_best = nullptr, *tp_all = nullptr;    // per-row best of this rank / of all ranks
+  const LayerW& layer(size_t l) const { return tp_world > 1 ? tp_layers[l] : m->layers[l]; }
   size_t layer_stride = 0, seq_stride = 0;  // elements: one layer's cache, one sequence's cache
   cudaStream_t stream = nullptr;
   std::vector<void*> dev_allocs, host_allocs;
@@ -1187,16 +1199,114 @@ struct LsBatch {
     *tks = std::max(*tks, nz * tiles32);
   }
 
-  LsBatch(LsModel* model, size_t batch, size_t ctx, size_t block) : m(model), B(batch), max_ctx(ctx), max_block(block) {
+  // A slice of a tiled matrix into new planes: row tiles [t0, t0 + nt) x columns [c0, c0 + nc).
+  QMat slice(const QMat& src, int t0, int nt, int c0, int nc) {
+    WeightFormat f;
+    f.bits = src.bits;
+    f.group = src.group;
+    uint8_t* p = dalloc<uint8_t>(qmat_bytes(nt * 32, nc, f));
+    QMat d = carve(p, nt * 32, nc, f);
+    const size_t cw = 128 / src.bits;  // columns per 16-byte chunk
+    LS_CUDA(cudaMemcpy2DAsync(const_cast<uint8_t*>(d.data), (size_t)d.chunks() * 512,
+                              src.data + ((size_t)t0 * src.chunks() + c0 / cw) * 512, (size_t)src.chunks() * 512,
+                              (size_t)d.chunks() * 512, nt, cudaMemcpyDeviceToDevice, stream));
+    LS_CUDA(cudaMemcpy2DAsync(const_cast<uint16_t*>(d.scales), (size_t)d.groups() * 64,
+                              src.scales + ((size_t)t0 * src.groups() + c0 / src.group) * 32, (size_t)src.groups() * 64,
+                              (size_t)d.groups() * 64, nt, cudaMemcpyDeviceToDevice, stream));
+    return d;
+  }
+  // Rows [r0, r0 + n) of planes (32-row aligned) appended into d's row tiles from tile dt.
+  void copy_rows(QMat& d, int dt, const QMat& src, int r0, int n) {
+    const int nt = n / 32, st = r0 / 32;
+    LS_CUDA(cudaMemcpyAsync(const_cast<uint8_t*>(d.data) + (size_t)dt * d.chunks() * 512, src.data + (size_t)st * src.chunks() * 512,
+                            (size_t)nt * src.chunks() * 512, cudaMemcpyDeviceToDevice, stream));
+    LS_CUDA(cudaMemcpyAsync(const_cast<uint16_t*>(d.scales) + (size_t)dt * d.groups() * 32,
+                            src.scales + (size_t)st * src.groups() * 32, (size_t)nt * src.groups() * 64, cudaMemcpyDeviceToDevice,
+                            stream));
+  }
+
+  // This rank's shard of every layer (column-parallel QKV by q heads and gate/up by intermediate
+  // slice; row-parallel O and down) and of the head's vocabulary, copied out of the resident
+  // planes on the device.
+  void make_shard(const uint8_t* nccl_id) {
+    const Config& c = m->cfg;
+    const int R = tp_world, r = tp_rank, hd = (int)c.head_dim, h = (int)c.hidden;
+    if (m->mode != LS_MODE_RESIDENT) LS_THROW(LS_ERR_ARG, "tensor parallelism needs a resident model");
+    if (c.heads % R) LS_THROW(LS_ERR_ARG, "the q heads do not split evenly over the ranks");
+    const int hl = (int)c.heads / R, group = (int)(c.heads / c.kv_heads);
+    int kvl, kv0;
+    if (R <= (int)c.kv_heads) {
+      if (c.kv_heads % R) LS_THROW(LS_ERR_ARG, "the kv heads do not split evenly over the ranks");
+      kvl = (int)c.kv_heads / R;
+      kv0 = r * kvl;
+    } else {
+      if (R % c.kv_heads || group % hl) LS_THROW(LS_ERR_ARG, "each rank's q heads must share one kv head");
+      kvl = 1;
+      kv0 = r * hl / group;
+    }
+    const int nb = (int)c.inter / 64;
+    const int i0 = 64 * (r * nb / R), i1 = 64 * ((r + 1) * nb / R);
+    if (c.inter % 64 || i1 <= i0) LS_THROW(LS_ERR_ARG, "the intermediate dimension does not split over the ranks in 64s");
+    dm = Dims{hl, kvl, hl * hd, kvl * hd, i1 - i0};
+    if (dm.q_dim % 64) LS_THROW(LS_ERR_ARG, "each rank's q width must be a multiple of 64");
+    const int gq = m->layers[0].o.group;
+    if (dm.q_dim % gq || (i1 - i0) % gq || (r * dm.q_dim) % gq || i0 % gq)
+      LS_THROW(LS_ERR_ARG, "each rank's column slice of O and down must hold whole quantization groups");
+    const int QF = (int)(c.heads * c.head_dim), KVf = (int)c.kv_dim(), QSl = dm.q_dim + 2 * dm.kv_dim;
+    tp_layers.resize(c.layers);
+    for (size_t l = 0; l < c.layers; l++) {
+      const LayerW& F = m->layers[l];
+      LayerW& W = tp_layers[l];
+      WeightFormat f;
+      f.bits = F.qkv.bits;
+      f.group = F.qkv.group;
+      uint8_t* qp = dalloc<uint8_t>(qmat_bytes(QSl, h, f));
+      W.qkv = carve(qp, QSl, h, f);
+      copy_rows(W.qkv, 0, F.qkv, r * dm.q_dim, dm.q_dim);
+      copy_rows(W.qkv, dm.q_dim / 32, F.qkv, QF + kv0 * hd, dm.kv_dim);
+      copy_rows(W.qkv, (dm.q_dim + dm.kv_dim) / 32, F.qkv, QF + KVf + kv0 * hd, dm.kv_dim);
+      W.o = slice(F.o, 0, F.o.rows_pad / 32, r * dm.q_dim, dm.q_dim);
+      W.o.rows = F.o.rows;
+      W.gu = slice(F.gu, i0 / 16, (i1 - i0) / 16, 0, h);  // a tile holds 16 gate rows then the same 16 up rows
+      W.gu.rows = 2 * (i1 - i0);
+      W.down = slice(F.down, 0, F.down.rows_pad / 32, i0, i1 - i0);
+      W.down.rows = F.down.rows;
+      W.in_norm = F.in_norm;
+      W.post_norm = F.post_norm;
+      W.qkv_bias = dalloc<uint16_t>(QSl);
+      LS_CUDA(cudaMemcpyAsync(W.qkv_bias, F.qkv_bias + r * dm.q_dim, dm.q_dim * 2, cudaMemcpyDeviceToDevice, stream));
+      LS_CUDA(cudaMemcpyAsync(W.qkv_bias + dm.q_dim, F.qkv_bias + QF + kv0 * hd, dm.kv_dim * 2, cudaMemcpyDeviceToDevice, stream));
+      LS_CUDA(cudaMemcpyAsync(W.qkv_bias + dm.q_dim + dm.kv_dim, F.qkv_bias + QF + KVf + kv0 * hd, dm.kv_dim * 2,
+                              cudaMemcpyDeviceToDevice, stream));
+    }
+    const int tiles = pad32((int)c.vocab) / 32, t0 = r * tiles / R, t1 = (r + 1) * tiles / R;
+    tp_v0 = 32 * t0;
+    tp_head = m->embed;
+    tp_head.data += (size_t)t0 * m->embed.chunks() * 512;
+    tp_head.scales += (size_t)t0 * m->embed.groups() * 32;
+    tp_head.rows = std::min((int)c.vocab, 32 * t1) - tp_v0;
+    tp_head.rows_pad = 32 * (t1 - t0);
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof id);
+    nccl_check(nccl_api().comm_init_rank(&comm, R, id, r), "ncclCommInitRank");
+  }
+
+  LsBatch(LsModel* model, size_t batch, size_t ctx, size_t block, int rank = 0, int world = 1,
+          const uint8_t* nccl_id = nullptr)
+      : m(model), B(batch), max_ctx(ctx), max_block(block), tp_rank(rank), tp_world(world) {
     if (B == 0 || B > 4096) LS_THROW(LS_ERR_ARG, "batch must be in 1..4096");
     if (max_block == 0 || max_block > (size_t)kMaxDraft + 1) LS_THROW(LS_ERR_ARG, "the verify block holds 1..33 tokens");
     if (max_ctx < 2 || max_ctx > (1u << 20)) LS_THROW(LS_ERR_ARG, "max_ctx must be in 2..2^20");
     const Config& c = m->cfg;
-    const size_t L = c.layers, kv = c.kv_dim(), h = c.hidden, I = c.inter, QS = h + 2 * kv;
+    if (tp_world < 1 || tp_rank < 0 || tp_rank >= tp_world) LS_THROW(LS_ERR_ARG, "rank must be in 0..world-1");
+    if (tp_world > 1 && !nccl_id) LS_THROW(LS_ERR_ARG, "a tensor-parallel batch needs the NCCL unique id");
     max_rows = std::max<size_t>(kMaxT, B * max_block);
     if (max_rows > 8192) LS_THROW(LS_ERR_ARG, "batch x block exceeds 8192 rows per pass");
     LS_CUDA(cudaSetDevice(m->device));
     LS_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    dm = Dims{(int)c.heads, (int)c.kv_heads, (int)(c.heads * c.head_dim), (int)c.kv_dim(), (int)c.inter};
+    if (tp_world > 1) make_shard(nccl_id);
+    const size_t L = c.layers, kv = dm.kv_dim, h = c.hidden, I = dm.inter, QS = dm.q_dim + 2 * kv;
     layer_stride = kv * max_ctx;
     seq_stride = L * layer_stride;
     kc = dalloc<uint16_t>(B * seq_stride);
@@ -1206,17 +1316,22 @@ struct LsBatch {
     LS_CUDA(cudaMemcpyAsync(rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, stream));
     x = dalloc<float>(max_rows * h);
     qkv = dalloc<float>(max_rows * QS);
-    attn = dalloc<float>(max_rows * h);
+    attn = dalloc<float>(max_rows * dm.q_dim);
     hbuf = dalloc<float>(max_rows * I);
+    if (tp_world > 1) {
+      ybuf = dalloc<float>(max_rows * h);
+      tp_best = dalloc<ArgPart>(max_rows);
+      tp_all = dalloc<ArgPart>((size_t)tp_world * max_rows);
+    }
     size_t pf = 0, tk = 0;
-    const LayerW& W = m->layers[0];
+    const LayerW& W = layer(0);
     for (int rows = 1; rows <= (int)max_rows; rows++)
       for (const QMat* w : {&W.qkv, &W.o, &W.gu, &W.down}) tc_scratch(*w, rows, &pf, &tk);
     partial = dalloc<float>(pf);
     tickets = dalloc<unsigned>(tk);
     parts = dalloc<ArgPart>((size_t)(pad32((int)c.vocab) / 128 + c.vocab / kHeadRows + 2) * max_rows);
-    att_part = dalloc<float>(c.heads * (size_t)16 * max_rows * (c.head_dim + 2));
-    att_tickets = dalloc<unsigned>(B * c.heads);
+    att_part = dalloc<float>(dm.heads * (size_t)16 * max_rows * (c.head_dim + 2));
+    att_tickets = dalloc<unsigned>(B * dm.heads);
     d_tok = dalloc<uint32_t>(max_rows);
     d_argmax = dalloc<uint32_t>(max_rows);
     d_m = dalloc<uint32_t>(B);
@@ -1234,6 +1349,7 @@ struct LsBatch {
   ~LsBatch() {
     cudaSetDevice(m->device);
     if (stream) cudaStreamSynchronize(stream);
+    if (comm) nccl_api().comm_destroy(comm);
     for (void* p : dev_allocs) cudaFree(p);
     for (void* p : host_allocs) cudaFreeHost(p);
     if (stream) cudaStreamDestroy(stream);
@@ -1289,9 +1405,16 @@ struct LsBatch {
   // One pass over sequences [s0, s0 + ns), M rows each. head_mode 0: advance only; 1: argmax of
   // every row and the acceptance rule per sequence (pos += m + 1); 2: argmax of the last row
   // (prefill of one sequence), pos += M.
+  // Sum of the row-parallel partial y over the ranks, then the residual add into x.
+  void reduce_into_x(size_t n) {
+    nccl_check(nccl_api().all_reduce(ybuf, ybuf, n, ncclFloat32, ncclSum, comm, stream), "ncclAllReduce");
+    launch_add(x, ybuf, n, stream);
+  }
+
   void pass(size_t s0, size_t ns, int M, const uint32_t* tokens, int head_mode) {
     const Config& c = m->cfg;
-    const int h = (int)c.hidden, kv = (int)c.kv_dim(), I = (int)c.inter, QS = h + 2 * kv;
+    const int h = (int)c.hidden, kv = dm.kv_dim, I = dm.inter, QS = dm.q_dim + 2 * kv;
+    const bool tp = tp_world > 1;
     const size_t T = ns * (size_t)M;
     if (T == 0 || T > max_rows) LS_THROW(LS_ERR_ARG, "pass of " + std::to_string(T) + " rows exceeds the batch's " + std::to_string(max_rows));
     if (s0 + ns > B) LS_THROW(LS_ERR_ARG, "sequence index out of range");
@@ -1330,8 +1453,8 @@ struct LsBatch {
       a.out = attn;
       a.part = att_part;
       a.tickets = att_tickets;
-      a.heads = (int)c.heads;
-      a.kv_heads = (int)c.kv_heads;
+      a.heads = dm.heads;
+      a.kv_heads = dm.kv_heads;
       a.hd = (int)c.head_dim;
       a.max_ctx = (int)max_ctx;
       a.M = M;
@@ -1341,9 +1464,19 @@ struct LsBatch {
       a.seq_stride = seq_stride;
       a.pdl = false;
       launch_attention(a, stream);
-      gemv(W.o, attn, h, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+      if (tp) {  // row-parallel O: this rank's heads' share of every output, summed over the ranks
+        gemv(W.o, attn, dm.q_dim, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+        reduce_into_x(T * h);
+      } else {
+        gemv(W.o, attn, dm.q_dim, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+      }
       gemv(W.gu, x, h, (int)T, EPI_SWIGLU, hbuf, I, W.post_norm, nullptr);
-      gemv(W.down, hbuf, I, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+      if (tp) {  // row-parallel down over this rank's intermediate slice
+        gemv(W.down, hbuf, I, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+        reduce_into_x(T * h);
+      } else {
+        gemv(W.down, hbuf, I, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+      }
     };
     // head over all T rows (verify) or the last row (prefill end)
     const float* hx = head_mode == 2 ? x + (T - 1) * h : x;
@@ -1353,11 +1486,24 @@ struct LsBatch {
     if (streamed) {
       m->stream_weights(head_mode != 0, stream, layer_fn, head_fn);
     } else {
-      for (size_t l = 0; l < c.layers; l++) layer_fn(m->layers[l], l);
-      if (head_mode) head_fn(m->embed, 0, (int)c.vocab);
+      for (size_t l = 0; l < c.layers; l++) layer_fn(layer(l), l);
+      if (head_mode) {
+        if (tp) head_fn(tp_head, tp_v0, tp_head.rows);
+        else head_fn(m->embed, 0, (int)c.vocab);
+      }
     }
-    if (head_mode == 1) launch_batch_accept(parts, nparts, (int)T, M, d_tok, d_argmax, d_m, d_next, stream);
-    else if (head_mode == 2) launch_batch_accept(parts, nparts, 1, 1, d_tok, d_argmax, d_m, d_next, stream);
+    const ArgPart* fparts = parts;
+    int fnparts = nparts;
+    if (tp && head_mode) {
+      // vocabulary-parallel head: each rank's first maximum per row (global ids), gathered from
+      // every rank, then reduced with the same first-maximum rule: identical on all ranks
+      launch_row_best(parts, nparts, hM, tp_best, stream);
+      nccl_check(nccl_api().all_gather(tp_best, tp_all, (size_t)hM * 2, ncclUint32, comm, stream), "ncclAllGather");
+      fparts = tp_all;
+      fnparts = tp_world;
+    }
+    if (head_mode == 1) launch_batch_accept(fparts, fnparts, (int)T, M, d_tok, d_argmax, d_m, d_next, stream);
+    else if (head_mode == 2) launch_batch_accept(fparts, fnparts, 1, 1, d_tok, d_argmax, d_m, d_next, stream);
     if (head_mode) {
       const size_t nres = head_mode == 1 ? ns : 1;
       LS_CUDA(cudaMemcpyAsync(h_m, d_m, nres * 4, cudaMemcpyDeviceToHost, stream));
@@ -1873,6 +2019,28 @@ int ls_batch_open(LsModel* m, uint64_t batch, uint64_t max_ctx, uint64_t max_blo
     *out = nullptr;
     LS_CUDA(cudaSetDevice(m->device));
     *out = new LsBatch(m, batch, max_ctx, max_block);
+  });
+}
+
+int ls_tp_unique_id(uint8_t* out, size_t cap) {
+  return guard([&] {
+    NEED(out);
+    if (cap < sizeof(ncclUniqueId)) LS_THROW(LS_ERR_ARG, "the id needs " + std::to_string(sizeof(ncclUniqueId)) + " bytes");
+    ncclUniqueId id;
+    nccl_check(nccl_api().get_unique_id(&id), "ncclGetUniqueId");
+    std::memcpy(out, &id, sizeof id);
+  });
+}
+
+int ls_batch_open_tp(LsModel* m, uint64_t batch, uint64_t max_ctx, uint64_t max_block, int rank, int world, const uint8_t* id,
+                     LsBatch** out) {
+  return guard([&] {
+    NEED(m);
+    NEED(out);
+    *out = nullptr;
+    if (world > 1) NEED(id);
+    LS_CUDA(cudaSetDevice(m->device));
+    *out = new LsBatch(m, batch, max_ctx, max_block, rank, world, id);
   });
 }
 

@@ -1,0 +1,93 @@
+"""Tensor-parallel batch (config 5b) on two GPUs against the CPU path (needs 2 B200s).
+
+Each rank holds its q heads (and their kv head), half of the intermediate dimension and half of
+the vocabulary; O and down are summed over the ranks (NCCL all-reduce) and the LM head's per-rank
+first maxima are gathered. Every rank must emit the same tokens, and they must match the CPU path
+wherever the top-2 logit margin exceeds the north-star tolerance.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import fixtures as F
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+WORLD = 2
+
+
+def _rank(rank, world, path, uid_q, out_q, prompts, max_new, k):
+    import torch
+
+    import layerstream_b200 as ls
+
+    torch.cuda.set_device(rank)
+    if rank == 0:
+        uid = ls.tp_unique_id()
+        for _ in range(world - 1):
+            uid_q.put(uid)
+    else:
+        uid = uid_q.get(timeout=120)
+    try:
+        m = ls.Model(path, device=rank, max_ctx=64)
+        b = ls.Batch(m, len(prompts), max_ctx=64, max_block=k + 1, tp=(rank, world, uid))
+        got, st = b.spec(np.array(prompts, np.uint32), max_new, k)
+        out_q.put((rank, got, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        out_q.put((rank, None, repr(e)))
+
+
+def _cpu_tokens(path, prompt, n):
+    c = O.Model(path, quantized=True, threads=4, max_ctx=64)
+    logits = c.forward(prompt)
+    toks, margins = [], []
+    for i in range(n):
+        srt = np.sort(logits)
+        toks.append(int(np.argmax(logits)))
+        margins.append(float(srt[-1] - srt[-2]))
+        if i + 1 < n:
+            logits = c.forward([toks[-1]])
+    return toks, margins
+
+
+def test_two_rank_tensor_parallel_batch_matches_the_cpu_path():
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    from layerstream_b200 import synth
+    import layerstream_b200 as ls
+
+    synth.SHAPES["tp-test"] = dict(hidden_size=2048, num_attention_heads=16, num_key_value_heads=2,
+                                   intermediate_size=256, num_hidden_layers=2, vocab_size=1000, rope_theta=1e6,
+                                   max_position_embeddings=4096)
+    d = F.TempDir("gpu-tp").path
+    synth.write_random_model(d, "tp-test", 5)
+    path = os.path.join(d, "tp.lsq")
+    O.quantize_model(d, path, (4, 32), (4, 32), clip=True)
+    prompts = [[(11 * i + 17 * s + 3) % 1000 for i in range(10)] for s in range(4)]
+    max_new, k = 12, 4
+    ctx = mp.get_context("spawn")
+    uid_q, out_q = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, WORLD, path, uid_q, out_q, prompts, max_new, k)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(WORLD):
+        r, got, err = out_q.get(timeout=600)
+        res[r] = (got, err)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(WORLD):
+        assert res[r][1] is None, res[r][1]
+    assert res[0][0] == res[1][0]  # every rank emits the same tokens
+    for pr, g in zip(prompts, res[0][0]):
+        toks, margins = _cpu_tokens(path, pr, max_new)
+        for i, (t, mg) in enumerate(zip(toks, margins)):
+            if mg <= TOL:
+                break
+            assert g[i] == t, (pr, i)
