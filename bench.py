@@ -71,13 +71,18 @@ def parse():
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--drafter", choices=["lookup", "model"], default=None)
     ap.add_argument("--root", default=os.environ.get("LS_BENCH_ROOT", "/tmp/ls_b200_bench"))
+    ap.add_argument("--tp", action="store_true",
+                    help="config 5 (b): the resident model split tensor-parallel over the launched ranks (NCCL), "
+                         "instead of 2-slot streaming per GPU")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-sample-tokens", type=int, default=0, help="decode tokens per CPU sample (0: auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="print the per-kernel profile to stderr")
-    ap.add_argument("--ncu-case", choices=["pass", "gemv"], default=None,
+    ap.add_argument("--ncu-case", choices=["pass", "gemv", "attention", "bgemm"], default=None,
                     help="short fixed workloads for ncu: 'pass' = prefill + 3 verify passes of the bench model, "
-                         "'gemv' = 3 launches of the LM-head GEMV (151936 x 896, int4 g32, M = 9)")
+                         "'gemv' = 3 launches of the LM-head GEMV (151936 x 896, int4 g32, M = 9), "
+                         "'attention' = 3 launches of the tensor-core attention (14/2 heads, hd 64, M = 5, "
+                         "context 8000), 'bgemm' = the batched GEMM on the 3B gate/up shape (M = 40)")
     return ap.parse_args()
 
 
@@ -89,6 +94,28 @@ def ncu_case(args, cfg):
     from layerstream_b200 import synth
 
     torch.cuda.set_device(0)
+    if args.ncu_case == "attention":
+        # the 0.5B attention shape (14 q / 2 kv heads, hd 64) for one sequence of 5 verify rows at
+        # context 8000: 63 chunks of 128 positions per kv head, 16 splits
+        heads, kvh, hd, pos0, M = 14, 2, 64, 8000, 5
+        rng = np.random.default_rng(7)
+        qkv = rng.standard_normal((M, (heads + 2 * kvh) * hd)).astype(np.float32)
+        kc = rng.standard_normal((kvh, pos0, hd)).astype(np.float16)
+        vc = rng.standard_normal((kvh, pos0, hd)).astype(np.float16)
+        for _ in range(3):
+            ls.attention(heads, kvh, hd, pos0, qkv, kc, vc)
+        print(json.dumps({"ncu_case": "attention", "heads": heads, "kv_heads": kvh, "hd": hd, "pos0": pos0, "M": M,
+                          "kv_bytes": 2 * kvh * (pos0 + M) * hd * 2}))
+        return
+    if args.ncu_case == "bgemm":
+        # the 3B gate/up projection (22016 x 2048, int4 g32) over the 40 rows of a config-5 verify
+        # pass (8 sequences x 5), through the batched GEMM
+        rows, cols, M = 22016, 2048, 40
+        raw = stored_rows(4, 32, rows, cols, seed=3)
+        x = np.random.default_rng(3).standard_normal((M, cols)).astype(np.float32)
+        _, ms = ls.bgemm(4, 32, raw, rows, cols, x, iters=3)
+        print(json.dumps({"ncu_case": "bgemm", "rows": rows, "cols": cols, "M": M, "ms": ms}))
+        return
     os.makedirs(args.root, exist_ok=True)
     t_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True)
     if args.ncu_case == "pass":
@@ -385,6 +412,43 @@ def microbench(args):
         print(json.dumps(line), flush=True)
 
 
+def qmat_bytes(rows, cols, bits, group):
+    """Stored bytes of a group-quantized matrix: packed codes + one bf16 scale per group."""
+    return rows * cols * bits // 8 + rows * (cols // group) * 2
+
+
+def tp_rank_bytes(info, world, rank):
+    """Weight bytes one verify pass reads on `rank` of a tensor-parallel split (the library's
+    split: q heads evenly, each rank's kv heads, the intermediate dimension in 64-row blocks, the
+    head's vocabulary in 32-row tiles); norms are counted whole on every rank."""
+    h, hd, L = info.hidden, info.head_dim, info.layers
+    hl = info.heads // world
+    kvl = info.kv_heads // world if world <= info.kv_heads else 1
+    nb = info.inter // 64
+    il = 64 * ((rank + 1) * nb // world) - 64 * (rank * nb // world)
+    b, g = info.bits, info.group
+    layer = (qmat_bytes((hl + 2 * kvl) * hd, h, b, g) + qmat_bytes(h, hl * hd, b, g) + qmat_bytes(2 * il, h, b, g)
+             + qmat_bytes(h, il, b, g) + 2 * h * 2 + (hl + 2 * kvl) * hd * 2)
+    tiles = (info.vocab + 31) // 32
+    t0, t1 = rank * tiles // world, (rank + 1) * tiles // world
+    rows = min(info.vocab, 32 * t1) - 32 * t0
+    return L * layer + qmat_bytes(rows, h, info.embed_bits, info.embed_group) + h * 4
+
+
+def class_split(prof):
+    """Per launch class of a profiled batch run: share of the pass time and achieved GB/s."""
+    tot = prof["pass"]["ms"] or 1e-9
+    out = {}
+    for c, v in prof.items():
+        if c == "pass" or not v["launches"]:
+            continue
+        out[c] = {"share": v["ms"] / tot, "ms": v["ms"], "launches": v["launches"],
+                  "gbs": v["bytes"] / (v["ms"] * 1e-3) / 1e9 if v["ms"] else None}
+    out["pass_ms_total"] = prof["pass"]["ms"]
+    out["passes"] = prof["pass"]["launches"]
+    return out
+
+
 def batch_bench(args, cfg):
     """Config 4: B independent sequences per GPU through one batched verify pass per decode step
     (ls_batch_spec, prompt-lookup drafter). value = tokens generated after the first, all
@@ -403,14 +467,21 @@ def batch_bench(args, cfg):
     if rank != 0:
         path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local)
     B, plen, max_new, k = cfg["batch"], cfg["prompt"], cfg["max_new"], cfg["k"]
-    slots = cfg.get("stream_slots")
+    tp = bool(args.tp and cfg.get("stream_slots"))
+    slots = None if tp else cfg.get("stream_slots")
     if slots:
         model = ls.Model(path, device=local, max_ctx=plen + 64, mode="stream", slots=slots)
     else:
         model = ls.Model(path, device=local, max_ctx=plen + 64)
     V = model.vocab
-    prompts = np.array([prompt_for(cfg, V, rank * B + i) for i in range(B)], np.uint32)
-    batch = ls.Batch(model, B, max_ctx=plen + max_new + k + 16, max_block=k + 1)
+    # data parallel: each rank its own B sequences; tensor parallel: the same B sequences on every rank
+    prompts = np.array([prompt_for(cfg, V, (0 if tp else rank * B) + i) for i in range(B)], np.uint32)
+    tp_arg = None
+    if tp and world > 1:
+        box = [ls.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        tp_arg = (rank, world, box[0])
+    batch = ls.Batch(model, B, max_ctx=plen + max_new + k + 16, max_block=k + 1, tp=tp_arg)
     for _ in range(max(args.warmup, 1)):
         batch.spec(prompts, 8, k)
     clocks = Clocks(local)
@@ -428,8 +499,20 @@ def batch_bench(args, cfg):
         dr += st["drafted"]
     clk = clocks.stop()
     r1 = model.report()
+    # per-class split of verify passes after the timed region (events add a little time): every
+    # sequence prefilled, then 32 (k+1)-row passes of all sequences
+    nxt = []
+    for i in range(B):
+        batch.truncate(i, 0)
+        nxt.append(batch.prefill(i, prompts[i]))
+    batch.profile_enable(1)
+    for _ in range(32):
+        _, nxt = batch.verify(np.array([[t] * (k + 1) for t in nxt], np.uint32))
+    prof = batch.profile()
+    batch.profile_enable(0)
     barrier(dist)
-    ms_max, tok_all = reduce_over_ranks(dist, decode_s * 1e3, tokens, device="cuda")
+    # tensor parallel: every rank emits the same tokens, counted once
+    ms_max, tok_all = reduce_over_ranks(dist, decode_s * 1e3, tokens if (rank == 0 or not tp) else 0, device="cuda")
     value = tok_all / (ms_max / 1e3)
     info = model.info
     avg_ctx = plen + max_new / 2
@@ -463,7 +546,8 @@ def batch_bench(args, cfg):
                          "avg_launch_us": pass_s * 1e6, "launches_per_pass": 2 + 5 * info.layers + 2},
             "spec": {"tokens_per_pass": tokens / max(passes, 1) / B, "accepted_over_drafted": acc / max(dr, 1),
                      "target_passes": passes, "prefill_s": first_s / max(args.steps, 1)},
-            "streaming": streamed}
+            "streaming": streamed,
+            "classes": class_split(prof)}
     if slots:
         # streamed weights: the bound is the host-to-device link, not HBM
         pcie = 64.0  # GB/s, nominal PCIe 5.0 x16 per direction (no measured figure on this pool)
@@ -475,6 +559,29 @@ def batch_bench(args, cfg):
                                       f"{max_new} new tokens, k={k}, lookup drafter, {slots}-slot layer streaming from pinned host")
         line["config"]["config"] = 5
         line["dtype"] = "f32 activations, int4 weights (bf16 scales), f16 KV"
+    if tp:
+        # per rank: its shard of the weights and the K/V of its kv heads; the pass also carries
+        # 2 all-reduces per layer and one all-gather over NVLink (NCCL)
+        kvl = info.kv_heads // world if world <= info.kv_heads else 1
+        kv_r = avg_ctx * info.layers * kvl * info.head_dim * 2 * 2 * B
+        w_r = max(tp_rank_bytes(info, world, r) for r in range(world))
+        ar_bytes = 2 * info.layers * B * (k + 1) * info.hidden * 4
+        line["scaling"] = "strong"
+        line["config"].update({
+            "workload": (f"config5b: 3b Qwen2 random-init int4 g32, {B} sequences, {plen}-token prompts, {max_new} new "
+                         f"tokens, k={k}, lookup drafter, resident, tensor parallel over {world} GPU(s)"),
+            "config": 5, "global_batch": B, "batch_per_gpu": B,
+            "parallelism": (f"tp{world}: column-parallel QKV (q heads) and gate/up, row-parallel O and down with NCCL "
+                            "all-reduce, vocabulary-parallel head with an all-gather of per-rank maxima")
+                           if world > 1 else "single GPU (tp1)"})
+        line["dtype"] = "f32 activations, int4 weights (bf16 scales), f16 KV"
+        line["gpu_launches"] = int(passes * (7 * info.layers + 5 if world > 1 else 5 * info.layers + 4))
+        line["roofline"] = {"bound": "hbm", "kernel": "tensor-parallel verify pass on the busiest rank (separate kernels)",
+                            "achieved": (w_r + kv_r) / pass_s / 1e9, "peak": peak, "unit": "GB/s",
+                            "frac": (w_r + kv_r) / pass_s / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                            "traffic": None, "algorithmic_bytes_per_launch": w_r + kv_r, "avg_launch_us": pass_s * 1e6,
+                            "allreduce_bytes_per_pass": ar_bytes if world > 1 else 0,
+                            "collectives_per_pass": 2 * info.layers + 1 if world > 1 else 0}
     if rank == 0:
         print(json.dumps(line), flush=True)
     batch.close()

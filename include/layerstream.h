@@ -91,6 +91,18 @@ typedef struct LsProfile {
   double busy_ms[LS_PROF_CLASSES];
 } LsProfile;
 
+/* Live profile of a batch: CUDA-event time of every launch class of its passes. Classes: 0 QKV,
+ * 1 attention, 2 O, 3 gate/up, 4 down, 5 LM head (argmax epilogue), 6 collectives of a
+ * tensor-parallel batch (all-reduce + residual add, all-gather), 7 the whole pass. bytes =
+ * algorithmic bytes (weights + scales + activations; attention: K/V rows read and written;
+ * collectives: bytes each rank sends). */
+#define LS_BATCH_PROF_CLASSES 8
+typedef struct LsBatchProfile {
+  uint64_t launches[LS_BATCH_PROF_CLASSES];
+  double ms[LS_BATCH_PROF_CLASSES];
+  double bytes[LS_BATCH_PROF_CLASSES];
+} LsBatchProfile;
+
 /* src/spec.rs:16-39 */
 typedef struct LsSpecStats {
   uint64_t target_passes, drafted, accepted, draft_forwards;
@@ -188,6 +200,9 @@ int ls_batch_verify(LsBatch *b, const uint32_t *blocks, uint64_t nseq, uint64_t 
 int ls_batch_spec(LsBatch *b, const uint32_t *prompts, uint64_t plen, uint64_t max_new, uint64_t k, const uint32_t *eos,
                   uint64_t neos, uint32_t *out_tokens, uint64_t *out_len, LsSpecStats *stats);
 int ls_batch_report(const LsBatch *b, uint64_t *passes, uint64_t *h2d_bytes, uint64_t *d2h_bytes);
+/* on: 0 off, 1 an event pair around every launch class of each pass; also clears the counters */
+int ls_batch_profile_enable(LsBatch *b, int on);
+int ls_batch_profile(const LsBatch *b, LsBatchProfile *out);
 
 /* ---- kernel-level entry points (microbenchmarks and parity tests) ---------------------------- */
 
@@ -197,6 +212,12 @@ int ls_batch_report(const LsBatch *b, uint64_t *passes, uint64_t *h2d_bytes, uin
  * kernels::matmul (src/kernels.rs:196-203). iters > 1 repeats the kernel and returns the mean
  * kernel time in *ms (may be NULL). */
 int ls_qgemv_host(int bits, int group, const uint8_t *rows_raw, uint64_t rows, uint64_t cols, const float *x, uint64_t M,
+                  float *y, int iters, double *ms);
+/* The batched weight GEMM of the verify / prefill pass (tensor cores, all M rows per weight tile):
+ * y[M][rows] = x[M][cols] . W^T for stored rows (the `.lsq` row format) on the current device;
+ * iters > 1 also times the GEMM alone (ms per launch). No reference counterpart: it is the kernel
+ * behind ls_batch_verify's projections, exposed for parity tests and timing. */
+int ls_bgemm_host(int bits, int group, const uint8_t *rows_raw, uint64_t rows, uint64_t cols, const float *x, uint64_t M,
                   float *y, int iters, double *ms);
 
 /* One layer's causal GQA attention (src/model.rs:261-282, src/kernels.rs:242-265) through the

@@ -45,6 +45,13 @@ class Profile(C.Structure):
                 ("busy_ms", C.c_double * 7)]
 
 
+BATCH_PROF_CLASSES = ("qkv", "attention", "o", "gate_up", "down", "head", "collective", "pass")
+
+
+class BatchProfile(C.Structure):
+    _fields_ = [("launches", C.c_uint64 * 8), ("ms", C.c_double * 8), ("bytes", C.c_double * 8)]
+
+
 class SpecStats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("target_passes", "drafted", "accepted", "draft_forwards")] + [
         (n, C.c_double) for n in ("target_secs", "draft_secs", "first_secs", "decode_secs")
@@ -80,6 +87,8 @@ _SIGS = {
                                     C.POINTER(C.c_double)]),
     "ls_qgemv_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p,
                                 C.c_int, C.POINTER(C.c_double)]),
+    "ls_bgemm_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p,
+                                C.c_int, C.POINTER(C.c_double)]),
     "ls_qweights_upload": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.POINTER(C.c_void_p)]),
     "ls_qweights_free": (C.c_int, [C.c_void_p]),
     "ls_qgemv_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p]),
@@ -96,6 +105,8 @@ _SIGS = {
     "ls_batch_spec": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64,
                                 C.c_void_p, C.c_void_p, C.POINTER(SpecStats)]),
     "ls_batch_report": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    "ls_batch_profile_enable": (C.c_int, [C.c_void_p, C.c_int]),
+    "ls_batch_profile": (C.c_int, [C.c_void_p, C.POINTER(BatchProfile)]),
     "ls_attention_host": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
     "ls_qgemv_rows_noalloc": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64,
@@ -296,6 +307,15 @@ class Batch:
         _check(lib().ls_batch_report(self._h, C.byref(a), C.byref(b), C.byref(c)))
         return {"passes": a.value, "h2d_bytes": b.value, "d2h_bytes": c.value}
 
+    def profile_enable(self, on=True):
+        """Live timing: CUDA events around every launch class of each pass (clears the counters)."""
+        _check(lib().ls_batch_profile_enable(self._h, int(on)))
+
+    def profile(self) -> dict:
+        p = BatchProfile()
+        _check(lib().ls_batch_profile(self._h, C.byref(p)))
+        return {c: {"launches": p.launches[i], "ms": p.ms[i], "bytes": p.bytes[i]} for i, c in enumerate(BATCH_PROF_CLASSES)}
+
     def close(self):
         if getattr(self, "_h", None):
             lib().ls_batch_free(self._h)
@@ -359,6 +379,18 @@ class QWeights:
         if getattr(self, "_h", None):
             lib().ls_qweights_free(self._h)
             self._h = None
+
+
+def bgemm(bits: int, group: int, rows_raw, rows: int, cols: int, x, iters: int = 1):
+    """The batched verify-pass GEMM: y = x W^T for M rows of x (stored rows in the .lsq format).
+    Returns (y M x rows, ms per launch when iters > 1)."""
+    w = np.ascontiguousarray(rows_raw, np.uint8)
+    xx = np.ascontiguousarray(x, np.float32)
+    M = xx.shape[0]
+    y = np.empty((M, rows), np.float32)
+    ms = C.c_double()
+    _check(lib().ls_bgemm_host(bits, group, _p(w), rows, cols, _p(xx), M, _p(y), iters, C.byref(ms)))
+    return y, ms.value
 
 
 def attention(heads: int, kv_heads: int, hd: int, pos0: int, qkv: np.ndarray, k_cache=None, v_cache=None,

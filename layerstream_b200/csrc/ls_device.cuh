@@ -139,6 +139,33 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc)
       : "memory");
 }
+// A and B both from shared memory (descriptors).
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// 3-D tiled TMA load of one box into shared memory, completing bytes on an mbarrier (no multicast).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(su32(bar))
+      : "memory");
+}
+// Plain (untiled) bulk copy global -> shared memory, completing bytes on an mbarrier.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst), "l"(src),
+               "r"(bytes), "r"(su32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
+}
 __device__ __forceinline__ void commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar)) : "memory");
 }
@@ -169,6 +196,15 @@ __device__ __forceinline__ uint32_t h2_sub_mul(uint32_t v, uint32_t sub, uint32_
   a = __hmul2(__hsub2(a, b), c);
   return *reinterpret_cast<uint32_t*>(&a);
 }
+// High nibble of a byte pair already placed as 1024 + 16 u (f16x2): (x / 16 - 72) = u - 8 exactly
+// in one fused multiply-add, then times the scale (the same single rounding as h2_sub_mul).
+__device__ __forceinline__ uint32_t h2_hi_mul(uint32_t v, uint32_t scale) {
+  const uint32_t sixteenth = 0x2C002C00u, m72 = 0xD480D480u;  // 1/16, -72 as f16x2
+  __half2 a = *reinterpret_cast<__half2*>(&v);
+  a = __hfma2(a, *reinterpret_cast<const __half2*>(&sixteenth), *reinterpret_cast<const __half2*>(&m72));
+  a = __hmul2(a, *reinterpret_cast<const __half2*>(&scale));
+  return *reinterpret_cast<uint32_t*>(&a);
+}
 __device__ __forceinline__ uint32_t h2_splat(float s) {
   const __half h = __float2half_rn(s);
   const uint16_t u = __half_as_ushort(h);
@@ -182,6 +218,61 @@ __host__ __device__ constexpr int tc_kb(int bits, int group) { return (bits == 4
 // Group scales one row needs per A block.
 __host__ __device__ constexpr int tc_ns(int bits, int group) {
   return tc_kb(bits, group) >= group ? tc_kb(bits, group) / group : 1;
+}
+
+// One 16-byte chunk per CPB of a row's packed K block (tc_kb(BITS, G) weights) -> f16 pairs in K
+// order, each weight (q - 8) * scale (int4, stored q = w + 8; group >= 32: low nibbles are K j,
+// high nibbles K j + G/2 of the group) or q * scale (int8). scur[s]: f16x2 splat of the block's
+// s-th group scale. Exact in f16 products of the int and the bf16 scale rounded to f16.
+template <int BITS, int G>
+__device__ __forceinline__ void tc_dequant_block(const uint4* wv, const uint32_t* scur, uint32_t* a) {
+  constexpr int KB = tc_kb(BITS, G);
+  constexpr int NS = tc_ns(BITS, G);
+  constexpr int CPB = KB / (128 / BITS);
+  const uint32_t sub8 = BITS == 8 ? 0x64806480u : 0x64086408u;  // 1152 | 1032 as f16x2
+#pragma unroll
+  for (int q = 0; q < CPB; q++) {
+    const uint32_t wd[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
+    if constexpr (BITS == 8) {
+      const uint32_t s2 = scur[(NS > 1) ? (q * 16) / G : 0];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const uint32_t p0 = (__byte_perm(wd[k], 0u, 0x4140u) ^ 0x00800080u) | 0x64006400u;
+        const uint32_t p1 = (__byte_perm(wd[k], 0u, 0x4342u) ^ 0x00800080u) | 0x64006400u;
+        a[q * 8 + 2 * k] = tc::h2_sub_mul(p0, sub8, s2);
+        a[q * 8 + 2 * k + 1] = tc::h2_sub_mul(p1, sub8, s2);
+      }
+    } else if constexpr (G == 16) {
+      // bytes 0..7: group 2q (low -> K 32q+j, high -> 32q+8+j); bytes 8..15: group 2q+1
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const uint32_t sc = scur[2 * q + (k < 2 ? 0 : 1)];
+        const int base = q * 16 + (k < 2 ? 0 : 8);
+        const int j = (k & 1) * 4;
+        const uint32_t p0 = __byte_perm(wd[k], 0u, 0x4140u), p1 = __byte_perm(wd[k], 0u, 0x4342u);
+        a[base + j / 2] = tc::h2_sub_mul((p0 & 0x000F000Fu) | 0x64006400u, sub8, sc);
+        a[base + j / 2 + 1] = tc::h2_sub_mul((p1 & 0x000F000Fu) | 0x64006400u, sub8, sc);
+        a[base + 4 + j / 2] = tc::h2_hi_mul((p0 & 0x00F000F0u) | 0x64006400u, sc);
+        a[base + 4 + j / 2 + 1] = tc::h2_hi_mul((p1 & 0x00F000F0u) | 0x64006400u, sc);
+      }
+    } else {
+      // group >= 32: chunk q holds bytes j0..j0+15 of its group; low nibbles are K j0+j,
+      // high nibbles K j0+j+G/2 (relative to the group start)
+      constexpr int HALF = G / 2;
+      const uint32_t sc = scur[(NS > 1) ? (q * 32) / G : 0];
+      const int j0 = (q * 16) % HALF;
+      const int gbase = ((q * 32) / G) * G;  // group start relative to the block start
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const uint32_t p0 = __byte_perm(wd[k], 0u, 0x4140u), p1 = __byte_perm(wd[k], 0u, 0x4342u);
+        const int lo = (gbase + j0 + 4 * k) / 2, hi = (gbase + j0 + HALF + 4 * k) / 2;
+        a[lo] = tc::h2_sub_mul((p0 & 0x000F000Fu) | 0x64006400u, sub8, sc);
+        a[lo + 1] = tc::h2_sub_mul((p1 & 0x000F000Fu) | 0x64006400u, sub8, sc);
+        a[hi] = tc::h2_hi_mul((p0 & 0x00F000F0u) | 0x64006400u, sc);
+        a[hi + 1] = tc::h2_hi_mul((p1 & 0x00F000F0u) | 0x64006400u, sc);
+      }
+    }
+  }
 }
 
 constexpr int GEMV_WARPS = 8;

@@ -127,7 +127,9 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
           make_uint4(w4[0], w4[1], w4[2], w4[3]);
     }
   }
-  if (has_norm) {
+  if (has_norm && g.inv_rms) {
+    for (int t = threadIdx.x; t < Mloc; t += TC_THREADS) s_inv[t] = g.inv_rms[m0 + t];
+  } else if (has_norm) {
     const int cols4 = g.w.cols >> 2;
     for (int t = warp; t < Mloc; t += NW) {
       float ss = 0.f;
@@ -148,7 +150,6 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
   const uint32_t d_col = tmem + 2 * ACOLS;
   const uint32_t idesc = tc::idesc_f16(NT);
   const uint32_t xb_addr = tc::su32(xb);
-  const uint32_t sub8 = BITS == 8 ? 0x64806480u : 0x64086408u;  // 1152 | 1032 as f16x2
 
   uint32_t uses[2] = {0u, 0u};
   uint32_t tiles_done = 0;
@@ -194,49 +195,7 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
 
       // ---- dequantise one K block of this row into f16 pairs in K order ----
       uint32_t a[ACOLS];
-#pragma unroll
-      for (int q = 0; q < CPB; q++) {
-        const uint32_t wd[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
-        if constexpr (BITS == 8) {
-          const uint32_t s2 = scur[(NS > 1) ? (q * 16) / G : 0];
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const uint32_t p0 = (__byte_perm(wd[k], 0u, 0x4140u) ^ 0x00800080u) | 0x64006400u;
-            const uint32_t p1 = (__byte_perm(wd[k], 0u, 0x4342u) ^ 0x00800080u) | 0x64006400u;
-            a[q * 8 + 2 * k] = tc::h2_sub_mul(p0, sub8, s2);
-            a[q * 8 + 2 * k + 1] = tc::h2_sub_mul(p1, sub8, s2);
-          }
-        } else if constexpr (G == 16) {
-          // bytes 0..7: group 2q (low -> K 32q+j, high -> 32q+8+j); bytes 8..15: group 2q+1
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const uint32_t sc = scur[2 * q + (k < 2 ? 0 : 1)];
-            const int base = q * 16 + (k < 2 ? 0 : 8);
-            const int j = (k & 1) * 4;
-            const uint32_t p0 = __byte_perm(wd[k], 0u, 0x4140u), p1 = __byte_perm(wd[k], 0u, 0x4342u);
-            a[base + j / 2] = tc::h2_sub_mul((p0 & 0x000F000Fu) | 0x64006400u, sub8, sc);
-            a[base + j / 2 + 1] = tc::h2_sub_mul((p1 & 0x000F000Fu) | 0x64006400u, sub8, sc);
-            a[base + 4 + j / 2] = tc::h2_sub_mul(((p0 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, sc);
-            a[base + 4 + j / 2 + 1] = tc::h2_sub_mul(((p1 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, sc);
-          }
-        } else {
-          // group >= 32: chunk q holds bytes j0..j0+15 of its group; low nibbles are K j0+j,
-          // high nibbles K j0+j+G/2 (relative to the group start)
-          constexpr int HALF = G / 2;
-          const uint32_t sc = scur[(NS > 1) ? (q * 32) / G : 0];
-          const int j0 = (q * 16) % HALF;
-          const int gbase = ((q * 32) / G) * G;  // group start relative to the block start
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const uint32_t p0 = __byte_perm(wd[k], 0u, 0x4140u), p1 = __byte_perm(wd[k], 0u, 0x4342u);
-            const int lo = (gbase + j0 + 4 * k) / 2, hi = (gbase + j0 + HALF + 4 * k) / 2;
-            a[lo] = tc::h2_sub_mul((p0 & 0x000F000Fu) | 0x64006400u, sub8, sc);
-            a[lo + 1] = tc::h2_sub_mul((p1 & 0x000F000Fu) | 0x64006400u, sub8, sc);
-            a[hi] = tc::h2_sub_mul(((p0 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, sc);
-            a[hi + 1] = tc::h2_sub_mul(((p1 >> 4) & 0x000F000Fu) | 0x64006400u, sub8, sc);
-          }
-        }
-      }
+      tc_dequant_block<BITS, G>(wv, scur, a);
 #pragma unroll
       for (int q = 0; q < NS; q++) {
         sraw0[q] = sraw1[q];
@@ -447,6 +406,27 @@ static void launch_tc_g(const GemvLaunch& g, cudaStream_t s) {
     case 48: return launch_tc_t<BITS, G, 48>(g, s);
     default: return launch_tc_t<BITS, G, 64>(g, s);
   }
+}
+
+// One warp per row, the same per-lane float4 order and warp sum as the GEMV norm prologue.
+__global__ void inv_rms_kernel(const float* __restrict__ x, int x_stride, int M, int cols, float eps, float* inv) {
+  const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= M) return;
+  const int cols4 = cols >> 2;
+  float ss = 0.f;
+#pragma unroll 4
+  for (int c4 = lane; c4 < cols4; c4 += 32) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(x + (size_t)t * x_stride) + c4);
+    ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) inv[t] = 1.0f / sqrtf(ss / (float)cols + eps);
+}
+
+void launch_inv_rms(const float* x, int x_stride, int M, int cols, float eps, float* inv, cudaStream_t s) {
+  if (M <= 0) return;
+  inv_rms_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, x_stride, M, cols, eps, inv);
+  LS_CUDA(cudaGetLastError());
 }
 
 void launch_gemv_tc(const GemvLaunch& g, cudaStream_t s) {

@@ -121,7 +121,7 @@ struct RepackSrc {
 
 // ---- kernels (ls_kernels.cu) -------------------------------------------------------------------
 
-enum Epilogue { EPI_STORE = 0, EPI_BIAS_STORE = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+enum Epilogue { EPI_STORE = 0, EPI_BIAS_STORE = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_SWIGLU_H = 5 };
 
 // Argmax partial: value then index, combined so that a larger value wins and, on equal values,
 // the smaller index wins (src/spec.rs:41-49 first-maximum rule).
@@ -155,6 +155,7 @@ struct GemvLaunch {
   const uint16_t* norm_bf16 = nullptr;
   const float* norm_f32 = nullptr;
   float eps = 0;
+  const float* inv_rms = nullptr;  // [M] 1/rms of every row, computed once (else per CTA)
   // epilogue
   int epi = EPI_STORE;
   float* y = nullptr;          // output [M][y_stride]
@@ -182,6 +183,8 @@ struct GemvLaunch {
 };
 
 void launch_gemv(const GemvLaunch& g, cudaStream_t s);
+// inv[t] = 1 / sqrt(mean(x[t]^2) + eps) for M rows of `cols` floats (the GEMV norm prologue's sum)
+void launch_inv_rms(const float* x, int x_stride, int M, int cols, float eps, float* inv, cudaStream_t s);
 // Smallest K-split whose staged activations fit in shared memory.
 int gemv_min_ksplit(const QMat& w, int M);
 int gemv_grid_x(const QMat& w, int ksplit, int M, int num_sms);
@@ -218,12 +221,62 @@ struct AttnLaunch {
   const int* pos0 = nullptr;
   size_t seq_stride = 0;
   bool pdl = true;  // false: plain launch (positions written by the previous kernel are read early)
+  int* err = nullptr;  // set to 1 when a bounded wait of the tensor-core kernel gives up
+  int max_total = 0;   // largest pos0 + M over the sequences when the host knows it (0: max_ctx)
+  uint16_t* out_h = nullptr;  // tensor-core kernel: output as f16 in the bt layout (K = heads * hd) instead of out
+  int out_h_n = 0;            // its token-group rows
 };
 void launch_attention(const AttnLaunch& a, cudaStream_t s);
+bool attention_tc_supported(const AttnLaunch& a);  // ls_attn_tc.cu
+void launch_attention_tc(const AttnLaunch& a, cudaStream_t s);
 
 void launch_set_ctl(Ctl* ctl, int pos0, int M, int n_logits, int mode, const uint32_t* tokens_dev_or_null, cudaStream_t s);
 void launch_quantize_rows(const uint16_t* src_bf16, int rows, int cols, int bits, int group, int clip, uint8_t* dst,
                           double* err_norm, cudaStream_t s);
+
+// ---- batched weight GEMM (ls_bgemm.cu) ----
+
+// Activations in the tensor-core B-operand layout ("bt") of a GEMM whose token groups hold N rows:
+// group g = t / N, 16-byte K chunk c = k / 8, element (t, k) at halves
+// ((g * (K / 8) + c) * N + t % N) * 8 + k % 8. Every K range of a group is one contiguous block of
+// 16-byte rows (chunk-major, token-minor), which the GEMM copies into shared memory with a single
+// bulk copy and reads as K-major core matrices (8 tokens x 16 bytes). Buffers hold ngroups * N
+// rows.
+__host__ __device__ inline size_t bt_off(int t, int k, int K, int N) {
+  const int g = t / N;
+  return (((size_t)g * (K >> 3) + (k >> 3)) * N + (t - g * N)) * 8 + (k & 7);
+}
+
+struct BgemmLaunch {
+  QMat w;
+  const uint16_t* x = nullptr;  // activations, bt layout with K = w.cols, M rows
+  int M = 0;
+  int epi = EPI_STORE;          // STORE / BIAS_STORE / RESID into y, SWIGLU_H into yh, ARGMAX
+  float* y = nullptr;
+  int y_stride = 0;
+  uint16_t* yh = nullptr;       // EPI_SWIGLU_H: f16 bt layout with K = rows / 2
+  const uint16_t* bias = nullptr;
+  ArgPart* arg_parts = nullptr; // EPI_ARGMAX: [part][M]
+  int n_valid_rows = 0, row_offset = 0, part_tile_offset = 0;
+  float* partial = nullptr;     // split-K scratch
+  unsigned* tickets = nullptr;
+  int* err = nullptr;
+};
+struct BgemmPlan {
+  int N = 16, ngroups = 1, ks = 1, stages = 2, kstage = 1, tmem_cols = 256;
+  size_t smem = 0, partial_floats = 0, tickets = 0;
+};
+// token groups of a pass of M rows (every GEMM of the pass uses the same): N rows each, ngroups
+void bgemm_groups(int M, int* N, int* ngroups);
+bool bgemm_supported(const QMat& w);
+BgemmPlan bgemm_plan(const QMat& w, int M, int num_sms, bool argmax);
+void launch_bgemm(const BgemmLaunch& g, const BgemmPlan& p, cudaStream_t s);
+// x (f32 rows) -> bt layout f16, with the RMSNorm folded in when a norm weight is given (x * inv *
+// w); rows M .. pad8(M) are zero.
+void launch_bt_prep(const float* x, int x_stride, int M, int K, const uint16_t* norm_bf16, const float* norm_f32,
+                    float eps, uint16_t* out, cudaStream_t s);
+// halves of a bt buffer of M rows and K columns (its token groups padded)
+size_t bt_elems(int M, int K);
 
 // ---- persistent pass kernel (ls_pass.cu) ----
 
@@ -305,5 +358,8 @@ int pass_kernel_blocks_per_sm(const WeightFormat& f, int T, size_t smem, int max
 // K blocks of 64 columns per weight-stream stage of the pass kernel, and the descriptors.
 int pass_kernel_stage_blocks(const WeightFormat& f);
 void pass_encode_maps(const QMat& w, QMaps* out);
+// 3-D tiled tensor maps of a matrix's planes (x = one 16-byte chunk of 32 rows / one group of 32
+// scales, y = chunk / group, z = 32-row group) with the given box.
+void encode_qmat_maps(const QMat& w, int box_chunks, int box_groups, int box_rowgroups, QMaps* out);
 
 }  // namespace ls

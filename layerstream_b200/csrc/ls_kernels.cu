@@ -622,6 +622,7 @@ static void launch_attention_t(const AttnLaunch& a, size_t smem, cudaStream_t s)
 }
 
 void launch_attention(const AttnLaunch& a, cudaStream_t s) {
+  if (attention_tc_supported(a)) return launch_attention_tc(a, s);
   const size_t smem = ((size_t)a.M * a.hd + 2 * ATT_TILE * (a.hd + 1) + (size_t)a.M * (a.hd + 2)) * 4;
   switch (a.hd) {
     case 16: return launch_attention_t<16>(a, smem, s);

@@ -790,6 +790,7 @@ struct LsModel {
     a.max_ctx = (int)max_ctx;
     a.M = T;
     a.max_splits = att_slots;
+    a.err = &ctl->err;
     // attention bytes: new K/V rows written (f16) + q|k|v in and out (f32); the cached rows read are
     // added per replay from that pass's pos0 (prof_collect)
     pi = pb(1, (double)T * kv * 2 * 2 + (double)T * (h + 2 * kv) * 4 + (double)T * h * 4);
@@ -1168,10 +1169,51 @@ struct LsBatch {
   ArgPart* parts = nullptr;
   uint32_t *d_tok = nullptr, *d_argmax = nullptr, *d_m = nullptr, *d_next = nullptr;
   int *d_pos0 = nullptr, *d_err = nullptr;
+  float* inv_rms = nullptr;  // [max_rows] 1/rms of the rows a normed GEMV reads
+  // batched weight GEMM path: activations as f16 in the bt layout, split-K scratch
+  bool use_bg = false;
+  uint16_t *bt_a = nullptr, *bt_h = nullptr;  // GEMM inputs (K = hidden or q width) / SwiGLU output (K = inter)
+  float* bg_partial = nullptr;
+  unsigned* bg_tickets = nullptr;
   uint32_t *h_tok = nullptr, *h_m = nullptr, *h_next = nullptr;
   int *h_pos0 = nullptr, *h_err = nullptr;
   std::vector<uint64_t> pos;
   uint64_t passes = 0, h2d_bytes = 0, d2h_bytes = 0;
+
+  // Live profile: an event pair around every launch class of a pass (classes as LsBatchProfile).
+  bool prof_on = false;
+  std::vector<cudaEvent_t> prof_ev;
+  std::vector<std::pair<int, double>> prof_rec;  // (class, algorithmic bytes) per event pair
+  LsBatchProfile prof{};
+  int prof_begin(int cls, double bytes) {
+    if (!prof_on) return -1;
+    const size_t i = prof_rec.size();
+    while (prof_ev.size() < 2 * (i + 1)) {
+      cudaEvent_t e;
+      LS_CUDA(cudaEventCreate(&e));
+      prof_ev.push_back(e);
+    }
+    prof_rec.push_back({cls, bytes});
+    LS_CUDA(cudaEventRecord(prof_ev[2 * i], stream));
+    return (int)i;
+  }
+  void prof_end(int i) {
+    if (i >= 0) LS_CUDA(cudaEventRecord(prof_ev[2 * i + 1], stream));
+  }
+  void prof_collect() {  // after the pass's stream synchronize
+    for (size_t i = 0; i < prof_rec.size(); i++) {
+      float ms = 0;
+      LS_CUDA(cudaEventElapsedTime(&ms, prof_ev[2 * i], prof_ev[2 * i + 1]));
+      const int c = prof_rec[i].first;
+      prof.launches[c]++;
+      prof.ms[c] += ms;
+      prof.bytes[c] += prof_rec[i].second;
+    }
+    prof_rec.clear();
+  }
+  static double qbytes(const QMat& w) {
+    return (double)w.rows_pad * ((double)w.cols * w.bits / 8 + (double)w.cols / w.group * 2);
+  }
 
   template <class T>
   T* dalloc(size_t n) {
@@ -1327,6 +1369,32 @@ struct LsBatch {
     const LayerW& W = layer(0);
     for (int rows = 1; rows <= (int)max_rows; rows++)
       for (const QMat* w : {&W.qkv, &W.o, &W.gu, &W.down}) tc_scratch(*w, rows, &pf, &tk);
+    {
+      const char* e = getenv("LS_BGEMM");
+      use_bg = !(e && std::string(e) == "0") && (dm.inter % 8) == 0;
+      QMat head_fmt;  // the LM head's format (its planes may be streamed)
+      head_fmt.bits = c.embed_format.bits;
+      head_fmt.group = c.embed_format.group;
+      head_fmt.cols = (int)c.hidden;
+      head_fmt.rows = head_fmt.rows_pad = 32;
+      for (const QMat* w : {&W.qkv, &W.o, &W.gu, &W.down, static_cast<const QMat*>(&head_fmt)})
+        use_bg = use_bg && bgemm_supported(*w);
+    }
+    if (use_bg) {
+      size_t bpf = 0, btk = 0;
+      for (int rows = 1; rows <= (int)max_rows; rows++)
+        for (const QMat* w : {&W.qkv, &W.o, &W.gu, &W.down}) {
+          const BgemmPlan p = bgemm_plan(*w, rows, m->num_sms, false);
+          bpf = std::max(bpf, p.partial_floats);
+          btk = std::max(btk, p.tickets);
+        }
+      size_t rows_bt = 0;  // padded token-group rows of the largest pass
+      for (int rows = 1; rows <= (int)max_rows; rows++) rows_bt = std::max(rows_bt, bt_elems(rows, 1));
+      bt_a = dalloc<uint16_t>(rows_bt * std::max((int)h, dm.q_dim));
+      bt_h = dalloc<uint16_t>(rows_bt * I);
+      bg_partial = dalloc<float>(bpf);
+      bg_tickets = dalloc<unsigned>(btk);
+    }
     partial = dalloc<float>(pf);
     tickets = dalloc<unsigned>(tk);
     parts = dalloc<ArgPart>((size_t)(pad32((int)c.vocab) / 128 + c.vocab / kHeadRows + 2) * max_rows);
@@ -1338,6 +1406,7 @@ struct LsBatch {
     d_next = dalloc<uint32_t>(B);
     d_pos0 = dalloc<int>(B);
     d_err = dalloc<int>(1);
+    inv_rms = dalloc<float>(max_rows);
     h_tok = halloc<uint32_t>(max_rows);
     h_m = halloc<uint32_t>(B);
     h_next = halloc<uint32_t>(B);
@@ -1350,6 +1419,7 @@ struct LsBatch {
     cudaSetDevice(m->device);
     if (stream) cudaStreamSynchronize(stream);
     if (comm) nccl_api().comm_destroy(comm);
+    for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
     for (void* p : dev_allocs) cudaFree(p);
     for (void* p : host_allocs) cudaFreeHost(p);
     if (stream) cudaStreamDestroy(stream);
@@ -1371,6 +1441,10 @@ struct LsBatch {
     g.partial = partial;
     g.tickets = tickets;
     g.err = d_err;
+    if (norm_bf16) {  // the row norms once, not in every CTA
+      launch_inv_rms(xin, x_stride, M, (int)w.cols, g.eps, inv_rms, stream);
+      g.inv_rms = inv_rms;
+    }
     if (use_tc(w)) {
       choose_tc(w, M, m->num_sms, false, &g.ksplit, &g.grid_x);
       launch_gemv_tc(g, stream);
@@ -1396,10 +1470,45 @@ struct LsBatch {
     g.part_tile_offset = part_off;
     g.finalize = 0;
     g.err = d_err;
+    if (part_off == 0) launch_inv_rms(xin, (int)m->cfg.hidden, M, (int)m->cfg.hidden, g.eps, inv_rms, stream);
+    g.inv_rms = inv_rms;
     if (!use_tc(w)) LS_THROW(LS_ERR_ARG, "batches need a weight format the tensor-core GEMV supports");
     choose_tc(w, M, m->num_sms, true, &g.ksplit, &g.grid_x, &g.max_nt);
     launch_gemv_tc(g, stream);
     return g.grid_x;
+  }
+
+  // Batched weight GEMM of M rows of bt-layout activations xin.
+  void bg(const QMat& w, const uint16_t* xin, int M, int epi, float* y, int y_stride, uint16_t* yh, const uint16_t* bias) {
+    BgemmLaunch g;
+    g.w = w;
+    g.x = xin;
+    g.M = M;
+    g.epi = epi;
+    g.y = y;
+    g.y_stride = y_stride;
+    g.yh = yh;
+    g.bias = bias;
+    g.partial = bg_partial;
+    g.tickets = bg_tickets;
+    g.err = d_err;
+    launch_bgemm(g, bgemm_plan(w, M, m->num_sms, false), stream);
+  }
+  // LM head rows [first, first + rows) with the argmax epilogue over M rows of bt_a; returns the
+  // number of argmax parts written after part_off.
+  int bg_head(const QMat& w, int first, int rows, int M, int part_off) {
+    BgemmLaunch g;
+    g.w = w;
+    g.x = bt_a;
+    g.M = M;
+    g.epi = EPI_ARGMAX;
+    g.arg_parts = parts;
+    g.n_valid_rows = rows;
+    g.row_offset = first;
+    g.part_tile_offset = part_off;
+    g.err = d_err;
+    launch_bgemm(g, bgemm_plan(w, M, m->num_sms, true), stream);
+    return (w.rows_pad / 32 + 3) / 4;
   }
 
   // One pass over sequences [s0, s0 + ns), M rows each. head_mode 0: advance only; 1: argmax of
@@ -1407,8 +1516,10 @@ struct LsBatch {
   // (prefill of one sequence), pos += M.
   // Sum of the row-parallel partial y over the ranks, then the residual add into x.
   void reduce_into_x(size_t n) {
+    const int pi = prof_begin(6, (double)n * 4 * 2 * (tp_world - 1) / tp_world);
     nccl_check(nccl_api().all_reduce(ybuf, ybuf, n, ncclFloat32, ncclSum, comm, stream), "ncclAllReduce");
     launch_add(x, ybuf, n, stream);
+    prof_end(pi);
   }
 
   void pass(size_t s0, size_t ns, int M, const uint32_t* tokens, int head_mode) {
@@ -1442,8 +1553,20 @@ struct LsBatch {
       launch_embed_tokens(m->embed, d_tok, (int)T, x, h, (int)c.vocab, d_err, stream);
     }
     const int slots = (int)std::max<size_t>(1, std::min<size_t>(16, (maxpos + M + 63) / 64));
+    const int pp = prof_begin(7, 0);
+    double kv_rows = 0;  // cached + new positions of the pass's sequences (K/V rows per layer)
+    for (size_t i = 0; i < ns; i++) kv_rows += (double)pos[s0 + i] + M;
+    const double act = (double)T * 4;
     auto layer_fn = [&](const LayerW& W, size_t l) {
-      gemv(W.qkv, x, h, (int)T, EPI_BIAS_STORE, qkv, QS, W.in_norm, W.qkv_bias);
+      int pi = prof_begin(0, qbytes(W.qkv) + act * (h + QS));
+      if (use_bg) {
+        launch_bt_prep(x, h, (int)T, h, W.in_norm, nullptr, m->cfg.eps, bt_a, stream);
+        bg(W.qkv, bt_a, (int)T, EPI_BIAS_STORE, qkv, QS, nullptr, W.qkv_bias);
+      } else {
+        gemv(W.qkv, x, h, (int)T, EPI_BIAS_STORE, qkv, QS, W.in_norm, W.qkv_bias);
+      }
+      prof_end(pi);
+      pi = prof_begin(1, kv_rows * kv * 2 * 2 + act * (QS + dm.q_dim));
       AttnLaunch a;
       a.qkv = qkv;
       a.qkv_stride = QS;
@@ -1463,26 +1586,77 @@ struct LsBatch {
       a.pos0 = d_pos0;
       a.seq_stride = seq_stride;
       a.pdl = false;
+      a.err = d_err;
+      a.max_total = (int)(maxpos + M);
+      if (use_bg && attention_tc_supported(a)) {  // straight into the O GEMM's operand
+        int gn = 16, gg = 1;
+        bgemm_groups((int)T, &gn, &gg);
+        a.out_h = bt_a;
+        a.out_h_n = gn;
+      }
       launch_attention(a, stream);
+      if (use_bg && !a.out_h) launch_bt_prep(attn, dm.q_dim, (int)T, dm.q_dim, nullptr, nullptr, 0.f, bt_a, stream);
+      prof_end(pi);
+      pi = prof_begin(2, qbytes(W.o) + act * (dm.q_dim + 2 * h));
+      if (use_bg) {
+        if (tp) {
+          bg(W.o, bt_a, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+          prof_end(pi);
+          reduce_into_x(T * h);
+        } else {
+          bg(W.o, bt_a, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+          prof_end(pi);
+        }
+        pi = prof_begin(3, qbytes(W.gu) + act * (h + I));
+        launch_bt_prep(x, h, (int)T, h, W.post_norm, nullptr, m->cfg.eps, bt_a, stream);
+        bg(W.gu, bt_a, (int)T, EPI_SWIGLU_H, nullptr, 0, bt_h, nullptr);
+        prof_end(pi);
+        pi = prof_begin(4, qbytes(W.down) + act * (I + 2 * h));
+        if (tp) {
+          bg(W.down, bt_h, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+          prof_end(pi);
+          reduce_into_x(T * h);
+        } else {
+          bg(W.down, bt_h, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+          prof_end(pi);
+        }
+        return;
+      }
       if (tp) {  // row-parallel O: this rank's heads' share of every output, summed over the ranks
         gemv(W.o, attn, dm.q_dim, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+        prof_end(pi);
         reduce_into_x(T * h);
       } else {
         gemv(W.o, attn, dm.q_dim, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+        prof_end(pi);
       }
+      pi = prof_begin(3, qbytes(W.gu) + act * (h + I));
       gemv(W.gu, x, h, (int)T, EPI_SWIGLU, hbuf, I, W.post_norm, nullptr);
+      prof_end(pi);
+      pi = prof_begin(4, qbytes(W.down) + act * (I + 2 * h));
       if (tp) {  // row-parallel down over this rank's intermediate slice
         gemv(W.down, hbuf, I, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+        prof_end(pi);
         reduce_into_x(T * h);
       } else {
         gemv(W.down, hbuf, I, (int)T, EPI_RESID, x, h, nullptr, nullptr);
+        prof_end(pi);
       }
     };
     // head over all T rows (verify) or the last row (prefill end)
     const float* hx = head_mode == 2 ? x + (T - 1) * h : x;
     const int hM = head_mode == 2 ? 1 : (int)T;
     int nparts = 0;
-    auto head_fn = [&](const QMat& w, int first, int rows) { nparts += head(w, first, rows, hx, hM, nparts); };
+    auto head_fn = [&](const QMat& w, int first, int rows) {
+      const int pi = prof_begin(5, qbytes(w) + (double)hM * h * 4);
+      if (use_bg) {
+        if (nparts == 0) launch_bt_prep(hx, h, hM, h, nullptr, m->final_norm, m->cfg.eps, bt_a, stream);
+        nparts += bg_head(w, first, rows, hM, nparts);
+      } else {
+        nparts += head(w, first, rows, hx, hM, nparts);
+      }
+      prof_end(pi);
+    };
     if (streamed) {
       m->stream_weights(head_mode != 0, stream, layer_fn, head_fn);
     } else {
@@ -1498,7 +1672,9 @@ struct LsBatch {
       // vocabulary-parallel head: each rank's first maximum per row (global ids), gathered from
       // every rank, then reduced with the same first-maximum rule: identical on all ranks
       launch_row_best(parts, nparts, hM, tp_best, stream);
+      const int pi = prof_begin(6, (double)hM * 8 * (tp_world - 1));
       nccl_check(nccl_api().all_gather(tp_best, tp_all, (size_t)hM * 2, ncclUint32, comm, stream), "ncclAllGather");
+      prof_end(pi);
       fparts = tp_all;
       fnparts = tp_world;
     }
@@ -1510,8 +1686,10 @@ struct LsBatch {
       LS_CUDA(cudaMemcpyAsync(h_next, d_next, nres * 4, cudaMemcpyDeviceToHost, stream));
       d2h_bytes += 2 * nres * 4;
     }
+    prof_end(pp);
     LS_CUDA(cudaMemcpyAsync(h_err, d_err, 4, cudaMemcpyDeviceToHost, stream));
     LS_CUDA(cudaStreamSynchronize(stream));
+    if (prof_on) prof_collect();
     passes++;
     if (*h_err == 1) LS_THROW(LS_ERR_DEVICE, "a tensor-core kernel gave up waiting on an mbarrier (bounded wait)");
     if (*h_err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
@@ -2115,6 +2293,23 @@ int ls_batch_report(const LsBatch* b, uint64_t* passes, uint64_t* h2d_bytes, uin
   });
 }
 
+int ls_batch_profile_enable(LsBatch* b, int on) {
+  return guard([&] {
+    NEED(b);
+    b->prof_on = on != 0;
+    b->prof = LsBatchProfile{};
+    b->prof_rec.clear();
+  });
+}
+
+int ls_batch_profile(const LsBatch* b, LsBatchProfile* out) {
+  return guard([&] {
+    NEED(b);
+    NEED(out);
+    *out = b->prof;
+  });
+}
+
 int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
                       const float* qkv, const uint16_t* k_cache, const uint16_t* v_cache, float* out, int iters, double* ms) {
   return guard([&] {
@@ -2180,6 +2375,8 @@ int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope
     a.max_ctx = (int)ctx;
     a.M = (int)M;
     a.max_splits = slots;
+    a.max_total = (int)(pos0 + M);
+    a.err = &dctl->err;
     launch_attention(a, st);
     if (iters > 1) {
       cudaEvent_t e0, e1;
@@ -2198,7 +2395,10 @@ int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope
       *ms = 0;
     }
     LS_CUDA(cudaMemcpyAsync(out, dout, M * H * 4, cudaMemcpyDeviceToHost, st));
+    int herr = 0;
+    LS_CUDA(cudaMemcpyAsync(&herr, &dctl->err, 4, cudaMemcpyDeviceToHost, st));
     LS_CUDA(cudaStreamSynchronize(st));
+    if (herr == 1) LS_THROW(LS_ERR_DEVICE, "the tensor-core attention gave up waiting on an mbarrier (bounded wait)");
     (void)dev;
   });
 }
@@ -2236,6 +2436,76 @@ int ls_qgemv_host(int bits, int group, const uint8_t* rows_raw, uint64_t rows, u
     }
     LS_CUDA(cudaMemcpy(y, dy, M * rows * 4, cudaMemcpyDeviceToHost));
     qweights_check(q.get());
+  });
+}
+
+int ls_bgemm_host(int bits, int group, const uint8_t* rows_raw, uint64_t rows, uint64_t cols, const float* x, uint64_t M, float* y,
+                  int iters, double* ms) {
+  return guard([&] {
+    NEED(rows_raw);
+    NEED(x);
+    NEED(y);
+    if (M == 0 || M > 8192) LS_THROW(LS_ERR_ARG, "1..8192 token rows");
+    if (cols % 8) LS_THROW(LS_ERR_ARG, "cols must be a multiple of 8");
+    int dev = 0, nsm = 0;
+    LS_CUDA(cudaGetDevice(&dev));
+    LS_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    std::unique_ptr<LsQWeights> q(new LsQWeights);
+    qweights_upload(q.get(), dev, bits, group, rows_raw, rows, cols);
+    if (!bgemm_supported(q->w)) LS_THROW(LS_ERR_ARG, "format not supported by the batched GEMM");
+    const BgemmPlan p = bgemm_plan(q->w, (int)M, nsm, false);
+    std::vector<void*> bufs;
+    auto dal = [&](size_t bytes) {
+      void* d = nullptr;
+      LS_CUDA(cudaMalloc(&d, std::max<size_t>(bytes, 16)));
+      bufs.push_back(d);
+      LS_CUDA(cudaMemset(d, 0, std::max<size_t>(bytes, 16)));
+      return d;
+    };
+    struct Free {
+      std::vector<void*>* b;
+      ~Free() {
+        for (void* d : *b) cudaFree(d);
+      }
+    } fr{&bufs};
+    auto* dx = static_cast<float*>(dal(M * cols * 4));
+    auto* dxh = static_cast<uint16_t*>(dal(bt_elems((int)M, (int)cols) * 2));
+    auto* dy = static_cast<float*>(dal(M * rows * 4));
+    auto* dpart = static_cast<float*>(dal(p.partial_floats * 4));
+    auto* dtick = static_cast<unsigned*>(dal(p.tickets * 4));
+    auto* derr = static_cast<int*>(dal(4));
+    LS_CUDA(cudaMemcpy(dx, x, M * cols * 4, cudaMemcpyHostToDevice));
+    launch_bt_prep(dx, (int)cols, (int)M, (int)cols, nullptr, nullptr, 0.f, dxh, 0);
+    BgemmLaunch g;
+    g.w = q->w;
+    g.x = dxh;
+    g.M = (int)M;
+    g.epi = EPI_STORE;
+    g.y = dy;
+    g.y_stride = (int)rows;
+    g.partial = dpart;
+    g.tickets = dtick;
+    g.err = derr;
+    launch_bgemm(g, p, 0);
+    LS_CUDA(cudaDeviceSynchronize());
+    if (iters > 1 && ms) {
+      cudaEvent_t a, b;
+      LS_CUDA(cudaEventCreate(&a));
+      LS_CUDA(cudaEventCreate(&b));
+      LS_CUDA(cudaEventRecord(a, 0));
+      for (int i = 0; i < iters; i++) launch_bgemm(g, p, 0);
+      LS_CUDA(cudaEventRecord(b, 0));
+      LS_CUDA(cudaEventSynchronize(b));
+      float t = 0;
+      LS_CUDA(cudaEventElapsedTime(&t, a, b));
+      *ms = t / iters;
+      cudaEventDestroy(a);
+      cudaEventDestroy(b);
+    }
+    int herr = 0;
+    LS_CUDA(cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost));
+    if (herr) LS_THROW(LS_ERR_DEVICE, "the batched GEMM gave up waiting on an mbarrier (bounded wait)");
+    LS_CUDA(cudaMemcpy(y, dy, M * rows * 4, cudaMemcpyDeviceToHost));
   });
 }
 

@@ -995,6 +995,15 @@ static size_t pass_stage_bytes(const WeightFormat& f) {
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
 void pass_encode_maps(const QMat& w, QMaps* out) {
+  WeightFormat f;
+  f.bits = w.bits;
+  f.group = w.group;
+  const int kb = tc_kb(w.bits, w.group), cpb = kb / (128 / w.bits), ns = kb >= w.group ? kb / w.group : 1;
+  const int nb = pass_kernel_stage_blocks(f);
+  encode_qmat_maps(w, cpb * nb, ns * nb, 8, out);
+}
+
+void encode_qmat_maps(const QMat& w, int box_chunks, int box_groups, int box_rowgroups, QMaps* out) {
   using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
                               const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                               CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -1006,17 +1015,14 @@ void pass_encode_maps(const QMat& w, QMaps* out) {
     if (q != cudaDriverEntryPointSuccess || !fn) LS_THROW(-3, "cuTensorMapEncodeTiled is not available from the driver");
     encode = reinterpret_cast<Encode>(fn);
   }
-  WeightFormat f;
-  f.bits = w.bits;
-  f.group = w.group;
-  const int kb = tc_kb(w.bits, w.group), cpb = kb / (128 / w.bits), ns = kb >= w.group ? kb / w.group : 1;
-  const int nb = pass_kernel_stage_blocks(f);
   const cuuint64_t tiles32 = (cuuint64_t)w.rows_pad / 32, nch = (cuuint64_t)w.chunks(), ngr = (cuuint64_t)w.groups();
   const cuuint32_t es[3] = {1, 1, 1};
+  if (box_chunks < 1 || box_chunks > 256 || box_groups < 1 || box_groups > 256 || box_rowgroups < 1 || box_rowgroups > 256)
+    LS_THROW(-3, "tensor map box out of range");
   {
     const cuuint64_t dims[3] = {128, nch, tiles32};
     const cuuint64_t strides[2] = {512, nch * 512};
-    const cuuint32_t box[3] = {128, (cuuint32_t)(cpb * nb), 8};
+    const cuuint32_t box[3] = {128, (cuuint32_t)box_chunks, (cuuint32_t)box_rowgroups};
     const CUresult r = encode(&out->data, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(w.data), dims, strides, box, es,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1025,7 +1031,7 @@ void pass_encode_maps(const QMat& w, QMaps* out) {
   {
     const cuuint64_t dims[3] = {32, ngr, tiles32};
     const cuuint64_t strides[2] = {64, ngr * 64};
-    const cuuint32_t box[3] = {32, (cuuint32_t)(ns * nb), 8};
+    const cuuint32_t box[3] = {32, (cuuint32_t)box_groups, (cuuint32_t)box_rowgroups};
     const CUresult r = encode(&out->scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(w.scales), dims, strides, box,
                               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
