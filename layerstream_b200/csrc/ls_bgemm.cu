@@ -64,7 +64,10 @@ struct BgShape {
 };
 
 template <int BITS, int G>
-__global__ void __launch_bounds__(BG_THREADS, 2)
+#ifndef BG_MIN_BLOCKS
+#define BG_MIN_BLOCKS 2
+#endif
+__global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
     bgemm_kernel(const __grid_constant__ BgemmLaunch g, const __grid_constant__ BgemmPlan p, const __grid_constant__ QMaps maps) {
   using SH = BgShape<BITS, G>;
   constexpr int KB = SH::KB, NS = SH::NS, CPB = SH::CPB, ACOLS = SH::ACOLS, ABUF = SH::ABUF;

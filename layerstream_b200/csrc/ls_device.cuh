@@ -102,10 +102,32 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on an mbarrier phase. Returns false (and raises the CTA's abort flag) on timeout.
+__device__ __forceinline__ bool mbar_poll(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes (or ~20 us pass)
+// instead of spinning, leaving the issue slots to the warps doing the work.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on an mbarrier phase (about a second at most). Returns false (and raises the CTA's
+// abort flag) on timeout. A non-blocking test first: a completed phase costs no suspension.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
-  for (uint32_t i = 0; i < (1u << 20); i++) {
-    if (mbar_try(b, parity)) return true;
+  if (mbar_poll(b, parity)) return true;
+  for (uint32_t i = 0; i < (1u << 16); i++) {
+    if (mbar_try_sleep(b, parity)) return true;
     if (*abort) return false;
   }
   *abort = 1;

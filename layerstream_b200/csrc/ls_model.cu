@@ -1175,6 +1175,8 @@ struct LsBatch {
   uint16_t *bt_a = nullptr, *bt_h = nullptr;  // GEMM inputs (K = hidden or q width) / SwiGLU output (K = inter)
   float* bg_partial = nullptr;
   unsigned* bg_tickets = nullptr;
+  bool graphs_on = true;                       // LS_BATCH_GRAPHS=0 launches every pass eagerly
+  std::map<int, cudaGraphExec_t> bgraphs;      // decode passes by block length
   uint32_t *h_tok = nullptr, *h_m = nullptr, *h_next = nullptr;
   int *h_pos0 = nullptr, *h_err = nullptr;
   std::vector<uint64_t> pos;
@@ -1380,6 +1382,10 @@ struct LsBatch {
       for (const QMat* w : {&W.qkv, &W.o, &W.gu, &W.down, static_cast<const QMat*>(&head_fmt)})
         use_bg = use_bg && bgemm_supported(*w);
     }
+    {
+      const char* e = getenv("LS_BATCH_GRAPHS");
+      graphs_on = !(e && std::string(e) == "0");
+    }
     if (use_bg) {
       size_t bpf = 0, btk = 0;
       for (int rows = 1; rows <= (int)max_rows; rows++)
@@ -1418,6 +1424,7 @@ struct LsBatch {
   ~LsBatch() {
     cudaSetDevice(m->device);
     if (stream) cudaStreamSynchronize(stream);
+    for (auto& kv : bgraphs) cudaGraphExecDestroy(kv.second);  // before the communicator its nodes use
     if (comm) nccl_api().comm_destroy(comm);
     for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
     for (void* p : dev_allocs) cudaFree(p);
@@ -1540,19 +1547,25 @@ struct LsBatch {
     for (size_t i = 0; i < T; i++)
       if (tokens[i] >= c.vocab) LS_THROW(LS_ERR_ARG, "token id " + std::to_string(tokens[i]) + " is outside the vocabulary");
     std::memcpy(h_tok, tokens, T * 4);
+    h2d_bytes += T * 4 + ns * 4;
+    const bool streamed = m->mode != LS_MODE_RESIDENT;
+    // A decode pass of every sequence on resident weights replays a captured graph (one per block
+    // length): positions and tokens come from the pinned buffers at replay time, the attention is
+    // sized for the whole context.
+    const bool graphed = graphs_on && !streamed && !prof_on && use_bg && s0 == 0 && ns == B && head_mode == 1;
+    auto enqueue = [&](bool for_graph) {
     LS_CUDA(cudaMemcpyAsync(d_tok, h_tok, T * 4, cudaMemcpyHostToDevice, stream));
     LS_CUDA(cudaMemcpyAsync(d_pos0, h_pos0, ns * 4, cudaMemcpyHostToDevice, stream));
     LS_CUDA(cudaMemsetAsync(d_err, 0, 4, stream));
-    h2d_bytes += T * 4 + ns * 4;
-    const bool streamed = m->mode != LS_MODE_RESIDENT;
     if (streamed) {
       launch_embed_raw_tokens(m->host_embed_dev, c.embed_row_bytes(), c.embed_format.bits, c.embed_format.group, d_tok, x, h,
                               (int)c.vocab, (int)T, d_err, stream);
-      m->bytes_read += T * c.embed_row_bytes();
+      m->bytes_read += T * c.embed_row_bytes();  // streamed passes are never graphed
     } else {
       launch_embed_tokens(m->embed, d_tok, (int)T, x, h, (int)c.vocab, d_err, stream);
     }
-    const int slots = (int)std::max<size_t>(1, std::min<size_t>(16, (maxpos + M + 63) / 64));
+    const size_t span = for_graph ? max_ctx : maxpos + M;  // positions the attention may see
+    const int slots = (int)std::max<size_t>(1, std::min<size_t>(16, (span + 63) / 64));
     const int pp = prof_begin(7, 0);
     double kv_rows = 0;  // cached + new positions of the pass's sequences (K/V rows per layer)
     for (size_t i = 0; i < ns; i++) kv_rows += (double)pos[s0 + i] + M;
@@ -1587,7 +1600,7 @@ struct LsBatch {
       a.seq_stride = seq_stride;
       a.pdl = false;
       a.err = d_err;
-      a.max_total = (int)(maxpos + M);
+      a.max_total = (int)span;
       if (use_bg && attention_tc_supported(a)) {  // straight into the O GEMM's operand
         int gn = 16, gg = 1;
         bgemm_groups((int)T, &gn, &gg);
@@ -1684,10 +1697,32 @@ struct LsBatch {
       const size_t nres = head_mode == 1 ? ns : 1;
       LS_CUDA(cudaMemcpyAsync(h_m, d_m, nres * 4, cudaMemcpyDeviceToHost, stream));
       LS_CUDA(cudaMemcpyAsync(h_next, d_next, nres * 4, cudaMemcpyDeviceToHost, stream));
-      d2h_bytes += 2 * nres * 4;
     }
     prof_end(pp);
     LS_CUDA(cudaMemcpyAsync(h_err, d_err, 4, cudaMemcpyDeviceToHost, stream));
+    };
+    if (graphed) {
+      auto it = bgraphs.find(M);
+      if (it == bgraphs.end()) {
+        cudaGraph_t graph;
+        LS_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+        try {
+          enqueue(true);
+        } catch (...) {
+          cudaStreamEndCapture(stream, &graph);
+          throw;
+        }
+        LS_CUDA(cudaStreamEndCapture(stream, &graph));
+        cudaGraphExec_t exec;
+        LS_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+        cudaGraphDestroy(graph);
+        it = bgraphs.emplace(M, exec).first;
+      }
+      LS_CUDA(cudaGraphLaunch(it->second, stream));
+    } else {
+      enqueue(false);
+    }
+    if (head_mode) d2h_bytes += 2 * (head_mode == 1 ? ns : 1) * 4;
     LS_CUDA(cudaStreamSynchronize(stream));
     if (prof_on) prof_collect();
     passes++;
