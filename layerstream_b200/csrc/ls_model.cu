@@ -26,6 +26,7 @@ using namespace ls;
 namespace {
 
 constexpr int kPrefillChunk = 128;  // src/model.rs:14
+constexpr size_t kPrefillSeqs = 16;  // sequences of a batch prefilled by one pass (<= 2048 rows)
 constexpr int kHeadRows = 4096;     // src/provider.rs:21
 constexpr int kMaxDraft = 32;       // src/spec.rs:52
 constexpr int kMaxT = kPrefillChunk;
@@ -1344,7 +1345,9 @@ struct LsBatch {
     const Config& c = m->cfg;
     if (tp_world < 1 || tp_rank < 0 || tp_rank >= tp_world) LS_THROW(LS_ERR_ARG, "rank must be in 0..world-1");
     if (tp_world > 1 && !nccl_id) LS_THROW(LS_ERR_ARG, "a tensor-parallel batch needs the NCCL unique id");
-    max_rows = std::max<size_t>(kMaxT, B * max_block);
+    // rows of a pass: a verify block of every sequence, or one prefill chunk of up to
+    // kPrefillSeqs sequences at a time
+    max_rows = std::max<size_t>({(size_t)kMaxT, B * max_block, std::min<size_t>(B, kPrefillSeqs) * kPrefillChunk});
     if (max_rows > 8192) LS_THROW(LS_ERR_ARG, "batch x block exceeds 8192 rows per pass");
     LS_CUDA(cudaSetDevice(m->device));
     LS_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
@@ -1462,11 +1465,11 @@ struct LsBatch {
 
   // Argmax parts of the LM head rows [first, first + rows) (planes w) over M rows of x (final
   // RMSNorm folded in), written after part_off earlier parts; returns this launch's CTA count.
-  int head(const QMat& w, int first, int rows, const float* xin, int M, int part_off) {
+  int head(const QMat& w, int first, int rows, const float* xin, int x_stride, int M, int part_off) {
     GemvLaunch g;
     g.w = w;
     g.x = xin;
-    g.x_stride = (int)m->cfg.hidden;
+    g.x_stride = x_stride;
     g.M = M;
     g.norm_f32 = m->final_norm;
     g.eps = m->cfg.eps;
@@ -1477,7 +1480,7 @@ struct LsBatch {
     g.part_tile_offset = part_off;
     g.finalize = 0;
     g.err = d_err;
-    if (part_off == 0) launch_inv_rms(xin, (int)m->cfg.hidden, M, (int)m->cfg.hidden, g.eps, inv_rms, stream);
+    if (part_off == 0) launch_inv_rms(xin, x_stride, M, (int)m->cfg.hidden, g.eps, inv_rms, stream);
     g.inv_rms = inv_rms;
     if (!use_tc(w)) LS_THROW(LS_ERR_ARG, "batches need a weight format the tensor-core GEMV supports");
     choose_tc(w, M, m->num_sms, true, &g.ksplit, &g.grid_x, &g.max_nt);
@@ -1657,16 +1660,18 @@ struct LsBatch {
       }
     };
     // head over all T rows (verify) or the last row (prefill end)
-    const float* hx = head_mode == 2 ? x + (T - 1) * h : x;
-    const int hM = head_mode == 2 ? 1 : (int)T;
+    // head rows: every row (verify) or the last row of every sequence (end of a prefill)
+    const float* hx = head_mode == 2 ? x + (size_t)(M - 1) * h : x;
+    const int hstride = head_mode == 2 ? M * h : h;
+    const int hM = head_mode == 2 ? (int)ns : (int)T;
     int nparts = 0;
     auto head_fn = [&](const QMat& w, int first, int rows) {
       const int pi = prof_begin(5, qbytes(w) + (double)hM * h * 4);
       if (use_bg) {
-        if (nparts == 0) launch_bt_prep(hx, h, hM, h, nullptr, m->final_norm, m->cfg.eps, bt_a, stream);
+        if (nparts == 0) launch_bt_prep(hx, hstride, hM, h, nullptr, m->final_norm, m->cfg.eps, bt_a, stream);
         nparts += bg_head(w, first, rows, hM, nparts);
       } else {
-        nparts += head(w, first, rows, hx, hM, nparts);
+        nparts += head(w, first, rows, hx, hstride, hM, nparts);
       }
       prof_end(pi);
     };
@@ -1692,9 +1697,9 @@ struct LsBatch {
       fnparts = tp_world;
     }
     if (head_mode == 1) launch_batch_accept(fparts, fnparts, (int)T, M, d_tok, d_argmax, d_m, d_next, stream);
-    else if (head_mode == 2) launch_batch_accept(fparts, fnparts, 1, 1, d_tok, d_argmax, d_m, d_next, stream);
+    else if (head_mode == 2) launch_batch_accept(fparts, fnparts, hM, 1, d_tok, d_argmax, d_m, d_next, stream);
     if (head_mode) {
-      const size_t nres = head_mode == 1 ? ns : 1;
+      const size_t nres = ns;
       LS_CUDA(cudaMemcpyAsync(h_m, d_m, nres * 4, cudaMemcpyDeviceToHost, stream));
       LS_CUDA(cudaMemcpyAsync(h_next, d_next, nres * 4, cudaMemcpyDeviceToHost, stream));
     }
@@ -1722,7 +1727,7 @@ struct LsBatch {
     } else {
       enqueue(false);
     }
-    if (head_mode) d2h_bytes += 2 * (head_mode == 1 ? ns : 1) * 4;
+    if (head_mode) d2h_bytes += 2 * ns * 4;
     LS_CUDA(cudaStreamSynchronize(stream));
     if (prof_on) prof_collect();
     passes++;
@@ -1743,6 +1748,27 @@ struct LsBatch {
     return h_next[0];
   }
 
+  // Every sequence's prompt from position 0 (src/model.rs:111-119 per sequence: 128-token chunks):
+  // chunk i of up to kPrefillSeqs sequences runs as one pass; returns each sequence's greedy token
+  // after its prompt.
+  std::vector<uint32_t> prefill_all(const uint32_t* prompts, uint64_t plen) {
+    if (plen == 0) LS_THROW(LS_ERR_ARG, "no tokens to process");
+    std::vector<uint32_t> firsts(B), chunk;
+    for (size_t s0 = 0; s0 < B; s0 += kPrefillSeqs) {
+      const size_t ns = std::min<size_t>(kPrefillSeqs, B - s0);
+      for (size_t i = 0; i < ns; i++)
+        if (pos[s0 + i] + plen > max_ctx) LS_THROW(LS_ERR_ARG, "context is full");
+      for (uint64_t off = 0; off < plen; off += kPrefillChunk) {
+        const uint64_t len = std::min<uint64_t>(kPrefillChunk, plen - off);
+        chunk.resize(ns * len);
+        for (size_t i = 0; i < ns; i++) std::memcpy(chunk.data() + i * len, prompts + (s0 + i) * plen + off, len * 4);
+        pass(s0, ns, (int)len, chunk.data(), off + len == plen ? 2 : 0);
+      }
+      for (size_t i = 0; i < ns; i++) firsts[s0 + i] = h_next[i];
+    }
+    return firsts;
+  }
+
   // The decode loop of src/spec.rs:94-149 for every sequence, with the prompt-lookup drafter; all
   // sequences verify one k+1 block per pass (a sequence that has finished stays in the pass at a
   // frozen position, its results ignored).
@@ -1756,9 +1782,10 @@ struct LsBatch {
     const double t0 = now_s();
     std::vector<std::vector<uint32_t>> outs(B), hist(B);
     std::vector<char> active(B, 1);
+    std::vector<uint32_t> firsts = prefill_all(prompts, plen);
     for (size_t sq = 0; sq < B; sq++) {
       const uint32_t* p = prompts + sq * plen;
-      const uint32_t a = prefill(sq, p, plen);
+      const uint32_t a = firsts[sq];
       outs[sq].push_back(a);
       hist[sq].assign(p, p + plen);
       hist[sq].push_back(a);
