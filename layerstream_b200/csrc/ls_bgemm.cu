@@ -92,6 +92,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
   const int nkb = kb1 - kb0, nst = (nkb + KST - 1) / KST;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) BG_CTA_TIME(0);
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
@@ -118,21 +119,37 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
   const uint32_t tmem = s_tmem;
   const uint32_t d_col = tmem + ABUF * ACOLS;
   bool failed = false;
+  // everything but the producer's early weight loads waits for the previous kernel (no-op without
+  // the launch attribute)
+  if (warp != BG_PRODUCER) pdl_wait();
 
   if (warp == BG_PRODUCER) {
     if (lane == 0) {
       int issued = 0;
       const uint16_t* xg = g.x + bt_off(m0, 0, K, N);  // this token group's block
-      for (int i = 0; i < nst; i++) {
-        const int s = i % S, kb = kb0 + i * KST, nv = min(KST, kb1 - kb);
-        if (i >= S && !tc::mbar_wait(&empty[s], ((i / S) & 1) ^ 1, &s_abort)) {
-          failed = true;
-          break;
-        }
+      // the weights do not depend on the previous kernel: the first ring of stages starts loading
+      // before griddepcontrol.wait (programmatic dependent launch), the activations after it
+      auto load_w = [&](int i) {
+        const int s = i % S, kb = kb0 + i * KST;
         const uint32_t st = tc::su32(smem + (size_t)s * STAGE);
-        tc::mbar_expect_tx(&full[s], W_ST + S_ST + X_KB * nv);
+        tc::mbar_expect_tx_only(&full[s], W_ST + S_ST);
         tc::tma_load_3d(st, &maps.data, 0, kb * CPB, t128 * 4, &full[s]);
         tc::tma_load_3d(st + W_ST, &maps.scales, 0, kb * NS, t128 * 4, &full[s]);
+      };
+      const int npre = min(S, nst);
+      for (int i = 0; i < npre; i++) load_w(i);
+      pdl_wait();
+      for (int i = 0; i < nst; i++) {
+        const int s = i % S, kb = kb0 + i * KST, nv = min(KST, kb1 - kb);
+        if (i >= S) {
+          if (!tc::mbar_wait(&empty[s], ((i / S) & 1) ^ 1, &s_abort)) {
+            failed = true;
+            break;
+          }
+          load_w(i);
+        }
+        const uint32_t st = tc::su32(smem + (size_t)s * STAGE);
+        tc::mbar_expect_tx(&full[s], X_KB * nv);  // the stage's arrival, with its activation bytes
         tc::bulk_load(st + W_ST + S_ST, xg + (size_t)kb * (KB / 8) * N * 8, X_KB * nv, &full[s]);
         BG_STAMP(0, i);
         issued = i + 1;
@@ -401,6 +418,8 @@ __global__ void bt_prep_kernel(const float* __restrict__ x, int x_stride, int M,
   const int t = blockIdx.x;
   __shared__ float s_red[4];
   __shared__ float s_inv;
+  pdl_trigger();
+  pdl_wait();  // x is the previous kernel's output
   const float* xr = x + (size_t)t * x_stride;
   const bool live = t < M;
   const bool norm = nb != nullptr || nf != nullptr;
@@ -450,8 +469,7 @@ void launch_bt_prep(const float* x, int x_stride, int M, int K, const uint16_t* 
   if (K % 8) LS_THROW(-1, "the bt layout needs K to be a multiple of 8");
   int N = 16, ng = 1;
   bgemm_groups(M, &N, &ng);
-  bt_prep_kernel<<<ng * N, 128, 0, s>>>(x, x_stride, M, K, N, norm_bf16, norm_f32, eps, out);
-  LS_CUDA(cudaGetLastError());
+  launch_pdl(bt_prep_kernel, dim3(ng * N), dim3(128), 0, s, x, x_stride, M, K, N, norm_bf16, norm_f32, eps, out);
 }
 
 // ---- host side ----
@@ -517,8 +535,7 @@ static void launch_bg_t(const BgemmLaunch& g, const BgemmPlan& p, cudaStream_t s
   const QMaps maps = bg_maps(g.w, p.kstage, SH::CPB, SH::NS);
   ensure_smem(bgemm_kernel<BITS, G>, p.smem);
   const dim3 grid((g.w.rows_pad / 32 + 3) / 4, p.ngroups, p.ks);
-  bgemm_kernel<BITS, G><<<grid, BG_THREADS, p.smem, s>>>(g, p, maps);
-  LS_CUDA(cudaGetLastError());
+  launch_pdl(bgemm_kernel<BITS, G>, grid, dim3(BG_THREADS), p.smem, s, g, p, maps);
 }
 
 void launch_bgemm(const BgemmLaunch& g, const BgemmPlan& p, cudaStream_t s) {

@@ -1601,7 +1601,7 @@ struct LsBatch {
       a.nseq = (int)ns;
       a.pos0 = d_pos0;
       a.seq_stride = seq_stride;
-      a.pdl = false;
+      a.pdl = use_bg;  // positions come from the pass's host upload, before every kernel
       a.err = d_err;
       a.max_total = (int)span;
       if (use_bg && attention_tc_supported(a)) {  // straight into the O GEMM's operand
