@@ -37,6 +37,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+# the pass kernel's critical CTA per phase (last to reach the closing barrier): where its time went
+CRIT_SEGMENTS = ("prep", "first_stage", "first_item", "more_items", "to_barrier", "barrier")
 MICRO_SHAPES = {"qkv": (1152, 896), "o": (896, 896), "gate_up": (9728, 896), "down": (896, 4864), "head": (151936, 896)}
 
 CONFIGS = {
@@ -755,7 +757,8 @@ def main():
                 if q["launches"]:
                     phases[c] = {"us": q["ms"] * 1e3 / q["launches"], "busy_us": q["busy_ms"] * 1e3 / q["launches"],
                                  "gbs": q["bytes"] / q["ms"] * 1e3 / 1e9 if q["ms"] > 0 else None,
-                                 "per": "layer" if c != "head" else "pass"}
+                                 "per": "layer" if c != "head" else "pass",
+                                 "critical_cta_us": dict(zip(CRIT_SEGMENTS, (v * 1e3 / q["launches"] for v in q["crit_ms"])))}
         roof = {"bound": "hbm", "kernel": "pass_kernel (one persistent launch per verify pass)", "achieved": achieved,
                 "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                 "traffic": profile_traffic(f"pass_kernel-config{args.config}"), "algorithmic_bytes_per_launch": b,

@@ -89,6 +89,13 @@ typedef struct LsProfile {
   double ms[LS_PROF_CLASSES];
   double bytes[LS_PROF_CLASSES];
   double busy_ms[LS_PROF_CLASSES];
+  /* Persistent pass kernel only: the phase's critical CTA (the last to arrive at the barrier that
+   * closes it), its time split into 0 preparation (RMS statistics; attention: query rows staged),
+   * 1 staging of its first item (attention: first context tile in shared memory), 2 the first
+   * item's K loop and epilogue (attention: scores, values, slot state published), 3 its further
+   * items (attention: the slot merge), 4 from its last item to its arrival at the barrier, 5 from
+   * that arrival until the last CTA left the barrier; averaged over the layers like ms. */
+  double crit_ms[LS_PROF_CLASSES][6];
 } LsProfile;
 
 /* Live profile of a batch: CUDA-event time of every launch class of its passes. Classes: 0 QKV,

@@ -42,7 +42,7 @@ PROF_CLASSES = ("qkv", "attention", "o", "gate_up", "down", "head", "pass")
 
 class Profile(C.Structure):
     _fields_ = [("launches", C.c_uint64 * 7), ("ms", C.c_double * 7), ("bytes", C.c_double * 7),
-                ("busy_ms", C.c_double * 7)]
+                ("busy_ms", C.c_double * 7), ("crit_ms", (C.c_double * 6) * 7)]
 
 
 BATCH_PROF_CLASSES = ("qkv", "attention", "o", "gate_up", "down", "head", "collective", "pass")
@@ -221,7 +221,8 @@ class Model:
     def profile(self) -> dict:
         p = Profile()
         _check(lib().ls_model_profile(self._h, C.byref(p)))
-        return {c: {"launches": p.launches[i], "ms": p.ms[i], "bytes": p.bytes[i], "busy_ms": p.busy_ms[i]}
+        return {c: {"launches": p.launches[i], "ms": p.ms[i], "bytes": p.bytes[i], "busy_ms": p.busy_ms[i],
+                    "crit_ms": list(p.crit_ms[i])}
                 for i, c in enumerate(PROF_CLASSES)}
 
     def report(self) -> dict:

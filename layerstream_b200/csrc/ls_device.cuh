@@ -122,6 +122,19 @@ __device__ __forceinline__ bool mbar_try_sleep(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Bounded wait without a suspend hint: try_wait blocks for a short hardware-defined time per call,
+// so a completed phase is seen with the least delay (for the short hand-offs inside a K loop).
+// Bounded by an iteration count (well under a few seconds); false (and the CTA's abort flag) on
+// timeout.
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t* b, uint32_t parity, volatile int* abort) {
+  if (mbar_poll(b, parity)) return true;
+  for (uint32_t i = 0; i < (1u << 22); i++) {
+    if (mbar_try(b, parity)) return true;
+    if ((i & 63) == 63 && *abort) return false;
+  }
+  *abort = 1;
+  return false;
+}
 // Bounded wait on an mbarrier phase (about a second at most). Returns false (and raises the CTA's
 // abort flag) on timeout. A non-blocking test first: a completed phase costs no suspension.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {

@@ -303,16 +303,17 @@ struct PassArgs {
   long long* x;     // [T][h] residual stream, fixed point
   long long* qkv;   // [T][h + 2 kv] q|k|v sums (bias included), fixed point
   long long* gu;    // [T][2 I] gate/up sums in the interleaved row order, fixed point
-  float* att_part;  // [heads][slots][T][hd + 2]
-  float* attn;      // [T][hidden] merged attention output
-  unsigned* att_cnt;  // [heads] slot arrival counters (zero between phases)
+  float* att_part;  // [heads][slots][T][hd + 2] slot states (m, l, acc)
   uint16_t* kc;     // [L][kv_heads][max_ctx][hd] f16
   uint16_t* vc;
   const float2* rope;
   ArgPart* arg_parts;  // [gridDim][T]
   float* logits;       // optional [n_logits][vocab]
   unsigned* bar;
-  unsigned* trace;     // optional [2 * barriers + 2][gridDim] globaltimer stamps (profiling)
+  unsigned* trace;     // optional globaltimer stamps (profiling): [2 * barriers + 2][gridDim] at the
+                       // barriers, then [phases][4][gridDim] inside the phases from slot trace_sub on
+  int trace_sub;
+  int kv_off;  // byte offset of the attention K/V region from the B-operand region
   int L, hidden, inter, heads, kv_heads, hd, vocab, max_ctx, T, n_logits, slots;
   int ks_qkv, ks_o, ks_gu, ks_down;
   float eps;
@@ -353,6 +354,7 @@ void qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t r
 int pass_kernel_nt(int T);
 bool pass_kernel_supported(const WeightFormat& body, const WeightFormat& embed, int T, int hd);
 size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down);
+size_t pass_kernel_kv_off(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down);
 void launch_pass(const PassArgs& a, const WeightFormat& f, size_t smem, int grid, cudaStream_t s);
 int pass_kernel_blocks_per_sm(const WeightFormat& f, int T, size_t smem, int max_per_sm);
 // K blocks of 64 columns per weight-stream stage of the pass kernel, and the descriptors.

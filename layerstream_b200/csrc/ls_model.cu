@@ -450,7 +450,7 @@ struct LsModel {
   // Launch plan of the pass kernel for one token tile (16, 32 or 48 tokens): CTAs, attention slots
   // per head, K slices per GEMV phase and dynamic shared memory.
   struct PassPlan {
-    int grid = 0, slots = 1, ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_down = 1;
+    int grid = 0, slots = 1, ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_down = 1, kv_off = 0;
     size_t smem = 0;
   };
   PassPlan pk_plan[3];
@@ -496,6 +496,7 @@ struct LsModel {
       P.ks_o = plan(layers[0].o, P.grid);
       P.ks_gu = plan(layers[0].gu, P.grid);
       P.slots = std::max(1, std::min(kMaxAttSlots, P.grid / (int)cfg.heads));
+      P.kv_off = (int)pass_kernel_kv_off(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down);
       max_grid = std::max(max_grid, P.grid);
     }
     if (getenv("LS_PASS_VERBOSE"))
@@ -534,14 +535,12 @@ struct LsModel {
     qkv_fix = dalloc<long long>((size_t)kMaxPassT * QS);
     gu_fix = dalloc<long long>((size_t)kMaxPassT * 2 * I);
     pk_att = dalloc<float>(cfg.heads * (size_t)kMaxAttSlots * kMaxPassT * (cfg.head_dim + 2));
-    pk_attn = dalloc<float>((size_t)kMaxPassT * h);
     pk_bar = dalloc<unsigned>(1 + cfg.heads);
     pk_parts = dalloc<ArgPart>((size_t)max_grid * kMaxPassT);
     LS_CUDA(cudaEventCreate(&pk_ev[0]));
     LS_CUDA(cudaEventCreate(&pk_ev[1]));
   }
   static constexpr int kMaxAttSlots = 16;  // equals the kernel's slot bound
-  float* pk_attn = nullptr;
 
   bool use_pass_kernel(int T) const { return T >= 1 && T <= 48 && pk_plan[pk_class(T)].grid > 0; }
 
@@ -557,8 +556,6 @@ struct LsModel {
     a.qkv = qkv_fix;
     a.gu = gu_fix;
     a.att_part = pk_att;
-    a.attn = pk_attn;
-    a.att_cnt = pk_bar + 1;
     a.kc = kc;
     a.vc = vc;
     a.rope = rope;
@@ -567,6 +564,8 @@ struct LsModel {
     a.bar = pk_bar;
     if (prof_timeline && !pk_trace) pk_trace = dalloc<unsigned>(pk_trace_slots() * (size_t)pk_max_grid);
     a.trace = prof_timeline ? pk_trace : nullptr;
+    a.trace_sub = (int)pk_trace_sub();
+    a.kv_off = P.kv_off;
     pk_T = T;
     pk_n_logits = n_logits;
     pk_traced = a.trace != nullptr;
@@ -587,8 +586,8 @@ struct LsModel {
     a.ks_gu = P.ks_gu;
     a.ks_down = P.ks_down;
     a.eps = cfg.eps;
-    // barrier counter and per-head attention counters start at zero
-    LS_CUDA(cudaMemsetAsync(pk_bar, 0, sizeof(unsigned) * (1 + cfg.heads), stream));
+    // the grid barrier's counter starts at zero
+    LS_CUDA(cudaMemsetAsync(pk_bar, 0, sizeof(unsigned), stream));
     if (prof_on) LS_CUDA(cudaEventRecord(pk_ev[0], stream));
     launch_pass(a, cfg.format, P.smem, P.grid, stream);
     if (prof_on) {
@@ -602,14 +601,17 @@ struct LsModel {
   int pk_T = 0, pk_n_logits = 0;
   bool pk_traced = false;
   // timeline slots of one pass: start, (arrive, leave) per grid barrier, end
-  size_t pk_trace_slots() const { return 2 * (2 + 5 * cfg.layers) + 2; }
+  // plus 4 stamps inside each phase (embedding, 5 per layer, head)
+  size_t pk_trace_sub() const { return 2 * (2 + 5 * cfg.layers) + 2; }
+  size_t pk_trace_slots() const { return pk_trace_sub() + 4 * (2 + 5 * cfg.layers); }
 
   // Turns the pass kernel's barrier timestamps into per-class phase spans (averaged over layers).
   void collect_pass_trace() {
     const int G = pk_grid_last, L = (int)cfg.layers, T = pk_T;
     const int nb = 1 + 5 * L + (pk_n_logits > 0 ? 1 : 0);
-    std::vector<uint32_t> tr((size_t)(2 * nb + 2) * G);
+    std::vector<uint32_t> tr(pk_trace_slots() * (size_t)G);
     LS_CUDA(cudaMemcpy(tr.data(), pk_trace, tr.size() * 4, cudaMemcpyDeviceToHost));
+    const int sub0 = (int)pk_trace_sub();
     auto at = [&](int slot, int c) { return tr[(size_t)slot * G + c]; };
     uint32_t t0 = at(0, 0);
     for (int c = 1; c < G; c++)
@@ -625,6 +627,27 @@ struct LsModel {
         busy += rel(2 * b - 1, c) - rel(2 * b - 2, c);
       }
       busy /= G;
+      // the critical CTA: last to arrive; its own stamps inside the phase (a stamp outside
+      // [its previous departure, its arrival] was not written this pass and merges into the next)
+      int cc = 0;
+      for (int c = 1; c < G; c++)
+        if (rel(2 * b - 1, c) > rel(2 * b - 1, cc)) cc = c;
+      double seg[6];
+      {
+        double t = rel(2 * b - 2, cc);
+        const double arr = rel(2 * b - 1, cc);
+        for (int k = 0; k < 4; k++) {
+          const double sk = rel(sub0 + 4 * (b - 1) + k, cc);
+          if (sk >= t && sk <= arr) {
+            seg[k] = sk - t;
+            t = sk;
+          } else {
+            seg[k] = 0;
+          }
+        }
+        seg[4] = arr - t;
+        seg[5] = leave - arr;
+      }
       double span = leave - prev_leave;
       prev_leave = leave;
       if (b == 1) continue;  // embedding rows: part of the whole-pass class only
@@ -638,6 +661,7 @@ struct LsModel {
       }
       prof.ms[cls] += span * scale;
       prof.busy_ms[cls] += busy * scale;
+      for (int k = 0; k < 6; k++) prof.crit_ms[cls][k] += seg[k] * scale;
     }
     const double pos0 = ctl_host->pos0;
     const double b_cls[5] = {gemv_bytes(W.qkv, T, h + 2 * kv),

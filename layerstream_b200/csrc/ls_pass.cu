@@ -38,7 +38,6 @@ constexpr int PK_PRODUCER = PK_ISSUER + PK_NWG;  // warp index of the weight-str
 constexpr int PK_STAGERS = PK_CT + 32 * PK_NWG;  // compute warps + issuers: the B-operand staging group
 constexpr int PK_THREADS = PK_STAGERS + 32;
 constexpr int PK_NW = PK_THREADS / 32;
-constexpr int PK_ATT_TILE = 64;
 constexpr int kMaxSlots = 16;  // attention slots per head (context tiles split across CTAs)
 // Weight stream: STAGES stages of one 256-row box of ~16 KB of packed weights (+ its scales),
 // filled by TMA. Bulk copies of >= 16 KB per stage stream at HBM bandwidth with one CTA per SM
@@ -80,8 +79,9 @@ __device__ bool grid_barrier(unsigned* bar, unsigned target, int* err) {
   __shared__ int s_ok;
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(bar, 1u);
+    // release: the CTA's writes (ordered before this thread's by the CTA barrier) are visible to
+    // whoever acquires the count; no round trip is waited for
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(bar), "r"(1u) : "memory");
     int ok = 1;
     for (uint32_t i = 0;; i++) {
       if (ld_acquire(bar) >= target) break;
@@ -96,8 +96,7 @@ __device__ bool grid_barrier(unsigned* bar, unsigned target, int* err) {
       }
       __nanosleep(32);
     }
-    __threadfence();
-    s_ok = ok;
+    s_ok = ok;  // the acquiring load orders the other CTAs' writes before this CTA's reads
   }
   __syncthreads();
   return s_ok != 0;
@@ -169,7 +168,7 @@ struct TcGemv {
     const uint32_t sub8 = BITS == 8 ? 0x64806480u : 0x64086408u;
     for (int kbs = kb0; kbs < kb1; kbs += NB) {
       const int slot = rpos % PK_STAGES;
-      bool fail = !tc::mbar_wait(&full[slot], (rpos / PK_STAGES) & 1, abort);
+      bool fail = !tc::mbar_wait_fast(&full[slot], (rpos / PK_STAGES) & 1, abort);
       if (__any_sync(0xffffffffu, fail)) return false;
       marks.mark(0, blk);
       rpos++;
@@ -232,7 +231,7 @@ struct TcGemv {
         // A buffer b is free once the MMAs of block blk - PK_ABUF have completed
         const int b = blk % PK_ABUF;
         const uint32_t u = blk / PK_ABUF;
-        fail = u > 0 && !tc::mbar_wait(&bar_a[g * PK_ABUF + b], (u - 1) & 1, abort);
+        fail = u > 0 && !tc::mbar_wait_fast(&bar_a[g * PK_ABUF + b], (u - 1) & 1, abort);
         if (__any_sync(0xffffffffu, fail)) return false;
         marks.mark(2, blk);
         tc::fence_after();
@@ -250,7 +249,7 @@ struct TcGemv {
     const int d = itc & 1;
     const uint32_t v = itc >> 1;
     itc++;
-    bool fail = !tc::mbar_wait(&bar_d[g * 2 + d], v & 1, abort);
+    bool fail = !tc::mbar_wait_fast(&bar_d[g * 2 + d], v & 1, abort);
     if (__any_sync(0xffffffffu, fail)) return false;
     tc::fence_after();
 #pragma unroll
@@ -278,14 +277,14 @@ struct TcGemv {
     bool fail = false;
     if (lane == 0) {
       // accumulator d is free once the compute threads have read item itc - 2
-      if (v > 0 && !tc::mbar_wait(&bar_dfree[g * 2 + d], (v - 1) & 1, abort)) fail = true;
+      if (v > 0 && !tc::mbar_wait_fast(&bar_dfree[g * 2 + d], (v - 1) & 1, abort)) fail = true;
       const uint64_t bd0 = tc::sdesc(xb_addr, 128u, sbo);  // start address field: 16-byte units
       const uint32_t dcol = d_col(d, g);
       for (int kb = kb0; kb < kb1 && !fail; kb++) {
         const int b = blk % PK_ABUF;
         const uint32_t u = blk / PK_ABUF;
         blk++;
-        if (!tc::mbar_wait(&bar_full[g * PK_ABUF + b], u & 1, abort)) {
+        if (!tc::mbar_wait_fast(&bar_full[g * PK_ABUF + b], u & 1, abort)) {
           fail = true;
           break;
         }
@@ -406,7 +405,7 @@ __device__ __forceinline__ void stage_b(uint8_t* xb, uint32_t sbo, int T, int co
 }
 
 // 1 / rms of the first T rows of x (fixed point, n columns, n even) into s_inv. Every thread reads
-// 16-byte pairs of columns (all loads of a batch in flight at once) and sums its own columns of
+// 16-byte pairs of columns (RMS_BATCH per thread in flight at once) and sums its own columns of
 // each token in a fixed order; red (T x PK_THREADS floats of shared memory) then holds the per-thread
 // partial sums, which one warp per token adds in a fixed order: the result is deterministic.
 __device__ __forceinline__ void rms_stats(const long long* x, int T, int n, float eps, float* s_inv, float* red) {
@@ -415,10 +414,11 @@ __device__ __forceinline__ void rms_stats(const long long* x, int T, int n, floa
   for (int t = 0; t < T; t++) red[t * PK_THREADS + tid] = 0.f;
   int cur = -1;
   float ss = 0.f;
-  for (int j0 = 0; j0 < total; j0 += 4 * PK_THREADS) {
-    longlong2 v[4];
+  constexpr int RMS_BATCH = 4;
+  for (int j0 = 0; j0 < total; j0 += RMS_BATCH * PK_THREADS) {
+    longlong2 v[RMS_BATCH];
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
+    for (int u = 0; u < RMS_BATCH; u++) {
       const int j = j0 + u * PK_THREADS + tid;
       if (j < total) {
         const int t = j / np;
@@ -426,7 +426,7 @@ __device__ __forceinline__ void rms_stats(const long long* x, int T, int n, floa
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
+    for (int u = 0; u < RMS_BATCH; u++) {
       const int j = j0 + u * PK_THREADS + tid;
       if (j < total) {
         const int t = j / np;
@@ -457,34 +457,74 @@ __device__ __forceinline__ void zero_ll(long long* p, size_t n) {
   for (size_t i = (size_t)blockIdx.x * PK_THREADS + threadIdx.x; i < n; i += (size_t)gridDim.x * PK_THREADS) p[i] = 0;
 }
 
-// Shared memory of one attention item: q [T][HD] f32, K and V tiles [64][HD + 2] f16 (the odd word
-// stride keeps the per-position reads free of bank conflicts), running state [T][HD + 2] f32.
-// The state region is reused by the slot merge ([T][S][3] floats).
+// Attention. The context is cut into chunks of PK_CHUNK positions; chunk c belongs to slot c % S
+// (S slots per query head, one CTA item each). A slot visits its chunks in tiles of pk_at(hd) rows
+// (several chunks side by side, in increasing position order), so which positions a tile holds and
+// the order in which they are summed depend only on absolute positions: a token's result does not
+// depend on how many tokens share the pass. Items write their slot state (m, l, acc); the O phase
+// merges the slots while staging its activations.
+constexpr int PK_CHUNK = 32;
+__host__ __device__ constexpr int pk_at(int hd) { return hd <= 64 ? 128 : 64; }
+// K/V tile row stride (halves): rows start on 16-byte boundaries (cp.async targets) and the
+// per-position 16-byte reads of a quarter warp hit distinct banks.
+__host__ __device__ constexpr int pk_hpk(int hd) { return hd + 8; }
+// Dedicated K/V tile region: K then V, [pk_at][pk_hpk] f16 each.
+__host__ __device__ constexpr size_t pk_kv_smem(int hd) { return 2 * (size_t)pk_at(hd) * pk_hpk(hd) * 2; }
+// Attention scratch in the B-operand region: q [T][HD] f32, running state [T][HD + 2] f32 (m, l,
+// acc), probabilities [PK_NW][pk_at] f32.
 __host__ __device__ constexpr size_t pk_att_smem(int T, int hd) {
-  return (size_t)T * hd * 4 + 2 * (size_t)PK_ATT_TILE * (hd + 2) * 2 +
-         (size_t)T * ((hd + 2) > 3 * kMaxSlots ? (hd + 2) : 3 * kMaxSlots) * 4;
+  return (size_t)T * hd * 4 + (size_t)T * (hd + 2) * 4 + (size_t)PK_NW * pk_at(hd) * 4;
 }
 
-// ---------------------------------------------------------------------------------------------
-// Attention item: query head hh over context tiles {slot, slot + S, ...}; writes (m, l, acc) of
-// the slot. The last CTA to finish a head (per-head arrival counter) merges the S slot states into
-// the attention output of that head.
-// ---------------------------------------------------------------------------------------------
-__device__ void attention_item(const PassArgs& a, int l, int hh, int slot, uint8_t* sm) {
-  __shared__ int s_last;
-  const int HD = a.hd, HALF = HD / 2, HP = HD + 2, T = a.T, S = a.slots;
+// Context position of row r of tile ti of slot `slot` (S slots, CPT chunks per tile).
+__device__ __forceinline__ int att_row_pos(int slot, int S, int ti, int cpt, int r) {
+  return (slot + S * (ti * cpt + r / PK_CHUNK)) * PK_CHUNK + r % PK_CHUNK;
+}
+
+// Starts the cp.async copies of the cached K/V rows (positions < pos0, which no phase of this pass
+// writes) of tile 0 of item (hh, slot) into the K/V region. Every thread commits one group.
+__device__ void attention_prefetch(const PassArgs& a, int l, int hh, int slot, uint8_t* kvb) {
+  const int HD = a.hd, HPK = pk_hpk(HD), AT = pk_at(HD), c8 = HD / 8;
+  const int g = hh / (a.heads / a.kv_heads), pos0 = a.ctl->pos0;
+  const size_t lstride = (size_t)a.kv_heads * a.max_ctx * HD;
+  const uint16_t* kc = a.kc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
+  const uint16_t* vc = a.vc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
+  __half* Ks = reinterpret_cast<__half*>(kvb);
+  __half* Vs = Ks + AT * HPK;
+  for (int i = threadIdx.x; i < AT * c8; i += PK_THREADS) {
+    const int r = i / c8, ch = i - r * c8;
+    const int p = att_row_pos(slot, a.slots, 0, AT / PK_CHUNK, r);
+    if (p < pos0) {
+      tc::cp_async16(tc::su32(Ks + r * HPK + ch * 8), kc + (size_t)p * HD + ch * 8);
+      tc::cp_async16(tc::su32(Vs + r * HPK + ch * 8), vc + (size_t)p * HD + ch * 8);
+    }
+  }
+  tc::cp_commit();
+}
+
+// Attention item: query head hh over the chunks of `slot`; writes the slot state (m, l, acc) of
+// every token to att_part. prefetched: tile 0's cached rows were started by attention_prefetch.
+// sub (optional, profiling): globaltimer stamps of thread 0, sub[0] after the query rows are
+// staged, sub[stride] after the first tile is in shared memory, sub[2 stride] once the slot state
+// is written.
+template <int PPL>
+__device__ void attention_item(const PassArgs& a, int l, int hh, int slot, uint8_t* sm, uint8_t* kvb, bool prefetched,
+                               unsigned* sub, int stride) {
+  constexpr int AT = 32 * PPL, CPT = AT / PK_CHUNK;
+  const int HD = a.hd, HALF = HD / 2, HP = HD + 2, HPK = HD + 8, T = a.T, S = a.slots;
   const int group = a.heads / a.kv_heads, g = hh / group;
   const int pos0 = a.ctl->pos0, total = pos0 + T;
-  const int ntiles = (total + PK_ATT_TILE - 1) / PK_ATT_TILE;
+  const int nch = (total + PK_CHUNK - 1) / PK_CHUNK;
   const int H = a.heads * HD, KV = a.kv_heads * HD, QS = H + 2 * KV;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t lstride = (size_t)a.kv_heads * a.max_ctx * HD;
-  uint16_t* kc = a.kc + (size_t)l * lstride;
-  uint16_t* vc = a.vc + (size_t)l * lstride;
-  float* qs = reinterpret_cast<float*>(sm);                         // [T][HD]
-  __half* Ks = reinterpret_cast<__half*>(qs + T * HD);              // [64][HP]
-  __half* Vs = Ks + PK_ATT_TILE * HP;                               // [64][HP]
-  float* st = reinterpret_cast<float*>(Vs + PK_ATT_TILE * HP);      // [T][HP]
+  uint16_t* kc = a.kc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
+  uint16_t* vc = a.vc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
+  float* qs = reinterpret_cast<float*>(sm);   // [T][HD]
+  float* st = qs + T * HD;                    // [T][HP]
+  float* es = st + T * HP;                    // [PK_NW][AT]
+  __half* Ks = reinterpret_cast<__half*>(kvb);  // [AT][HPK]
+  __half* Vs = Ks + AT * HPK;
   const float scale = 1.0f / sqrtf((float)HD);
   for (int i = threadIdx.x; i < T * HALF; i += PK_THREADS) {
     const int t = i / HALF, d = i - t * HALF;
@@ -495,27 +535,25 @@ __device__ void attention_item(const PassArgs& a, int l, int hh, int slot, uint8
     qs[t * HD + d + HALF] = x2 * cs.x + x1 * cs.y;
   }
   for (int i = threadIdx.x; i < T * HP; i += PK_THREADS) st[i] = (i % HP == 0) ? -CUDART_INF_F : 0.f;
+  if (sub && threadIdx.x == 0) sub[0] = gtimer();
   const bool writer = (hh % group) == 0;
-  const int c8 = HD / 8;  // 16-byte chunks per cached row
-  for (int tile = slot; tile < ntiles; tile += S) {
-    const int p0 = tile * PK_ATT_TILE;
-    __syncthreads();
-    // cached rows: 16-byte loads, all of a thread's chunks in flight together
-    for (int i = threadIdx.x; i < PK_ATT_TILE * c8; i += PK_THREADS) {
-      const int pl = i / c8, ch = i - pl * c8, p = p0 + pl;
-      if (p < pos0) {
-        const size_t base = ((size_t)g * a.max_ctx + p) * HD + ch * 8;
-        const uint4 kv4 = __ldcg(reinterpret_cast<const uint4*>(kc + base));
-        const uint4 vv4 = __ldcg(reinterpret_cast<const uint4*>(vc + base));
-        uint32_t* kd = reinterpret_cast<uint32_t*>(Ks + pl * HP + ch * 8);
-        uint32_t* vd = reinterpret_cast<uint32_t*>(Vs + pl * HP + ch * 8);
-        kd[0] = kv4.x, kd[1] = kv4.y, kd[2] = kv4.z, kd[3] = kv4.w;
-        vd[0] = vv4.x, vd[1] = vv4.y, vd[2] = vv4.z, vd[3] = vv4.w;
+  const int c8 = HD / 8;
+  for (int ti = 0; slot + S * ti * CPT < nch; ti++) {
+    if (ti > 0 || !prefetched) {
+      __syncthreads();  // the previous tile's readers are done
+      for (int i = threadIdx.x; i < AT * c8; i += PK_THREADS) {
+        const int r = i / c8, ch = i - r * c8;
+        const int p = att_row_pos(slot, S, ti, CPT, r);
+        if (p < pos0) {
+          tc::cp_async16(tc::su32(Ks + r * HPK + ch * 8), kc + (size_t)p * HD + ch * 8);
+          tc::cp_async16(tc::su32(Vs + r * HPK + ch * 8), vc + (size_t)p * HD + ch * 8);
+        }
       }
+      tc::cp_commit();
     }
-    // rows of this block (rotated, rounded to f16, appended to the cache) and zero padding
-    for (int i = threadIdx.x; i < PK_ATT_TILE * HALF; i += PK_THREADS) {
-      const int pl = i / HALF, d = i - pl * HALF, p = p0 + pl;
+    // rows of this pass's block (rotated, rounded to f16, appended to the cache) and zero padding
+    for (int i = threadIdx.x; i < AT * HALF; i += PK_THREADS) {
+      const int r = i / HALF, d = i - r * HALF, p = att_row_pos(slot, S, ti, CPT, r);
       if (p < pos0) continue;
       __half k1 = __float2half_rn(0.f), k2 = k1, v1 = k1, v2 = k1;
       if (p < total) {
@@ -529,111 +567,185 @@ __device__ void attention_item(const PassArgs& a, int l, int hh, int slot, uint8
         v1 = __float2half_rn(from_fix(ldcg_ll(vr + d)));
         v2 = __float2half_rn(from_fix(ldcg_ll(vr + d + HALF)));
         if (writer) {
-          const size_t base = ((size_t)g * a.max_ctx + p) * HD;
-          kc[base + d] = __half_as_ushort(k1);
-          kc[base + d + HALF] = __half_as_ushort(k2);
-          vc[base + d] = __half_as_ushort(v1);
-          vc[base + d + HALF] = __half_as_ushort(v2);
+          kc[(size_t)p * HD + d] = __half_as_ushort(k1);
+          kc[(size_t)p * HD + d + HALF] = __half_as_ushort(k2);
+          vc[(size_t)p * HD + d] = __half_as_ushort(v1);
+          vc[(size_t)p * HD + d + HALF] = __half_as_ushort(v2);
         }
       }
-      Ks[pl * HP + d] = k1;
-      Ks[pl * HP + d + HALF] = k2;
-      Vs[pl * HP + d] = v1;
-      Vs[pl * HP + d + HALF] = v2;
+      Ks[r * HPK + d] = k1;
+      Ks[r * HPK + d + HALF] = k2;
+      Vs[r * HPK + d] = v1;
+      Vs[r * HPK + d + HALF] = v2;
     }
+    tc::cp_wait<0>();
     __syncthreads();
+    if (sub && ti == 0 && threadIdx.x == 0) sub[stride] = gtimer();
+    float* ew = es + warp * AT;
     for (int t = warp; t < T; t += PK_NW) {
+      // valid rows: a prefix of the tile (positions grow with the row)
       const int ctx = pos0 + t + 1;
-      if (p0 >= ctx) continue;
-      const float* q = qs + t * HD;
-      // scores of positions p0 + lane and p0 + 32 + lane: four independent FMA chains
-      const __half2* kr0 = reinterpret_cast<const __half2*>(Ks + lane * HP);
-      const __half2* kr1 = reinterpret_cast<const __half2*>(Ks + (lane + 32) * HP);
-      float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-      for (int d = 0; d < HD; d += 4) {
-        const float2 ka = __half22float2(kr0[d / 2]), kb = __half22float2(kr0[d / 2 + 1]);
-        const float2 kc2 = __half22float2(kr1[d / 2]), kd = __half22float2(kr1[d / 2 + 1]);
-        a0 = fmaf(q[d], ka.x, a0);
-        a0 = fmaf(q[d + 1], ka.y, a0);
-        a1 = fmaf(q[d + 2], kb.x, a1);
-        a1 = fmaf(q[d + 3], kb.y, a1);
-        b0 = fmaf(q[d], kc2.x, b0);
-        b0 = fmaf(q[d + 1], kc2.y, b0);
-        b1 = fmaf(q[d + 2], kd.x, b1);
-        b1 = fmaf(q[d + 3], kd.y, b1);
+      int lim = 0;
+      for (int k = 0; k < CPT; k++) {
+        const int c0 = (slot + S * (ti * CPT + k)) * PK_CHUNK;
+        if (c0 >= ctx) break;
+        lim = k * PK_CHUNK + min(PK_CHUNK, ctx - c0);
       }
-      const float s0 = (p0 + lane < ctx) ? (a0 + a1) * scale : -CUDART_INF_F;
-      const float s1 = (p0 + 32 + lane < ctx) ? (b0 + b1) * scale : -CUDART_INF_F;
-      const float tmax = warp_max(fmaxf(s0, s1));
+      if (lim == 0) continue;
+      // scores of rows lane + 32 j: 16-byte K reads, two FMA chains per row
+      float sa[PPL], sb[PPL];
+#pragma unroll
+      for (int j = 0; j < PPL; j++) sa[j] = sb[j] = 0.f;
+      const float* q = qs + t * HD;
+      for (int d = 0; d < HD; d += 8) {
+        const float4 qa = *reinterpret_cast<const float4*>(q + d), qb = *reinterpret_cast<const float4*>(q + d + 4);
+#pragma unroll
+        for (int j = 0; j < PPL; j++) {
+          if (32 * j >= lim) break;
+          const uint4 kv = *reinterpret_cast<const uint4*>(Ks + (lane + 32 * j) * HPK + d);
+          const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kv.x));
+          const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kv.y));
+          const float2 k2 = __half22float2(*reinterpret_cast<const __half2*>(&kv.z));
+          const float2 k3 = __half22float2(*reinterpret_cast<const __half2*>(&kv.w));
+          sa[j] = fmaf(qa.x, k0.x, sa[j]);
+          sb[j] = fmaf(qa.y, k0.y, sb[j]);
+          sa[j] = fmaf(qa.z, k1.x, sa[j]);
+          sb[j] = fmaf(qa.w, k1.y, sb[j]);
+          sa[j] = fmaf(qb.x, k2.x, sa[j]);
+          sb[j] = fmaf(qb.y, k2.y, sb[j]);
+          sa[j] = fmaf(qb.z, k3.x, sa[j]);
+          sb[j] = fmaf(qb.w, k3.y, sb[j]);
+        }
+      }
+      float sc[PPL], tmax = -CUDART_INF_F;
+#pragma unroll
+      for (int j = 0; j < PPL; j++) {
+        sc[j] = (lane + 32 * j < lim) ? (sa[j] + sb[j]) * scale : -CUDART_INF_F;
+        tmax = fmaxf(tmax, sc[j]);
+      }
+      tmax = warp_max(tmax);
       float* Sx = st + t * HP;
       const float m_old = Sx[0], m_new = fmaxf(m_old, tmax);
       const float corr = (m_old == -CUDART_INF_F) ? 0.f : expf(m_old - m_new);
-      const float e0 = (s0 == -CUDART_INF_F) ? 0.f : expf(s0 - m_new);
-      const float e1 = (s1 == -CUDART_INF_F) ? 0.f : expf(s1 - m_new);
-      const float lsum = warp_sum(e0 + e1);
-      for (int d0 = 0; d0 < HD; d0 += 32) {
-        const int d = d0 + lane;
-        const int dc = d < HD ? d : 0;
-        float acc = (d < HD) ? Sx[2 + d] * corr : 0.f, acc2 = 0.f;
-        for (int pl = 0; pl < 32; pl++) {
-          const float ea = __shfl_sync(0xffffffffu, e0, pl), eb = __shfl_sync(0xffffffffu, e1, pl);
-          acc = fmaf(ea, __half2float(Vs[pl * HP + dc]), acc);
-          acc2 = fmaf(eb, __half2float(Vs[(pl + 32) * HP + dc]), acc2);
+      float esum = 0.f;
+#pragma unroll
+      for (int j = 0; j < PPL; j++) {
+        const float e = (sc[j] == -CUDART_INF_F) ? 0.f : expf(sc[j] - m_new);
+        ew[lane + 32 * j] = e;
+        esum += e;
+      }
+      const float lsum = warp_sum(esum);
+      __syncwarp();
+      // values: lane owns columns d0 + 2 lane, d0 + 2 lane + 1; even and odd rows in two chains
+      for (int d0 = 0; d0 < HD; d0 += 64) {
+        const int d = d0 + 2 * lane;
+        if (d < HD) {
+          float ax = 0.f, ay = 0.f, bx = 0.f, by = 0.f;
+          int p = 0;
+          for (; p + 1 < lim; p += 2) {
+            const float e0 = ew[p], e1 = ew[p + 1];
+            const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(Vs + p * HPK + d));
+            const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(Vs + (p + 1) * HPK + d));
+            ax = fmaf(e0, v0.x, ax);
+            ay = fmaf(e0, v0.y, ay);
+            bx = fmaf(e1, v1.x, bx);
+            by = fmaf(e1, v1.y, by);
+          }
+          if (p < lim) {
+            const float e0 = ew[p];
+            const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(Vs + p * HPK + d));
+            ax = fmaf(e0, v0.x, ax);
+            ay = fmaf(e0, v0.y, ay);
+          }
+          Sx[2 + d] = fmaf(Sx[2 + d], corr, ax + bx);
+          Sx[3 + d] = fmaf(Sx[3 + d], corr, ay + by);
         }
-        if (d < HD) Sx[2 + d] = acc + acc2;
       }
       __syncwarp();
       if (lane == 0) {
-        Sx[1] = Sx[1] * corr + lsum;
+        Sx[1] = fmaf(Sx[1], corr, lsum);
         Sx[0] = m_new;
       }
       __syncwarp();
     }
   }
+  if (prefetched && slot >= nch) tc::cp_wait<0>();  // no tile: the prefetch group (empty) retires here
   __syncthreads();
   float* part = a.att_part + ((size_t)hh * S + slot) * T * HP;
   for (int i = threadIdx.x; i < T * HP; i += PK_THREADS) part[i] = st[i];
-  // publish the slot state; the last of the S slots merges them
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&a.att_cnt[hh], 1u) == (unsigned)(S - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // merge: slot weights e^(m_s - m*) / L per token (T x S, into shared memory), then every output
-  // element is a weighted sum over the slots with all S loads in flight
-  const float* hp = a.att_part + (size_t)hh * S * T * HP;
-  float* ml = st;           // [T][S][2] (m, l) — st is free once the part is written
-  float* wts = ml + T * S * 2;  // [T][S]
-  for (int i = threadIdx.x; i < T * S; i += PK_THREADS) {
-    const int t = i / S, s2 = i - t * S;
-    const float2 v = __ldcg(reinterpret_cast<const float2*>(hp + ((size_t)s2 * T + t) * HP));
-    ml[2 * i] = v.x;
-    ml[2 * i + 1] = v.y;
-  }
-  __syncthreads();
-  for (int t = threadIdx.x; t < T; t += PK_THREADS) {
-    const float* r = ml + t * S * 2;
-    float mx = -CUDART_INF_F;
-    for (int s2 = 0; s2 < S; s2++) mx = fmaxf(mx, r[2 * s2]);
-    float L = 0.f;
-    for (int s2 = 0; s2 < S; s2++) L += (r[2 * s2] == -CUDART_INF_F) ? 0.f : r[2 * s2 + 1] * expf(r[2 * s2] - mx);
-    for (int s2 = 0; s2 < S; s2++) wts[t * S + s2] = (r[2 * s2] == -CUDART_INF_F) ? 0.f : expf(r[2 * s2] - mx) / L;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < T * HD; i += PK_THREADS) {
-    const int t = i / HD, d = i - t * HD;
-    const float* base = hp + (size_t)t * HP + 2 + d;
-    float v[kMaxSlots];
-#pragma unroll
-    for (int s2 = 0; s2 < kMaxSlots; s2++) v[s2] = s2 < S ? __ldcg(base + (size_t)s2 * T * HP) : 0.f;
-    float o = 0.f;
+  if (sub && threadIdx.x == 0) sub[2 * (size_t)stride] = gtimer();
+}
+
+// O-phase staging of attention columns [col0, col0 + ncol): merges the S slot states. A warp makes
+// 32 adjacent column pairs of one token (a whole warp always shares the token and, for head widths
+// that are multiples of 64, the head: then lane s computes slot s's weight e^(m_s - m*) / L once and
+// the warp shares it). Every lane loads the two values of each slot at once (one round trip) and
+// sums in slot order. Rows T..NT-1 are zero.
+template <int NT>
+__device__ __forceinline__ void stage_attention(const PassArgs& a, uint8_t* xb, uint32_t sbo, int col0, int ncol) {
+  const int HD = a.hd, HP = HD + 2, S = a.slots, T = a.T, np = ncol / 2;
+  const int lane = threadIdx.x & 31;
+  const size_t sstride = (size_t)T * HP;  // between the slots of one head
+  auto put = [&](int t, int c, float ox, float oy) {
+    const int kc = (c - col0) / 8, e = (c - col0) % 8;
+    *reinterpret_cast<__half2*>(xb + (size_t)(t / 8) * sbo + (size_t)kc * 128 + (t % 8) * 16 + e * 2) =
+        __floats2half2_rn(ox, oy);
+  };
+  // np is a multiple of 32 (K slices are whole 64-column blocks) and so is PK_STAGERS: a warp's 32
+  // pairs never straddle a token
+#pragma unroll 1
+  for (int i0 = threadIdx.x - lane; i0 < T * np; i0 += PK_STAGERS) {
+    const int i = i0 + lane, t = i / np, c = col0 + 2 * (i - t * np);
+    const int hh = c / HD, d = c - hh * HD;
+    const float* base = a.att_part + (size_t)hh * S * sstride + (size_t)t * HP;
+    float2 v[kMaxSlots];
 #pragma unroll
     for (int s2 = 0; s2 < kMaxSlots; s2++)
-      if (s2 < S) o = fmaf(v[s2], wts[t * S + s2], o);
-    a.attn[(size_t)t * a.hidden + hh * HD + d] = o;
+      v[s2] = s2 < S ? __ldcg(reinterpret_cast<const float2*>(base + s2 * sstride + 2 + d)) : make_float2(0.f, 0.f);
+    const bool one_head = __all_sync(0xffffffffu, hh == __shfl_sync(0xffffffffu, hh, 0));
+    float ox = 0.f, oy = 0.f;
+    if (one_head) {
+      const float2 ml = lane < S ? __ldcg(reinterpret_cast<const float2*>(base + lane * sstride))
+                                 : make_float2(-CUDART_INF_F, 0.f);
+      const float mx = warp_max(ml.x);
+      const float e = (ml.x == -CUDART_INF_F) ? 0.f : __expf(ml.x - mx);
+      const float w = __fdividef(e, warp_sum(ml.y * e));
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxSlots; s2++) {
+        const float ws = __shfl_sync(0xffffffffu, w, s2);
+        if (s2 < S) {
+          ox = fmaf(v[s2].x, ws, ox);
+          oy = fmaf(v[s2].y, ws, oy);
+        }
+      }
+    } else {  // head widths that are not multiples of 64: every lane weighs its own head's slots
+      float2 ml[kMaxSlots];
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxSlots; s2++) {
+        ml[s2] = s2 < S ? __ldcg(reinterpret_cast<const float2*>(base + s2 * sstride)) : make_float2(-CUDART_INF_F, 0.f);
+        mx = fmaxf(mx, ml[s2].x);
+      }
+      float L = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxSlots; s2++) {
+        ml[s2].x = (ml[s2].x == -CUDART_INF_F) ? 0.f : __expf(ml[s2].x - mx);
+        L = fmaf(ml[s2].y, ml[s2].x, L);
+      }
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxSlots; s2++) {
+        const float ws = __fdividef(ml[s2].x, L);
+        ox = fmaf(v[s2].x, ws, ox);
+        oy = fmaf(v[s2].y, ws, oy);
+      }
+    }
+    put(t, c, ox, oy);
   }
-  if (threadIdx.x == 0) a.att_cnt[hh] = 0;  // the counter is reused by the next layer
+  for (int i = T * np + threadIdx.x; i < NT * np; i += PK_STAGERS) {
+    const int t = i / np;
+    put(t, col0 + 2 * (i - t * np), 0.f, 0.f);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -662,6 +774,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* xb = ring + (size_t)PK_STAGES * Str::kStage;
   float* red = reinterpret_cast<float*>(xb);
+  uint8_t* kvb = xb + a.kv_off;  // attention K/V tiles
   const uint32_t xb_addr = tc::su32(xb);
 
   if (threadIdx.x == 0) {
@@ -728,6 +841,14 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     stamp(2 * nbar);
     return ok;
   };
+  // Stamps inside the phase that follows barrier nbar (thread 0's progress): 0 = phase prepared
+  // (RMS statistics), 1 = first item staged, 2 = first item done, 3 = last item done.
+  auto sub_ptr = [&](int k) -> unsigned* {
+    return a.trace ? a.trace + ((size_t)a.trace_sub + 4 * nbar + k) * gridDim.x + blockIdx.x : nullptr;
+  };
+  auto sub = [&](int k) {
+    if (a.trace && threadIdx.x == 0) *sub_ptr(k) = gtimer();
+  };
   // Starts the weight stream of this CTA's items of the next GEMV phase (before the barrier):
   // as many stages as the ring has free, without waiting.
   auto prefetch = [&](const QMat& w, const QMaps* maps, int ks) {
@@ -742,6 +863,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   // barriers match even after a failure, when the work is skipped and bounded waits return).
   auto gemv_phase = [&](const QMat& w, int ks, auto stage, auto epi) {
     const Split sp = make_split<BITS, G>(w, ks);
+    sub(0);
     if (warp == PK_PRODUCER) {
       if (producer) {
         while (ok && !pr.done()) {
@@ -756,6 +878,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     }
     int staged = -1;
     for (int i = blockIdx.x; i < sp.items(); i += gridDim.x) {
+      const bool first = i == (int)blockIdx.x;
       int t256, kb0, kb1;
       sp.item(i, &t256, &kb0, &kb1);
       const int kslice = i / sp.tiles;
@@ -767,6 +890,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
         stagers_sync();
         staged = kslice;
       }
+      if (first) sub(1);
       if (!ok) continue;
       if (compute) {
         float tot[NT];
@@ -775,6 +899,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
         } else {
           const int t32 = t256 * 8 + warp;
           if (t32 < w.rows_pad / 32) epi(t32 * 32 + lane, kslice, tot);
+          if (first) sub(2);
+          sub(3);
         }
       } else if (!gm.issue(warp - PK_ISSUER, kb0, kb1, xb_addr, sbo)) {
         ok = false;
@@ -819,6 +945,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
 
   for (int l = 0; l < a.L && ok; l++) {
     const PassLayer& W = a.layers[l];
+    // cached K/V rows of this CTA's first attention item: they stream in during the QKV phase
+    if ((int)blockIdx.x < a.heads * a.slots) attention_prefetch(a, l, blockIdx.x / a.slots, blockIdx.x % a.slots, kvb);
     // ---- QKV: RMSNorm(x) -> q|k|v sums (+ bias once) ----
     rms_stats(a.x, T, h, a.eps, s_inv, red);
     gemv_phase(
@@ -837,10 +965,15 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
         });
     if (!barrier()) break;
 
-    // ---- attention (the block's K/V appended to the cache); zero the gate/up accumulators ----
+    // ---- attention slot states (the block's K/V appended to the cache); zero the gate/up sums ----
     for (int it = blockIdx.x; it < a.heads * a.slots; it += gridDim.x) {
       __syncthreads();
-      attention_item(a, l, it / a.slots, it % a.slots, xb);
+      const bool first = it == (int)blockIdx.x;
+      if (a.hd <= 64)
+        attention_item<4>(a, l, it / a.slots, it % a.slots, xb, kvb, first, first ? sub_ptr(0) : nullptr, (int)gridDim.x);
+      else
+        attention_item<2>(a, l, it / a.slots, it % a.slots, xb, kvb, first, first ? sub_ptr(0) : nullptr, (int)gridDim.x);
+      sub(3);
     }
     zero_ll(a.gu, (size_t)T * 2 * I);
     prefetch(W.o, &W.maps[1], a.ks_o);
@@ -848,10 +981,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
 
     // ---- O: residual add into x ----
     gemv_phase(
-        W.o, a.ks_o,
-        [&](int col0, int ncol, uint32_t sbo) {
-          stage_b<NT>(xb, sbo, T, col0, ncol, [&](int t, int c) { return __ldcg(a.attn + (size_t)t * h + c); });
-        },
+        W.o, a.ks_o, [&](int col0, int ncol, uint32_t sbo) { stage_attention<NT>(a, xb, sbo, col0, ncol); },
         [&](int r, int, float (&tot)[NT]) {
           if (r >= h) return;
 #pragma unroll
@@ -887,7 +1017,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
           stage_b<NT>(xb, sbo, T, col0, ncol, [&](int t, int j) {
             const long long* row = a.gu + (size_t)t * 2 * I + (j / 16) * 32 + (j % 16);
             const float gt = from_fix(ldcg_ll(row)), up = from_fix(ldcg_ll(row + 16));
-            return gt / (1.0f + expf(-gt)) * up;
+            return gt * __frcp_rn(1.0f + __expf(-gt)) * up;
           });
         },
         [&](int r, int, float (&tot)[NT]) {
@@ -950,6 +1080,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   __syncthreads();
   stamp(2 * nbar + 1);
 
+  tc::cp_wait<0>();  // an attention prefetch left by an aborted layer
   // ---- release tensor memory (after the issuer's MMAs and the stream's copies have all
   // completed, also after an abort) ----
   if (warp >= PK_ISSUER && warp < PK_ISSUER + PK_NWG && lane == 0) {
@@ -1039,7 +1170,8 @@ void encode_qmat_maps(const QMat& w, int box_chunks, int box_groups, int box_row
   }
 }
 
-size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down) {
+// Bytes of the B-operand region (rounded to 128): the attention K/V region follows it.
+size_t pass_kernel_kv_off(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down) {
   const int NT = pass_kernel_nt(T);
   const int kb = tc_kb(f.bits, f.group);
   // largest B operand: the full hidden width (QKV, O, gate/up, head) or a K slice of down
@@ -1048,7 +1180,12 @@ size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int
   size_t b = (size_t)NT * std::max(hidden, down_cols) * 2;
   b = std::max(b, (size_t)T * PK_THREADS * 4);  // rms partial sums
   b = std::max(b, pk_att_smem(T, hd));
-  return 1024 + (size_t)PK_STAGES * pass_stage_bytes(f) + b;  // 1 KB for aligning the ring
+  return (b + 127) & ~(size_t)127;
+}
+
+size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down) {
+  return 1024 + (size_t)PK_STAGES * pass_stage_bytes(f) + pass_kernel_kv_off(f, T, hidden, inter, hd, ks_down) +
+         pk_kv_smem(hd);  // 1 KB for aligning the ring
 }
 
 template <int BITS, int G, int NT>
