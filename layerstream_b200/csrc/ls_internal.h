@@ -314,6 +314,7 @@ struct PassArgs {
                        // barriers, then [phases][4][gridDim] inside the phases from slot trace_sub on
   int trace_sub;
   int kv_off;  // byte offset of the attention K/V region from the B-operand region
+  int stages;  // weight-stream ring depth
   int L, hidden, inter, heads, kv_heads, hd, vocab, max_ctx, T, n_logits, slots;
   int ks_qkv, ks_o, ks_gu, ks_down;
   float eps;
@@ -353,7 +354,8 @@ void qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t r
 
 int pass_kernel_nt(int T);
 bool pass_kernel_supported(const WeightFormat& body, const WeightFormat& embed, int T, int hd);
-size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down);
+size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, int stages);
+int pass_kernel_stages(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, size_t budget);
 size_t pass_kernel_kv_off(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down);
 void launch_pass(const PassArgs& a, const WeightFormat& f, size_t smem, int grid, cudaStream_t s);
 int pass_kernel_blocks_per_sm(const WeightFormat& f, int T, size_t smem, int max_per_sm);

@@ -450,7 +450,7 @@ struct LsModel {
   // Launch plan of the pass kernel for one token tile (16, 32 or 48 tokens): CTAs, attention slots
   // per head, K slices per GEMV phase and dynamic shared memory.
   struct PassPlan {
-    int grid = 0, slots = 1, ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_down = 1, kv_off = 0;
+    int grid = 0, slots = 1, ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_down = 1, kv_off = 0, stages = 0;
     size_t smem = 0;
   };
   PassPlan pk_plan[3];
@@ -476,20 +476,15 @@ struct LsModel {
         const int tiles = (w.rows_pad / 32 + 7) / 8, nblk = w.cols / kb;
         return std::max(1, std::min(std::max(1, nblk / nbs), grid / tiles));
       };
-      // the down slice width sets the shared memory, which sets the CTAs per SM: settle both
+      // one CTA per SM (it takes the whole tensor memory); the weight ring takes the shared memory
+      // the rest leaves (LS_PASS_STAGES caps it)
       P.ks_down = plan(layers[0].down, num_sms);
-      size_t smem = pass_kernel_smem(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down);
-      if (smem > 220 * 1024) continue;
-      int per_sm = pass_kernel_blocks_per_sm(cfg.format, T, smem, max_per_sm);
+      P.stages = pass_kernel_stages(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, 220 * 1024);
+      if (const char* st = getenv("LS_PASS_STAGES")) P.stages = std::min(P.stages, std::max(2, atoi(st)));
+      if (P.stages == 0) continue;
+      const size_t smem = pass_kernel_smem(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, P.stages);
+      const int per_sm = pass_kernel_blocks_per_sm(cfg.format, T, smem, max_per_sm);
       if (per_sm < 1) continue;
-      for (int iter = 0; iter < 3; iter++) {
-        const int ks = plan(layers[0].down, per_sm * num_sms);
-        const size_t sm2 = pass_kernel_smem(cfg.format, T, h, I, (int)cfg.head_dim, ks);
-        const int ps2 = pass_kernel_blocks_per_sm(cfg.format, T, sm2, max_per_sm);
-        if (ps2 < per_sm) break;
-        P.ks_down = ks;
-        smem = sm2;
-      }
       P.grid = per_sm * num_sms;
       P.smem = smem;
       P.ks_qkv = plan(layers[0].qkv, P.grid);
@@ -501,8 +496,9 @@ struct LsModel {
     }
     if (getenv("LS_PASS_VERBOSE"))
       for (int c = 0; c < 3; c++)
-        fprintf(stderr, "pass plan T<=%d: grid %d slots %d ks qkv %d o %d gu %d down %d smem %zu\n", 16 * (c + 1),
-                pk_plan[c].grid, pk_plan[c].slots, pk_plan[c].ks_qkv, pk_plan[c].ks_o, pk_plan[c].ks_gu, pk_plan[c].ks_down,
+        fprintf(stderr, "pass plan T<=%d: grid %d slots %d stages %d ks qkv %d o %d gu %d down %d smem %zu\n",
+                16 * (c + 1), pk_plan[c].grid, pk_plan[c].slots, pk_plan[c].stages, pk_plan[c].ks_qkv, pk_plan[c].ks_o,
+                pk_plan[c].ks_gu, pk_plan[c].ks_down,
                 pk_plan[c].smem);
     if (pk_plan[0].grid == 0) return;
     pk_max_grid = max_grid;
@@ -566,6 +562,7 @@ struct LsModel {
     a.trace = prof_timeline ? pk_trace : nullptr;
     a.trace_sub = (int)pk_trace_sub();
     a.kv_off = P.kv_off;
+    a.stages = P.stages;
     pk_T = T;
     pk_n_logits = n_logits;
     pk_traced = a.trace != nullptr;

@@ -42,7 +42,7 @@ constexpr int kMaxSlots = 16;  // attention slots per head (context tiles split 
 // Weight stream: STAGES stages of one 256-row box of ~16 KB of packed weights (+ its scales),
 // filled by TMA. Bulk copies of >= 16 KB per stage stream at HBM bandwidth with one CTA per SM
 // (per-thread 16-byte copies top out near a third of it).
-constexpr int PK_STAGES = 4;
+constexpr int PK_MAX_STAGES = 8;  // the launch's stage count (a.stages) fills the shared memory left
 constexpr int PK_STAGE_DATA = 16384;
 constexpr int PK_TMEM_COLS = 512;  // one CTA per SM: the whole tensor memory
 constexpr int PK_ABUF = 4;         // A buffers per warpgroup (dequantizers run ahead of the MMAs)
@@ -105,7 +105,7 @@ __device__ bool grid_barrier(unsigned* bar, unsigned target, int* err) {
 // ---------------------------------------------------------------------------------------------
 // The tensor-core GEMV of one item: rows [256 t256, 256 t256 + 256) over K blocks [kb0, kb1).
 // The producer warp streams the item's weights (and group scales) as 256-row TMA boxes of NB K
-// blocks into a PK_STAGES ring (full / empty mbarriers); each compute warpgroup dequantizes its
+// blocks into a ring of `nst` stages (full / empty mbarriers); each compute warpgroup dequantizes its
 // 128 rows block by block into its A buffer in tensor memory; the issuer warp runs the MMAs.
 // State is kept across items and phases; all roles walk the same item / block sequence.
 // Tensor memory columns: A buffer (b, g) at (b PK_NWG + g) ACOLS, accumulator (d, g) at
@@ -149,7 +149,8 @@ struct TcGemv {
   static_assert(PK_ABUF * PK_NWG * ACOLS + 2 * PK_NWG * NT <= PK_TMEM_COLS, "tensor memory");
   uint32_t tmem;
   uint8_t* ring;
-  uint64_t *full, *empty;        // [PK_STAGES] weight stream
+  uint64_t *full, *empty;        // [nst] weight stream
+  int nst;
   uint64_t *bar_a, *bar_full;    // [PK_NWG][PK_ABUF] A buffers: MMAs done / A written
   uint64_t *bar_d, *bar_dfree;   // [PK_NWG][2] accumulators: ready / read
   int* abort;
@@ -166,10 +167,24 @@ struct TcGemv {
     const int g = threadIdx.x >> 7, warp8 = threadIdx.x >> 5, warp = warp8 & 3, lane = threadIdx.x & 31;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     const uint32_t sub8 = BITS == 8 ? 0x64806480u : 0x64086408u;
+    // The tensor-memory store of block j completes while block j + 1 is dequantized; only then is
+    // block j handed to the issuer (pend = its A buffer's barrier, or null).
+    uint64_t* pend = nullptr;
+    auto hand_off = [&]() {
+      if (pend == nullptr) return;
+      tc::wait_st();
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(pend)) : "memory");
+      pend = nullptr;
+    };
     for (int kbs = kb0; kbs < kb1; kbs += NB) {
-      const int slot = rpos % PK_STAGES;
-      bool fail = !tc::mbar_wait_fast(&full[slot], (rpos / PK_STAGES) & 1, abort);
-      if (__any_sync(0xffffffffu, fail)) return false;
+      const int slot = rpos % nst;
+      bool fail = !tc::mbar_wait_fast(&full[slot], (rpos / nst) & 1, abort);
+      if (__any_sync(0xffffffffu, fail)) {
+        tc::wait_st();
+        return false;
+      }
       marks.mark(0, blk);
       rpos++;
       const uint8_t* st = ring + (size_t)slot * S::kStage;
@@ -228,6 +243,7 @@ struct TcGemv {
           if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&empty[slot])) : "memory");
         }
         marks.mark(1, blk + (a[ACOLS - 1] == 0x7fffffffu ? 1u : 0u));
+        hand_off();  // the previous block
         // A buffer b is free once the MMAs of block blk - PK_ABUF have completed
         const int b = blk % PK_ABUF;
         const uint32_t u = blk / PK_ABUF;
@@ -237,15 +253,12 @@ struct TcGemv {
         tc::fence_after();
 #pragma unroll
         for (int q = 0; q < ACOLS / 16; q++) tc::st16(a_col(b, g) + lane_base + q * 16, a + q * 16);
-        tc::wait_st();
-        tc::fence_before();
-        __syncwarp();
-        if (lane == 0)
-          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_full[g * PK_ABUF + b])) : "memory");
+        pend = &bar_full[g * PK_ABUF + b];
         marks.mark(3, blk);
         blk++;
       }
     }
+    hand_off();  // the item's last block
     const int d = itc & 1;
     const uint32_t v = itc >> 1;
     itc++;
@@ -335,6 +348,7 @@ struct Producer {
   using S = Stream<BITS, G>;
   uint8_t* ring;
   uint64_t *full, *empty;
+  int nst;
   int* abort;
   uint32_t lpos;  // stages issued so far
   const QMaps* maps;
@@ -355,8 +369,8 @@ struct Producer {
   // Issues the next stage. wait == false: returns false at once when its slot is still in use.
   // A timeout also returns false (and raises *abort).
   __device__ bool issue_one(bool wait) {
-    const int slot = lpos % PK_STAGES;
-    const uint32_t use = lpos / PK_STAGES;
+    const int slot = lpos % nst;
+    const uint32_t use = lpos / nst;
     if (use > 0) {
       if (!wait) {
         if (!mbar_test(&empty[slot], (use - 1) & 1)) return false;
@@ -758,7 +772,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t bar_a[PK_NWG * PK_ABUF], bar_full[PK_NWG * PK_ABUF], bar_d[PK_NWG * 2], bar_dfree[PK_NWG * 2],
       bar_fin[PK_NWG];
-  __shared__ uint64_t s_full[PK_STAGES], s_empty[PK_STAGES];
+  __shared__ uint64_t s_full[PK_MAX_STAGES], s_empty[PK_MAX_STAGES];
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ float s_inv[NT];
@@ -772,7 +786,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   int* err = &a.ctl->err;
   // shared memory: [weight-stream ring (1 KB aligned)][B operand, or attention scratch, or rms sums]
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* xb = ring + (size_t)PK_STAGES * Str::kStage;
+  const int nst = a.stages;
+  uint8_t* xb = ring + (size_t)nst * Str::kStage;
   float* red = reinterpret_cast<float*>(xb);
   uint8_t* kvb = xb + a.kv_off;  // attention K/V tiles
   const uint32_t xb_addr = tc::su32(xb);
@@ -786,7 +801,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
       tc::mbar_init(&bar_d[i], 1);
       tc::mbar_init(&bar_dfree[i], 4);
     }
-    for (int i = 0; i < PK_STAGES; i++) {
+    for (int i = 0; i < nst; i++) {
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&s_empty[i], PK_NWG * 4);
     }
@@ -805,6 +820,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   Gemv gm;
   gm.tmem = s_tmem;
   gm.ring = ring;
+  gm.nst = nst;
   gm.full = s_full;
   gm.empty = s_empty;
   gm.bar_a = bar_a;
@@ -815,6 +831,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   gm.blk = gm.itc = gm.rpos = 0;
   Producer<BITS, G> pr;
   pr.ring = ring;
+  pr.nst = nst;
   pr.full = s_full;
   pr.empty = s_empty;
   pr.abort = &s_abort;
@@ -1090,8 +1107,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   }
   if (producer) {
     volatile int no_abort = 0;
-    for (uint32_t p = pr.lpos > PK_STAGES ? pr.lpos - PK_STAGES : 0; p < pr.lpos; p++)
-      tc::mbar_wait(&s_full[p % PK_STAGES], (p / PK_STAGES) & 1, &no_abort);
+    for (uint32_t p = pr.lpos > (uint32_t)nst ? pr.lpos - nst : 0; p < pr.lpos; p++)
+      tc::mbar_wait(&s_full[p % nst], (p / nst) & 1, &no_abort);
   }
   tc::fence_before();
   __syncthreads();
@@ -1183,9 +1200,18 @@ size_t pass_kernel_kv_off(const WeightFormat& f, int T, int hidden, int inter, i
   return (b + 127) & ~(size_t)127;
 }
 
-size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down) {
-  return 1024 + (size_t)PK_STAGES * pass_stage_bytes(f) + pass_kernel_kv_off(f, T, hidden, inter, hd, ks_down) +
+size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, int stages) {
+  return 1024 + (size_t)stages * pass_stage_bytes(f) + pass_kernel_kv_off(f, T, hidden, inter, hd, ks_down) +
          pk_kv_smem(hd);  // 1 KB for aligning the ring
+}
+
+// The deepest weight ring (2 .. PK_MAX_STAGES stages) whose shared memory fits `budget` bytes; 0 if
+// none does. A deeper ring keeps more bytes in flight per SM (the LM head streams at the ring's
+// depth over the memory latency).
+int pass_kernel_stages(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, size_t budget) {
+  for (int st = PK_MAX_STAGES; st >= 2; st--)
+    if (pass_kernel_smem(f, T, hidden, inter, hd, ks_down, st) <= budget) return st;
+  return 0;
 }
 
 template <int BITS, int G, int NT>
