@@ -146,20 +146,20 @@ struct TcGemv {
   using S = Stream<BITS, G>;
   Marks marks;
   static constexpr int KB = S::KB, NS = S::NS, CPB = S::CPB, NB = S::NB, ACOLS = KB / 2;
-  static_assert(PK_ABUF * PK_NWG * ACOLS + 2 * PK_NWG * NT <= PK_TMEM_COLS, "tensor memory");
+  // One A buffer holds a whole stream stage (NB K blocks side by side): one hand-off per stage.
+  static constexpr int AC = NB * ACOLS, AB = (256 / (PK_NWG * AC)) < PK_ABUF ? 256 / (PK_NWG * AC) : PK_ABUF;
+  static_assert(AB >= 2 && AB * PK_NWG * AC + 2 * PK_NWG * NT <= PK_TMEM_COLS, "tensor memory");
   uint32_t tmem;
   uint8_t* ring;
   uint64_t *full, *empty;        // [nst] weight stream
   int nst;
-  uint64_t *bar_a, *bar_full;    // [PK_NWG][PK_ABUF] A buffers: MMAs done / A written
+  uint64_t *bar_a, *bar_full;    // [PK_NWG][AB] A buffers: MMAs done / A written
   uint64_t *bar_d, *bar_dfree;   // [PK_NWG][2] accumulators: ready / read
   int* abort;
-  uint32_t blk, itc, rpos;  // K blocks, items and stream stages consumed so far
+  uint32_t blk, itc, rpos;  // A hand-offs (stages), items and stream stages consumed so far
 
-  __device__ uint32_t a_col(int b, int g) const { return tmem + (uint32_t)((b * PK_NWG + g) * ACOLS); }
-  __device__ uint32_t d_col(int d, int g) const {
-    return tmem + (uint32_t)(PK_ABUF * PK_NWG * ACOLS + (d * PK_NWG + g) * NT);
-  }
+  __device__ uint32_t a_col(int b, int g) const { return tmem + (uint32_t)((b * PK_NWG + g) * AC); }
+  __device__ uint32_t d_col(int d, int g) const { return tmem + (uint32_t)(AB * PK_NWG * AC + (d * PK_NWG + g) * NT); }
 
   // Compute threads: the K loop of an item over the streamed stages, then the accumulators.
   // false on a timeout.
@@ -167,8 +167,8 @@ struct TcGemv {
     const int g = threadIdx.x >> 7, warp8 = threadIdx.x >> 5, warp = warp8 & 3, lane = threadIdx.x & 31;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     const uint32_t sub8 = BITS == 8 ? 0x64806480u : 0x64086408u;
-    // The tensor-memory store of block j completes while block j + 1 is dequantized; only then is
-    // block j handed to the issuer (pend = its A buffer's barrier, or null).
+    // The tensor-memory stores of stage j complete while stage j + 1's first block is dequantized;
+    // only then is stage j handed to the issuer (pend = its A buffer's barrier, or null).
     uint64_t* pend = nullptr;
     auto hand_off = [&]() {
       if (pend == nullptr) return;
@@ -189,7 +189,12 @@ struct TcGemv {
       rpos++;
       const uint8_t* st = ring + (size_t)slot * S::kStage;
       const int nb = min(NB, kb1 - kbs);
-      for (int bi = 0; bi < nb; bi++) {
+      // the stage's blocks go to one A buffer side by side (block bi at column bi ACOLS); each
+      // block's store is issued as soon as it is dequantized, the stage is handed off once
+      const int b = blk % AB;
+#pragma unroll
+      for (int bi = 0; bi < NB; bi++) {
+        if (bi >= nb) break;
         // this warp's 32 rows (row group warp8 of the box): chunk (bi CPB + q), group (bi NS + s)
         uint4 wv[CPB];
 #pragma unroll
@@ -238,27 +243,29 @@ struct TcGemv {
             }
           }
         }
-        if (bi == nb - 1) {  // this warp is done with the stage: the producer may refill it
-          __syncwarp();
-          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&empty[slot])) : "memory");
+        if (bi == 0) {
+          marks.mark(1, blk + (a[ACOLS - 1] == 0x7fffffffu ? 1u : 0u));
+          hand_off();  // the previous stage
+          // A buffer b is free once the MMAs of hand-off blk - AB have completed
+          const uint32_t u = blk / AB;
+          fail = u > 0 && !tc::mbar_wait_fast(&bar_a[g * AB + b], (u - 1) & 1, abort);
+          if (__any_sync(0xffffffffu, fail)) {
+            tc::wait_st();
+            return false;
+          }
+          marks.mark(2, blk);
+          tc::fence_after();
         }
-        marks.mark(1, blk + (a[ACOLS - 1] == 0x7fffffffu ? 1u : 0u));
-        hand_off();  // the previous block
-        // A buffer b is free once the MMAs of block blk - PK_ABUF have completed
-        const int b = blk % PK_ABUF;
-        const uint32_t u = blk / PK_ABUF;
-        fail = u > 0 && !tc::mbar_wait_fast(&bar_a[g * PK_ABUF + b], (u - 1) & 1, abort);
-        if (__any_sync(0xffffffffu, fail)) return false;
-        marks.mark(2, blk);
-        tc::fence_after();
 #pragma unroll
-        for (int q = 0; q < ACOLS / 16; q++) tc::st16(a_col(b, g) + lane_base + q * 16, a + q * 16);
-        pend = &bar_full[g * PK_ABUF + b];
-        marks.mark(3, blk);
-        blk++;
+        for (int q = 0; q < ACOLS / 16; q++) tc::st16(a_col(b, g) + bi * ACOLS + lane_base + q * 16, a + q * 16);
       }
+      __syncwarp();  // this warp is done with the stage: the producer may refill it
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&empty[slot])) : "memory");
+      pend = &bar_full[g * AB + b];
+      marks.mark(3, blk);
+      blk++;
     }
-    hand_off();  // the item's last block
+    hand_off();  // the item's last stage
     const int d = itc & 1;
     const uint32_t v = itc >> 1;
     itc++;
@@ -293,27 +300,31 @@ struct TcGemv {
       if (v > 0 && !tc::mbar_wait_fast(&bar_dfree[g * 2 + d], (v - 1) & 1, abort)) fail = true;
       const uint64_t bd0 = tc::sdesc(xb_addr, 128u, sbo);  // start address field: 16-byte units
       const uint32_t dcol = d_col(d, g);
-      for (int kb = kb0; kb < kb1 && !fail; kb++) {
-        const int b = blk % PK_ABUF;
-        const uint32_t u = blk / PK_ABUF;
+      for (int kbs = kb0; kbs < kb1 && !fail; kbs += NB) {
+        const int nb = min(NB, kb1 - kbs);
+        const int b = blk % AB;
+        const uint32_t u = blk / AB;
         blk++;
-        if (!tc::mbar_wait_fast(&bar_full[g * PK_ABUF + b], u & 1, abort)) {
+        if (!tc::mbar_wait_fast(&bar_full[g * AB + b], u & 1, abort)) {
           fail = true;
           break;
         }
         marks.mark(4, blk - 1);
         tc::fence_after();
         const uint32_t acol = a_col(b, g);
-        const uint64_t bdk = bd0 + (uint64_t)((kb - kb0) * KB);  // K column kpos sits kpos / 8 * 128 bytes in
+        for (int bi = 0; bi < nb; bi++) {
+          const uint64_t bdk = bd0 + (uint64_t)((kbs + bi - kb0) * KB);  // K column kpos sits kpos / 8 * 128 bytes in
 #pragma unroll
-        for (int j = 0; j < KB / 16; j++)
-          tc::mma_f16_ts(dcol, acol + j * 8, bdk + (uint64_t)(j * 16), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
-        tc::commit(&bar_a[g * PK_ABUF + b]);
+          for (int j = 0; j < KB / 16; j++)
+            tc::mma_f16_ts(dcol, acol + bi * ACOLS + j * 8, bdk + (uint64_t)(j * 16), idesc,
+                           (kbs + bi > kb0 || j > 0) ? 1u : 0u);
+        }
+        tc::commit(&bar_a[g * AB + b]);
         marks.mark(5, blk - 1);
       }
       if (!fail) tc::commit(&bar_d[g * 2 + d]);
     } else {
-      blk += kb1 - kb0;
+      blk += (kb1 - kb0 + NB - 1) / NB;
     }
     blk = __shfl_sync(0xffffffffu, blk, 0);
     return !__any_sync(0xffffffffu, fail);
