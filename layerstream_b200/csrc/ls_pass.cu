@@ -429,53 +429,37 @@ __device__ __forceinline__ void stage_b(uint8_t* xb, uint32_t sbo, int T, int co
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// 1 / rms of the first T rows of x (fixed point, n columns, n even) into s_inv. Every thread reads
-// 16-byte pairs of columns (RMS_BATCH per thread in flight at once) and sums its own columns of
-// each token in a fixed order; red (T x PK_THREADS floats of shared memory) then holds the per-thread
-// partial sums, which one warp per token adds in a fixed order: the result is deterministic.
-__device__ __forceinline__ void rms_stats(const long long* x, int T, int n, float eps, float* s_inv, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-  const int np = n >> 1, total = T * np;
-  for (int t = 0; t < T; t++) red[t * PK_THREADS + tid] = 0.f;
-  int cur = -1;
-  float ss = 0.f;
-  constexpr int RMS_BATCH = 4;
-  for (int j0 = 0; j0 < total; j0 += RMS_BATCH * PK_THREADS) {
-    longlong2 v[RMS_BATCH];
-#pragma unroll
-    for (int u = 0; u < RMS_BATCH; u++) {
-      const int j = j0 + u * PK_THREADS + tid;
-      if (j < total) {
-        const int t = j / np;
-        v[u] = __ldcg(reinterpret_cast<const longlong2*>(x + (size_t)t * n) + (j - t * np));
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < RMS_BATCH; u++) {
-      const int j = j0 + u * PK_THREADS + tid;
-      if (j < total) {
-        const int t = j / np;
-        if (t != cur) {
-          if (cur >= 0) red[cur * PK_THREADS + tid] = ss;
-          ss = 0.f;
-          cur = t;
-        }
-        const float f0 = from_fix(v[u].x), f1 = from_fix(v[u].y);
+// 1 / rms of the first T rows of x (fixed point, n columns, n even) into s_inv. The rows are copied
+// into shared memory (buf, buf_bytes) with cp.async, every 16-byte chunk in flight at once (as many
+// rows per round as fit; one round trip to L2 for a verify block of a small model), then warp w sums
+// the squares of row t's columns (lane l: column pairs l, l + 32, ...) in a fixed order that
+// depends only on n, so a token's statistics do not depend on its place in the pass.
+__device__ __forceinline__ void rms_stats(const long long* x, int T, int n, float eps, float* s_inv, uint8_t* buf,
+                                          size_t buf_bytes) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, np = n >> 1;
+  const int per = max(1, (int)(buf_bytes / ((size_t)n * 8)));
+  const longlong2* rows = reinterpret_cast<const longlong2*>(buf);
+  for (int t0 = 0; t0 < T; t0 += per) {
+    const int tn = min(per, T - t0);
+    const longlong2* src = reinterpret_cast<const longlong2*>(x + (size_t)t0 * n);
+    for (int i = threadIdx.x; i < tn * np; i += PK_THREADS) tc::cp_async16(tc::su32(buf + (size_t)i * 16), src + i);
+    tc::cp_commit();
+    tc::cp_wait<0>();
+    __syncthreads();
+    for (int t = warp; t < tn; t += PK_NW) {
+      const longlong2* r = rows + (size_t)t * np;
+      float ss = 0.f;
+      for (int p = lane; p < np; p += 32) {
+        const longlong2 v = r[p];
+        const float f0 = from_fix(v.x), f1 = from_fix(v.y);
         ss = fmaf(f0, f0, ss);
         ss = fmaf(f1, f1, ss);
       }
+      ss = warp_sum(ss);
+      if (lane == 0) s_inv[t0 + t] = 1.0f / sqrtf(ss / (float)n + eps);
     }
+    __syncthreads();
   }
-  if (cur >= 0) red[cur * PK_THREADS + tid] = ss;
-  __syncthreads();
-  for (int t = warp; t < T; t += PK_NW) {
-    float v = 0.f;
-#pragma unroll
-    for (int k = 0; k < PK_THREADS / 32; k++) v += red[t * PK_THREADS + k * 32 + lane];
-    v = warp_sum(v);
-    if (lane == 0) s_inv[t] = 1.0f / sqrtf(v / (float)n + eps);
-  }
-  __syncthreads();
 }
 
 __device__ __forceinline__ void zero_ll(long long* p, size_t n) {
@@ -799,8 +783,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int nst = a.stages;
   uint8_t* xb = ring + (size_t)nst * Str::kStage;
-  float* red = reinterpret_cast<float*>(xb);
   uint8_t* kvb = xb + a.kv_off;  // attention K/V tiles
+  // the B operand and K/V regions are contiguous: the RMS statistics copy rows of x into both
+  const size_t rms_bytes = (size_t)a.kv_off + pk_kv_smem(a.hd);
   const uint32_t xb_addr = tc::su32(xb);
 
   if (threadIdx.x == 0) {
@@ -973,10 +958,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
 
   for (int l = 0; l < a.L && ok; l++) {
     const PassLayer& W = a.layers[l];
+    // ---- QKV: RMSNorm(x) -> q|k|v sums (+ bias once) ----
+    rms_stats(a.x, T, h, a.eps, s_inv, xb, rms_bytes);
     // cached K/V rows of this CTA's first attention item: they stream in during the QKV phase
     if ((int)blockIdx.x < a.heads * a.slots) attention_prefetch(a, l, blockIdx.x / a.slots, blockIdx.x % a.slots, kvb);
-    // ---- QKV: RMSNorm(x) -> q|k|v sums (+ bias once) ----
-    rms_stats(a.x, T, h, a.eps, s_inv, red);
     gemv_phase(
         W.qkv, a.ks_qkv,
         [&](int col0, int ncol, uint32_t sbo) {
@@ -1021,7 +1006,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     if (!barrier()) break;
 
     // ---- gate/up: RMSNorm(x) -> gate/up sums ----
-    rms_stats(a.x, T, h, a.eps, s_inv, red);
+    rms_stats(a.x, T, h, a.eps, s_inv, xb, rms_bytes);
     gemv_phase(
         W.gu, a.ks_gu,
         [&](int col0, int ncol, uint32_t sbo) {
@@ -1066,7 +1051,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
       (&s_bv[0][0])[i] = -CUDART_INF_F;
       (&s_bi[0][0])[i] = 0xffffffffu;
     }
-    rms_stats(a.x + (size_t)r0 * h, n, h, a.eps, s_inv, red);
+    rms_stats(a.x + (size_t)r0 * h, n, h, a.eps, s_inv, xb, rms_bytes);
     gemv_phase(
         a.embed, 1,
         [&](int col0, int ncol, uint32_t sbo) {
@@ -1206,7 +1191,6 @@ size_t pass_kernel_kv_off(const WeightFormat& f, int T, int hidden, int inter, i
   const int nblk_down = inter / kb;
   const int down_cols = ((nblk_down + ks_down - 1) / ks_down) * kb;
   size_t b = (size_t)NT * std::max(hidden, down_cols) * 2;
-  b = std::max(b, (size_t)T * PK_THREADS * 4);  // rms partial sums
   b = std::max(b, pk_att_smem(T, hd));
   return (b + 127) & ~(size_t)127;
 }
