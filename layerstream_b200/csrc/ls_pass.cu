@@ -492,9 +492,9 @@ __device__ __forceinline__ int att_row_pos(int slot, int S, int ti, int cpt, int
 
 // Starts the cp.async copies of the cached K/V rows (positions < pos0, which no phase of this pass
 // writes) of tile 0 of item (hh, slot) into the K/V region. Every thread commits one group.
-__device__ void attention_prefetch(const PassArgs& a, int l, int hh, int slot, uint8_t* kvb) {
+__device__ void attention_prefetch(const PassArgs& a, int pos0, int l, int hh, int slot, uint8_t* kvb) {
   const int HD = a.hd, HPK = pk_hpk(HD), AT = pk_at(HD), c8 = HD / 8;
-  const int g = hh / (a.heads / a.kv_heads), pos0 = a.ctl->pos0;
+  const int g = hh / (a.heads / a.kv_heads);
   const size_t lstride = (size_t)a.kv_heads * a.max_ctx * HD;
   const uint16_t* kc = a.kc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
   const uint16_t* vc = a.vc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
@@ -517,12 +517,12 @@ __device__ void attention_prefetch(const PassArgs& a, int l, int hh, int slot, u
 // staged, sub[stride] after the first tile is in shared memory, sub[2 stride] once the slot state
 // is written.
 template <int PPL>
-__device__ void attention_item(const PassArgs& a, int l, int hh, int slot, uint8_t* sm, uint8_t* kvb, bool prefetched,
-                               unsigned* sub, int stride) {
+__device__ void attention_item(const PassArgs& a, int pos0, int l, int hh, int slot, uint8_t* sm, uint8_t* kvb,
+                               bool prefetched, unsigned* sub, int stride) {
   constexpr int AT = 32 * PPL, CPT = AT / PK_CHUNK;
   const int HD = a.hd, HALF = HD / 2, HP = HD + 2, HPK = HD + 8, T = a.T, S = a.slots;
   const int group = a.heads / a.kv_heads, g = hh / group;
-  const int pos0 = a.ctl->pos0, total = pos0 + T;
+  const int total = pos0 + T;
   const int nch = (total + PK_CHUNK - 1) / PK_CHUNK;
   const int H = a.heads * HD, KV = a.kv_heads * HD, QS = H + 2 * KV;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -769,7 +769,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
       bar_fin[PK_NWG];
   __shared__ uint64_t s_full[PK_MAX_STAGES], s_empty[PK_MAX_STAGES];
   __shared__ uint32_t s_tmem;
-  __shared__ int s_abort;
+  __shared__ int s_abort, s_pos0;
   __shared__ float s_inv[NT];
   __shared__ float s_bv[PK_NW][NT];
   __shared__ uint32_t s_bi[PK_NW][NT];
@@ -803,6 +803,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     }
     for (int i = 0; i < PK_NWG; i++) tc::mbar_init(&bar_fin[i], 1);
     s_abort = 0;
+    s_pos0 = a.ctl->pos0;  // the pass's start position: only CTA 0 advances it, after the last barrier
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
@@ -813,6 +814,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   }
   __syncthreads();
   tc::fence_after();
+  const int pos0 = s_pos0;
   Gemv gm;
   gm.tmem = s_tmem;
   gm.ring = ring;
@@ -961,7 +963,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     // ---- QKV: RMSNorm(x) -> q|k|v sums (+ bias once) ----
     rms_stats(a.x, T, h, a.eps, s_inv, xb, rms_bytes);
     // cached K/V rows of this CTA's first attention item: they stream in during the QKV phase
-    if ((int)blockIdx.x < a.heads * a.slots) attention_prefetch(a, l, blockIdx.x / a.slots, blockIdx.x % a.slots, kvb);
+    if ((int)blockIdx.x < a.heads * a.slots) attention_prefetch(a, pos0, l, blockIdx.x / a.slots, blockIdx.x % a.slots, kvb);
     gemv_phase(
         W.qkv, a.ks_qkv,
         [&](int col0, int ncol, uint32_t sbo) {
@@ -983,9 +985,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
       __syncthreads();
       const bool first = it == (int)blockIdx.x;
       if (a.hd <= 64)
-        attention_item<4>(a, l, it / a.slots, it % a.slots, xb, kvb, first, first ? sub_ptr(0) : nullptr, (int)gridDim.x);
+        attention_item<4>(a, pos0, l, it / a.slots, it % a.slots, xb, kvb, first, first ? sub_ptr(0) : nullptr, (int)gridDim.x);
       else
-        attention_item<2>(a, l, it / a.slots, it % a.slots, xb, kvb, first, first ? sub_ptr(0) : nullptr, (int)gridDim.x);
+        attention_item<2>(a, pos0, l, it / a.slots, it % a.slots, xb, kvb, first, first ? sub_ptr(0) : nullptr, (int)gridDim.x);
       sub(3);
     }
     zero_ll(a.gu, (size_t)T * 2 * I);
