@@ -76,7 +76,7 @@ def parse():
     ap.add_argument("--tp", action="store_true",
                     help="config 5 (b): the resident model split tensor-parallel over the launched ranks (NCCL), "
                          "instead of 2-slot streaming per GPU")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-sample-tokens", type=int, default=0, help="decode tokens per CPU sample (0: auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="print the per-kernel profile to stderr")
@@ -89,7 +89,7 @@ def parse():
 
 
 def ncu_case(args, cfg):
-    """Small deterministic workloads to capture under ncu (see profiles/)."""
+    """Small deterministic workloads to capture under ncu."""
     import torch
 
     import layerstream_b200 as ls
@@ -157,19 +157,16 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(kernel_class: str):
-    """DRAM bytes per launch from the committed ncu summary (profiles/*.md lines `traffic <class>: <bytes>`)."""
-    d = os.path.join(ROOT, "profiles")
-    if not os.path.isdir(d):
+def profile_traffic(key: str):
+    """DRAM bytes (read + write) per launch of a kernel on a bench workload, as an ncu capture of
+    that workload measured them (dram__bytes_read.sum + dram__bytes_write.sum). ncu cannot run
+    inside the timed region, so the figures are recorded beside the profile summaries in
+    profiles/traffic.json, keyed "<kernel>-<workload>"; None when no capture exists."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
         return None
-    for f in sorted(os.listdir(d)):
-        if not f.endswith(".md"):
-            continue
-        for line in open(os.path.join(d, f)):
-            m = re.match(rf"\s*[-*]?\s*traffic {re.escape(kernel_class)}:\s*([0-9.eE+]+)", line)
-            if m:
-                return float(m.group(1))
-    return None
+    v = json.load(open(p)).get(key)
+    return float(v["bytes_per_launch"]) if isinstance(v, dict) and v.get("bytes_per_launch") is not None else None
 
 
 class Clocks:
@@ -245,18 +242,26 @@ def reduce_over_ranks(dist, ms: float, tokens: float, device="cpu"):
 
     t_ms = torch.tensor([float(ms)], device=device)
     t_tok = torch.tensor([float(tokens)], device=device)
+    per_rank = [float(ms)]
     if dist is not None:
+        g = torch.zeros(dist.get_world_size(), device=device)
+        dist.all_gather_into_tensor(g, t_ms.clone())
+        per_rank = [float(v) for v in g.tolist()]
         dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
         dist.all_reduce(t_tok, op=dist.ReduceOp.SUM)
+    reduce_over_ranks.per_rank_ms = per_rank
     return float(t_ms.item()), float(t_tok.item())
 
 
-def prompt_for(cfg, vocab, rank):
+def prompt_for(cfg, vocab, index):
+    """Prompt `index` of a config's seeded prompt set. Every rank of a data-parallel run takes the
+    same indices, so each GPU does identical work (weak scaling that measures the hardware, not
+    the acceptance rate of different prompts)."""
     from layerstream_b200 import synth
 
     if cfg["repeats"]:
-        return synth.make_prompt(cfg["prompt"], vocab, cfg["span"], cfg["repeats"], seed=1000 + rank)
-    return synth.make_prompt_spans(cfg["prompt"], vocab, cfg["span"], seed=1000 + rank)
+        return synth.make_prompt(cfg["prompt"], vocab, cfg["span"], cfg["repeats"], seed=1000 + index)
+    return synth.make_prompt_spans(cfg["prompt"], vocab, cfg["span"], seed=1000 + index)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -285,9 +290,10 @@ def cpu_files(args, cfg, rank, dist):
     return t, dr
 
 
-def cpu_sample(args, cfg, target_path, draft_path, steps, warmup):
+def cpu_sample(args, cfg, target_path, draft_path, steps, warmup, keep=None):
     """Times the oracle's decode loop on a bounded sample: prefill once, then `steps` decodes of
-    n_tok tokens from the prefilled state. Returns (tokens/s, per-step list, sample text, cores)."""
+    n_tok tokens from the prefilled state. Returns (tokens/s, per-step list, sample text, cores).
+    keep (a dict): receives the prefilled CPU model, its greedy first token and the prompt."""
     from oracle import oracle as O
 
     threads = os.cpu_count() or 1
@@ -310,7 +316,62 @@ def cpu_sample(args, cfg, target_path, draft_path, steps, warmup):
             rates.append((len(toks) - 1) / max(st["decode_secs"], 1e-9))
     sample = (f"decode of {n_tok} tokens (of {cfg['max_new']}) from the prefilled {plen}-token prompt, "
               f"{cfg['drafter']} drafter, k={k}, {steps} timed samples")
+    if keep is not None:
+        T.truncate(plen)
+        keep.update(model=T, first=first, prompt=prompt)
     return float(np.mean(rates)), rates, sample, threads
+
+
+def file_digest(path):
+    import hashlib
+
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for b in iter(lambda: f.read(1 << 24), b""):
+            h.update(b)
+    return h.hexdigest()
+
+
+def dtype_note(bits):
+    """The arithmetic the verify pass computes in."""
+    w = (f"int{bits} weights dequantized exactly to f16 ((q - 8) * scale)" if bits == 4 else
+         "int8 weights split exactly into two f16 MMA operands (hi + lo = q * scale)")
+    return f"u{bits}/bf16-scale weights; {w}; activations rounded to f16 MMA operands; f32 accumulation; f16 KV cache"
+
+
+def cpu_parity(keep, gpu_tokens, n, tol=2e-2):
+    """Token parity of the GPU's decode with the CPU path on the same prompt and model bytes,
+    teacher-forced on the GPU's tokens: the CPU model (prefilled) runs one pass over the GPU's
+    first n tokens and takes its own greedy choice at every position. A position is checked when
+    the CPU path's top-2 logit margin there exceeds tol (the north star's logit tolerance), and
+    skipped as a near-tie otherwise."""
+    from oracle import oracle as O
+
+    T, first = keep["model"], keep["first"]
+    toks = [int(t) for t in gpu_tokens[:n]]
+    rows = T.forward_multi(toks[:-1], len(toks) - 1) if len(toks) > 1 else np.zeros((0, T.vocab), np.float32)
+    choice = [first] + [int(O.argmax(r)) for r in rows]
+    # the margin of the first choice needs the prefill logits: recompute the last prompt position
+    T.truncate(len(keep["prompt"]) - 1)
+    margins = [0.0] * len(toks)
+    lc0 = T.forward(keep["prompt"][-1:])
+    for i, r in enumerate([lc0] + list(rows)):
+        top2 = np.partition(r, -2)[-2:]
+        margins[i] = float(top2[1] - top2[0])
+    checked = agreed = skipped = 0
+    mismatches = []
+    for i, t in enumerate(toks):
+        if margins[i] > tol:
+            checked += 1
+            if choice[i] == t:
+                agreed += 1
+            else:
+                mismatches.append(i)
+        else:
+            skipped += 1
+    return {"checked": checked, "agreed": agreed, "skipped_near_ties": skipped, "positions": len(toks),
+            "tolerance": tol, "mismatch_positions": mismatches[:8],
+            "method": "teacher-forced on the GPU's decode tokens; CPU restatement on the same .lsq bytes"}
 
 
 # ------------------------------------------------------------------------------------------------
@@ -476,8 +537,9 @@ def batch_bench(args, cfg):
     else:
         model = ls.Model(path, device=local, max_ctx=plen + 64)
     V = model.vocab
-    # data parallel: each rank its own B sequences; tensor parallel: the same B sequences on every rank
-    prompts = np.array([prompt_for(cfg, V, (0 if tp else rank * B) + i) for i in range(B)], np.uint32)
+    # data parallel: every rank decodes its own copy of the same B seeded sequences (identical
+    # work per GPU); tensor parallel: the same B sequences split over the ranks' weight shards
+    prompts = np.array([prompt_for(cfg, V, i) for i in range(B)], np.uint32)
     tp_arg = None
     if tp and world > 1:
         box = [ls.tp_unique_id() if rank == 0 else None]
@@ -530,7 +592,7 @@ def batch_bench(args, cfg):
                     "bytes_per_pass": info.weight_bytes, "note": "every pass streams all layers and the head over PCIe"}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / max(args.steps, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": f"f32 activations, int{cfg['body'][0]} weights (bf16 scales), f16 KV", "data": "synthetic",
+            "dtype": dtype_note(cfg["body"][0]), "data": "synthetic",
             "config": {"workload": f"config4: 0.5b Qwen2 random-init int8 g64, {B} sequences per GPU, {plen}-token prompts, "
                                    f"{max_new} new tokens each, k={k}, lookup drafter, batched verify",
                        "config": 4, "batch_per_gpu": B, "global_batch": B * world,
@@ -548,7 +610,7 @@ def batch_bench(args, cfg):
                          "avg_launch_us": pass_s * 1e6, "launches_per_pass": 2 + 5 * info.layers + 2},
             "spec": {"tokens_per_pass": tokens / max(passes, 1) / B, "accepted_over_drafted": acc / max(dr, 1),
                      "target_passes": passes, "prefill_s": first_s / max(args.steps, 1)},
-            "streaming": streamed,
+            "streaming": streamed, "per_rank_ms": reduce_over_ranks.per_rank_ms,
             "classes": class_split(prof)}
     if slots:
         # streamed weights: the bound is the host-to-device link, not HBM
@@ -560,7 +622,7 @@ def batch_bench(args, cfg):
         line["config"]["workload"] = (f"config5: 3b Qwen2 random-init int4 g32, {B} sequences, {plen}-token prompts, "
                                       f"{max_new} new tokens, k={k}, lookup drafter, {slots}-slot layer streaming from pinned host")
         line["config"]["config"] = 5
-        line["dtype"] = "f32 activations, int4 weights (bf16 scales), f16 KV"
+        line["dtype"] = dtype_note(4)
     if tp:
         # per rank: its shard of the weights and the K/V of its kv heads; the pass also carries
         # 2 all-reduces per layer and one all-gather over NVLink (NCCL)
@@ -576,7 +638,7 @@ def batch_bench(args, cfg):
             "parallelism": (f"tp{world}: column-parallel QKV (q heads) and gate/up, row-parallel O and down with NCCL "
                             "all-reduce, vocabulary-parallel head with an all-gather of per-rank maxima")
                            if world > 1 else "single GPU (tp1)"})
-        line["dtype"] = "f32 activations, int4 weights (bf16 scales), f16 KV"
+        line["dtype"] = dtype_note(4)
         line["gpu_launches"] = int(passes * (7 * info.layers + 5 if world > 1 else 5 * info.layers + 4))
         line["roofline"] = {"bound": "hbm", "kernel": "tensor-parallel verify pass on the busiest rank (separate kernels)",
                             "achieved": (w_r + kv_r) / pass_s / 1e9, "peak": peak, "unit": "GB/s",
@@ -659,7 +721,7 @@ def main():
     draft = ls.Model(d_path, device=local, max_ctx=max_ctx) if d_path else None
     V = target.vocab
     info = target.info
-    prompt = prompt_for(cfg, V, rank)
+    prompt = prompt_for(cfg, V, 0)
     stream = torch.cuda.ExternalStream(target.stream, device=torch.device("cuda", local))
 
     first = target.forward(prompt, want_logits=False)
@@ -671,8 +733,10 @@ def main():
         if draft is not None:
             draft.truncate(plen)
         toks, st = ls.spec_continue(target, draft, prompt, first, max_new, k)
+        last_tokens[:] = toks
         return len(toks) - 1, st
 
+    last_tokens = []
     for _ in range(args.warmup):
         step()
 
@@ -732,10 +796,9 @@ def main():
     d2h = (r1["d2h_bytes"] - r0["d2h_bytes"]) // max(args.e2e_steps, 1)
 
     # roofline of the dominant kernel (live CUDA-event timing of its launches). With the persistent
-    # pass kernel a verify pass is one launch (profiles/pass_kernel_config2.md): algorithmic bytes =
-    # weights + the K/V rows read and written at that pass's context. Otherwise the tensor-core GEMV
-    # launches dominate (profiles/verify_pass_launches_config2.md): QKV, O, gate/up and down on
-    # every layer (timed on one sampled layer, times L) plus the LM head.
+    # pass kernel a verify pass is one launch: algorithmic bytes = weights + the K/V rows read and
+    # written at that pass's context. Otherwise the tensor-core GEMV launches dominate: QKV, O,
+    # gate/up and down on every layer (timed on one sampled layer, times L) plus the LM head.
     peak, peak_kind = peaks()
     L = info.layers
     per_pass = {}
@@ -792,12 +855,16 @@ def main():
     dr = sum(s["drafted"] for s in stats)
     tp = sum(s["target_passes"] for s in stats)
 
-    cpu = None
+    cpu, parity = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             tpc, dpc = cpu_files(args, cfg, rank, None)
-            v, _, sample, cores = cpu_sample(args, cfg, tpc, dpc, steps=2, warmup=0)
+            keep = {}
+            v, _, sample, cores = cpu_sample(args, cfg, tpc, dpc, steps=10, warmup=1, keep=keep)
             cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+            # outside every timed region: the GPU's decoded tokens against the CPU path's choices
+            parity = cpu_parity(keep, last_tokens, min(len(last_tokens), 48))
+            parity["model_bytes_identical"] = file_digest(tpc) == file_digest(t_path)
         except Exception as e:  # the baseline is reported, never required
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
 
@@ -805,13 +872,14 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": f"f32 activations, int{cfg['body'][0]} weights (bf16 scales), f16 KV", "data": "synthetic",
-        "config": base_cfg, "clocks": clk,
+        "dtype": dtype_note(cfg["body"][0]), "data": "synthetic",
+        "config": base_cfg, "clocks": clk, "parity": parity,
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "steps": args.e2e_steps, "includes": "prefill + decode through ls_speculative_greedy, host buffers"},
         "gpu_launches": int(passes * (1 if info.persistent_pass else kernels_per_pass)),
         "roofline": roof, "verify_step": vstep,
         "spec": {"tokens_per_pass": tokens / max(tp, 1), "accepted_over_drafted": acc / max(dr, 1), "target_passes": tp},
+        "per_rank_ms": reduce_over_ranks.per_rank_ms,
         "cpu_baseline": cpu,
     }
     if args.profile and rank == 0:

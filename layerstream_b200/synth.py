@@ -22,6 +22,9 @@ SHAPES = {
     "3b": dict(hidden_size=2048, num_attention_heads=16, num_key_value_heads=2, intermediate_size=11008,
                num_hidden_layers=36, vocab_size=151936, rope_theta=1000000.0, max_position_embeddings=32768),
 }
+# The 3B widths (head size 128, 16 / 2 heads, FFN 11008, full vocabulary) with 2 layers: parity
+# tests at those shapes without 36 layers of CPU work per token.
+SHAPES["3b-2l"] = dict(SHAPES["3b"], num_hidden_layers=2)
 
 SUFFIXES = [
     "input_layernorm.weight", "mlp.down_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight",
