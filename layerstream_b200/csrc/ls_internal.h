@@ -359,6 +359,7 @@ int pass_kernel_stages(const WeightFormat& f, int T, int hidden, int inter, int 
 size_t pass_kernel_kv_off(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down);
 void launch_pass(const PassArgs& a, const WeightFormat& f, size_t smem, int grid, cudaStream_t s);
 int pass_kernel_blocks_per_sm(const WeightFormat& f, int T, size_t smem, int max_per_sm);
+size_t pass_kernel_smem_budget(const WeightFormat& f, int T);
 // K blocks of 64 columns per weight-stream stage of the pass kernel, and the descriptors.
 int pass_kernel_stage_blocks(const WeightFormat& f);
 void pass_encode_maps(const QMat& w, QMaps* out);

@@ -479,7 +479,7 @@ struct LsModel {
       // one CTA per SM (it takes the whole tensor memory); the weight ring takes the shared memory
       // the rest leaves (LS_PASS_STAGES caps it)
       P.ks_down = plan(layers[0].down, num_sms);
-      P.stages = pass_kernel_stages(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, 220 * 1024);
+      P.stages = pass_kernel_stages(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, pass_kernel_smem_budget(cfg.format, T));
       if (const char* st = getenv("LS_PASS_STAGES")) P.stages = std::min(P.stages, std::max(2, atoi(st)));
       if (P.stages == 0) continue;
       const size_t smem = pass_kernel_smem(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, P.stages);

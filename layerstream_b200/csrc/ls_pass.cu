@@ -118,12 +118,20 @@ struct Stream {
   static constexpr uint32_t kData = 8 * CPB * NB * 512, kScales = 8 * NS * NB * 64, kStage = kData + kScales;
 };
 
-__device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+// Weight-stream load: each weight byte is read once per pass, so the copy is marked first to be
+// evicted from L2, which keeps the pass's activations and small per-layer tensors there.
+__device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar,
+                                          uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(
           dst),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(tc::su32(bar))
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(tc::su32(bar)), "l"(policy)
       : "memory");
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
   uint32_t ok;
@@ -392,8 +400,9 @@ struct Producer {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::su32(&full[slot])), "r"(S::kStage)
                  : "memory");
     const uint32_t dst = tc::su32(ring + (size_t)slot * S::kStage);
-    tma_load3(dst, &maps->data, 0, kb * S::CPB, t256 * 8, &full[slot]);
-    tma_load3(dst + S::kData, &maps->scales, 0, kb * S::NS, t256 * 8, &full[slot]);
+    const uint64_t pol = evict_first_policy();
+    tma_load3(dst, &maps->data, 0, kb * S::CPB, t256 * 8, &full[slot], pol);
+    tma_load3(dst + S::kData, &maps->scales, 0, kb * S::NS, t256 * 8, &full[slot], pol);
     lpos++;
     kb += S::NB;
     if (kb >= kb1) {
@@ -1241,6 +1250,28 @@ void launch_pass(const PassArgs& a, const WeightFormat& f, size_t smem, int grid
   LS_PK(4, 32)
 #undef LS_PK
   LS_THROW(-1, "format not supported by the pass kernel");
+}
+
+// Dynamic shared memory a pass-kernel launch for T tokens may use: the device's per-block opt-in
+// limit less the kernel's static shared memory (mbarriers, per-token sums, argmax parts).
+size_t pass_kernel_smem_budget(const WeightFormat& f, int T) {
+  const int NT = pass_kernel_nt(T);
+  int dev = 0, optin = 0;
+  LS_CUDA(cudaGetDevice(&dev));
+  LS_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  cudaFuncAttributes fa{};
+#define LS_PKA(B, GG)                                                                  \
+  if (f.bits == B && f.group == GG) {                                                  \
+    if (NT == 16) LS_CUDA(cudaFuncGetAttributes(&fa, pass_kernel<B, GG, 16>));         \
+    else if (NT == 32) LS_CUDA(cudaFuncGetAttributes(&fa, pass_kernel<B, GG, 32>));    \
+    else LS_CUDA(cudaFuncGetAttributes(&fa, pass_kernel<B, GG, 48>));                  \
+  }
+  LS_PKA(8, 32)
+  LS_PKA(8, 64)
+  LS_PKA(4, 16)
+  LS_PKA(4, 32)
+#undef LS_PKA
+  return (size_t)optin > fa.sharedSizeBytes ? (size_t)optin - fa.sharedSizeBytes : 0;
 }
 
 // CTAs of the token tile of T that are resident per SM at once (the cooperative launch needs the
