@@ -24,6 +24,11 @@
  *   ls_speculative_greedy        <- spec::speculative_greedy (src/spec.rs:57-152)
  *   ls_quantize_model            <- quant::quantize_model (src/quant.rs:158-251)
  *   ls_model_report              <- provider::ProviderReport (src/provider.rs:29-37) + source::IoStats (src/source.rs:13-21)
+ *
+ * The K/V cache (src/model.rs:67-68: [max_ctx x kv_dim] per layer, rolled back by a length,
+ * src/model.rs:137-140) is paged here: per layer a pool of pages of kv_page positions shared by the
+ * sequences of a model or batch, a page table per sequence, pages taken as a sequence grows and
+ * returned when it is truncated or reset.
  */
 #ifndef LAYERSTREAM_B200_H
 #define LAYERSTREAM_B200_H
@@ -61,6 +66,9 @@ typedef struct LsModelInfo {
   uint64_t embed_row_bytes;    /* bytes of one stored embedding row */
   uint64_t weight_bytes;       /* layers * layer_bytes + vocab * embed_row_bytes */
   int32_t persistent_pass;     /* 1: passes of 1..48 tokens run as one persistent kernel launch */
+  int32_t kv_page;             /* positions per page of the paged K/V cache (LS_KV_PAGE, default 64) */
+  uint64_t kv_pages_total;     /* pages in the model's pool */
+  uint64_t kv_pages_used;      /* pages its sequence holds now (ceil(pos / kv_page)) */
 } LsModelInfo;
 
 /* src/provider.rs:29-37, src/source.rs:13-21 */
@@ -236,6 +244,16 @@ int ls_bgemm_host(int bits, int group, const uint8_t *rows_raw, uint64_t rows, u
  * iters > 1 repeats the kernel and returns its mean time in *ms (may be NULL). */
 int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
                       const float *qkv, const uint16_t *k_cache, const uint16_t *v_cache, float *out, int iters, double *ms);
+
+/* The same attention through a paged K/V cache given by the caller: k_pool, v_pool are kv_heads x
+ * num_pages x page x hd f16 (page a power of two, 8..65536); table[i] is the pool page holding
+ * positions [i * page, (i + 1) * page) of the context, for every page of the pos0 + M positions. The
+ * block's rows are rotated, rounded to f16 and written into their pages, and both pools are copied
+ * back. No reference counterpart beyond src/model.rs:261-282: the page table is this build's cache
+ * layout. */
+int ls_attention_paged_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
+                            const float *qkv, uint16_t *k_pool, uint16_t *v_pool, uint64_t num_pages, uint64_t page,
+                            const int32_t *table, float *out, int iters, double *ms);
 
 /* The same GEMV on device buffers prepared once by ls_qweights_upload (for timing loops). */
 typedef struct LsQWeights LsQWeights;

@@ -30,7 +30,8 @@ class ModelInfo(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("hidden", "inter", "layers", "heads", "kv_heads", "head_dim", "vocab", "max_ctx")] + [
         (n, C.c_int32) for n in ("bits", "group", "embed_bits", "embed_group")
     ] + [("eps", C.c_float), ("rope_theta", C.c_float), ("layer_bytes", C.c_uint64), ("embed_row_bytes", C.c_uint64),
-         ("weight_bytes", C.c_uint64), ("persistent_pass", C.c_int32)]
+         ("weight_bytes", C.c_uint64), ("persistent_pass", C.c_int32), ("kv_page", C.c_int32),
+         ("kv_pages_total", C.c_uint64), ("kv_pages_used", C.c_uint64)]
 
 
 class Report(C.Structure):
@@ -109,6 +110,9 @@ _SIGS = {
     "ls_batch_profile": (C.c_int, [C.c_void_p, C.POINTER(BatchProfile)]),
     "ls_attention_host": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
+    "ls_attention_paged_host": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p,
+                                          C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p, C.c_int,
+                                          C.POINTER(C.c_double)]),
     "ls_qgemv_rows_noalloc": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64,
                                         C.c_void_p, C.c_void_p]),
     "ls_dequant_rows_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p]),
@@ -154,9 +158,7 @@ class Model:
         md = {"resident": MODE_RESIDENT, "stream": MODE_STREAM}[mode]
         _check(lib().ls_model_open(str(path).encode(), device, max_ctx, md, slots, C.byref(h)))
         self._h = h
-        info = ModelInfo()
-        _check(lib().ls_model_info(h, C.byref(info)))
-        self.info = info
+        info = self.info
         self.vocab = info.vocab
         self.max_ctx = max_ctx
         self.mode = mode
@@ -171,6 +173,13 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    @property
+    def info(self) -> ModelInfo:
+        """ls_model_info, read now (the K/V page counts change as the cache grows and shrinks)."""
+        info = ModelInfo()
+        _check(lib().ls_model_info(self._h, C.byref(info)))
+        return info
 
     @property
     def pos(self) -> int:
@@ -406,6 +415,24 @@ def attention(heads: int, kv_heads: int, hd: int, pos0: int, qkv: np.ndarray, k_
     ms = C.c_double()
     _check(lib().ls_attention_host(heads, kv_heads, hd, rope_theta, pos0, M, _p(q), _p(kc) if kc is not None else None,
                                    _p(vc) if vc is not None else None, _p(out), iters, C.byref(ms)))
+    return out, ms.value
+
+
+def attention_paged(heads: int, kv_heads: int, hd: int, pos0: int, qkv: np.ndarray, k_pool: np.ndarray, v_pool: np.ndarray,
+                    page: int, table, rope_theta: float = 1e6, iters: int = 1):
+    """The same attention through a paged K/V cache: k_pool, v_pool are kv_heads x num_pages x page x
+    hd f16 arrays, table[i] the pool page of positions [i * page, (i + 1) * page). The block's K/V rows
+    are written into their pages (the pools are updated in place). Returns (out, ms)."""
+    q = np.ascontiguousarray(qkv, np.float32)
+    M = q.shape[0]
+    if k_pool.dtype != np.float16 or v_pool.dtype != np.float16 or not k_pool.flags.c_contiguous or not v_pool.flags.c_contiguous:
+        raise ValueError("k_pool and v_pool must be C-contiguous float16 arrays")
+    num_pages = k_pool.shape[1]
+    t = np.ascontiguousarray(table, np.int32)
+    out = np.empty((M, heads * hd), np.float32)
+    ms = C.c_double()
+    _check(lib().ls_attention_paged_host(heads, kv_heads, hd, rope_theta, pos0, M, _p(q), _p(k_pool), _p(v_pool), num_pages, page,
+                                         _p(t), _p(out), iters, C.byref(ms)))
     return out, ms.value
 
 

@@ -35,7 +35,7 @@ namespace ls {
 
 constexpr int AT_THREADS = 256;  // two warps per tensor-memory lane quadrant
 constexpr int AT_CH = 128;       // positions per chunk: N of the score MMA, K of the value MMA
-constexpr int AT_MAX_SPLITS = 16;
+constexpr int AT_MAX_SPLITS = 64;
 // tensor-memory columns: scores [0, 128), P as f16 pairs [128, 192), output [192, 192 + hd)
 constexpr int AT_COL_P = 128, AT_COL_O = 192;
 __host__ __device__ constexpr int at_tmem_cols(int hd) { return AT_COL_O + hd <= 256 ? 256 : 512; }
@@ -125,8 +125,9 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
   const int nch = (total + AT_CH - 1) / AT_CH;
   const int c0 = (int)((long long)split * nch / nsplit), c1 = (int)((long long)(split + 1) * nch / nsplit);
   const float* qkv = a.qkv + (size_t)seq * M * a.qkv_stride;
-  uint16_t* kcache = a.k_cache + (size_t)seq * a.seq_stride + (size_t)g * a.max_ctx * HD;
-  uint16_t* vcache = a.v_cache + (size_t)seq * a.seq_stride + (size_t)g * a.max_ctx * HD;
+  uint16_t* kcache = a.k_cache;  // this layer's page pools, shared by the sequences
+  uint16_t* vcache = a.v_cache;
+  const int32_t* pg = a.pages + (size_t)seq * a.max_pages;
   // scores in the log2 domain: u = q . k * (log2(e) / sqrt(hd)), softmax weights 2^(u - max)
   const float c1s = 1.4426950408889634f / sqrtf((float)HD);
 
@@ -148,12 +149,11 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
     const int p0 = c * AT_CH;
     const int ncached = max(0, min(AT_CH, pos0 - p0));
     const uint32_t kb = tc::su32(sk + b * SM::kK), vb = tc::su32(sv + b * SM::kV);
-    const uint16_t* ks = kcache + (size_t)p0 * HD;
-    const uint16_t* vs = vcache + (size_t)p0 * HD;
     for (int i = tid; i < ncached * C8; i += AT_THREADS) {
       const int pl = i / C8, cc = i - pl * C8;
-      tc::cp_async16(kb + km_off(pl, cc * 8, SBO_HD), ks + i * 8);
-      tc::cp_async16(vb + (uint32_t)i * 16u, vs + i * 8);
+      const size_t row = kv_row(pg, a.page_shift, a.num_pages, g, p0 + pl) * HD + cc * 8;
+      tc::cp_async16(kb + km_off(pl, cc * 8, SBO_HD), kcache + row);
+      tc::cp_async16(vb + (uint32_t)i * 16u, vcache + row);
     }
     tc::cp_commit();
   };
@@ -178,8 +178,9 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
       *reinterpret_cast<uint4*>(kt + km_off(pl, cc * 8, SBO_HD)) = kh;
       *reinterpret_cast<uint4*>(vt + (pl * HD + cc * 8) * 2) = vh;
       if (rb == 0) {
-        *reinterpret_cast<uint4*>(kcache + (size_t)p * HD + cc * 8) = kh;
-        *reinterpret_cast<uint4*>(vcache + (size_t)p * HD + cc * 8) = vh;
+        const size_t row = kv_row(pg, a.page_shift, a.num_pages, g, p) * HD + cc * 8;
+        *reinterpret_cast<uint4*>(kcache + row) = kh;
+        *reinterpret_cast<uint4*>(vcache + row) = vh;
       }
     }
     const int pz = max(p0, total);
@@ -412,28 +413,31 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
   }
   if (!last_cta(a.tickets + unit * nrb + rb, (unsigned)nsplit)) return;
   // weight of every split for every row (shared memory is free: all MMAs have completed)
+  // (the weights of a row are computed by the two threads of its lane, each for half the splits:
+  // the max and the sum are combined through shared memory in a fixed order)
   float* s_w = reinterpret_cast<float*>(smem);  // [AT_MAX_SPLITS][128]
-  if (row_ok && hf == 0) {
-    float ms[AT_MAX_SPLITS], ls[AT_MAX_SPLITS];
-    float mm = -CUDART_INF_F;
-#pragma unroll
-    for (int s = 0; s < AT_MAX_SPLITS; s++) {
-      const float2 v = s < nsplit ? __ldcg(reinterpret_cast<const float2*>(pml) + (size_t)s * R + r0 + rl)
-                                  : make_float2(-CUDART_INF_F, 0.f);
-      ms[s] = v.x;
-      ls[s] = v.y;
-      mm = fmaxf(mm, v.x);
+  const float2* ml = reinterpret_cast<const float2*>(pml) + r0 + rl;
+  const int sh0 = hf * ((nsplit + 1) / 2), sh1 = hf ? nsplit : (nsplit + 1) / 2;
+  float mm = -CUDART_INF_F;
+  if (row_ok)
+    for (int s = sh0; s < sh1; s++) mm = fmaxf(mm, __ldcg(ml + (size_t)s * R).x);
+  s_red[hf][L] = mm;
+  __syncthreads();
+  mm = fmaxf(s_red[0][L], s_red[1][L]);
+  float Lsum = 0.f;
+  if (row_ok)
+    for (int s = sh0; s < sh1; s++) {
+      const float2 v = __ldcg(ml + (size_t)s * R);
+      const float w = (v.x == -CUDART_INF_F) ? 0.f : ex2(v.x - mm);
+      s_w[s * 128 + rl] = w;
+      Lsum += v.y * w;
     }
-    float Lsum = 0.f;
-#pragma unroll
-    for (int s = 0; s < AT_MAX_SPLITS; s++) {
-      ms[s] = (ms[s] == -CUDART_INF_F) ? 0.f : ex2(ms[s] - mm);
-      Lsum += ls[s] * ms[s];
-    }
-    const float inv = 1.0f / Lsum;
-#pragma unroll
-    for (int s = 0; s < AT_MAX_SPLITS; s++)
-      if (s < nsplit) s_w[s * 128 + rl] = ms[s] * inv;
+  __syncthreads();
+  s_red[hf][L] = Lsum;
+  __syncthreads();
+  if (row_ok) {
+    const float inv = 1.0f / (s_red[0][L] + s_red[1][L]);
+    for (int s = sh0; s < sh1; s++) s_w[s * 128 + rl] *= inv;
   }
   __syncthreads();
   constexpr int D4 = HD / 4;

@@ -203,11 +203,23 @@ void launch_embed_raw(const uint8_t* table, size_t row_bytes, int bits, int grou
 void launch_advance(Ctl* ctl, cudaStream_t s);
 void launch_argmax_finalize(const ArgPart* parts, int nparts, int M, Ctl* ctl, cudaStream_t s);
 
+// ---- paged K/V cache ----
+//
+// Per layer a pool of pages for K and one for V, [kv_heads][num_pages][page][hd] f16; a sequence's
+// position p lives in pool page table[p >> page_shift] at row p & (page - 1). Pages are handed out
+// as a sequence grows and returned when it is rolled back or reset, so sequences of a batch share
+// one pool. With the identity table the pool is the dense [kv_heads][max_ctx][hd] layout.
+__host__ __device__ inline size_t kv_row(const int32_t* table, int page_shift, int num_pages, int g, int p) {
+  return ((size_t)((size_t)g * num_pages + table[p >> page_shift]) << page_shift) + (size_t)(p & ((1 << page_shift) - 1));
+}
+
 struct AttnLaunch {
   const float* qkv = nullptr;  // [M][qkv_stride] f32: q | k | v (pre-RoPE, bias added)
   int qkv_stride = 0;
-  uint16_t* k_cache = nullptr;  // [kv_heads][max_ctx][hd] f16 bits
+  uint16_t* k_cache = nullptr;  // this layer's page pool [kv_heads][num_pages][page][hd] f16 bits
   uint16_t* v_cache = nullptr;
+  const int32_t* pages = nullptr;  // [nseq][max_pages] page table (sequence s at pages + s * max_pages)
+  int page_shift = 6, num_pages = 0, max_pages = 0;
   const float2* rope = nullptr;  // [max_ctx][hd/2] (cos, sin)
   const Ctl* ctl = nullptr;
   float* out = nullptr;  // [M][heads*hd]
@@ -215,11 +227,10 @@ struct AttnLaunch {
   unsigned* tickets = nullptr;
   int heads = 0, kv_heads = 0, hd = 0, max_ctx = 0, M = 0, split = 64, max_splits = 0;
   // batches: grid.z = nseq sequences of M rows each (rows s*M .. s*M+M-1 of qkv and out); sequence
-  // s has its cache at k_cache/v_cache + s * seq_stride, its position pos0[s], its partials and
-  // tickets after those of sequences < s. pos0 == nullptr: one sequence at ctl->pos0.
+  // s has its page table row s, its position pos0[s], its partials and tickets after those of
+  // sequences < s. pos0 == nullptr: one sequence at ctl->pos0.
   int nseq = 1;
   const int* pos0 = nullptr;
-  size_t seq_stride = 0;
   bool pdl = true;  // false: plain launch (positions written by the previous kernel are read early)
   int* err = nullptr;  // set to 1 when a bounded wait of the tensor-core kernel gives up
   int max_total = 0;   // largest pos0 + M over the sequences when the host knows it (0: max_ctx)
@@ -304,8 +315,11 @@ struct PassArgs {
   long long* qkv;   // [T][h + 2 kv] q|k|v sums (bias included), fixed point
   long long* gu;    // [T][2 I] gate/up sums in the interleaved row order, fixed point
   float* att_part;  // [heads][slots][T][hd + 2] slot states (m, l, acc)
-  uint16_t* kc;     // [L][kv_heads][max_ctx][hd] f16
+  uint16_t* kc;     // [L] page pools [kv_heads][num_pages][page][hd] f16 (layer stride kv_layer)
   uint16_t* vc;
+  const int32_t* pages;  // the sequence's page table
+  size_t kv_layer;
+  int page_shift, num_pages;
   const float2* rope;
   ArgPart* arg_parts;  // [gridDim][T]
   float* logits;       // optional [n_logits][vocab]

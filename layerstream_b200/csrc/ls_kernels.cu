@@ -407,8 +407,8 @@ __device__ __forceinline__ float f16_round(float v) { return __half2float(__floa
 
 // Cached K/V rows [p0, p0+64) below pos0 of kv head g into the f32 tiles (16-byte loads).
 template <int HD>
-__device__ __forceinline__ void att_load_cached(const AttnLaunch& a, const uint16_t* kcache, const uint16_t* vcache, int g,
-                                                int p0, int pos0, float* Ks, float* Vs) {
+__device__ __forceinline__ void att_load_cached(const AttnLaunch& a, const uint16_t* kcache, const uint16_t* vcache,
+                                                const int32_t* pg, int g, int p0, int pos0, float* Ks, float* Vs) {
   constexpr int HP = HD + 1, V8 = HD / 8;
   for (int i = threadIdx.x; i < ATT_TILE * V8; i += ATT_THREADS) {
     const int pl = i / V8, d8 = (i - pl * V8) * 8;
@@ -421,7 +421,7 @@ __device__ __forceinline__ void att_load_cached(const AttnLaunch& a, const uint1
       }
       continue;
     }
-    const size_t base = ((size_t)g * a.max_ctx + p) * HD + d8;
+    const size_t base = kv_row(pg, a.page_shift, a.num_pages, g, p) * HD + d8;
     const uint4 kr = __ldg(reinterpret_cast<const uint4*>(kcache + base));
     const uint4 vr = __ldg(reinterpret_cast<const uint4*>(vcache + base));
     const __half* kh = reinterpret_cast<const __half*>(&kr);
@@ -450,8 +450,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
   const int H = a.heads * HD, KV = a.kv_heads * HD;
   const float* qkv = a.qkv + (size_t)sq * M * a.qkv_stride;
   float* out = a.out + (size_t)sq * M * H;
-  uint16_t* kcache = a.k_cache + (size_t)sq * a.seq_stride;
-  uint16_t* vcache = a.v_cache + (size_t)sq * a.seq_stride;
+  uint16_t* kcache = a.k_cache;  // this layer's page pools, shared by the sequences
+  uint16_t* vcache = a.v_cache;
+  const int32_t* pg = a.pages + (size_t)sq * a.max_pages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* qs = sm;                       // [M][HD]
   float* Ks = qs + M * HD;              // [64][HP]
@@ -461,7 +462,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
 
   pdl_trigger();
   // the cached part of the first tile does not depend on the previous kernel
-  if (slot < ntiles) att_load_cached<HD>(a, kcache, vcache, g, slot * ATT_TILE, pos0, Ks, Vs);
+  if (slot < ntiles) att_load_cached<HD>(a, kcache, vcache, pg, g, slot * ATT_TILE, pos0, Ks, Vs);
   for (int i = threadIdx.x; i < M * (HD + 2); i += ATT_THREADS) st[i] = (i % (HD + 2) == 0) ? -CUDART_INF_F : 0.f;
   pdl_wait();
 
@@ -480,7 +481,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
     const int p0 = tile * ATT_TILE;
     if (!first) {
       __syncthreads();
-      att_load_cached<HD>(a, kcache, vcache, g, p0, pos0, Ks, Vs);
+      att_load_cached<HD>(a, kcache, vcache, pg, g, p0, pos0, Ks, Vs);
     }
     first = false;
     __syncthreads();
@@ -500,7 +501,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
       Vs[pl * HP + d] = v1;
       Vs[pl * HP + d + HALF] = v2;
       if (writer) {
-        const size_t base = ((size_t)g * a.max_ctx + p) * HD;
+        const size_t base = kv_row(pg, a.page_shift, a.num_pages, g, p) * HD;
         kcache[base + d] = __half_as_ushort(__float2half_rn(k1));
         kcache[base + d + HALF] = __half_as_ushort(__float2half_rn(k2));
         vcache[base + d] = __half_as_ushort(__float2half_rn(v1));
@@ -612,7 +613,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnLaunch
 template <int HD>
 static void launch_attention_t(const AttnLaunch& a, size_t smem, cudaStream_t s) {
   ensure_smem(attention_kernel<HD>, smem);
-  const dim3 grid(a.heads, a.max_splits, a.nseq);
+  const dim3 grid(a.heads, std::min(a.max_splits, ATT_MAX_SLOTS), a.nseq);
   if (a.pdl) {
     launch_pdl(attention_kernel<HD>, grid, dim3(ATT_THREADS), smem, s, a);
   } else {

@@ -39,6 +39,64 @@ double now_s() {
 
 size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
+// Page size of the K/V cache: LS_KV_PAGE positions (a power of two, 8 .. 65536), else 64.
+int kv_page_shift() {
+  int page = 64;
+  if (const char* e = getenv("LS_KV_PAGE")) page = atoi(e);
+  int sh = 0;
+  while ((1 << sh) < page && sh < 16) sh++;
+  if ((1 << sh) != page || sh < 3) LS_THROW(LS_ERR_ARG, "LS_KV_PAGE must be a power of two in 8..65536");
+  return sh;
+}
+
+// Pages of a paged K/V cache (the same page ids index every layer's pool): a LIFO free list, each
+// sequence's table of pool pages (a pinned host mirror and the device copy the kernels read), and
+// the number of logical pages each sequence holds. A sequence takes pages as it grows (ensure) and
+// returns those past its length when it is rolled back (shrink): a rollback is a length, and the
+// freed pages serve the next growth of any sequence. Table uploads are stream-ordered before the
+// pass that reads them; the host changes the mirror only between passes it has synchronized.
+struct PagePool {
+  int shift = 6, nseq = 0, max_pages = 0, num_pages = 0;
+  std::vector<int32_t> free_list;
+  std::vector<int> held;       // logical pages per sequence
+  int32_t* h_table = nullptr;  // [nseq][max_pages], pinned
+  int32_t* d_table = nullptr;
+  uint64_t* h2d = nullptr;     // bytes counter to charge uploads to
+
+  int page() const { return 1 << shift; }
+  void init(int seqs, size_t max_ctx, int32_t* host_table, int32_t* dev_table) {
+    nseq = seqs;
+    max_pages = (int)((max_ctx + page() - 1) >> shift);
+    num_pages = nseq * max_pages;
+    h_table = host_table;
+    d_table = dev_table;
+    held.assign(nseq, 0);
+    free_list.clear();
+    for (int p = num_pages - 1; p >= 0; p--) free_list.push_back(p);  // page 0 handed out first
+  }
+  // Sequence s holds the pages of positions [0, n).
+  void ensure(int s, size_t n, cudaStream_t st) {
+    const int need = (int)((n + page() - 1) >> shift);
+    if (need <= held[s]) return;
+    if (need > max_pages || (int)free_list.size() < need - held[s]) LS_THROW(LS_ERR_ARG, "the K/V page pool is exhausted");
+    const int first = held[s];
+    for (int i = first; i < need; i++) {
+      h_table[(size_t)s * max_pages + i] = free_list.back();
+      free_list.pop_back();
+    }
+    held[s] = need;
+    const size_t off = (size_t)s * max_pages + first, bytes = (size_t)(need - first) * 4;
+    LS_CUDA(cudaMemcpyAsync(d_table + off, h_table + off, bytes, cudaMemcpyHostToDevice, st));
+    if (h2d) *h2d += bytes;
+  }
+  // Sequence s keeps only the pages of positions [0, n).
+  void shrink(int s, size_t n) {
+    const int keep = (int)((n + page() - 1) >> shift);
+    while (held[s] > keep) free_list.push_back(h_table[(size_t)s * max_pages + --held[s]]);
+  }
+  int used() const { return num_pages - (int)free_list.size(); }
+};
+
 // RoPE (cos, sin) table [n_pos][hd/2] with the float steps of src/model.rs:62-65 and
 // src/kernels.rs:242-252: inv_freq in f64 then f32, angle = pos as f32 * inv_freq, libm cosf/sinf.
 std::vector<float2> rope_table(float theta, size_t hd, size_t n_pos) {
@@ -173,7 +231,9 @@ struct LsModel {
   size_t raw_slot_bytes = 0;
 
   // cache, tables and activations
-  uint16_t *kc = nullptr, *vc = nullptr;
+  uint16_t *kc = nullptr, *vc = nullptr;  // page pools of every layer, kv_layer elements apart
+  size_t kv_layer = 0;
+  PagePool pool;
   float2* rope = nullptr;
   float *x = nullptr, *qkv = nullptr, *attn = nullptr, *hbuf = nullptr, *logits = nullptr;
   ArgPart* arg_parts = nullptr;
@@ -414,10 +474,20 @@ struct LsModel {
       resident_weight_bytes = (size_t)slots * (raw_slot_bytes + per);
     }
 
-    // KV cache [L][kv_heads][max_ctx][hd] f16 and the RoPE table, computed here with the same float
-    // steps as src/model.rs:62-65 and src/kernels.rs:242-252 (so the angles match the CPU path)
-    kc = dalloc<uint16_t>(L * kv * max_ctx);
-    vc = dalloc<uint16_t>(L * kv * max_ctx);
+    // K/V cache: per layer a pool [kv_heads][pages][page][hd] f16 (src/model.rs:67-68 reserves the
+    // same capacity up front) with this sequence's page table; the RoPE table, computed here with the
+    // same float steps as src/model.rs:62-65 and src/kernels.rs:242-252 (so the angles match the CPU
+    // path)
+    {
+      const int sh = kv_page_shift();
+      const size_t pages = (max_ctx + ((size_t)1 << sh) - 1) >> sh;
+      kv_layer = kv * (pages << sh);
+      kc = dalloc<uint16_t>(L * kv_layer);
+      vc = dalloc<uint16_t>(L * kv_layer);
+      pool.shift = sh;
+      pool.init(1, max_ctx, halloc<int32_t>(pages), dalloc<int32_t>(pages));
+      pool.h2d = &h2d_bytes;
+    }
     const size_t half = cfg.head_dim / 2;
     const std::vector<float2> tab = rope_table(cfg.rope_theta, cfg.head_dim, max_ctx);
     rope = dalloc<float2>(max_ctx * half);
@@ -436,7 +506,9 @@ struct LsModel {
     partial_floats = (size_t)max_tiles * 32 * 16 * 32 * (kMaxT / 16 + 1);
     partial = dalloc<float>(partial_floats);
     arg_ticket = dalloc<unsigned>(1);
-    att_slots = (int)std::max<size_t>(1, std::min<size_t>(16, (max_ctx + 63) / 64));  // <= ATT_MAX_SLOTS
+    // context splits of the attention of one sequence: up to 64 (the tensor-core kernel's bound; the
+    // CUDA-core kernel takes at most 16), so that long contexts spread over the SMs
+    att_slots = (int)std::max<size_t>(1, std::min<size_t>(64, (max_ctx + 63) / 64));
     att_part_floats = cfg.heads * (size_t)att_slots * kMaxT * (cfg.head_dim + 2);
     att_part = dalloc<float>(att_part_floats);
     att_tickets = dalloc<unsigned>(cfg.heads);
@@ -554,6 +626,10 @@ struct LsModel {
     a.att_part = pk_att;
     a.kc = kc;
     a.vc = vc;
+    a.pages = pool.d_table;
+    a.kv_layer = kv_layer;
+    a.page_shift = pool.shift;
+    a.num_pages = pool.num_pages;
     a.rope = rope;
     a.arg_parts = pk_parts;
     a.logits = want_logits ? logits : nullptr;
@@ -799,8 +875,12 @@ struct LsModel {
     AttnLaunch a;
     a.qkv = qkv;
     a.qkv_stride = h + 2 * kv;
-    a.k_cache = kc + l * cfg.kv_dim() * max_ctx;
-    a.v_cache = vc + l * cfg.kv_dim() * max_ctx;
+    a.k_cache = kc + l * kv_layer;
+    a.v_cache = vc + l * kv_layer;
+    a.pages = pool.d_table;
+    a.page_shift = pool.shift;
+    a.num_pages = pool.num_pages;
+    a.max_pages = pool.max_pages;
     a.rope = rope;
     a.ctl = ctl;
     a.out = attn;
@@ -961,6 +1041,7 @@ struct LsModel {
   }
 
   void push_ctl(int T, int n_logits, int md, const uint32_t* ids) {
+    pool.ensure(0, pos + T, stream);  // pages for the pass's new rows
     ctl_host->pos0 = (int32_t)pos;
     ctl_host->M = T;
     ctl_host->n_logits = n_logits;
@@ -1026,6 +1107,7 @@ struct LsModel {
     run_pass((int)n, (int)n, false);
     fetch_result();
     pos += (size_t)ctl_host->m + 1;
+    pool.shrink(0, pos);  // the rejected rows' pages go back to the pool
     *m_out = (uint32_t)ctl_host->m;
     *next_out = ctl_host->next;
   }
@@ -1033,6 +1115,7 @@ struct LsModel {
   void truncate(uint64_t p) {
     if (p > pos) LS_THROW(LS_ERR_ARG, "cannot truncate to " + std::to_string(p) + ": only " + std::to_string(pos) + " tokens are cached");
     pos = p;
+    pool.shrink(0, pos);
   }
 };
 
@@ -1181,7 +1264,8 @@ struct LsBatch {
   float* ybuf = nullptr;                            // partial sums of row-parallel projections
   ArgPart *tp_best = nullptr, *tp_all = nullptr;    // per-row best of this rank / of all ranks
   const LayerW& layer(size_t l) const { return tp_world > 1 ? tp_layers[l] : m->layers[l]; }
-  size_t layer_stride = 0, seq_stride = 0;  // elements: one layer's cache, one sequence's cache
+  size_t kv_layer = 0;  // elements of one layer's page pool (K or V)
+  PagePool pool;        // pages shared by the batch's sequences
   cudaStream_t stream = nullptr;
   std::vector<void*> dev_allocs, host_allocs;
   uint16_t *kc = nullptr, *vc = nullptr;
@@ -1375,10 +1459,18 @@ struct LsBatch {
     dm = Dims{(int)c.heads, (int)c.kv_heads, (int)(c.heads * c.head_dim), (int)c.kv_dim(), (int)c.inter};
     if (tp_world > 1) make_shard(nccl_id);
     const size_t L = c.layers, kv = dm.kv_dim, h = c.hidden, I = dm.inter, QS = dm.q_dim + 2 * kv;
-    layer_stride = kv * max_ctx;
-    seq_stride = L * layer_stride;
-    kc = dalloc<uint16_t>(B * seq_stride);
-    vc = dalloc<uint16_t>(B * seq_stride);
+    // per layer one page pool for all sequences (as many pages as B full contexts need), handed
+    // to the sequences as they grow
+    {
+      const int sh = kv_page_shift();
+      const size_t per_seq = (max_ctx + ((size_t)1 << sh) - 1) >> sh;
+      kv_layer = kv * ((B * per_seq) << sh);
+      kc = dalloc<uint16_t>(L * kv_layer);
+      vc = dalloc<uint16_t>(L * kv_layer);
+      pool.shift = sh;
+      pool.init((int)B, max_ctx, halloc<int32_t>(B * per_seq), dalloc<int32_t>(B * per_seq));
+      pool.h2d = &h2d_bytes;
+    }
     const std::vector<float2> tab = rope_table(c.rope_theta, c.head_dim, max_ctx);
     rope = dalloc<float2>(tab.size());
     LS_CUDA(cudaMemcpyAsync(rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, stream));
@@ -1553,6 +1645,12 @@ struct LsBatch {
     prof_end(pi);
   }
 
+  // A sequence's length; the pages past it go back to the pool.
+  void set_pos(size_t sq, uint64_t p) {
+    pos[sq] = p;
+    pool.shrink((int)sq, p);
+  }
+
   void pass(size_t s0, size_t ns, int M, const uint32_t* tokens, int head_mode) {
     const Config& c = m->cfg;
     const int h = (int)c.hidden, kv = dm.kv_dim, I = dm.inter, QS = dm.q_dim + 2 * kv;
@@ -1570,6 +1668,7 @@ struct LsBatch {
     }
     for (size_t i = 0; i < T; i++)
       if (tokens[i] >= c.vocab) LS_THROW(LS_ERR_ARG, "token id " + std::to_string(tokens[i]) + " is outside the vocabulary");
+    for (size_t i = 0; i < ns; i++) pool.ensure((int)(s0 + i), pos[s0 + i] + M, stream);  // pages for the new rows
     std::memcpy(h_tok, tokens, T * 4);
     h2d_bytes += T * 4 + ns * 4;
     const bool streamed = m->mode != LS_MODE_RESIDENT;
@@ -1607,8 +1706,12 @@ struct LsBatch {
       AttnLaunch a;
       a.qkv = qkv;
       a.qkv_stride = QS;
-      a.k_cache = kc + s0 * seq_stride + l * layer_stride;
-      a.v_cache = vc + s0 * seq_stride + l * layer_stride;
+      a.k_cache = kc + l * kv_layer;
+      a.v_cache = vc + l * kv_layer;
+      a.pages = pool.d_table + s0 * pool.max_pages;
+      a.page_shift = pool.shift;
+      a.num_pages = pool.num_pages;
+      a.max_pages = pool.max_pages;
       a.rope = rope;
       a.out = attn;
       a.part = att_part;
@@ -1621,7 +1724,6 @@ struct LsBatch {
       a.max_splits = slots;
       a.nseq = (int)ns;
       a.pos0 = d_pos0;
-      a.seq_stride = seq_stride;
       a.pdl = use_bg;  // positions come from the pass's host upload, before every kernel
       a.err = d_err;
       a.max_total = (int)span;
@@ -1754,7 +1856,7 @@ struct LsBatch {
     passes++;
     if (*h_err == 1) LS_THROW(LS_ERR_DEVICE, "a tensor-core kernel gave up waiting on an mbarrier (bounded wait)");
     if (*h_err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
-    for (size_t i = 0; i < ns; i++) pos[s0 + i] += head_mode == 1 ? h_m[i] + 1 : (uint64_t)M;
+    for (size_t i = 0; i < ns; i++) set_pos(s0 + i, pos[s0 + i] + (head_mode == 1 ? h_m[i] + 1 : (uint64_t)M));
   }
 
   // src/model.rs:111-119 for one sequence: 128-token chunks; returns the greedy token after them.
@@ -1799,7 +1901,7 @@ struct LsBatch {
     if (plen == 0 || max_new == 0) LS_THROW(LS_ERR_ARG, "need a prompt and at least one token to generate");
     if (plen + max_new + k + 1 > max_ctx) LS_THROW(LS_ERR_ARG, "prompt + max_new + k exceeds the batch's context");
     std::memset(st, 0, sizeof *st);
-    std::fill(pos.begin(), pos.end(), 0);
+    for (size_t sq = 0; sq < B; sq++) set_pos(sq, 0);
     const double t0 = now_s();
     std::vector<std::vector<uint32_t>> outs(B), hist(B);
     std::vector<char> active(B, 1);
@@ -1835,7 +1937,7 @@ struct LsBatch {
       st->target_passes++;
       for (size_t sq = 0; sq < B; sq++) {
         if (!active[sq]) {
-          pos[sq] = frozen[sq];
+          set_pos(sq, frozen[sq]);
           continue;
         }
         const uint32_t mm = h_m[sq], next = h_next[sq];
@@ -2106,6 +2208,9 @@ int ls_model_info(const LsModel* m, LsModelInfo* o) {
     o->embed_row_bytes = c.embed_row_bytes();
     o->weight_bytes = c.layers * m->file.layout.total + c.vocab * c.embed_row_bytes();
     o->persistent_pass = m->pk_max_grid > 0 ? 1 : 0;
+    o->kv_page = m->pool.page();
+    o->kv_pages_total = (uint64_t)m->pool.num_pages;
+    o->kv_pages_used = (uint64_t)m->pool.used();
   });
 }
 
@@ -2160,6 +2265,7 @@ int ls_reset(LsModel* m) {
   return guard([&] {
     NEED(m);
     m->pos = 0;
+    m->pool.shrink(0, 0);
   });
 }
 
@@ -2324,7 +2430,7 @@ int ls_batch_truncate(LsBatch* b, uint64_t seq, uint64_t pos) {
     NEED(b);
     if (seq >= b->B) LS_THROW(LS_ERR_ARG, "sequence index out of range");
     if (pos > b->pos[seq]) LS_THROW(LS_ERR_ARG, "cannot truncate to a position beyond the cache");
-    b->pos[seq] = pos;
+    b->set_pos(seq, pos);
   });
 }
 
@@ -2393,96 +2499,147 @@ int ls_batch_profile(const LsBatch* b, LsBatchProfile* out) {
   });
 }
 
+namespace {
+
+// One layer's attention through the CUDA kernels on host buffers: the cached rows live in page
+// pools (k_pool, v_pool: kv_heads x num_pages x 2^page_shift x hd f16) addressed through `table`
+// (the pool page of each logical page of the context); the block's rows are written to the pools,
+// which are copied back when k_out / v_out are given.
+void attention_host_impl(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
+                         const float* qkv, const uint16_t* k_pool, const uint16_t* v_pool, int page_shift, uint64_t num_pages,
+                         const int32_t* table, float* out, int iters, double* ms, uint16_t* k_out, uint16_t* v_out) {
+  if (heads == 0 || kv_heads == 0 || heads % kv_heads || heads > 256) LS_THROW(LS_ERR_ARG, "heads must be a multiple of kv_heads");
+  if (hd != 16 && hd != 32 && hd != 64 && hd != 128) LS_THROW(LS_ERR_ARG, "head_dim must be 16, 32, 64 or 128");
+  if (M == 0 || M > 64) LS_THROW(LS_ERR_ARG, "the attention block takes 1..64 rows");
+  if (pos0 + M > (1u << 20)) LS_THROW(LS_ERR_ARG, "context beyond 2^20 positions");
+  const size_t ctx = pos0 + M, KV = kv_heads * hd, H = heads * hd, QS = H + 2 * KV, page = (size_t)1 << page_shift;
+  const size_t ctx_pages = (ctx + page - 1) / page;
+  for (size_t i = 0; i < ctx_pages; i++)
+    if (table[i] < 0 || (uint64_t)table[i] >= num_pages) LS_THROW(LS_ERR_ARG, "page table entry outside the pool");
+  const size_t pool_elems = kv_heads * num_pages * page * hd;
+  cudaStream_t st;
+  LS_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  std::vector<void*> owned;
+  auto dmalloc = [&](size_t bytes) {
+    void* p = nullptr;
+    LS_CUDA(cudaMalloc(&p, std::max<size_t>(bytes, 16)));
+    owned.push_back(p);
+    return p;
+  };
+  struct Cleanup {
+    std::vector<void*>& o;
+    cudaStream_t s;
+    ~Cleanup() {
+      cudaStreamSynchronize(s);
+      for (void* p : o) cudaFree(p);
+      cudaStreamDestroy(s);
+    }
+  } cleanup{owned, st};
+  auto* dq = static_cast<float*>(dmalloc(M * QS * 4));
+  auto* dk = static_cast<uint16_t*>(dmalloc(pool_elems * 2));
+  auto* dv = static_cast<uint16_t*>(dmalloc(pool_elems * 2));
+  auto* dtab = static_cast<int32_t*>(dmalloc(ctx_pages * 4));
+  auto* dout = static_cast<float*>(dmalloc(M * H * 4));
+  auto* drope = static_cast<float2*>(dmalloc(ctx * (hd / 2) * sizeof(float2)));
+  const int slots = (int)std::max<size_t>(1, std::min<size_t>(64, (ctx + 63) / 64));
+  auto* dpart = static_cast<float*>(dmalloc(heads * (size_t)slots * M * (hd + 2) * 4));
+  auto* dtick = static_cast<unsigned*>(dmalloc(heads * 4));
+  auto* dctl = static_cast<Ctl*>(dmalloc(sizeof(Ctl)));
+  LS_CUDA(cudaMemsetAsync(dtick, 0, heads * 4, st));
+  LS_CUDA(cudaMemcpyAsync(dq, qkv, M * QS * 4, cudaMemcpyHostToDevice, st));
+  LS_CUDA(cudaMemcpyAsync(dk, k_pool, pool_elems * 2, cudaMemcpyHostToDevice, st));
+  LS_CUDA(cudaMemcpyAsync(dv, v_pool, pool_elems * 2, cudaMemcpyHostToDevice, st));
+  LS_CUDA(cudaMemcpyAsync(dtab, table, ctx_pages * 4, cudaMemcpyHostToDevice, st));
+  const std::vector<float2> tab = rope_table(rope_theta, hd, ctx);
+  LS_CUDA(cudaMemcpyAsync(drope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, st));
+  launch_set_ctl(dctl, (int)pos0, (int)M, 0, 0, nullptr, st);
+  AttnLaunch a;
+  a.qkv = dq;
+  a.qkv_stride = (int)QS;
+  a.k_cache = dk;
+  a.v_cache = dv;
+  a.pages = dtab;
+  a.page_shift = page_shift;
+  a.num_pages = (int)num_pages;
+  a.max_pages = (int)ctx_pages;
+  a.rope = drope;
+  a.ctl = dctl;
+  a.out = dout;
+  a.part = dpart;
+  a.tickets = dtick;
+  a.heads = (int)heads;
+  a.kv_heads = (int)kv_heads;
+  a.hd = (int)hd;
+  a.max_ctx = (int)ctx;
+  a.M = (int)M;
+  a.max_splits = slots;
+  a.max_total = (int)(pos0 + M);
+  a.err = &dctl->err;
+  launch_attention(a, st);
+  if (k_out) LS_CUDA(cudaMemcpyAsync(k_out, dk, pool_elems * 2, cudaMemcpyDeviceToHost, st));
+  if (v_out) LS_CUDA(cudaMemcpyAsync(v_out, dv, pool_elems * 2, cudaMemcpyDeviceToHost, st));
+  if (iters > 1) {
+    cudaEvent_t e0, e1;
+    LS_CUDA(cudaEventCreate(&e0));
+    LS_CUDA(cudaEventCreate(&e1));
+    LS_CUDA(cudaEventRecord(e0, st));
+    for (int i = 0; i < iters; i++) launch_attention(a, st);
+    LS_CUDA(cudaEventRecord(e1, st));
+    LS_CUDA(cudaEventSynchronize(e1));
+    float t = 0;
+    LS_CUDA(cudaEventElapsedTime(&t, e0, e1));
+    if (ms) *ms = t / iters;
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+  } else if (ms) {
+    *ms = 0;
+  }
+  LS_CUDA(cudaMemcpyAsync(out, dout, M * H * 4, cudaMemcpyDeviceToHost, st));
+  int herr = 0;
+  LS_CUDA(cudaMemcpyAsync(&herr, &dctl->err, 4, cudaMemcpyDeviceToHost, st));
+  LS_CUDA(cudaStreamSynchronize(st));
+  if (herr == 1) LS_THROW(LS_ERR_DEVICE, "the tensor-core attention gave up waiting on an mbarrier (bounded wait)");
+}
+
+}  // namespace
+
 int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
                       const float* qkv, const uint16_t* k_cache, const uint16_t* v_cache, float* out, int iters, double* ms) {
   return guard([&] {
     NEED(qkv);
     NEED(out);
     if (pos0 && (!k_cache || !v_cache)) LS_THROW(LS_ERR_ARG, "k_cache and v_cache must not be NULL when pos0 > 0");
-    if (heads == 0 || kv_heads == 0 || heads % kv_heads || heads > 256) LS_THROW(LS_ERR_ARG, "heads must be a multiple of kv_heads");
-    if (hd != 16 && hd != 32 && hd != 64 && hd != 128) LS_THROW(LS_ERR_ARG, "head_dim must be 16, 32, 64 or 128");
-    if (M == 0 || M > 64) LS_THROW(LS_ERR_ARG, "the attention block takes 1..64 rows");
-    if (pos0 + M > (1u << 20)) LS_THROW(LS_ERR_ARG, "context beyond 2^20 positions");
-    const size_t ctx = pos0 + M, KV = kv_heads * hd, H = heads * hd, QS = H + 2 * KV;
-    int dev = 0;
-    LS_CUDA(cudaGetDevice(&dev));
-    cudaStream_t st;
-    LS_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
-    std::vector<void*> owned;
-    auto dmalloc = [&](size_t bytes) {
-      void* p = nullptr;
-      LS_CUDA(cudaMalloc(&p, std::max<size_t>(bytes, 16)));
-      owned.push_back(p);
-      return p;
-    };
-    struct Cleanup {
-      std::vector<void*>& o;
-      cudaStream_t s;
-      ~Cleanup() {
-        cudaStreamSynchronize(s);
-        for (void* p : o) cudaFree(p);
-        cudaStreamDestroy(s);
-      }
-    } cleanup{owned, st};
-    auto* dq = static_cast<float*>(dmalloc(M * QS * 4));
-    auto* dk = static_cast<uint16_t*>(dmalloc(kv_heads * ctx * hd * 2));
-    auto* dv = static_cast<uint16_t*>(dmalloc(kv_heads * ctx * hd * 2));
-    auto* dout = static_cast<float*>(dmalloc(M * H * 4));
-    auto* drope = static_cast<float2*>(dmalloc(ctx * (hd / 2) * sizeof(float2)));
-    const int slots = (int)std::max<size_t>(1, std::min<size_t>(16, (ctx + 63) / 64));
-    auto* dpart = static_cast<float*>(dmalloc(heads * (size_t)slots * M * (hd + 2) * 4));
-    auto* dtick = static_cast<unsigned*>(dmalloc(heads * 4));
-    auto* dctl = static_cast<Ctl*>(dmalloc(sizeof(Ctl)));
-    LS_CUDA(cudaMemsetAsync(dtick, 0, heads * 4, st));
-    LS_CUDA(cudaMemcpyAsync(dq, qkv, M * QS * 4, cudaMemcpyHostToDevice, st));
-    if (pos0) {
-      LS_CUDA(cudaMemcpy2DAsync(dk, ctx * hd * 2, k_cache, pos0 * hd * 2, pos0 * hd * 2, kv_heads, cudaMemcpyHostToDevice, st));
-      LS_CUDA(cudaMemcpy2DAsync(dv, ctx * hd * 2, v_cache, pos0 * hd * 2, pos0 * hd * 2, kv_heads, cudaMemcpyHostToDevice, st));
+    if (kv_heads == 0 || hd == 0) LS_THROW(LS_ERR_ARG, "heads must be a multiple of kv_heads");
+    // the dense cache as a pool of 64-position pages in order (the identity page table)
+    const int sh = 6;
+    const size_t page = (size_t)1 << sh, ctx = pos0 + M, np = (ctx + page - 1) / page;
+    std::vector<uint16_t> kp(kv_heads * np * page * hd, 0), vp(kp.size(), 0);
+    for (uint64_t g = 0; g < kv_heads && pos0; g++) {
+      std::memcpy(kp.data() + g * np * page * hd, k_cache + g * pos0 * hd, pos0 * hd * 2);
+      std::memcpy(vp.data() + g * np * page * hd, v_cache + g * pos0 * hd, pos0 * hd * 2);
     }
-    const std::vector<float2> tab = rope_table(rope_theta, hd, ctx);
-    LS_CUDA(cudaMemcpyAsync(drope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, st));
-    launch_set_ctl(dctl, (int)pos0, (int)M, 0, 0, nullptr, st);
-    AttnLaunch a;
-    a.qkv = dq;
-    a.qkv_stride = (int)QS;
-    a.k_cache = dk;
-    a.v_cache = dv;
-    a.rope = drope;
-    a.ctl = dctl;
-    a.out = dout;
-    a.part = dpart;
-    a.tickets = dtick;
-    a.heads = (int)heads;
-    a.kv_heads = (int)kv_heads;
-    a.hd = (int)hd;
-    a.max_ctx = (int)ctx;
-    a.M = (int)M;
-    a.max_splits = slots;
-    a.max_total = (int)(pos0 + M);
-    a.err = &dctl->err;
-    launch_attention(a, st);
-    if (iters > 1) {
-      cudaEvent_t e0, e1;
-      LS_CUDA(cudaEventCreate(&e0));
-      LS_CUDA(cudaEventCreate(&e1));
-      LS_CUDA(cudaEventRecord(e0, st));
-      for (int i = 0; i < iters; i++) launch_attention(a, st);
-      LS_CUDA(cudaEventRecord(e1, st));
-      LS_CUDA(cudaEventSynchronize(e1));
-      float t = 0;
-      LS_CUDA(cudaEventElapsedTime(&t, e0, e1));
-      if (ms) *ms = t / iters;
-      cudaEventDestroy(e0);
-      cudaEventDestroy(e1);
-    } else if (ms) {
-      *ms = 0;
-    }
-    LS_CUDA(cudaMemcpyAsync(out, dout, M * H * 4, cudaMemcpyDeviceToHost, st));
-    int herr = 0;
-    LS_CUDA(cudaMemcpyAsync(&herr, &dctl->err, 4, cudaMemcpyDeviceToHost, st));
-    LS_CUDA(cudaStreamSynchronize(st));
-    if (herr == 1) LS_THROW(LS_ERR_DEVICE, "the tensor-core attention gave up waiting on an mbarrier (bounded wait)");
-    (void)dev;
+    std::vector<int32_t> table(np);
+    for (size_t i = 0; i < np; i++) table[i] = (int32_t)i;
+    attention_host_impl(heads, kv_heads, hd, rope_theta, pos0, M, qkv, kp.data(), vp.data(), sh, np, table.data(), out, iters, ms,
+                        nullptr, nullptr);
+  });
+}
+
+int ls_attention_paged_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
+                            const float* qkv, uint16_t* k_pool, uint16_t* v_pool, uint64_t num_pages, uint64_t page,
+                            const int32_t* table, float* out, int iters, double* ms) {
+  return guard([&] {
+    NEED(qkv);
+    NEED(out);
+    NEED(k_pool);
+    NEED(v_pool);
+    NEED(table);
+    int sh = 0;
+    while (((uint64_t)1 << sh) < page && sh < 16) sh++;
+    if (((uint64_t)1 << sh) != page || sh < 3) LS_THROW(LS_ERR_ARG, "page must be a power of two in 8..65536");
+    if (num_pages == 0 || num_pages > (1u << 24)) LS_THROW(LS_ERR_ARG, "num_pages must be in 1..2^24");
+    attention_host_impl(heads, kv_heads, hd, rope_theta, pos0, M, qkv, k_pool, v_pool, sh, num_pages, table, out, iters, ms,
+                        k_pool, v_pool);
   });
 }
 

@@ -504,17 +504,17 @@ __device__ __forceinline__ int att_row_pos(int slot, int S, int ti, int cpt, int
 __device__ void attention_prefetch(const PassArgs& a, int pos0, int l, int hh, int slot, uint8_t* kvb) {
   const int HD = a.hd, HPK = pk_hpk(HD), AT = pk_at(HD), c8 = HD / 8;
   const int g = hh / (a.heads / a.kv_heads);
-  const size_t lstride = (size_t)a.kv_heads * a.max_ctx * HD;
-  const uint16_t* kc = a.kc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
-  const uint16_t* vc = a.vc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
+  const uint16_t* kc = a.kc + (size_t)l * a.kv_layer;
+  const uint16_t* vc = a.vc + (size_t)l * a.kv_layer;
   __half* Ks = reinterpret_cast<__half*>(kvb);
   __half* Vs = Ks + AT * HPK;
   for (int i = threadIdx.x; i < AT * c8; i += PK_THREADS) {
     const int r = i / c8, ch = i - r * c8;
     const int p = att_row_pos(slot, a.slots, 0, AT / PK_CHUNK, r);
     if (p < pos0) {
-      tc::cp_async16(tc::su32(Ks + r * HPK + ch * 8), kc + (size_t)p * HD + ch * 8);
-      tc::cp_async16(tc::su32(Vs + r * HPK + ch * 8), vc + (size_t)p * HD + ch * 8);
+      const size_t row = kv_row(a.pages, a.page_shift, a.num_pages, g, p) * HD + ch * 8;
+      tc::cp_async16(tc::su32(Ks + r * HPK + ch * 8), kc + row);
+      tc::cp_async16(tc::su32(Vs + r * HPK + ch * 8), vc + row);
     }
   }
   tc::cp_commit();
@@ -535,9 +535,8 @@ __device__ void attention_item(const PassArgs& a, int pos0, int l, int hh, int s
   const int nch = (total + PK_CHUNK - 1) / PK_CHUNK;
   const int H = a.heads * HD, KV = a.kv_heads * HD, QS = H + 2 * KV;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t lstride = (size_t)a.kv_heads * a.max_ctx * HD;
-  uint16_t* kc = a.kc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
-  uint16_t* vc = a.vc + (size_t)l * lstride + (size_t)g * a.max_ctx * HD;
+  uint16_t* kc = a.kc + (size_t)l * a.kv_layer;  // this layer's page pools
+  uint16_t* vc = a.vc + (size_t)l * a.kv_layer;
   float* qs = reinterpret_cast<float*>(sm);   // [T][HD]
   float* st = qs + T * HD;                    // [T][HP]
   float* es = st + T * HP;                    // [PK_NW][AT]
@@ -563,8 +562,9 @@ __device__ void attention_item(const PassArgs& a, int pos0, int l, int hh, int s
         const int r = i / c8, ch = i - r * c8;
         const int p = att_row_pos(slot, S, ti, CPT, r);
         if (p < pos0) {
-          tc::cp_async16(tc::su32(Ks + r * HPK + ch * 8), kc + (size_t)p * HD + ch * 8);
-          tc::cp_async16(tc::su32(Vs + r * HPK + ch * 8), vc + (size_t)p * HD + ch * 8);
+          const size_t row = kv_row(a.pages, a.page_shift, a.num_pages, g, p) * HD + ch * 8;
+          tc::cp_async16(tc::su32(Ks + r * HPK + ch * 8), kc + row);
+          tc::cp_async16(tc::su32(Vs + r * HPK + ch * 8), vc + row);
         }
       }
       tc::cp_commit();
@@ -585,10 +585,11 @@ __device__ void attention_item(const PassArgs& a, int pos0, int l, int hh, int s
         v1 = __float2half_rn(from_fix(ldcg_ll(vr + d)));
         v2 = __float2half_rn(from_fix(ldcg_ll(vr + d + HALF)));
         if (writer) {
-          kc[(size_t)p * HD + d] = __half_as_ushort(k1);
-          kc[(size_t)p * HD + d + HALF] = __half_as_ushort(k2);
-          vc[(size_t)p * HD + d] = __half_as_ushort(v1);
-          vc[(size_t)p * HD + d + HALF] = __half_as_ushort(v2);
+          const size_t row = kv_row(a.pages, a.page_shift, a.num_pages, g, p) * HD;
+          kc[row + d] = __half_as_ushort(k1);
+          kc[row + d + HALF] = __half_as_ushort(k2);
+          vc[row + d] = __half_as_ushort(v1);
+          vc[row + d + HALF] = __half_as_ushort(v2);
         }
       }
       Ks[r * HPK + d] = k1;
