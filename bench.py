@@ -412,9 +412,10 @@ def ref_batch(args, cfg):
 
 
 def microbench(args):
-    """Config 3: the verify-path kernels one at a time on one 0.5B layer's shapes. GEMV: every
-    launch timed alone with CUDA events after a 256 MB write that evicts L2 (so weights come from
-    HBM). Attention: KV length sweep, back-to-back launches (K/V up to 16.8 MB stay in L2)."""
+    """Config 3: the verify-path kernels one at a time on one 0.5B layer's shapes. Every launch is
+    timed alone with CUDA events after a 256 MB read that evicts L2 (weights and K/V come from
+    HBM). GEMV: each projection shape x M; attention (tensor-core kernel, context split over up to
+    64 CTAs per kv head): KV length sweep 512 .. 32768 with its roofline per length."""
     import torch
 
     import layerstream_b200 as ls
@@ -422,7 +423,9 @@ def microbench(args):
     rank, world, local, dist = setup_dist(args)
     torch.cuda.set_device(local)
     peak, peak_kind = peaks()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    # L2 eviction before every timed launch by READING 256 MB (a write would leave dirty lines whose
+    # write-back the timed kernel would pay for)
+    flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
     s = torch.cuda.current_stream()
     gemv = []
     reps = max(args.steps, 3)
@@ -436,7 +439,7 @@ def microbench(args):
                     w.gemv(x.data_ptr(), M, y.data_ptr(), s.cuda_stream)
                 ts = []
                 for _ in range(reps):
-                    flush.fill_(1)
+                    flush.sum()
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record(s)
                     w.gemv(x.data_ptr(), M, y.data_ptr(), s.cuda_stream)
@@ -458,7 +461,8 @@ def microbench(args):
         vc = rng.standard_normal((kvh, pos0, hd)).astype(np.float16)
         _, ms = ls.attention(heads, kvh, hd, pos0, qkv, kc, vc, iters=max(20, reps))
         b = L * kvh * hd * 2 * 2 + M * (heads + 2 * kvh) * hd * 4 + M * heads * hd * 4
-        att.append({"kv_len": L, "M": M, "us": ms * 1e3, "bytes": b, "gbs": b / (ms * 1e3) / 1e3})
+        att.append({"kv_len": L, "M": M, "us": ms * 1e3, "bytes": b, "gbs": b / (ms * 1e3) / 1e3,
+                    "frac": b / (ms * 1e3) / 1e3 / peak})
     head8 = [g for g in gemv if g["shape"] == "head" and g["fmt"] == "int8-g64" and g["M"] == 8][0]
     line = {"metric": "verify-kernel microbench: LM-head GEMV HBM GB/s (int8 g64, M = 8)", "value": head8["gbs"],
             "unit": "GB/s", "n_gpus": 1, "steps": reps, "warmup": args.warmup, "ms_per_step": head8["us"] / 1e3,
@@ -466,7 +470,7 @@ def microbench(args):
             "data": "synthetic",
             "config": {"workload": "config3: one 0.5B layer's GEMV shapes x M in 1..16, int8 g64 and int4 g32; GQA "
                                    "attention 14/2 heads, hd 64, M = 9, KV 512..32768",
-                       "l2": "GEMV: 256 MB write before every timed launch; attention: back-to-back, K/V in L2"},
+                       "l2": "256 MB read before every timed launch (GEMV and attention): L2 holds clean lines only"},
             "roofline": {"bound": "hbm", "kernel": "gemv_tc_kernel (LM head, int8 g64, M = 8)", "achieved": head8["gbs"],
                          "peak": peak, "unit": "GB/s", "frac": head8["gbs"] / peak, "peak_source": f"{peak_kind} hbm_gbs",
                          "traffic": None},

@@ -241,7 +241,8 @@ int ls_bgemm_host(int bits, int group, const uint8_t *rows_raw, uint64_t rows, u
  * cached rows (k_cache, v_cache: kv_heads x pos0 x hd, f16 bits, keys already rotated) and their
  * own rows; row i sees pos0 + i + 1 positions. The block's K/V rows are rotated (theta =
  * rope_theta) and rounded to f16 as the cache stores them. out: M x heads * hd f32. Host buffers;
- * iters > 1 repeats the kernel and returns its mean time in *ms (may be NULL). */
+ * iters > 1 repeats the kernel, each launch timed alone after a read that evicts L2 (so K/V come
+ * from HBM), and returns its mean time in *ms (may be NULL). */
 int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
                       const float *qkv, const uint16_t *k_cache, const uint16_t *v_cache, float *out, int iters, double *ms);
 

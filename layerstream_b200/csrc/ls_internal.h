@@ -201,6 +201,8 @@ void launch_embed(const QMat& e, const Ctl* ctl, float* x, int hidden, int M, cu
 void launch_embed_raw(const uint8_t* table, size_t row_bytes, int bits, int group, const Ctl* ctl, float* x, int hidden,
                       int vocab, int M, cudaStream_t s);
 void launch_advance(Ctl* ctl, cudaStream_t s);
+// Reads `bytes` (a multiple of 16, more than L2 holds) so that L2 holds only clean lines of it.
+void launch_l2_evict(const void* buf, size_t bytes, unsigned* sink, cudaStream_t s);
 void launch_argmax_finalize(const ArgPart* parts, int nparts, int M, Ctl* ctl, cudaStream_t s);
 
 // ---- paged K/V cache ----

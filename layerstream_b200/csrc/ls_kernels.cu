@@ -636,6 +636,25 @@ void launch_attention(const AttnLaunch& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------
+// L2 eviction for timing loops: reads a buffer larger than L2, so the lines it leaves are clean
+// (a write would leave dirty lines whose write-back the next, timed kernel would pay for).
+// ------------------------------------------------------------------------------------------------
+__global__ void l2_evict_kernel(const uint4* p, size_t n, unsigned* sink) {
+  unsigned acc = 0;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const uint4 v = __ldcg(p + i);
+    acc ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  acc = __reduce_xor_sync(0xffffffffu, acc);
+  if ((threadIdx.x & 31) == 0 && acc == 0x9e3779b9u) sink[blockIdx.x & 255] = acc;  // keeps the loads
+}
+
+void launch_l2_evict(const void* buf, size_t bytes, unsigned* sink, cudaStream_t s) {
+  l2_evict_kernel<<<1184, 512, 0, s>>>(static_cast<const uint4*>(buf), bytes / 16, sink);
+  LS_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------------------------------------
 // Embedding gather + dequantisation (bit-exact with src/kernels.rs:95-121)
 // ------------------------------------------------------------------------------------------------
 
