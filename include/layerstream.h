@@ -215,6 +215,20 @@ int ls_batch_verify(LsBatch *b, const uint32_t *blocks, uint64_t nseq, uint64_t 
 int ls_batch_spec(LsBatch *b, const uint32_t *prompts, uint64_t plen, uint64_t max_new, uint64_t k, const uint32_t *eos,
                   uint64_t neos, uint32_t *out_tokens, uint64_t *out_len, LsSpecStats *stats);
 int ls_batch_report(const LsBatch *b, uint64_t *passes, uint64_t *h2d_bytes, uint64_t *d2h_bytes);
+/* Test hook, no reference counterpart: the model's next persistent-pass launch (passes of 1..48
+ * tokens, resident mode) makes grid barrier `barrier` (1-based: 1 closes the embedding phase, then 5
+ * per layer and 1 after the LM head) wait for an arrival that never comes, with a short poll limit
+ * (about 5 ms): its bounded wait runs out, the kernel releases its tensor memory and returns, and the
+ * call fails with LS_ERR_DEVICE. Nothing faults on the GPU; the model stays usable. 0 clears it. */
+int ls_model_inject_stall(LsModel *m, int barrier);
+
+/* Test hook, no reference counterpart (the reference's failure tests inject I/O errors through a
+ * failing Source, tests/pipeline.rs:170-198): the batch's next pass reports error code 4 from the
+ * device as a failed kernel would, without any fault on the GPU. On a tensor-parallel batch the
+ * error word is reduced over the ranks, so injecting on one rank makes every rank's pass fail with
+ * LS_ERR_DEVICE; a batch whose pass failed releases its communicator with ncclCommAbort. code 0
+ * clears a pending injection. */
+int ls_batch_inject_error(LsBatch *b, int code);
 /* on: 0 off, 1 an event pair around every launch class of each pass; also clears the counters */
 int ls_batch_profile_enable(LsBatch *b, int on);
 int ls_batch_profile(const LsBatch *b, LsBatchProfile *out);
@@ -273,7 +287,9 @@ int ls_qgemv_device(const LsQWeights *w, const float *x_dev, uint64_t M, float *
  * cudaStream_t or NULL. The K-split partial sums go to a fixed 4 MiB array in the library's device
  * memory that every GPU loading the library holds until exit; requests beyond it (M > 16 or
  * M x rows > 262144) fail with LS_ERR_ARG. The first call on a device looks up that array's
- * address, so make it before any stream capture. All calls on a GPU share the array, and every
+ * address (once per device, kept for the life of the process), so make it before any stream
+ * capture, and do not use the entry point on a device after cudaDeviceReset (the address kept
+ * would belong to the context that was reset). All calls on a GPU share the array, and every
  * call overwrites what it reads: calls that overlap on the GPU (other streams, other threads)
  * race and must be serialized by the caller. */
 int ls_qgemv_rows_noalloc(int bits, int group, const uint8_t *rows_dev, uint64_t rows, uint64_t cols, const float *x_dev,

@@ -110,6 +110,8 @@ _SIGS = {
     "ls_batch_profile": (C.c_int, [C.c_void_p, C.POINTER(BatchProfile)]),
     "ls_attention_host": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
+    "ls_batch_inject_error": (C.c_int, [C.c_void_p, C.c_int]),
+    "ls_model_inject_stall": (C.c_int, [C.c_void_p, C.c_int]),
     "ls_attention_paged_host": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p,
                                           C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p, C.c_int,
                                           C.POINTER(C.c_double)]),
@@ -234,6 +236,11 @@ class Model:
                     "crit_ms": list(p.crit_ms[i])}
                 for i, c in enumerate(PROF_CLASSES)}
 
+    def inject_stall(self, barrier: int):
+        """Test hook: the next persistent pass waits at grid barrier `barrier` until its bounded
+        wait runs out (the call then fails with a device error; the model stays usable)."""
+        _check(lib().ls_model_inject_stall(self._h, barrier))
+
     def report(self) -> dict:
         r = Report()
         _check(lib().ls_model_report(self._h, C.byref(r)))
@@ -311,6 +318,10 @@ class Batch:
         st = SpecStats()
         _check(lib().ls_batch_spec(self._h, _p(p), plen, max_new, k, _p(e), len(eos), _p(out), _p(n), C.byref(st)))
         return [out[i, : int(n[i])].tolist() for i in range(B)], st.as_dict()
+
+    def inject_error(self, code: int = 4):
+        """Test hook: the next pass fails with a device error (no fault on the GPU)."""
+        _check(lib().ls_batch_inject_error(self._h, code))
 
     def report(self) -> dict:
         a, b, c = C.c_uint64(), C.c_uint64(), C.c_uint64()

@@ -55,7 +55,9 @@ __device__ __forceinline__ void deq_sync() { asm volatile("bar.sync 1, 128;" :::
 
 template <int BITS, int G>
 struct BgShape {
-  static constexpr int KB = tc_kb(BITS, G), NS = tc_ns(BITS, G), CPB = KB / (128 / BITS), ACOLS = KB / 2;
+  static constexpr int KB = tc_kb(BITS, G), NS = tc_ns(BITS, G), CPB = KB / (128 / BITS);
+  // one A buffer: a K block's f16 pairs (two per column), for int8 its exact hi then lo parts
+  static constexpr int HCOLS = KB / 2, ACOLS = HCOLS * tc_parts(BITS);
   static constexpr int ABUF = ACOLS <= 32 ? 4 : 2;  // A buffers: 128 columns of tensor memory
   // per K block: 128 rows of packed ints, their group scales, N tokens of f16 activations
   static constexpr uint32_t W_KB = 4u * CPB * 512u;
@@ -70,7 +72,7 @@ template <int BITS, int G>
 __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
     bgemm_kernel(const __grid_constant__ BgemmLaunch g, const __grid_constant__ BgemmPlan p, const __grid_constant__ QMaps maps) {
   using SH = BgShape<BITS, G>;
-  constexpr int KB = SH::KB, NS = SH::NS, CPB = SH::CPB, ACOLS = SH::ACOLS, ABUF = SH::ABUF;
+  constexpr int KB = SH::KB, NS = SH::NS, CPB = SH::CPB, ACOLS = SH::ACOLS, ABUF = SH::ABUF, HCOLS = SH::HCOLS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t full[BG_MAX_STAGES], empty[BG_MAX_STAGES], bar_a[4], bar_af[4], bar_d, bar_fin[BG_NISS];
   __shared__ uint32_t s_tmem;
@@ -183,9 +185,11 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
           tc::fence_after();
           const uint32_t xa = tc::su32(smem + (size_t)s * STAGE + W_ST + S_ST) + (uint32_t)j * X_KB;
 #pragma unroll
-          for (int jj = 0; jj < KB / 16; jj++)
-            tc::mma_f16_ts(dacc, tmem + b * ACOLS + jj * 8, tc::sdesc(xa + jj * 2u * N * 16u, (uint32_t)N * 16u, 128u), idesc,
-                           (!first || jj > 0) ? 1u : 0u);
+          for (int jj = 0; jj < KB / 16; jj++) {
+            const uint64_t bd = tc::sdesc(xa + jj * 2u * N * 16u, (uint32_t)N * 16u, 128u);
+            tc::mma_f16_ts(dacc, tmem + b * ACOLS + jj * 8, bd, idesc, (!first || jj > 0) ? 1u : 0u);
+            if constexpr (ACOLS > HCOLS) tc::mma_f16_ts(dacc, tmem + b * ACOLS + HCOLS + jj * 8, bd, idesc, 1u);
+          }
           first = false;
           tc::commit(&bar_a[b]);  // the A buffer is free once these MMAs have read it
           BG_STAMP(2, i);
@@ -216,7 +220,8 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
 #pragma unroll
       for (int q = 0; q < NS; q++)
         scur[q] = tc::h2_splat(bf16f(*reinterpret_cast<const uint16_t*>(st + W_ST + ((wq * KST + j) * NS + q) * 64 + lane * 2)));
-      tc_dequant_block<BITS, G>(wv, scur, a);
+      if constexpr (ACOLS > HCOLS) tc_dequant_block_i8<G>(wv, scur, a, a + HCOLS);
+      else tc_dequant_block<BITS, G>(wv, scur, a);
       if (wq == 0 && lane == 0) BG_STAMP(3, i);
       return true;
     };
@@ -475,7 +480,8 @@ void launch_bt_prep(const float* x, int x_stride, int M, int K, const uint16_t* 
 // ---- host side ----
 
 bool bgemm_supported(const QMat& w) {
-  const bool fmt = (w.bits == 8 && (w.group == 16 || w.group == 32 || w.group == 64 || w.group == 128)) ||
+  // (an int8 K block is 64 columns: its scales are whole groups only for groups of at most 64)
+  const bool fmt = (w.bits == 8 && (w.group == 16 || w.group == 32 || w.group == 64)) ||
                    (w.bits == 4 && (w.group == 16 || w.group == 32 || w.group == 64 || w.group == 128));
   return fmt && (w.cols % tc_kb(w.bits, w.group)) == 0 && w.rows_pad % 32 == 0;
 }
@@ -489,13 +495,19 @@ BgemmPlan bgemm_plan(const QMat& w, int M, int num_sms, bool argmax) {
   const int base = tiles128 * p.ngroups;
   p.ks = 1;
   if (!argmax && base < num_sms) p.ks = std::min({(num_sms + base - 1) / base, std::max(1, nblk / 4), 16});
-  const int acols = (KB / 2 <= 32 ? 4 : 2) * (KB / 2);
+  const int aw = KB / 2 * tc_parts(w.bits), acols = (aw <= 32 ? 4 : 2) * aw;
   p.tmem_cols = acols + BG_NISS * p.N <= 256 ? 256 : 512;
   // stages of kstage K blocks (~24 KB each, within the slice); two CTAs per SM when tensor memory
   // allows it: keep the ring near 96 KB, else up to ~200 KB
   const uint32_t per_kb = 4u * CPB * 512u + 4u * NS * 64u + (uint32_t)p.N * KB * 2u;
   const int min_slice = nblk / p.ks;
   p.kstage = (int)std::max<uint32_t>(1, std::min<uint32_t>({8u, 24u * 1024 / per_kb, (uint32_t)std::max(1, min_slice)}));
+  // K block i uses A buffer i % ABUF, and the two issuers take alternate stages of kstage blocks:
+  // blocks i and i + ABUF (consecutive uses of a buffer) must belong to the same issuer, which
+  // waits for the buffer's mbarrier phases in order (a parity wait two phases ahead would read
+  // the stale phase as complete). That holds when kstage divides ABUF / 2.
+  const int abuf = aw <= 32 ? 4 : 2;
+  while ((abuf / 2) % p.kstage) p.kstage--;
   const uint32_t st = per_kb * p.kstage;
   const uint32_t budget = p.tmem_cols == 256 ? 96u * 1024 : 200u * 1024;
   p.stages = (int)std::max<uint32_t>(2, std::min<uint32_t>(BG_MAX_STAGES, budget / st));

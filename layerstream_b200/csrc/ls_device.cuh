@@ -259,6 +259,44 @@ __host__ __device__ constexpr int tc_ns(int bits, int group) {
   return tc_kb(bits, group) >= group ? tc_kb(bits, group) / group : 1;
 }
 
+// The MMA operand parts of one dequantized weight: int4 weights (q - 8) * scale have at most 4 + 8
+// significant bits and are exact in f16 (one part); int8 weights q * scale have up to 7 + 8 and
+// enter the MMA as two f16 parts, hi = f16(q * scale) and lo = q * scale - hi (exact in f16 for
+// scales >= 2^-17: the remainder has at most 5 significant bits), whose products the tensor core
+// adds into the same f32 accumulator, so the weights it multiplies are the exact dequantized ones.
+__host__ __device__ constexpr int tc_parts(int bits) { return bits == 8 ? 2 : 1; }
+
+namespace tc {
+// hi = v * s rounded to f16, lo = v * s - hi in one fused multiply-add (exact, see tc_parts)
+__device__ __forceinline__ void h2_mul_split(uint32_t v, uint32_t sub, uint32_t scale, uint32_t& hi, uint32_t& lo) {
+  __half2 a = *reinterpret_cast<__half2*>(&v);
+  a = __hsub2(a, *reinterpret_cast<const __half2*>(&sub));  // the exact integer q
+  const __half2 sc = *reinterpret_cast<const __half2*>(&scale);
+  const __half2 h = __hmul2(a, sc);
+  const __half2 l = __hfma2(a, sc, __hneg2(h));
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+}  // namespace tc
+
+// int8 K block -> hi parts in a[0 .. KB/2) and lo parts in lo[0 .. KB/2) (f16 pairs in K order).
+template <int G>
+__device__ __forceinline__ void tc_dequant_block_i8(const uint4* wv, const uint32_t* scur, uint32_t* a, uint32_t* lo) {
+  constexpr int KB = 64, NS = tc_ns(8, G), CPB = KB / 16;
+#pragma unroll
+  for (int q = 0; q < CPB; q++) {
+    const uint32_t wd[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
+    const uint32_t s2 = scur[(NS > 1) ? (q * 16) / G : 0];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t p0 = (__byte_perm(wd[k], 0u, 0x4140u) ^ 0x00800080u) | 0x64006400u;
+      const uint32_t p1 = (__byte_perm(wd[k], 0u, 0x4342u) ^ 0x00800080u) | 0x64006400u;
+      tc::h2_mul_split(p0, 0x64806480u, s2, a[q * 8 + 2 * k], lo[q * 8 + 2 * k]);
+      tc::h2_mul_split(p1, 0x64806480u, s2, a[q * 8 + 2 * k + 1], lo[q * 8 + 2 * k + 1]);
+    }
+  }
+}
+
 // One 16-byte chunk per CPB of a row's packed K block (tc_kb(BITS, G) weights) -> f16 pairs in K
 // order, each weight (q - 8) * scale (int4, stored q = w + 8; group >= 32: low nibbles are K j,
 // high nibbles K j + G/2 of the group) or q * scale (int8). scur[s]: f16x2 splat of the block's

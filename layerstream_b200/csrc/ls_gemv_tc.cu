@@ -30,8 +30,10 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
   constexpr int NS = tc_ns(BITS, G);   // scales per row per block
   constexpr int WPC = 128 / BITS;      // weights per 16-byte chunk
   constexpr int CPB = KB / WPC;        // chunks per block
-  constexpr int ACOLS = KB / 2;        // TMEM columns of one A buffer (two f16 per column)
-  constexpr int TCOLS = (2 * ACOLS + NT <= 128) ? 128 : 256;
+  constexpr int PARTS = tc_parts(BITS);  // int8: exact hi and lo f16 parts of every weight
+  constexpr int HCOLS = KB / 2;          // TMEM columns of one part of a block (two f16 per column)
+  constexpr int ACOLS = HCOLS * PARTS;   // TMEM columns of one A buffer
+  constexpr int TCOLS = (2 * ACOLS + NT <= 128) ? 128 : (2 * ACOLS + NT <= 256) ? 256 : 512;
   constexpr int NW = TC_THREADS / 32;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ uint64_t bar_a[2], bar_full[2], bar_d;
@@ -194,8 +196,9 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
       for (int q = 0; q < CPB; q++) wv[q] = row_valid ? *reinterpret_cast<const uint4*>(rs + q * 16) : make_uint4(0, 0, 0, 0);
 
       // ---- dequantise one K block of this row into f16 pairs in K order ----
-      uint32_t a[ACOLS];
-      tc_dequant_block<BITS, G>(wv, scur, a);
+      uint32_t a[HCOLS], alo[PARTS == 2 ? HCOLS : 1];
+      if constexpr (PARTS == 2) tc_dequant_block_i8<G>(wv, scur, a, alo);
+      else tc_dequant_block<BITS, G>(wv, scur, a);
 #pragma unroll
       for (int q = 0; q < NS; q++) {
         sraw0[q] = sraw1[q];
@@ -212,7 +215,11 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
       tc::fence_after();
       __syncwarp();
 #pragma unroll
-      for (int q = 0; q < ACOLS / 16; q++) tc::st16(tmem + lane_base + b * ACOLS + q * 16, a + q * 16);
+      for (int q = 0; q < HCOLS / 16; q++) tc::st16(tmem + lane_base + b * ACOLS + q * 16, a + q * 16);
+      if constexpr (PARTS == 2) {
+#pragma unroll
+        for (int q = 0; q < HCOLS / 16; q++) tc::st16(tmem + lane_base + b * ACOLS + HCOLS + q * 16, alo + q * 16);
+      }
       tc::wait_st();
       tc::fence_before();
       // block written: one arrival per thread; only the MMA issuer waits for all 128
@@ -227,6 +234,7 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
             const uint32_t kpos = (uint32_t)(it * KB + j * 16);  // K offset inside the staged slice
             const uint64_t bd = tc::sdesc(xb_addr + (kpos / 8) * 128u, 128u, sbo);
             tc::mma_f16_ts(d_col, tmem + b * ACOLS + j * 8, bd, idesc, (it > 0 || j > 0) ? 1u : 0u);
+            if constexpr (PARTS == 2) tc::mma_f16_ts(d_col, tmem + b * ACOLS + HCOLS + j * 8, bd, idesc, 1u);
           }
           tc::commit(&bar_a[b]);
         }

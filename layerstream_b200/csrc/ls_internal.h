@@ -330,6 +330,8 @@ struct PassArgs {
                        // barriers, then [phases][4][gridDim] inside the phases from slot trace_sub on
   int trace_sub;
   int kv_off;  // byte offset of the attention K/V region from the B-operand region
+  int stall_barrier;    // test hook: this grid barrier (1-based) never completes, 0 = none
+  unsigned poll_limit;  // polls of a grid-barrier wait before the CTA gives up with error 3
   int stages;  // weight-stream ring depth
   int L, hidden, inter, heads, kv_heads, hd, vocab, max_ctx, T, n_logits, slots;
   int ks_qkv, ks_o, ks_gu, ks_down;
@@ -359,6 +361,7 @@ struct NcclApi {
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;  // for a communicator left in a failed state
   const char* (*error_string)(ncclResult_t) = nullptr;
 };
 const NcclApi& nccl_api();  // throws when libnccl.so.2 cannot be loaded

@@ -639,6 +639,12 @@ struct LsModel {
     a.trace_sub = (int)pk_trace_sub();
     a.kv_off = P.kv_off;
     a.stages = P.stages;
+    a.poll_limit = 1u << 21;  // polls of ~0.5 us: about a second
+    if (stall_barrier) {      // test hook: one barrier wait runs out after ~5 ms
+      a.stall_barrier = stall_barrier;
+      a.poll_limit = 1u << 13;
+      stall_barrier = 0;
+    }
     pk_T = T;
     pk_n_logits = n_logits;
     pk_traced = a.trace != nullptr;
@@ -669,6 +675,7 @@ struct LsModel {
     }
   }
   int pk_grid_last = 0;
+  int stall_barrier = 0;  // test hook (ls_model_inject_stall): the next pass kernel stalls at this barrier
   bool pk_pending = false;
   unsigned* pk_trace = nullptr;
   int pk_T = 0, pk_n_logits = 0;
@@ -1285,6 +1292,8 @@ struct LsBatch {
   std::map<int, cudaGraphExec_t> bgraphs;      // decode passes by block length
   uint32_t *h_tok = nullptr, *h_m = nullptr, *h_next = nullptr;
   int *h_pos0 = nullptr, *h_err = nullptr;
+  int inject_err = 0;      // test hook: the next pass reports this error code (a host-made fault)
+  bool tp_failed = false;  // a tensor-parallel pass reported an error
   std::vector<uint64_t> pos;
   uint64_t passes = 0, h2d_bytes = 0, d2h_bytes = 0;
 
@@ -1541,7 +1550,8 @@ struct LsBatch {
     cudaSetDevice(m->device);
     if (stream) cudaStreamSynchronize(stream);
     for (auto& kv : bgraphs) cudaGraphExecDestroy(kv.second);  // before the communicator its nodes use
-    if (comm) nccl_api().comm_destroy(comm);
+    // a failed tensor-parallel pass may leave collectives in flight on a peer: abort, do not wait
+    if (comm) (tp_failed ? nccl_api().comm_abort : nccl_api().comm_destroy)(comm);
     for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
     for (void* p : dev_allocs) cudaFree(p);
     for (void* p : host_allocs) cudaFreeHost(p);
@@ -1675,7 +1685,7 @@ struct LsBatch {
     // A decode pass of every sequence on resident weights replays a captured graph (one per block
     // length): positions and tokens come from the pinned buffers at replay time, the attention is
     // sized for the whole context.
-    const bool graphed = graphs_on && !streamed && !prof_on && use_bg && s0 == 0 && ns == B && head_mode == 1;
+    const bool graphed = graphs_on && !streamed && !prof_on && use_bg && s0 == 0 && ns == B && head_mode == 1 && !inject_err;
     auto enqueue = [&](bool for_graph) {
     LS_CUDA(cudaMemcpyAsync(d_tok, h_tok, T * 4, cudaMemcpyHostToDevice, stream));
     LS_CUDA(cudaMemcpyAsync(d_pos0, h_pos0, ns * 4, cudaMemcpyHostToDevice, stream));
@@ -1827,6 +1837,14 @@ struct LsBatch {
       LS_CUDA(cudaMemcpyAsync(h_next, d_next, nres * 4, cudaMemcpyDeviceToHost, stream));
     }
     prof_end(pp);
+    if (inject_err) {  // never captured: an injected pass runs eagerly
+      *h_err = inject_err;
+      LS_CUDA(cudaMemcpyAsync(d_err, h_err, 4, cudaMemcpyHostToDevice, stream));
+      LS_CUDA(cudaStreamSynchronize(stream));
+    }
+    // tensor parallel: every rank must see every rank's error, so that all of them stop on the same
+    // pass (a rank that went on would wait in its next collective for a peer that has stopped)
+    if (tp) nccl_check(nccl_api().all_reduce(d_err, d_err, 1, ncclInt32, ncclMax, comm, stream), "ncclAllReduce (error)");
     LS_CUDA(cudaMemcpyAsync(h_err, d_err, 4, cudaMemcpyDeviceToHost, stream));
     };
     if (graphed) {
@@ -1854,7 +1872,10 @@ struct LsBatch {
     LS_CUDA(cudaStreamSynchronize(stream));
     if (prof_on) prof_collect();
     passes++;
+    inject_err = 0;
+    if (*h_err) tp_failed = tp;
     if (*h_err == 1) LS_THROW(LS_ERR_DEVICE, "a tensor-core kernel gave up waiting on an mbarrier (bounded wait)");
+    if (*h_err == 4) LS_THROW(LS_ERR_DEVICE, "a pass reported an injected error (test hook)");
     if (*h_err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
     for (size_t i = 0; i < ns; i++) set_pos(s0 + i, pos[s0 + i] + (head_mode == 1 ? h_m[i] + 1 : (uint64_t)M));
   }
@@ -2488,6 +2509,23 @@ int ls_batch_profile_enable(LsBatch* b, int on) {
     b->prof_on = on != 0;
     b->prof = LsBatchProfile{};
     b->prof_rec.clear();
+  });
+}
+
+int ls_model_inject_stall(LsModel* m, int barrier) {
+  return guard([&] {
+    NEED(m);
+    if (barrier < 0 || barrier > 1 + 5 * (int)m->cfg.layers + 1) LS_THROW(LS_ERR_ARG, "no such grid barrier in a pass");
+    if (barrier && m->pk_max_grid == 0) LS_THROW(LS_ERR_ARG, "this model does not run the persistent pass kernel");
+    m->stall_barrier = barrier;
+  });
+}
+
+int ls_batch_inject_error(LsBatch* b, int code) {
+  return guard([&] {
+    NEED(b);
+    if (code != 0 && code != 4) LS_THROW(LS_ERR_ARG, "the injected error code must be 4 (or 0 to clear)");
+    b->inject_err = code;
   });
 }
 

@@ -30,6 +30,7 @@ const NcclApi& nccl_api() {
     api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
     api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+    api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
   });
   if (!failure.empty()) LS_THROW(-3, failure);

@@ -86,7 +86,9 @@ __global__ void noalloc_reduce_kernel(const float* __restrict__ part, int rows, 
 }
 
 // Device address of the scratch array on the current device, looked up once per device (the first
-// call on each device does it, with that device current).
+// call on each device does it, with that device current) and kept for the life of the process: a
+// cudaDeviceReset would leave the kept address pointing into the old context, so the entry point is
+// not for use on a device after a reset.
 static float* noalloc_scratch() {
   constexpr int kMaxDevices = 64;
   static std::mutex mu;

@@ -73,9 +73,11 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   return v;
 }
 
-// Grid-wide barrier over a counter zeroed before the launch. Bounded: returns false when any CTA
-// has recorded an error (including this one timing out).
-__device__ bool grid_barrier(unsigned* bar, unsigned target, int* err) {
+// Grid-wide barrier over a counter zeroed before the launch, taken by every thread of every CTA
+// (also after a failure, so that the CTA barriers inside always match). Bounded: after `limit`
+// polls the CTA records error 3; returns false when any CTA has recorded an error (including this
+// one timing out) or this CTA has aborted.
+__device__ bool grid_barrier(unsigned* bar, unsigned target, int* err, unsigned limit, const volatile int* local_abort) {
   __shared__ int s_ok;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -85,11 +87,11 @@ __device__ bool grid_barrier(unsigned* bar, unsigned target, int* err) {
     int ok = 1;
     for (uint32_t i = 0;; i++) {
       if (ld_acquire(bar) >= target) break;
-      if (*(volatile int*)err) {
+      if (*(volatile int*)err || *local_abort) {
         ok = 0;
         break;
       }
-      if (i > (1u << 21)) {
+      if (i > limit) {
         atomicExch(err, 3);
         ok = 0;
         break;
@@ -153,7 +155,8 @@ template <int BITS, int G, int NT, class Marks = NoMarks>
 struct TcGemv {
   using S = Stream<BITS, G>;
   Marks marks;
-  static constexpr int KB = S::KB, NS = S::NS, CPB = S::CPB, NB = S::NB, ACOLS = KB / 2;
+  // one K block: its f16 pairs (two per column), for int8 its exact hi then lo parts
+  static constexpr int KB = S::KB, NS = S::NS, CPB = S::CPB, NB = S::NB, HC = KB / 2, ACOLS = HC * tc_parts(BITS);
   // One A buffer holds a whole stream stage (NB K blocks side by side): one hand-off per stage.
   static constexpr int AC = NB * ACOLS, AB = (256 / (PK_NWG * AC)) < PK_ABUF ? 256 / (PK_NWG * AC) : PK_ABUF;
   static_assert(AB >= 2 && AB * PK_NWG * AC + 2 * PK_NWG * NT <= PK_TMEM_COLS, "tensor memory");
@@ -213,18 +216,11 @@ struct TcGemv {
         for (int q = 0; q < NS; q++)
           sc[q] = tc::h2_splat(bf16f(reinterpret_cast<const uint16_t*>(st + S::kData + (size_t)(warp8 * NS * NB + bi * NS + q) * 64)[lane]));
         uint32_t a[ACOLS];
+        if constexpr (BITS == 8) tc_dequant_block_i8<G>(wv, sc, a, a + HC);
 #pragma unroll
         for (int q = 0; q < CPB; q++) {
           const uint32_t wd[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
           if constexpr (BITS == 8) {
-            const uint32_t s2 = sc[(NS > 1) ? (q * 16) / G : 0];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-              const uint32_t p0 = (__byte_perm(wd[k], 0u, 0x4140u) ^ 0x00800080u) | 0x64006400u;
-              const uint32_t p1 = (__byte_perm(wd[k], 0u, 0x4342u) ^ 0x00800080u) | 0x64006400u;
-              a[q * 8 + 2 * k] = tc::h2_sub_mul(p0, sub8, s2);
-              a[q * 8 + 2 * k + 1] = tc::h2_sub_mul(p1, sub8, s2);
-            }
           } else if constexpr (G == 16) {
 #pragma unroll
             for (int k = 0; k < 4; k++) {
@@ -323,9 +319,11 @@ struct TcGemv {
         for (int bi = 0; bi < nb; bi++) {
           const uint64_t bdk = bd0 + (uint64_t)((kbs + bi - kb0) * KB);  // K column kpos sits kpos / 8 * 128 bytes in
 #pragma unroll
-          for (int j = 0; j < KB / 16; j++)
+          for (int j = 0; j < KB / 16; j++) {
             tc::mma_f16_ts(dcol, acol + bi * ACOLS + j * 8, bdk + (uint64_t)(j * 16), idesc,
                            (kbs + bi > kb0 || j > 0) ? 1u : 0u);
+            if constexpr (BITS == 8) tc::mma_f16_ts(dcol, acol + bi * ACOLS + HC + j * 8, bdk + (uint64_t)(j * 16), idesc, 1u);
+          }
         }
         tc::commit(&bar_a[g * AB + b]);
         marks.mark(5, blk - 1);
@@ -861,7 +859,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
       __syncthreads();
       stamp(2 * nbar - 1);
     }
-    if (ok && !grid_barrier(a.bar, nbar * gridDim.x, err)) ok = false;
+    // a test hook (stall_barrier) makes one barrier wait for an arrival that never comes, so that
+    // its bounded wait runs out
+    const unsigned target = nbar * gridDim.x + (nbar == (unsigned)a.stall_barrier ? 1u : 0u);
+    if (!grid_barrier(a.bar, target, err, a.poll_limit, &s_abort)) ok = false;
     if (s_abort) ok = false;
     stamp(2 * nbar);
     return ok;

@@ -130,3 +130,23 @@ def test_gpu_quantizer_on_grid_weights_is_exact():
         O.quantize_model(d, a, (8, 32), (4, 16), clip=True)
         ls.quantize_model(d, b, (8, 32), (4, 16), clip=True)
         assert open(a, "rb").read() == open(b, "rb").read()
+
+
+@pytest.mark.parametrize("bits,group", [(8, 64), (8, 32), (8, 16), (8, 128), (4, 32), (4, 16)])
+@pytest.mark.parametrize("M", [1, 9, 40])
+def test_dequantized_weights_enter_the_tensor_cores_exactly(bits, group, M):
+    # With activations exactly representable in f16 the only rounding left in the tensor-core paths
+    # is the f32 accumulation: int4 weights (q - 8) * s are exact f16 values and int8 weights
+    # q * s enter as exact hi + lo f16 parts, so both GEMMs agree with kernels::matmul
+    # (src/kernels.rs:53-92) to ~1e-6 relative. (An int8 weight rounded to f16 would be off by up
+    # to 2^-11 of itself: about 1e-3 here.)
+    rows, cols = 300, 896
+    raw = rand_rows(rows, cols, bits, group, 7 + M)
+    x = np.random.default_rng(M).standard_normal((M, cols)).astype(np.float16).astype(np.float32)
+    want = O.matmul(bits, group, raw, rows, cols, x)
+    scale = np.sqrt(np.mean(want.astype(np.float64) ** 2))
+    y, _ = ls.qgemv(bits, group, raw, rows, cols, x)
+    assert np.max(np.abs(y - want)) <= 2e-5 * scale, float(np.max(np.abs(y - want)) / scale)
+    if not (bits == 8 and group > 64):  # the batched GEMM takes int8 groups of up to 64
+        yb, _ = ls.bgemm(bits, group, raw, rows, cols, x)
+        assert np.max(np.abs(yb - want)) <= 2e-5 * scale, float(np.max(np.abs(yb - want)) / scale)

@@ -91,3 +91,78 @@ def test_two_rank_tensor_parallel_batch_matches_the_cpu_path():
             if mg <= TOL:
                 break
             assert g[i] == t, (pr, i)
+
+
+def _rank_fail(rank, world, path, uid_q, out_q, inject_rank):
+    # failure-path test: NVLS off (a rank that stops must not leave multicast objects behind)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+
+    import layerstream_b200 as ls
+
+    torch.cuda.set_device(rank)
+    if rank == 0:
+        uid = ls.tp_unique_id()
+        for _ in range(world - 1):
+            uid_q.put(uid)
+    else:
+        uid = uid_q.get(timeout=120)
+    try:
+        m = ls.Model(path, device=rank, max_ctx=64)
+        b = ls.Batch(m, 2, max_ctx=64, max_block=5, tp=(rank, world, uid))
+        firsts = [b.prefill(i, [(7 * i + j) % 1000 for j in range(9)]) for i in range(2)]
+        blocks = np.array([[f, 1, 2, 3, 4] for f in firsts], np.uint32)
+        want = b.verify(blocks)
+        for i in range(2):
+            b.truncate(i, 9)
+        if rank == inject_rank:
+            b.inject_error()
+        codes = []
+        for _ in range(2):  # the injected pass, then one more: the ranks stayed in step
+            try:
+                codes.append(("ok", b.verify(blocks)))
+            except ls.LayerstreamError as e:
+                codes.append((e.code, None))
+        b.close()  # the failed communicator is aborted, not drained
+        m.close()
+        out_q.put((rank, (want, codes), None))
+    except Exception as e:
+        out_q.put((rank, None, repr(e)))
+
+
+def test_an_error_on_one_rank_stops_every_rank_on_the_same_pass():
+    # ADVICE: one rank's device error must not leave its peer waiting in the next collective
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    from layerstream_b200 import synth
+
+    synth.SHAPES["tp-fail"] = dict(hidden_size=512, num_attention_heads=8, num_key_value_heads=2,
+                                   intermediate_size=256, num_hidden_layers=2, vocab_size=1000, rope_theta=1e6,
+                                   max_position_embeddings=4096)
+    d = F.TempDir("gpu-tp-fail").path
+    synth.write_random_model(d, "tp-fail", 6)
+    path = os.path.join(d, "tp.lsq")
+    O.quantize_model(d, path, (4, 32), (4, 32), clip=True)
+    ctx = mp.get_context("spawn")
+    uid_q, out_q = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank_fail, args=(r, WORLD, path, uid_q, out_q, 1)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(WORLD):
+            r, got, err = out_q.get(timeout=300)
+            res[r] = (got, err)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(WORLD):
+        assert res[r][1] is None, res[r][1]
+        want, codes = res[r][0]
+        assert codes[0] == (-4, None), (r, codes)  # LS_ERR_DEVICE on both ranks, same pass
+        assert codes[1] == ("ok", want), (r, codes)
