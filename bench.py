@@ -72,6 +72,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--drafter", choices=["lookup", "model"], default=None)
+    ap.add_argument("--target", choices=["quantized", "bf16"], default="quantized",
+                    help="configs 1/2: the target's weights, quantized as the config says or the unquantized bf16 "
+                         "model (the reference's matmul_bf16 path)")
     ap.add_argument("--root", default=os.environ.get("LS_BENCH_ROOT", "/tmp/ls_b200_bench"))
     ap.add_argument("--tp", action="store_true",
                     help="config 5 (b): the resident model split tensor-parallel over the launched ranks (NCCL), "
@@ -285,7 +288,7 @@ def cpu_files(args, cfg, rank, dist):
             os.replace(tmp, p)
         return p
 
-    t = lsq(cfg["body"], cfg["embed"])
+    t = d if cfg.get("bf16_target") else lsq(cfg["body"], cfg["embed"])
     dr = lsq(cfg["draft"], cfg["draft"]) if cfg["drafter"] == "model" else None
     return t, dr
 
@@ -300,7 +303,7 @@ def cpu_sample(args, cfg, target_path, draft_path, steps, warmup, keep=None):
     plen, k = cfg["prompt"], cfg["k"]
     n_tok = args.cpu_sample_tokens or (2 * (k + 1) + 1)
     max_ctx = plen + cfg["max_new"] + k + 16
-    T = O.Model(target_path, quantized=True, threads=threads, max_ctx=max_ctx)
+    T = O.Model(target_path, quantized=not os.path.isdir(target_path), threads=threads, max_ctx=max_ctx)
     D = O.Model(draft_path, quantized=True, threads=threads, max_ctx=max_ctx) if draft_path else None
     prompt = prompt_for(cfg, T.vocab, 0)
     first = O.forward_argmax(T, prompt)
@@ -325,6 +328,8 @@ def cpu_sample(args, cfg, target_path, draft_path, steps, warmup, keep=None):
 def file_digest(path):
     import hashlib
 
+    if os.path.isdir(path):  # an unquantized safetensors model directory
+        path = os.path.join(path, "model.safetensors")
     h = hashlib.sha256()
     with open(path, "rb") as f:
         for b in iter(lambda: f.read(1 << 24), b""):
@@ -334,6 +339,9 @@ def file_digest(path):
 
 def dtype_note(bits):
     """The arithmetic the verify pass computes in."""
+    if bits == 16:
+        return ("bf16 weights converted exactly to f16 MMA operands (|w| >= 2^-17); activations rounded to f16 MMA "
+                "operands; f32 accumulation; f16 KV cache")
     w = (f"int{bits} weights dequantized exactly to f16 ((q - 8) * scale)" if bits == 4 else
          "int8 weights split exactly into two f16 MMA operands (hi + lo = q * scale)")
     return f"u{bits}/bf16-scale weights; {w}; activations rounded to f16 MMA operands; f32 accumulation; f16 KV cache"
@@ -674,15 +682,20 @@ def main():
         return
     if args.drafter:
         cfg["drafter"] = args.drafter
+    if args.target == "bf16":
+        cfg["bf16_target"] = True
+        cfg["body"] = cfg["embed"] = (16, 0)
     if args.ncu_case:
         ncu_case(args, cfg)
         return
     rank, world, local, dist = setup_dist(args)
-    workload = (f"config{args.config}: {cfg['shape']} Qwen2 random-init int{cfg['body'][0]} g{cfg['body'][1]}, "
+    wname = "bf16 (unquantized)" if cfg.get("bf16_target") else f"int{cfg['body'][0]} g{cfg['body'][1]}"
+    workload = (f"config{args.config}: {cfg['shape']} Qwen2 random-init {wname}, "
                 f"{cfg['prompt']}-token prompt, {cfg['max_new']} new tokens, k={cfg['k']}, batch 1 per GPU, "
                 f"{cfg['drafter']} drafter")
     base_cfg = {"workload": workload, "config": args.config, "model": f"qwen2-{cfg['shape']}-arch random-init",
-                "weights": f"int{cfg['body'][0]}-g{cfg['body'][1]}", "embed": f"int{cfg['embed'][0]}-g{cfg['embed'][1]}",
+                "weights": "bf16" if cfg.get("bf16_target") else f"int{cfg['body'][0]}-g{cfg['body'][1]}",
+                "embed": "bf16" if cfg.get("bf16_target") else f"int{cfg['embed'][0]}-g{cfg['embed'][1]}",
                 "prompt_tokens": cfg["prompt"], "max_new": cfg["max_new"], "k": cfg["k"], "drafter": cfg["drafter"],
                 "global_batch": world, "parallelism": f"dp{world} (independent sequences, no collective)",
                 "l2": "inputs larger than L2 (weights streamed from HBM every pass)"}
@@ -710,12 +723,14 @@ def main():
     torch.cuda.set_device(local)
     os.makedirs(args.root, exist_ok=True)
     if rank == 0:
-        t_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local)
+        t_path = (synth.ensure_model(args.root, cfg["shape"], 0) if cfg.get("bf16_target") else
+                  synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local))
         d_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["draft"], cfg["draft"], clip=True,
                                   device=local) if cfg["drafter"] == "model" else None
     barrier(dist)
     if rank != 0:
-        t_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local)
+        t_path = (synth.ensure_model(args.root, cfg["shape"], 0) if cfg.get("bf16_target") else
+                  synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True, device=local))
         d_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["draft"], cfg["draft"], clip=True,
                                   device=local) if cfg["drafter"] == "model" else None
 

@@ -254,9 +254,10 @@ __device__ __forceinline__ uint32_t h2_splat(float s) {
 
 // K elements per A block: one group for int4 groups of 128, else 64.
 __host__ __device__ constexpr int tc_kb(int bits, int group) { return (bits == 4 && group > 64) ? group : 64; }
+// (bf16 weights, bits 16, have no group scales: one unused slot keeps the arrays non-empty)
 // Group scales one row needs per A block.
 __host__ __device__ constexpr int tc_ns(int bits, int group) {
-  return tc_kb(bits, group) >= group ? tc_kb(bits, group) / group : 1;
+  return bits == 16 ? 1 : tc_kb(bits, group) >= group ? tc_kb(bits, group) / group : 1;
 }
 
 // The MMA operand parts of one dequantized weight: int4 weights (q - 8) * scale have at most 4 + 8
@@ -303,6 +304,20 @@ __device__ __forceinline__ void tc_dequant_block_i8(const uint4* wv, const uint3
 // s-th group scale. Exact in f16 products of the int and the bf16 scale rounded to f16.
 template <int BITS, int G>
 __device__ __forceinline__ void tc_dequant_block(const uint4* wv, const uint32_t* scur, uint32_t* a) {
+  if constexpr (BITS == 16) {
+    // bf16 weights: 8 per chunk, converted to f16 pairs in K order. The conversion is exact for
+    // |w| >= 2^-17 (below that, f16 keeps multiples of 2^-24); no scales.
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const uint32_t wd[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const __half2 h = __floats2half2_rn(__uint_as_float(wd[k] << 16), __uint_as_float(wd[k] & 0xFFFF0000u));
+        a[q * 4 + k] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
+    return;
+  }
   constexpr int KB = tc_kb(BITS, G);
   constexpr int NS = tc_ns(BITS, G);
   constexpr int CPB = KB / (128 / BITS);

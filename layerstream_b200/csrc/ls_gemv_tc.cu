@@ -166,8 +166,12 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
     auto load_scales = [&](int kb, uint16_t (&sc)[NS]) {
 #pragma unroll
       for (int s = 0; s < NS; s++) {
-        const int gi = (kb * KB) / G + s;
-        sc[s] = (row_valid && kb < kb1) ? sb[(size_t)gi * 32] : (uint16_t)0;
+        if constexpr (BITS == 16) {
+          sc[s] = 0;  // bf16 weights carry no scales
+        } else {
+          const int gi = (kb * KB) / G + s;
+          sc[s] = (row_valid && kb < kb1) ? sb[(size_t)gi * 32] : (uint16_t)0;
+        }
       }
     };
     uint16_t sraw0[NS], sraw1[NS], sraw2[NS];
@@ -375,6 +379,7 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
 static int tc_nt(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64; }
 
 bool gemv_tc_supported(const QMat& w) {
+  if (w.bits == 16) return (w.cols % 64) == 0;  // bf16 weights, converted to f16 operands
   if (w.bits == 8) return w.group >= 16 && w.group <= 128 && (w.cols % 64) == 0;
   return (w.group == 16 || w.group == 32 || w.group == 64 || w.group == 128) && (w.cols % tc_kb(4, w.group)) == 0;
 }
@@ -442,6 +447,7 @@ void launch_gemv_tc(const GemvLaunch& g, cudaStream_t s) {
   if (!gemv_tc_supported(g.w)) LS_THROW(-1, "format not supported by the tensor-core GEMV");
   if (g.ksplit < gemv_tc_min_ksplit(g.w, g.M, g.max_nt)) LS_THROW(-1, "tensor-core GEMV split too small for shared memory");
   if (g.ksplit > 1 && (!g.partial || !g.tickets)) LS_THROW(-1, "a split tensor-core GEMV needs partial-sum scratch");
+  if (g.w.bits == 16) return launch_tc_g<16, 16>(g, s);  // (the group argument is unused for bf16)
   if (g.w.bits == 8) {
     switch (g.w.group) {
       case 16: return launch_tc_g<8, 16>(g, s);

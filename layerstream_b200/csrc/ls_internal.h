@@ -103,9 +103,9 @@ struct QMat {
   const uint16_t* scales = nullptr; // tiled scale plane (bf16 bits)
   int rows = 0, rows_pad = 0, cols = 0, bits = 8, group = 64;
   __host__ __device__ size_t data_bytes() const { return (size_t)rows_pad * cols * bits / 8; }
-  __host__ __device__ size_t scale_bytes() const { return (size_t)rows_pad * (cols / group) * 2; }
+  __host__ __device__ size_t scale_bytes() const { return (size_t)rows_pad * groups() * 2; }
   __host__ __device__ int chunks() const { return cols * bits / 128; }
-  __host__ __device__ int groups() const { return cols / group; }
+  __host__ __device__ int groups() const { return bits == 16 ? 0 : cols / group; }  // bf16: no scales
 };
 
 inline int pad32(int r) { return (r + 31) / 32 * 32; }

@@ -663,6 +663,11 @@ __device__ __forceinline__ void embed_row(const QMat& e, uint32_t tok, float* xr
   const int nch = e.chunks();
   const uint8_t* row = e.data + ((size_t)(tok / 32) * nch) * 512 + (tok % 32) * 16;
   const uint16_t* sc = e.scales + (size_t)(tok / 32) * e.groups() * 32 + (tok % 32);
+  if (e.bits == 16) {  // bf16 rows: 8 values per 16-byte chunk, widened exactly
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x)
+      xr[c] = bf16f(*reinterpret_cast<const uint16_t*>(row + (size_t)(c / 8) * 512 + (c % 8) * 2));
+    return;
+  }
   for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
     float q;
     int g = c / e.group;
@@ -857,8 +862,9 @@ __global__ void repack_kernel(const RepackSrc src, int bits, int group, int cols
   const int d = blockIdx.x;
   const int tile = d / 32, lr = d % 32;
   const size_t dbytes = (size_t)cols * bits / 8;
-  const size_t row_bytes = dbytes + (size_t)cols / group * 2;
-  const int nch = cols * bits / 128, ng = cols / group;
+  const int ng = bits == 16 ? 0 : cols / group;  // bf16 rows carry no scales
+  const size_t row_bytes = dbytes + (size_t)ng * 2;
+  const int nch = cols * bits / 128;
   // find the source row
   const uint8_t* s = nullptr;
   if (src.interleave16) {

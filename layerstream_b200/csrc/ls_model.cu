@@ -196,10 +196,14 @@ int choose_ksplit(const QMat& w, int M, int num_sms) {
 }
 
 void check_gpu_format(const Config& c) {
+  if (c.format.quant() != c.embed_format.quant())
+    LS_THROW(LS_ERR_ARG, "the CUDA path takes bf16 layers only with a bf16 embedding table");
   for (const WeightFormat* f : {&c.format, &c.embed_format}) {
-    if (!f->quant()) LS_THROW(LS_ERR_ARG, "the CUDA path reads quantized (.lsq) models; bf16 weights are not supported yet");
-    if (f->group & (f->group - 1)) LS_THROW(LS_ERR_ARG, "the CUDA path needs a power-of-two group size, not " + std::to_string(f->group));
+    if (f->quant() && (f->group & (f->group - 1)))
+      LS_THROW(LS_ERR_ARG, "the CUDA path needs a power-of-two group size, not " + std::to_string(f->group));
   }
+  if (!c.format.quant() && (c.hidden % 64 || c.inter % 64))
+    LS_THROW(LS_ERR_ARG, "bf16 weights need hidden and intermediate sizes that are multiples of 64");
   if (c.head_dim != 16 && c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128)
     LS_THROW(LS_ERR_ARG, "head dimension " + std::to_string(c.head_dim) + " is not supported by the CUDA path");
   if (c.inter % 16) LS_THROW(LS_ERR_ARG, "intermediate size must be a multiple of 16");
@@ -209,7 +213,8 @@ void check_gpu_format(const Config& c) {
 
 struct LsModel {
   int device = 0;
-  LsqFile file;
+  LsqFile file;                   // the model's offsets (a .lsq file, or a bf16 safetensors model)
+  std::vector<uint64_t> layer_off;  // file offset of each layer's block
   Config cfg;
   int mode = LS_MODE_RESIDENT, slots = 1;
   size_t max_ctx = 0;
@@ -375,7 +380,28 @@ struct LsModel {
   }
 
   void open(const char* path, int dev, uint64_t mctx, int md, int nslots) {
-    file = LsqFile::open(path);
+    struct stat stt;
+    const bool dir = ::stat(path, &stt) == 0 && S_ISDIR(stt.st_mode);
+    std::string data_path = path;
+    if (dir) {
+      // an unquantized (bf16) safetensors model directory, read as the reference's
+      // ModelFiles::open does (src/weights.rs:271-324): each layer's tensors one contiguous block
+      const SafetensorsModel st = SafetensorsModel::open(path);
+      file = LsqFile();
+      file.path = st.file;
+      file.config_text = st.config_text;
+      file.cfg = st.cfg;
+      file.layout = st.layout;
+      file.data_start = st.layer_start[0];
+      file.embed_start = st.embed_start;
+      file.norm_start = st.norm_start;
+      layer_off = st.layer_start;
+      data_path = st.file;
+      if (md != LS_MODE_RESIDENT) LS_THROW(LS_ERR_ARG, "streaming reads quantized (.lsq) files; open a bf16 model resident");
+    } else {
+      file = LsqFile::open(path);
+      for (size_t l = 0; l < file.cfg.layers; l++) layer_off.push_back(file.data_start + l * file.layout.total);
+    }
     cfg = file.cfg;
     check_gpu_format(cfg);
     device = dev;
@@ -391,8 +417,8 @@ struct LsModel {
 
     const size_t h = cfg.hidden, kv = cfg.kv_dim(), I = cfg.inter, V = cfg.vocab, L = cfg.layers;
     const size_t lt = file.layout.total, rb = cfg.embed_row_bytes();
-    int fd = ::open(path, O_RDONLY);
-    if (fd < 0) LS_THROW(LS_ERR_IO, std::string(path) + ": cannot open");
+    int fd = ::open(data_path.c_str(), O_RDONLY);
+    if (fd < 0) LS_THROW(LS_ERR_IO, data_path + ": cannot open");
     struct FdGuard {
       int fd;
       ~FdGuard() { ::close(fd); }
@@ -437,7 +463,7 @@ struct LsModel {
         k ^= 1;
       };
       for (size_t l = 0; l < L; l++)
-        step(file.data_start + l * lt, lt, [&](const uint8_t* r) { repack_layer(r, layers[l], stream); });
+        step(layer_off[l], lt, [&](const uint8_t* r) { repack_layer(r, layers[l], stream); });
       for (size_t first = 0; first < V; first += chunk_rows) {
         const size_t rows = std::min(chunk_rows, V - first);
         step(file.embed_start + first * rb, rows * rb, [&](const uint8_t* r) { repack_embed_rows(r, (int)first, (int)rows, embed, stream); });
@@ -779,7 +805,7 @@ struct LsModel {
     if (i >= 0) LS_CUDA(cudaEventRecordWithFlags(prof_ev[2 * i + 1], s, cudaEventRecordExternal));
   }
   double gemv_bytes(const QMat& w, int M, int out_rows) const {
-    const double rb = (double)w.cols * w.bits / 8 + (double)w.cols / w.group * 2;
+    const double rb = (double)w.cols * w.bits / 8 + (double)w.groups() * 2;
     return (double)w.rows * rb + (double)M * w.cols * 4 + (double)M * out_rows * 4;
   }
   void prof_collect() {
@@ -1329,7 +1355,7 @@ struct LsBatch {
     prof_rec.clear();
   }
   static double qbytes(const QMat& w) {
-    return (double)w.rows_pad * ((double)w.cols * w.bits / 8 + (double)w.cols / w.group * 2);
+    return (double)w.rows_pad * ((double)w.cols * w.bits / 8 + (double)w.groups() * 2);
   }
 
   template <class T>
@@ -1408,6 +1434,7 @@ struct LsBatch {
     if (c.inter % 64 || i1 <= i0) LS_THROW(LS_ERR_ARG, "the intermediate dimension does not split over the ranks in 64s");
     dm = Dims{hl, kvl, hl * hd, kvl * hd, i1 - i0};
     if (dm.q_dim % 64) LS_THROW(LS_ERR_ARG, "each rank's q width must be a multiple of 64");
+    if (!c.format.quant()) LS_THROW(LS_ERR_ARG, "tensor parallelism takes quantized models");
     const int gq = m->layers[0].o.group;
     if (dm.q_dim % gq || (i1 - i0) % gq || (r * dm.q_dim) % gq || i0 % gq)
       LS_THROW(LS_ERR_ARG, "each rank's column slice of O and down must hold whole quantization groups");
@@ -2105,8 +2132,12 @@ static void qweights_upload(LsQWeights* q, int dev, int bits, int group, const u
   WeightFormat f;
   f.bits = bits;
   f.group = group;
-  if ((bits != 8 && bits != 4) || group < 16 || group > 256 || (group & (group - 1)) || cols % (uint64_t)group || cols % 32)
+  if (bits == 16) {  // bf16 rows: no groups
+    if (cols % 64) LS_THROW(LS_ERR_ARG, "bf16 rows need a multiple of 64 columns");
+    f.group = group = 0;
+  } else if ((bits != 8 && bits != 4) || group < 16 || group > 256 || (group & (group - 1)) || cols % (uint64_t)group || cols % 32) {
     LS_THROW(LS_ERR_ARG, "unsupported GEMV format or shape");
+  }
   q->device = dev;
   LS_CUDA(cudaSetDevice(dev));
   LS_CUDA(cudaDeviceGetAttribute(&q->num_sms, cudaDevAttrMultiProcessorCount, dev));
@@ -2824,7 +2855,8 @@ int ls_dequant_rows_host(int bits, int group, const uint8_t* rows_raw, uint64_t 
 }
 
 uint64_t ls_qgemv_bytes(int bits, int group, uint64_t rows, uint64_t cols, uint64_t M) {
-  return rows * (cols * (uint64_t)bits / 8 + cols / (uint64_t)group * 2) + M * cols * 4 + M * rows * 4;
+  const uint64_t scale_bytes = (bits == 16 || group == 0) ? 0 : cols / (uint64_t)group * 2;  // bf16 rows: none
+  return rows * (cols * (uint64_t)bits / 8 + scale_bytes) + M * cols * 4 + M * rows * 4;
 }
 
 }  // extern "C"
