@@ -83,11 +83,12 @@ def parse():
     ap.add_argument("--cpu-sample-tokens", type=int, default=0, help="decode tokens per CPU sample (0: auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="print the per-kernel profile to stderr")
-    ap.add_argument("--ncu-case", choices=["pass", "gemv", "attention", "bgemm"], default=None,
+    ap.add_argument("--ncu-case", choices=["pass", "gemv", "attention", "bgemm", "bgemm4"], default=None,
                     help="short fixed workloads for ncu: 'pass' = prefill + 3 verify passes of the bench model, "
                          "'gemv' = 3 launches of the LM-head GEMV (151936 x 896, int4 g32, M = 9), "
-                         "'attention' = 3 launches of the tensor-core attention (14/2 heads, hd 64, M = 5, "
-                         "context 8000), 'bgemm' = the batched GEMM on the 3B gate/up shape (M = 40)")
+                         "'attention' = 3 launches of the tensor-core attention (14/2 heads, hd 64, M = 9, "
+                         "KV length 32768), 'bgemm' = the batched GEMM on the 3B gate/up shape (M = 40), "
+                         "'bgemm4' = the batched GEMM on config 4's gate/up (9728 x 896, int8 g64, M = 320)")
     return ap.parse_args()
 
 
@@ -100,9 +101,10 @@ def ncu_case(args, cfg):
 
     torch.cuda.set_device(0)
     if args.ncu_case == "attention":
-        # the 0.5B attention shape (14 q / 2 kv heads, hd 64) for one sequence of 5 verify rows at
-        # context 8000: 63 chunks of 128 positions per kv head, 16 splits
-        heads, kvh, hd, pos0, M = 14, 2, 64, 8000, 5
+        # the config-3 attention shape (14 q / 2 kv heads, hd 64, 9 verify rows) at KV length 32768:
+        # 256 chunks of 128 positions per kv head over 148 context splits, then the merge kernel
+        heads, kvh, hd, M = 14, 2, 64, 9
+        pos0 = 32768 - M
         rng = np.random.default_rng(7)
         qkv = rng.standard_normal((M, (heads + 2 * kvh) * hd)).astype(np.float32)
         kc = rng.standard_normal((kvh, pos0, hd)).astype(np.float16)
@@ -120,6 +122,15 @@ def ncu_case(args, cfg):
         x = np.random.default_rng(3).standard_normal((M, cols)).astype(np.float32)
         _, ms = ls.bgemm(4, 32, raw, rows, cols, x, iters=3)
         print(json.dumps({"ncu_case": "bgemm", "rows": rows, "cols": cols, "M": M, "ms": ms}))
+        return
+    if args.ncu_case == "bgemm4":
+        # config 4's gate/up projection (9728 x 896, int8 g64) over the 320 rows of a verify pass of
+        # 64 sequences x 5
+        rows, cols, M = 9728, 896, 320
+        raw = stored_rows(8, 64, rows, cols, seed=4)
+        x = np.random.default_rng(4).standard_normal((M, cols)).astype(np.float32)
+        _, ms = ls.bgemm(8, 64, raw, rows, cols, x, iters=3)
+        print(json.dumps({"ncu_case": "bgemm4", "rows": rows, "cols": cols, "M": M, "ms": ms}))
         return
     os.makedirs(args.root, exist_ok=True)
     t_path = synth.ensure_lsq(args.root, cfg["shape"], 0, cfg["body"], cfg["embed"], clip=True)
@@ -420,10 +431,13 @@ def ref_batch(args, cfg):
 
 
 def microbench(args):
-    """Config 3: the verify-path kernels one at a time on one 0.5B layer's shapes. Every launch is
-    timed alone with CUDA events after a 256 MB read that evicts L2 (weights and K/V come from
-    HBM). GEMV: each projection shape x M; attention (tensor-core kernel, context split over up to
-    64 CTAs per kv head): KV length sweep 512 .. 32768 with its roofline per length."""
+    """Config 3: the verify-path kernels one at a time on one 0.5B layer's shapes, timed with CUDA
+    events two ways. "Stream": back-to-back launches captured in one CUDA graph, each over its own
+    replica of the weights (or of the K/V cache), the replicas together at least 256 MB (twice L2),
+    so every launch reads from HBM as the layers of a pass do; time = span / launches. "Cold": one launch alone after a 256 MB
+    read that evicts L2 (and the TLB), median of the repeats. GEMV: each projection shape x M;
+    attention (tensor-core kernel, context split over up to 160 CTAs per kv head, a many-CTA merge):
+    KV length sweep 512 .. 32768 with its roofline per length."""
     import torch
 
     import layerstream_b200 as ls
@@ -439,9 +453,16 @@ def microbench(args):
     reps = max(args.steps, 3)
     for bits, group in ((8, 64), (4, 32)):
         for name, (rows, cols) in MICRO_SHAPES.items():
-            w = ls.QWeights(bits, group, stored_rows(bits, group, rows, cols, seed=rows), rows, cols, device=local)
+            raw = stored_rows(bits, group, rows, cols, seed=rows)
+            w = ls.QWeights(bits, group, raw, rows, cols, device=local)
+            nrep = int(min(4096, max(2, (256 << 20) // qmat_bytes(rows, cols, bits, group) + 1)))  # as the library picks
             for M in (1, 2, 4, 8, 16):
-                x = torch.randn(M, cols, device="cuda")
+                xh = np.random.default_rng(M).standard_normal((M, cols)).astype(np.float32)
+                # stream: the library's host entry times one CUDA graph of launches over device
+                # replicas of the planes (>= 256 MB together)
+                _, ms = ls.qgemv(bits, group, raw, rows, cols, xh, iters=2)
+                us = ms * 1e3
+                x = torch.from_numpy(xh).cuda()
                 y = torch.empty(M, rows, device="cuda")
                 for _ in range(args.warmup):
                     w.gemv(x.data_ptr(), M, y.data_ptr(), s.cuda_stream)
@@ -454,10 +475,11 @@ def microbench(args):
                     e1.record(s)
                     torch.cuda.synchronize()
                     ts.append(e0.elapsed_time(e1))
-                us = float(np.median(ts)) * 1e3
+                us_cold = float(np.median(ts)) * 1e3
                 b = w.bytes(M)
                 gemv.append({"fmt": f"int{bits}-g{group}", "shape": name, "rows": rows, "cols": cols, "M": M, "us": us,
-                             "bytes": b, "gbs": b / us / 1e3, "frac": b / us / 1e3 / peak})
+                             "bytes": b, "gbs": b / us / 1e3, "frac": b / us / 1e3 / peak, "replicas": nrep,
+                             "us_cold": us_cold, "gbs_cold": b / us_cold / 1e3})
             del w
     att = []
     heads, kvh, hd, M = 14, 2, 64, 9
@@ -478,11 +500,14 @@ def microbench(args):
             "data": "synthetic",
             "config": {"workload": "config3: one 0.5B layer's GEMV shapes x M in 1..16, int8 g64 and int4 g32; GQA "
                                    "attention 14/2 heads, hd 64, M = 9, KV 512..32768",
-                       "l2": "256 MB read before every timed launch (GEMV and attention): L2 holds clean lines only"},
+                       "l2": "stream: back-to-back launches (one CUDA graph) over weight / K-V replicas totalling "
+                             ">= 256 MB (twice L2), every launch reads HBM; cold (GEMV us_cold): one launch after a "
+                             "256 MB read"},
             "roofline": {"bound": "hbm", "kernel": "gemv_tc_kernel (LM head, int8 g64, M = 8)", "achieved": head8["gbs"],
                          "peak": peak, "unit": "GB/s", "frac": head8["gbs"] / peak, "peak_source": f"{peak_kind} hbm_gbs",
                          "traffic": None},
-            "gemv": gemv, "attention": att, "gpu_launches": len(gemv) * (reps + args.warmup)}
+            "gemv": gemv, "attention": att,
+            "gpu_launches": sum(2 * g["replicas"] + 1 + args.warmup + reps for g in gemv)}
     if rank == 0:
         print(json.dumps(line), flush=True)
 

@@ -270,6 +270,19 @@ int ls_attention_paged_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, floa
                             const float *qkv, uint16_t *k_pool, uint16_t *v_pool, uint64_t num_pages, uint64_t page,
                             const int32_t *table, float *out, int iters, double *ms);
 
+/* ChaCha20-Poly1305 (RFC 8439 section 2.8) on the GPU: the cipher of sealed model files
+ * (src/seal.rs:340-400, seal_in_place / open_in_place). data: len bytes in host memory. seal = 1:
+ * encrypted in place, tags written; seal = 0: every tag is checked, then the data decrypted in
+ * place; LS_ERR_IO when a tag does not match (*bad_chunk = the lowest failing chunk, whose bytes are
+ * left as they were). chunk_bytes = 0: one message under nonce[12] and aad. chunk_bytes > 0: chunks
+ * of chunk_bytes (the last one shorter), chunk i under nonce[0..8) || le32(first + i) with
+ * associated data aad || le32(first + i): the sealed file's per-chunk messages
+ * (src/seal.rs:25-27); tags holds 16 bytes per chunk. iters > 1 (seal only): *ms = the device time of
+ * one call over all chunks, averaged over iters launches. */
+int ls_aead_host(int seal, const uint8_t *key, const uint8_t *nonce, const uint8_t *aad, uint64_t aad_len, uint8_t *data,
+                 uint64_t len, uint64_t chunk_bytes, uint32_t first, uint8_t *tags, int iters, double *ms,
+                 int64_t *bad_chunk);
+
 /* The same GEMV on device buffers prepared once by ls_qweights_upload (for timing loops). */
 typedef struct LsQWeights LsQWeights;
 int ls_qweights_upload(int device, int bits, int group, const uint8_t *rows_raw, uint64_t rows, uint64_t cols,

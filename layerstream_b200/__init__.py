@@ -118,6 +118,8 @@ _SIGS = {
     "ls_qgemv_rows_noalloc": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64,
                                         C.c_void_p, C.c_void_p]),
     "ls_dequant_rows_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p]),
+    "ls_aead_host": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64, C.c_uint64,
+                               C.c_uint32, C.c_void_p, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
 }
 
 
@@ -412,6 +414,38 @@ def bgemm(bits: int, group: int, rows_raw, rows: int, cols: int, x, iters: int =
     ms = C.c_double()
     _check(lib().ls_bgemm_host(bits, group, _p(w), rows, cols, _p(xx), M, _p(y), iters, C.byref(ms)))
     return y, ms.value
+
+
+def aead_seal(key: bytes, nonce: bytes, aad: bytes, data: bytes, chunk_bytes: int = 0, first: int = 0, iters: int = 1):
+    """ChaCha20-Poly1305 sealing on the GPU (RFC 8439 2.8; chunk_bytes > 0: the sealed file's
+    per-chunk messages, chunk i under nonce[:8] + le32(first + i) and aad + le32(first + i)).
+    Returns (ciphertext, tags: one 16-byte tag per chunk, ms per call when iters > 1)."""
+    buf = np.frombuffer(bytes(data), np.uint8).copy()
+    n = 1 if chunk_bytes == 0 or len(data) == 0 else -(-len(data) // chunk_bytes)
+    tags = np.zeros(16 * n, np.uint8)
+    k, nn, a = _bytes_arr(key, 32), _bytes_arr(nonce, 12), np.frombuffer(bytes(aad) or b"\0", np.uint8)
+    ms, bad = C.c_double(), C.c_int64()
+    _check(lib().ls_aead_host(1, _p(k), _p(nn), _p(a), len(aad), _p(buf), len(data), chunk_bytes, first, _p(tags), iters,
+                              C.byref(ms), C.byref(bad)))
+    return buf.tobytes(), [tags[16 * i:16 * i + 16].tobytes() for i in range(n)], ms.value
+
+
+def aead_open(key: bytes, nonce: bytes, aad: bytes, data: bytes, tags, chunk_bytes: int = 0, first: int = 0):
+    """ChaCha20-Poly1305 opening on the GPU: every tag is checked, then the data decrypted. Raises
+    LayerstreamError (LS_ERR_IO) on a mismatch; returns the plaintext."""
+    buf = np.frombuffer(bytes(data), np.uint8).copy()
+    t = np.frombuffer(b"".join(bytes(x) for x in tags), np.uint8).copy()
+    k, nn, a = _bytes_arr(key, 32), _bytes_arr(nonce, 12), np.frombuffer(bytes(aad) or b"\0", np.uint8)
+    ms, bad = C.c_double(), C.c_int64()
+    _check(lib().ls_aead_host(0, _p(k), _p(nn), _p(a), len(aad), _p(buf), len(data), chunk_bytes, first, _p(t), 1,
+                              C.byref(ms), C.byref(bad)))
+    return buf.tobytes()
+
+
+def _bytes_arr(b: bytes, n: int) -> np.ndarray:
+    if len(b) != n:
+        raise ValueError(f"expected {n} bytes, got {len(b)}")
+    return np.frombuffer(bytes(b), np.uint8).copy()
 
 
 def attention(heads: int, kv_heads: int, hd: int, pos0: int, qkv: np.ndarray, k_cache=None, v_cache=None,

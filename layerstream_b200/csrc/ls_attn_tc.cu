@@ -19,9 +19,11 @@
 // warps busy. K/V chunks stream through a two-buffer cp.async ring; the block's own new rows (RoPE
 // on K, both rounded to f16 as the cache stores them) are computed from qkv in place of cache
 // reads and written to the cache by the CTA that owns their chunk. Splits of one (sequence, kv
-// head, row block) leave (m, l, O) partials; the last of them merges in split order. Every
-// mbarrier wait is bounded: on a timeout the kernel records the error and returns after releasing
-// tensor memory.
+// head, row block) leave (m, l, O) partials. Up to AT_LAST_MERGE splits, the last of them merges
+// in split order; more splits (long contexts spread over every SM) are merged by
+// attention_merge_kernel, one CTA per query row, so that the partials (16 KB per split and kv head
+// at M = 9) are read by many SMs instead of one. Every mbarrier wait is bounded: on a timeout the
+// kernel records the error and returns after releasing tensor memory.
 //
 // Scores are exact f16 x f16 products accumulated in f32 (then scaled in f32); q and P are rounded
 // to f16 for the tensor core, which keeps the output within the north-star logit tolerance of the
@@ -35,7 +37,8 @@ namespace ls {
 
 constexpr int AT_THREADS = 256;  // two warps per tensor-memory lane quadrant
 constexpr int AT_CH = 128;       // positions per chunk: N of the score MMA, K of the value MMA
-constexpr int AT_MAX_SPLITS = 64;
+constexpr int AT_MAX_SPLITS = 160;  // > 148: a single sequence's two kv heads fill every SM twice
+constexpr int AT_LAST_MERGE = 8;    // splits merged by the last CTA; above, by attention_merge_kernel
 // tensor-memory columns: scores [0, 128), P as f16 pairs [128, 192), output [192, 192 + hd)
 constexpr int AT_COL_P = 128, AT_COL_O = 192;
 __host__ __device__ constexpr int at_tmem_cols(int hd) { return AT_COL_O + hd <= 256 ? 256 : 512; }
@@ -120,6 +123,15 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
   const bool row_ok = rl < nrows;
   const bool quad_active = quad < nrows;       // warp-uniform: the quadrant holds a valid row
   // written by the host before the pass (or, for batches launched without PDL, by an earlier kernel)
+  // profiling timeline (a.trace): 0 start, 1 after the first chunk's loads are issued and the
+  // previous kernel has finished, 2 Q staged; per chunk of the first two (k = 0, 1): 3 + 4k loads
+  // landed, 4 + 4k scores ready, 5 + 4k P stored, 6 + 4k O added; 11 partials written
+  auto mark = [&](int k) {
+    if (a.trace && tid == 0)
+      a.trace[((size_t)blockIdx.x + gridDim.x * ((size_t)blockIdx.y + gridDim.y * blockIdx.z)) * AT_TRACE_SLOTS + k] =
+          (unsigned)clock();
+  };
+  mark(0);
   const int pos0 = a.pos0 ? a.pos0[seq] : a.ctl->pos0;
   const int total = pos0 + M;
   const int nch = (total + AT_CH - 1) / AT_CH;
@@ -144,16 +156,41 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
 
-  // cached rows (positions < pos0) of chunk c into buffer b: K as core matrices, V as stored
+  // Cached rows (positions < pos0) of chunk c into buffer b: K as core matrices, V as stored; one
+  // cp.async per 16-byte piece (row pl, column chunk cc). K: each warp fills tiles of 8 rows x 4
+  // column chunks (lane = row % 8 + 8 x chunk % 4), so a quarter warp writes the 8 distinct 16-byte
+  // slots of a core matrix (no shared-memory bank conflicts) and reads 64 contiguous bytes of each
+  // row; V: consecutive pieces of one row per 8 lanes. The page-table entries of all the thread's
+  // pieces are read first, in one round trip.
+  constexpr int LPER = AT_CH * C8 / AT_THREADS;  // pieces of K (and of V) per thread: hd 64: 4, hd 128: 8
   auto load_chunk = [&](int c, int b) {
     const int p0 = c * AT_CH;
     const int ncached = max(0, min(AT_CH, pos0 - p0));
     const uint32_t kb = tc::su32(sk + b * SM::kK), vb = tc::su32(sv + b * SM::kV);
-    for (int i = tid; i < ncached * C8; i += AT_THREADS) {
-      const int pl = i / C8, cc = i - pl * C8;
-      const size_t row = kv_row(pg, a.page_shift, a.num_pages, g, p0 + pl) * HD + cc * 8;
-      tc::cp_async16(kb + km_off(pl, cc * 8, SBO_HD), kcache + row);
-      tc::cp_async16(vb + (uint32_t)i * 16u, vcache + row);
+    const int pmask = (1 << a.page_shift) - 1;
+    int kpl[LPER], kcc[LPER], kent[LPER], vent[LPER];
+#pragma unroll
+    for (int k = 0; k < LPER; k++) {
+      const int t = warp + 8 * k, rg = t % (AT_CH / 8), cq = t / (AT_CH / 8);
+      kpl[k] = rg * 8 + (lane & 7);
+      kcc[k] = cq * 4 + (lane >> 3);
+      const int vpl = (tid + AT_THREADS * k) / C8;
+      kent[k] = kpl[k] < ncached ? pg[(p0 + kpl[k]) >> a.page_shift] : 0;
+      vent[k] = vpl < ncached ? pg[(p0 + vpl) >> a.page_shift] : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < LPER; k++) {
+      if (kpl[k] < ncached) {
+        const int p = p0 + kpl[k];
+        const size_t row = ((((size_t)g * a.num_pages + kent[k]) << a.page_shift) + (size_t)(p & pmask)) * HD + kcc[k] * 8;
+        tc::cp_async16(kb + km_off(kpl[k], kcc[k] * 8, SBO_HD), kcache + row);
+      }
+      const int i = tid + AT_THREADS * k, vpl = i / C8, vcc = i - vpl * C8;
+      if (vpl < ncached) {
+        const int p = p0 + vpl;
+        const size_t row = ((((size_t)g * a.num_pages + vent[k]) << a.page_shift) + (size_t)(p & pmask)) * HD + vcc * 8;
+        tc::cp_async16(vb + (uint32_t)i * 16u, vcache + row);
+      }
     }
     tc::cp_commit();
   };
@@ -193,24 +230,49 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
 
   if (c0 < c1) load_chunk(c0, 0);  // the cache rows below pos0 do not depend on the previous kernel
   pdl_wait();
+  mark(1);
 
   // Q rows of this block (row r = q head j of the group x token t, r = j * M + t) at their lanes,
-  // RoPE at pos0 + t; lanes without a row are zero
-  for (int i = tid; i < 128 * C8; i += AT_THREADS) {
-    const int ln = i / C8, cc = i - ln * C8;
-    const int rr = at_row(ln);
-    uint4 qh = make_uint4(0, 0, 0, 0);
-    if (rr < nrows) {
+  // RoPE at pos0 + t; lanes without a row are zero. The rows (f32, before RoPE) and, when they fit,
+  // the RoPE rows of the block's positions are first copied into shared memory that the chunk loop
+  // has not used yet (the second V buffer and the V^T tile: 128 rows x hd floats; the second K
+  // buffer), every piece in flight at once: one round trip instead of one per piece.
+  {
+    float* qst = reinterpret_cast<float*>(sv + SM::kV);    // [nrows][HD]
+    float2* rst = reinterpret_cast<float2*>(sk + SM::kK);  // [M][HALF]
+    const bool rope_smem = (size_t)M * HD * 4 <= (size_t)SM::kK;
+    for (int i = tid; i < nrows * (HD / 4); i += AT_THREADS) {
+      const int rr = i / (HD / 4), c4 = i - rr * (HD / 4);
       const int r = r0 + rr, j = r / M, t = r - j * M;
-      float q8[8];
-      rope8<HD>(qkv + (size_t)t * a.qkv_stride + (g * G + j) * HD, a.rope + (size_t)(pos0 + t) * HALF, cc * 8, q8);
-      qh = make_uint4(pack_h2(q8[0], q8[1]), pack_h2(q8[2], q8[3]), pack_h2(q8[4], q8[5]), pack_h2(q8[6], q8[7]));
+      tc::cp_async16(tc::su32(qst + (size_t)rr * HD + c4 * 4), qkv + (size_t)t * a.qkv_stride + (g * G + j) * HD + c4 * 4);
     }
-    *reinterpret_cast<uint4*>(sq + km_off(ln, cc * 8, SBO_HD)) = qh;
+    if (rope_smem)
+      for (int i = tid; i < M * (HALF / 2); i += AT_THREADS) {
+        const int t = i / (HALF / 2), c2 = i - t * (HALF / 2);
+        tc::cp_async16(tc::su32(rst + (size_t)t * HALF + c2 * 2), a.rope + (size_t)(pos0 + t) * HALF + c2 * 2);
+      }
+    tc::cp_commit();
+    tc::cp_wait<0>();  // (also the first chunk's rows, which the loop needs next)
+    __syncthreads();
+    // (the K tiles' mapping: a quarter warp writes the 8 rows of one core matrix, no bank conflicts)
+#pragma unroll 1
+    for (int k = 0; k < LPER; k++) {
+      const int tq = warp + 8 * k, ln = (tq % 16) * 8 + (lane & 7), cc = (tq / 16) * 4 + (lane >> 3);
+      const int rr = at_row(ln);
+      uint4 qh = make_uint4(0, 0, 0, 0);
+      if (rr < nrows) {
+        const int t = (r0 + rr) % M;
+        float q8[8];
+        rope8<HD>(qst + (size_t)rr * HD, rope_smem ? rst + (size_t)t * HALF : a.rope + (size_t)(pos0 + t) * HALF, cc * 8, q8);
+        qh = make_uint4(pack_h2(q8[0], q8[1]), pack_h2(q8[2], q8[3]), pack_h2(q8[4], q8[5]), pack_h2(q8[6], q8[7]));
+      }
+      *reinterpret_cast<uint4*>(sq + km_off(ln, cc * 8, SBO_HD)) = qh;
+    }
   }
 
   __syncthreads();
   tc::fence_after();
+  mark(2);
   const uint32_t tmem = s_tmem;
   const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
   int lim = -1;  // last position this row may attend to
@@ -233,6 +295,7 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
     fill_chunk(c, b);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
+    if (it < 2) mark(3 + 4 * it);
 
     // ---- scores ----
     if (tid == 0) {
@@ -262,11 +325,12 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
       }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    if (__syncthreads_or(!tc::mbar_wait(&bar_s, it & 1, &s_abort))) {
+    if (__syncthreads_or(!tc::mbar_wait_fast(&bar_s, it & 1, &s_abort))) {
       failed = true;
       break;
     }
     tc::fence_after();
+    if (it < 2) mark(4 + 4 * it);
 
     // ---- softmax: each half of the warps takes 64 positions of every row ----
     const int pb = p0 + hf * 64;       // first position of this half
@@ -331,6 +395,7 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
     tc::fence_before();
     __syncthreads();
 
+    if (it < 2) mark(5 + 4 * it);
     // ---- O += P . V ----
     if (tid == 0) {
       tc::fence_after();
@@ -340,7 +405,7 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
                        tc::idesc_f16(HD), j > 0 ? 1u : 0u);
       tc::commit(&bar_o);
     }
-    if (__syncthreads_or(!tc::mbar_wait(&bar_o, it & 1, &s_abort))) {
+    if (__syncthreads_or(!tc::mbar_wait_fast(&bar_o, it & 1, &s_abort))) {
       failed = true;
       break;
     }
@@ -356,6 +421,7 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
       }
     }
     tc::fence_before();
+    if (it < 2) mark(6 + 4 * it);
   }
 
   // ---- release tensor memory (also on the error path) ----
@@ -411,11 +477,15 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
     for (int d4 = 0; d4 < HO / 4; d4++) pp[d4] = make_float4(o[4 * d4], o[4 * d4 + 1], o[4 * d4 + 2], o[4 * d4 + 3]);
     if (hf == 0) reinterpret_cast<float2*>(pml)[(size_t)split * R + r0 + rl] = make_float2(m_run, l_run);
   }
-  if (!last_cta(a.tickets + unit * nrb + rb, (unsigned)nsplit)) return;
+  if (a.trace) {
+    __syncthreads();
+    mark(11);
+  }
+  if (nsplit > AT_LAST_MERGE || !last_cta(a.tickets + unit * nrb + rb, (unsigned)nsplit)) return;
   // weight of every split for every row (shared memory is free: all MMAs have completed)
   // (the weights of a row are computed by the two threads of its lane, each for half the splits:
   // the max and the sum are combined through shared memory in a fixed order)
-  float* s_w = reinterpret_cast<float*>(smem);  // [AT_MAX_SPLITS][128]
+  float* s_w = reinterpret_cast<float*>(smem);  // [AT_LAST_MERGE][128]
   const float2* ml = reinterpret_cast<const float2*>(pml) + r0 + rl;
   const int sh0 = hf * ((nsplit + 1) / 2), sh1 = hf ? nsplit : (nsplit + 1) / 2;
   float mm = -CUDART_INF_F;
@@ -462,6 +532,105 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
   }
 }
 
+// Merge of the context splits of one query row (row = blockIdx.x of the (sequence, kv head) unit
+// blockIdx.z, blockIdx.y): o = sum_s w_s O_s / sum_s w_s l_s with w_s = 2^(m_s - max m). Every
+// load is issued up front (one L2 round trip): thread (split group sg, float4 column d4) holds
+// O_s for s = sg, sg + NG, ... and (m, l) of splits tid, tid + 128; it sums its splits in order and
+// the groups are added in order, so the result does not depend on timing.
+template <int HD>
+__global__ void __launch_bounds__(128) attention_merge_kernel(const AttnLaunch a, int nsplit) {
+  constexpr int D4 = HD / 4, NG = 128 / D4, PER = (AT_MAX_SPLITS + NG - 1) / NG, BATCH = PER < 20 ? PER : 20;
+  constexpr int MLPER = (AT_MAX_SPLITS + 127) / 128;
+  __shared__ float s_w[AT_MAX_SPLITS];
+  __shared__ float s_r[2][4];
+  __shared__ float4 s_acc[NG][D4];
+  pdl_trigger();
+  const int G = a.heads / a.kv_heads, M = a.M, R = G * M;
+  const int row = blockIdx.x, g = blockIdx.y, seq = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int d4 = tid % D4, sg = tid / D4;
+  pdl_wait();  // the attention kernel's partials
+  const size_t unit = (size_t)seq * a.kv_heads + g;
+  const float4* src = reinterpret_cast<const float4*>(a.part + unit * nsplit * (size_t)R * HD + (size_t)row * HD) + d4;
+  const float2* pml =
+      reinterpret_cast<const float2*>(a.part + (size_t)a.nseq * a.kv_heads * nsplit * (size_t)R * HD) + unit * nsplit * (size_t)R + row;
+  float2 ml[MLPER];
+#pragma unroll
+  for (int q = 0; q < MLPER; q++) {
+    const int s = tid + 128 * q;
+    ml[q] = s < nsplit ? __ldcg(pml + (size_t)s * R) : make_float2(-CUDART_INF_F, 0.f);
+  }
+  float4 v[BATCH];
+#pragma unroll
+  for (int j = 0; j < BATCH; j++) {
+    const int s = sg + NG * j;
+    v[j] = s < nsplit ? __ldcg(src + (size_t)s * R * D4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mm = -CUDART_INF_F;
+#pragma unroll
+  for (int q = 0; q < MLPER; q++) mm = fmaxf(mm, ml[q].x);
+  mm = warp_max(mm);
+  if (lane == 0) s_r[0][warp] = mm;
+  __syncthreads();
+  mm = fmaxf(fmaxf(s_r[0][0], s_r[0][1]), fmaxf(s_r[0][2], s_r[0][3]));
+  float ls = 0.f;
+#pragma unroll
+  for (int q = 0; q < MLPER; q++) {
+    const int s = tid + 128 * q;
+    if (s < nsplit) {
+      const float w = (ml[q].x == -CUDART_INF_F) ? 0.f : ex2(ml[q].x - mm);
+      s_w[s] = w;
+      ls += ml[q].y * w;
+    }
+  }
+  ls = warp_sum(ls);
+  if (lane == 0) s_r[1][warp] = ls;
+  __syncthreads();
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < BATCH; j++) {
+    const int s = sg + NG * j;
+    if (s < nsplit) {
+      const float w = s_w[s];
+      acc.x += w * v[j].x;
+      acc.y += w * v[j].y;
+      acc.z += w * v[j].z;
+      acc.w += w * v[j].w;
+    }
+  }
+  for (int j = BATCH; j < PER; j++) {  // (head_dim 128: the splits beyond the first batch)
+    const int s = sg + NG * j;
+    if (s < nsplit) {
+      const float w = s_w[s];
+      const float4 u = __ldcg(src + (size_t)s * R * D4);
+      acc.x += w * u.x;
+      acc.y += w * u.y;
+      acc.z += w * u.z;
+      acc.w += w * u.w;
+    }
+  }
+  s_acc[sg][d4] = acc;
+  __syncthreads();
+  if (tid < D4) {
+    const float inv = 1.0f / (((s_r[1][0] + s_r[1][1]) + s_r[1][2]) + s_r[1][3]);
+    float4 t = s_acc[0][tid];
+#pragma unroll
+    for (int q = 1; q < NG; q++) {
+      t.x += s_acc[q][tid].x;
+      t.y += s_acc[q][tid].y;
+      t.z += s_acc[q][tid].z;
+      t.w += s_acc[q][tid].w;
+    }
+    t = make_float4(t.x * inv, t.y * inv, t.z * inv, t.w * inv);
+    const int j = row / M, tt = row - j * M, H = a.heads * HD;
+    if (a.out_h)
+      *reinterpret_cast<uint2*>(a.out_h + bt_off(seq * M + tt, (g * G + j) * HD + 4 * tid, H, a.out_h_n)) =
+          make_uint2(pack_h2(t.x, t.y), pack_h2(t.z, t.w));
+    else
+      reinterpret_cast<float4*>(a.out + ((size_t)seq * M + tt) * H + (size_t)(g * G + j) * HD)[tid] = t;
+  }
+}
+
 static int num_sms_cached() {
   static int n = 0;
   if (!n) {
@@ -480,7 +649,12 @@ static void launch_att_tc_t(const AttnLaunch& a, cudaStream_t s) {
   // chunks of the longest context this launch can see: every split gets at least one
   const int most = a.max_total > 0 ? a.max_total : a.max_ctx;
   const int nch = (most + AT_CH - 1) / AT_CH;
-  const int nsplit = std::max(1, std::min({a.max_splits, want, nch, AT_MAX_SPLITS}));
+  int nsplit = std::max(1, std::min({want, nch, AT_MAX_SPLITS}));
+  // as many splits as the caller's partial buffer holds (O rows and (m, l) of every split)
+  if (a.part_floats == 0)
+    nsplit = std::max(1, std::min(nsplit, a.max_splits));
+  else
+    while (nsplit > 1 && (size_t)a.nseq * a.kv_heads * nsplit * R * (HD + 2) > a.part_floats) nsplit--;
   const size_t smem = AtSmem<HD>::kTotal;
   ensure_smem(attention_tc_kernel<HD>, smem);
   const dim3 grid(nsplit, a.kv_heads * nrb, a.nseq);
@@ -490,6 +664,7 @@ static void launch_att_tc_t(const AttnLaunch& a, cudaStream_t s) {
     attention_tc_kernel<HD><<<grid, AT_THREADS, smem, s>>>(a, nsplit, nrb);
     LS_CUDA(cudaGetLastError());
   }
+  if (nsplit > AT_LAST_MERGE) launch_pdl(attention_merge_kernel<HD>, dim3(R, a.kv_heads, a.nseq), dim3(128), 0, s, a, nsplit);
 }
 
 bool attention_tc_supported(const AttnLaunch& a) {

@@ -13,7 +13,10 @@
 //   warps 9-10 one thread each issues tcgen05.mma for alternate stages (A = weights in tensor
 //           memory, B = activations in shared memory, N = the token group, f32 accumulator of its own
 //           in tensor memory), then commits the stage and the A buffer back to their producers; two
-//           issuers keep the tensor pipe fed, their two accumulators are summed in the epilogue
+//           issuers keep the tensor pipe fed for small groups, their two accumulators are summed in
+//           the epilogue. Large groups (whose MMAs are long) take one issuer and one accumulator,
+//           which leaves tensor memory for four A buffers: two per warpgroup, so a warpgroup
+//           dequantises and stores its next block while the MMAs of its last one run
 //   epilogue warps 0-3 read D (tcgen05.ld; thread = weight row) and store, add the residual, add
 //           the bias, apply SwiGLU into the next GEMM's f16 operand, or take per-token argmax parts.
 // Each weight tile is dequantised once per pass for all tokens of the group. Small matrices split
@@ -41,7 +44,7 @@ constexpr int BG_DEQ_WARPS = 4;   // warps of one dequantising warpgroup (and of
 constexpr int BG_WG = 2;          // dequantising warpgroups: warpgroup g takes the K blocks i % 2 == g
 constexpr int BG_PRODUCER = 8;    // warp index
 constexpr int BG_ISSUER = 9;      // warps 9, 10: issuer g takes the stages s % 2 == g into accumulator g
-constexpr int BG_NISS = 2;
+constexpr int BG_NISS = 2;  // issuer warps (a plan uses 1 or 2 of them)
 constexpr int BG_THREADS = 352;
 constexpr int BG_MAX_STAGES = 8;
 constexpr int BG_MAX_N = 192;  // two accumulators of N columns next to the A buffers (<= 512 columns)
@@ -58,7 +61,6 @@ struct BgShape {
   static constexpr int KB = tc_kb(BITS, G), NS = tc_ns(BITS, G), CPB = KB / (128 / BITS);
   // one A buffer: a K block's f16 pairs (two per column), for int8 its exact hi then lo parts
   static constexpr int HCOLS = KB / 2, ACOLS = HCOLS * tc_parts(BITS);
-  static constexpr int ABUF = ACOLS <= 32 ? 4 : 2;  // A buffers: 128 columns of tensor memory
   // per K block: 128 rows of packed ints, their group scales, N tokens of f16 activations
   static constexpr uint32_t W_KB = 4u * CPB * 512u;
   static constexpr uint32_t S_KB = 4u * NS * 64u;
@@ -72,7 +74,8 @@ template <int BITS, int G>
 __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
     bgemm_kernel(const __grid_constant__ BgemmLaunch g, const __grid_constant__ BgemmPlan p, const __grid_constant__ QMaps maps) {
   using SH = BgShape<BITS, G>;
-  constexpr int KB = SH::KB, NS = SH::NS, CPB = SH::CPB, ACOLS = SH::ACOLS, ABUF = SH::ABUF, HCOLS = SH::HCOLS;
+  constexpr int KB = SH::KB, NS = SH::NS, CPB = SH::CPB, ACOLS = SH::ACOLS, HCOLS = SH::HCOLS;
+  const int ABUF = p.abuf, NISS = p.niss;  // A buffers (2 or 4), issuers (1 or 2)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t full[BG_MAX_STAGES], empty[BG_MAX_STAGES], bar_a[4], bar_af[4], bar_d, bar_fin[BG_NISS];
   __shared__ uint32_t s_tmem;
@@ -105,7 +108,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
       tc::mbar_init(&bar_a[b], 1);
       tc::mbar_init(&bar_af[b], BG_DEQ_WARPS);
     }
-    tc::mbar_init(&bar_d, BG_NISS);
+    tc::mbar_init(&bar_d, NISS);
     for (int q = 0; q < BG_NISS; q++) tc::mbar_init(&bar_fin[q], 1);
     s_abort = 0;
     s_epi_fail = 0;
@@ -144,7 +147,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
       for (int i = 0; i < nst; i++) {
         const int s = i % S, kb = kb0 + i * KST, nv = min(KST, kb1 - kb);
         if (i >= S) {
-          if (!tc::mbar_wait(&empty[s], ((i / S) & 1) ^ 1, &s_abort)) {
+          if (!tc::mbar_wait_fast(&empty[s], ((i / S) & 1) ^ 1, &s_abort)) {
             failed = true;
             break;
           }
@@ -161,15 +164,17 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
       volatile int no_abort = 0;
       for (int i = max(0, issued - S); i < issued; i++) tc::mbar_wait(&full[i % S], (i / S) & 1, &no_abort);
     }
-  } else if (warp >= BG_ISSUER && warp < BG_ISSUER + BG_NISS) {
+  } else if (warp >= BG_ISSUER + NISS && warp < BG_ISSUER + BG_NISS) {
+    // an issuer warp the plan does not use
+  } else if (warp >= BG_ISSUER && warp < BG_ISSUER + NISS) {
     if (lane == 0) {
       const int ig = warp - BG_ISSUER;
       const uint32_t idesc = tc::idesc_f16(N);
       const uint32_t dacc = d_col + ig * N;
       bool first = true;
-      for (int st_i = ig; st_i < nst && !failed; st_i += BG_NISS) {
+      for (int st_i = ig; st_i < nst && !failed; st_i += NISS) {
         const int s = st_i % S;
-        if (!tc::mbar_wait(&full[s], (st_i / S) & 1, &s_abort)) {
+        if (!tc::mbar_wait_fast(&full[s], (st_i / S) & 1, &s_abort)) {
           failed = true;
           break;
         }
@@ -177,7 +182,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
         for (int i = st_i * KST; i < i_end; i++) {
           const int j = i - st_i * KST, b = i % ABUF;
           BG_STAMP(6, i);
-          if (!tc::mbar_wait(&bar_af[b], (i / ABUF) & 1, &s_abort)) {
+          if (!tc::mbar_wait_fast(&bar_af[b], (i / ABUF) & 1, &s_abort)) {
             failed = true;
             break;
           }
@@ -210,7 +215,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
     // block this warpgroup takes from it)
     auto load_block = [&](int i, uint32_t* a) -> bool {
       const int st_i = i / KST, j = i - st_i * KST, s = st_i % S;
-      if (j < 2 && !tc::mbar_wait(&full[s], (st_i / S) & 1, &s_abort)) return false;
+      if (j < 2 && !tc::mbar_wait_fast(&full[s], (st_i / S) & 1, &s_abort)) return false;
       const uint8_t* st = smem + (size_t)s * STAGE;
       uint4 wv[CPB];
 #pragma unroll
@@ -231,7 +236,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
     if (have && !load_block(i, acur)) failed = true;
     while (have && !__any_sync(0xffffffffu, failed)) {
       const int b = i % ABUF;
-      if (i >= ABUF && !tc::mbar_wait(&bar_a[b], ((i / ABUF) & 1) ^ 1, &s_abort)) failed = true;
+      if (i >= ABUF && !tc::mbar_wait_fast(&bar_a[b], ((i / ABUF) & 1) ^ 1, &s_abort)) failed = true;
       if (__any_sync(0xffffffffu, failed)) break;
       tc::fence_after();
 #pragma unroll
@@ -254,7 +259,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
       // the epilogue belongs to warpgroup 0; a failure here shows up there as a missing commit
     } else {
     // ---- epilogue (the four warps agree on failure before their named barriers) ----
-    if (!failed && !tc::mbar_wait(&bar_d, 0, &s_abort)) failed = true;
+    if (!failed && !tc::mbar_wait_fast(&bar_d, 0, &s_abort)) failed = true;
     failed = __any_sync(0xffffffffu, failed);
     if (failed && lane == 0) s_epi_fail = 1;
     deq_sync();
@@ -268,7 +273,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
         tc::wait_ld();
 #pragma unroll
         for (int e = 0; e < 16; e++) v[e] = __uint_as_float(u[e]);
-        if (nst > 1) {
+        if (NISS > 1 && nst > 1) {
           tc::ld16(d_col + N + lane_base + n16 * 16, u);
           tc::wait_ld();
 #pragma unroll
@@ -495,19 +500,28 @@ BgemmPlan bgemm_plan(const QMat& w, int M, int num_sms, bool argmax) {
   const int base = tiles128 * p.ngroups;
   p.ks = 1;
   if (!argmax && base < num_sms) p.ks = std::min({(num_sms + base - 1) / base, std::max(1, nblk / 4), 16});
-  const int aw = KB / 2 * tc_parts(w.bits), acols = (aw <= 32 ? 4 : 2) * aw;
-  p.tmem_cols = acols + BG_NISS * p.N <= 256 ? 256 : 512;
+  // Tensor memory: A buffers of aw columns (4 for int4, 2 for int8's hi + lo parts) and one
+  // N-column accumulator per issuer. Two issuers measured faster than one with 4 int8 buffers
+  // (config 4's gate/up, N = 160: 45 vs 50 us); LS_BGEMM_ISSUERS=1 selects one issuer (4 buffers).
+  const int aw = KB / 2 * tc_parts(w.bits);
+  static const int issuers = [] {
+    const char* e = getenv("LS_BGEMM_ISSUERS");
+    return (e && std::string(e) == "1") ? 1 : 2;
+  }();
+  p.niss = issuers;
+  p.abuf = (issuers == 1 || aw <= 32) ? 4 : 2;
+  p.tmem_cols = p.abuf * aw + p.niss * p.N <= 256 ? 256 : 512;
   // stages of kstage K blocks (~24 KB each, within the slice); two CTAs per SM when tensor memory
   // allows it: keep the ring near 96 KB, else up to ~200 KB
   const uint32_t per_kb = 4u * CPB * 512u + 4u * NS * 64u + (uint32_t)p.N * KB * 2u;
   const int min_slice = nblk / p.ks;
   p.kstage = (int)std::max<uint32_t>(1, std::min<uint32_t>({8u, 24u * 1024 / per_kb, (uint32_t)std::max(1, min_slice)}));
-  // K block i uses A buffer i % ABUF, and the two issuers take alternate stages of kstage blocks:
+  // K block i uses A buffer i % ABUF, and two issuers take alternate stages of kstage blocks:
   // blocks i and i + ABUF (consecutive uses of a buffer) must belong to the same issuer, which
   // waits for the buffer's mbarrier phases in order (a parity wait two phases ahead would read
-  // the stale phase as complete). That holds when kstage divides ABUF / 2.
-  const int abuf = aw <= 32 ? 4 : 2;
-  while ((abuf / 2) % p.kstage) p.kstage--;
+  // the stale phase as complete). That holds when kstage divides ABUF / 2 (one issuer: always).
+  if (p.niss == 2)
+    while ((p.abuf / 2) % p.kstage) p.kstage--;
   const uint32_t st = per_kb * p.kstage;
   const uint32_t budget = p.tmem_cols == 256 ? 96u * 1024 : 200u * 1024;
   p.stages = (int)std::max<uint32_t>(2, std::min<uint32_t>(BG_MAX_STAGES, budget / st));
@@ -555,6 +569,10 @@ void launch_bgemm(const BgemmLaunch& g, const BgemmPlan& p, cudaStream_t s) {
   if (!bgemm_supported(g.w)) LS_THROW(-1, "format not supported by the batched GEMM");
   if (p.N % 16 || p.N > BG_MAX_N || p.ngroups * p.N < g.M) LS_THROW(-1, "batched GEMM plan does not cover the tokens");
   if (p.stages < 2 || p.stages > BG_MAX_STAGES || p.kstage < 1) LS_THROW(-1, "batched GEMM plan: bad stage count");
+  if ((p.abuf != 2 && p.abuf != 4) || (p.niss != 1 && p.niss != 2) ||
+      p.abuf * (tc_kb(g.w.bits, g.w.group) / 2 * tc_parts(g.w.bits)) + p.niss * p.N > p.tmem_cols ||
+      (p.niss == 2 && (p.abuf / 2) % p.kstage))
+    LS_THROW(-1, "batched GEMM plan: bad tensor-memory split");
   {
     int N = 0, ng = 0;
     bgemm_groups(g.M, &N, &ng);

@@ -472,6 +472,89 @@ std::string inject_quant(const std::string& cfg, WeightFormat body, WeightFormat
          std::to_string(body.group) + extra + "}}";
 }
 
+// src/seal.rs:574-591 (SealedLayout::to_json): the header's JSON text, in the same key order and
+// string escaping, so that a file sealed here is byte-identical to the reference's for the same key
+// and nonce prefix.
+std::string sealed_header_json(const std::string& config_text, const LayerLayout& layout, size_t layer_chunk,
+                               size_t embed_chunk_rows, size_t final_norm_bytes) {
+  std::string ranges;
+  for (int s = 0; s < N_SLOTS; s++) {
+    if (s) ranges += ",";
+    ranges += "[" + std::to_string(layout.off[s]) + "," + std::to_string(layout.len[s]) + "]";
+  }
+  return "{\"format\":\"layerstream-sealed-1\",\"config_json\":" + quote(config_text) + ",\"layer_bytes\":" +
+         std::to_string(layout.total) + ",\"layer_chunk\":" + std::to_string(layer_chunk) + ",\"embed_chunk_rows\":" +
+         std::to_string(embed_chunk_rows) + ",\"final_norm_bytes\":" + std::to_string(final_norm_bytes) +
+         ",\"layer_layout\":[" + ranges + "]}";
+}
+
+// src/seal.rs:13-27 (layout), 593-627 (SealedLayout::from_json), 860-903 (SealedSource::open)
+SealedFile SealedFile::open(const std::string& path) {
+  Fd f(path);
+  SealedFile sf;
+  sf.path = path;
+  sf.file_len = f.len;
+  uint8_t frame[kSealFrame];
+  if (f.len < kSealFrame) LS_THROW(-2, "file too short to be a sealed model");
+  pread_all(f.fd, frame, kSealFrame, 0);
+  if (std::memcmp(frame, "LSS1", 4) != 0) LS_THROW(-2, "not a sealed layerstream model (bad magic bytes)");
+  const uint32_t version = frame[4] | (frame[5] << 8) | (frame[6] << 16) | ((uint32_t)frame[7] << 24);
+  if (version != 1) LS_THROW(-2, "unsupported sealed format version " + std::to_string(version));
+  std::memcpy(sf.nonce_prefix, frame + 8, 8);
+  const uint32_t hl = frame[16] | (frame[17] << 8) | (frame[18] << 16) | ((uint32_t)frame[19] << 24);
+  if (hl == 0 || hl > (1u << 20) || kSealFrame + (uint64_t)hl > f.len) LS_THROW(-2, "implausible sealed header length");
+  sf.aad_prefix.resize(kSealFrame + hl);
+  pread_all(f.fd, sf.aad_prefix.data(), sf.aad_prefix.size(), 0);
+  const std::string text(reinterpret_cast<const char*>(sf.aad_prefix.data()) + kSealFrame, hl);
+  J j = parse_json(text);
+  const J* fm = j.get("format");
+  if (!fm || fm->k != J::Str || fm->s != "layerstream-sealed-1") LS_THROW(-2, "unknown sealed format");
+  auto u = [&](const char* k) {
+    const J* v = j.get(k);
+    uint64_t o;
+    if (!v || !v->u64(&o)) LS_THROW(-2, std::string("sealed header: missing ") + k);
+    return (size_t)o;
+  };
+  const J* cj = j.get("config_json");
+  if (!cj || cj->k != J::Str) LS_THROW(-2, "sealed header: missing config");
+  sf.config_text = cj->s;
+  sf.cfg = parse_config(sf.config_text);
+  const J* lj = j.get("layer_layout");
+  if (!lj || lj->k != J::Arr) LS_THROW(-2, "sealed header: missing layout");
+  if (lj->a.size() != N_SLOTS) LS_THROW(-2, "sealed header: layout must list 12 tensors");
+  size_t total = 0;
+  for (int s = 0; s < N_SLOTS; s++) {
+    const J& pr = lj->a[s];
+    uint64_t o, l;
+    if (pr.k != J::Arr || pr.a.size() != 2 || !pr.a[0].u64(&o) || !pr.a[1].u64(&l)) LS_THROW(-2, "sealed header: bad layout entry");
+    sf.layout.off[s] = (size_t)o;
+    sf.layout.len[s] = (size_t)l;
+    total = std::max(total, (size_t)(o + l));
+  }
+  sf.layout.total = total;
+  if (u("layer_bytes") != total) LS_THROW(-2, "sealed header: layer layout does not add up");
+  sf.layer_chunk = u("layer_chunk");
+  sf.embed_chunk_rows = u("embed_chunk_rows");
+  if (sf.layer_chunk == 0 || sf.embed_chunk_rows == 0) LS_THROW(-2, "sealed header: zero chunk size");
+  sf.final_norm_bytes = u("final_norm_bytes");
+  if (sf.final_norm_bytes != sf.cfg.hidden * 2 || sf.cfg.layers == 0 || sf.cfg.layers > 4096)
+    LS_THROW(-2, "sealed header: inconsistent sizes");
+  // every tensor of the layer block must be the size the configuration implies
+  for (int s = 0; s < N_SLOTS; s++) {
+    size_t r, k;
+    const size_t want = matrix_shape(s, sf.cfg, &r, &k) ? r * sf.cfg.format.row_bytes(k) : tensor_shape(s, sf.cfg)[0] * 2;
+    if (sf.layout.len[s] != want) LS_THROW(-2, "sealed header: a tensor of the layer layout has the wrong size");
+  }
+  const uint64_t nch = sf.n_chunks();
+  sf.tags_off = sf.aad_prefix.size();
+  sf.ct_base = sf.tags_off + 16 * nch;
+  if (f.len != sf.ct_base + sf.total_plain())
+    LS_THROW(-2, "file is " + std::to_string(f.len) + " bytes but its header implies " + std::to_string(sf.ct_base + sf.total_plain()));
+  sf.tags.resize(16 * nch);
+  pread_all(f.fd, sf.tags.data(), sf.tags.size(), sf.tags_off);
+  return sf;
+}
+
 // src/weights.rs:345-358
 std::string lsq_header_bytes(const std::string& config_text, size_t layer_bytes, size_t embed_bytes, size_t norm_bytes) {
   std::string json = "{\"format\":\"layerstream-quant-1\",\"config_json\":" + quote(config_text) +

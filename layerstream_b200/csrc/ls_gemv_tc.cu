@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
 
       // ---- A buffer reuse: the MMAs that read it two blocks ago must have completed ----
       const int b = it & 1;
-      if (uses[b] > 0 && !tc::mbar_wait(&bar_a[b], (uses[b] - 1) & 1, &s_abort)) failed = true;
+      if (uses[b] > 0 && !tc::mbar_wait_fast(&bar_a[b], (uses[b] - 1) & 1, &s_abort)) failed = true;
       if (__any_sync(0xffffffffu, failed)) {  // warp-uniform before the warp-collective stores
         failed = true;
         break;
@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
       // block written: one arrival per thread; only the MMA issuer waits for all 128
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::su32(&bar_full[b])) : "memory");
       if (threadIdx.x == 0) {
-        if (!tc::mbar_wait(&bar_full[b], uses[b] & 1, &s_abort)) {
+        if (!tc::mbar_wait_fast(&bar_full[b], uses[b] & 1, &s_abort)) {
           failed = true;
         } else {
           tc::fence_after();
@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const GemvLaunch g)
 
     // ---- accumulators of this tile ----
     if (threadIdx.x == 0) tc::commit(&bar_d);
-    if (!tc::mbar_wait(&bar_d, tiles_done & 1, &s_abort)) failed = true;
+    if (!tc::mbar_wait_fast(&bar_d, tiles_done & 1, &s_abort)) failed = true;
     if (__any_sync(0xffffffffu, failed)) {
       failed = true;
       break;

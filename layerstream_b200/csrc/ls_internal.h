@@ -85,6 +85,34 @@ struct SafetensorsModel {
   static SafetensorsModel open(const std::string& dir);
 };
 
+// A sealed model file (src/seal.rs:13-27): frame (magic "LSS1", version 1, 8-byte nonce prefix,
+// header length), JSON header, 16-byte tags (one per chunk), then the ciphertext of every layer
+// block, the embedding table and the final norm. Layer blocks are cut into layer_chunk-byte chunks,
+// the table into embed_chunk_rows-row chunks, the norm is one chunk; chunk i's message has nonce
+// prefix || le32(i) and associated data = frame + header || le32(i).
+constexpr size_t kSealFrame = 20;
+struct SealedFile {
+  std::string path, config_text;
+  Config cfg;
+  LayerLayout layout;  // from the header
+  size_t layer_chunk = 0, embed_chunk_rows = 0, final_norm_bytes = 0;
+  uint8_t nonce_prefix[8] = {0};
+  std::vector<uint8_t> aad_prefix;  // frame + header bytes
+  std::vector<uint8_t> tags;        // 16 x n_chunks
+  uint64_t tags_off = 0, ct_base = 0, file_len = 0;
+  size_t layer_chunks() const { return (layout.total + layer_chunk - 1) / layer_chunk; }
+  size_t embed_bytes() const { return cfg.vocab * cfg.embed_row_bytes(); }
+  size_t embed_chunks() const { return (cfg.vocab + embed_chunk_rows - 1) / embed_chunk_rows; }
+  size_t embed_first_chunk() const { return cfg.layers * layer_chunks(); }
+  size_t final_chunk() const { return embed_first_chunk() + embed_chunks(); }
+  size_t n_chunks() const { return final_chunk() + 1; }
+  uint64_t embed_plain_off() const { return (uint64_t)cfg.layers * layout.total; }
+  uint64_t total_plain() const { return embed_plain_off() + embed_bytes() + final_norm_bytes; }
+  static SealedFile open(const std::string& path);
+};
+std::string sealed_header_json(const std::string& config_text, const LayerLayout& layout, size_t layer_chunk,
+                               size_t embed_chunk_rows, size_t final_norm_bytes);
+
 std::string inject_quant(const std::string& config_text, WeightFormat body, WeightFormat embed);
 std::string lsq_header_bytes(const std::string& config_text, size_t layer_bytes, size_t embed_bytes, size_t norm_bytes);
 std::string read_file_text(const std::string& path);
@@ -226,6 +254,7 @@ struct AttnLaunch {
   const Ctl* ctl = nullptr;
   float* out = nullptr;  // [M][heads*hd]
   float* part = nullptr; // split partials
+  size_t part_floats = 0; // their capacity (tensor-core kernel: bounds its splits; 0 = max_splits bounds them)
   unsigned* tickets = nullptr;
   int heads = 0, kv_heads = 0, hd = 0, max_ctx = 0, M = 0, split = 64, max_splits = 0;
   // batches: grid.z = nseq sequences of M rows each (rows s*M .. s*M+M-1 of qkv and out); sequence
@@ -238,7 +267,11 @@ struct AttnLaunch {
   int max_total = 0;   // largest pos0 + M over the sequences when the host knows it (0: max_ctx)
   uint16_t* out_h = nullptr;  // tensor-core kernel: output as f16 in the bt layout (K = heads * hd) instead of out
   int out_h_n = 0;            // its token-group rows
+  // profiling (tensor-core kernel): clock() stamps of thread 0 of every CTA, AT_TRACE_SLOTS per CTA
+  // (CTA index = x + gridDim.x (y + gridDim.y z)); null = off
+  unsigned* trace = nullptr;
 };
+constexpr int AT_TRACE_SLOTS = 16;
 void launch_attention(const AttnLaunch& a, cudaStream_t s);
 bool attention_tc_supported(const AttnLaunch& a);  // ls_attn_tc.cu
 void launch_attention_tc(const AttnLaunch& a, cudaStream_t s);
@@ -277,6 +310,7 @@ struct BgemmLaunch {
 };
 struct BgemmPlan {
   int N = 16, ngroups = 1, ks = 1, stages = 2, kstage = 1, tmem_cols = 256;
+  int abuf = 4, niss = 2;  // A buffers in tensor memory (2 or 4); MMA issuers, each with its own accumulator (1 or 2)
   size_t smem = 0, partial_floats = 0, tickets = 0;
 };
 // token groups of a pass of M rows (every GEMM of the pass uses the same): N rows each, ngroups
@@ -333,6 +367,7 @@ struct PassArgs {
   int stall_barrier;    // test hook: this grid barrier (1-based) never completes, 0 = none
   unsigned poll_limit;  // polls of a grid-barrier wait before the CTA gives up with error 3
   int stages;  // weight-stream ring depth
+  int xs;      // 1: x rows (f32) and the norm weights stay in shared memory after the RMS statistics
   int L, hidden, inter, heads, kv_heads, hd, vocab, max_ctx, T, n_logits, slots;
   int ks_qkv, ks_o, ks_gu, ks_down;
   float eps;
@@ -354,6 +389,26 @@ void launch_embed_raw_tokens(const uint8_t* table, size_t row_bytes, int bits, i
 void launch_batch_accept(const ArgPart* parts, int nparts, int T, int M, const uint32_t* tokens, uint32_t* argmax,
                          uint32_t* m_out, uint32_t* next_out, cudaStream_t s);
 
+// ---- ChaCha20-Poly1305 on the GPU (ls_seal.cu), the cipher of sealed model files ----
+// One AEAD message (RFC 8439 2.8): data in device memory, opened (tag checked, then decrypted) or
+// sealed (encrypted, then tagged) in place; its associated data = a prefix shared by the launch's
+// chunks followed by tail_len (0..4) bytes of `tail` (little-endian).
+struct AeadChunk {
+  uint8_t* data;
+  uint64_t len;
+  uint32_t nonce[3];
+  uint32_t tail, tail_len;
+  uint32_t tag[4];
+};
+size_t aead_scratch_bytes(int nchunks, uint64_t max_len, uint32_t aad_len);
+// d_chunks, d_aad, d_key (8 words) in device memory; opening: *d_bad (preset to INT_MAX by the
+// caller) becomes min(failing chunk + 1) and the failing chunks stay untouched; sealing writes the
+// tags into d_chunks.
+void launch_aead(AeadChunk* d_chunks, int nchunks, uint64_t max_len, const uint8_t* d_aad, uint32_t aad_len, const uint32_t* d_key,
+                 bool seal, void* scratch, size_t scratch_bytes, int* d_bad, cudaStream_t s);
+int aead_host(bool seal, const uint8_t* key, const uint8_t* nonce12, bool indexed, uint32_t first, const uint8_t* aad,
+              uint64_t aad_len, uint8_t* data, uint64_t len, uint64_t chunk_bytes, uint8_t* tags, int iters, double* ms);
+
 // ---- NCCL, loaded at run time (ls_nccl.cpp) ----
 struct NcclApi {
   ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
@@ -373,8 +428,11 @@ void qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t r
 
 int pass_kernel_nt(int T);
 bool pass_kernel_supported(const WeightFormat& body, const WeightFormat& embed, int T, int hd);
-size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, int stages);
-int pass_kernel_stages(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, size_t budget);
+// xs: the launch keeps the RMS-normalised rows' source (x as f32, and the norm weights) in shared
+// memory for the staging (pass_kernel_xs_bytes more shared memory)
+size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, int stages, bool xs);
+int pass_kernel_stages(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, size_t budget, bool xs);
+size_t pass_kernel_xs_bytes(int T, int hidden);
 size_t pass_kernel_kv_off(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down);
 void launch_pass(const PassArgs& a, const WeightFormat& f, size_t smem, int grid, cudaStream_t s);
 int pass_kernel_blocks_per_sm(const WeightFormat& f, int T, size_t smem, int max_per_sm);

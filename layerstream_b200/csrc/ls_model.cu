@@ -246,6 +246,12 @@ struct LsModel {
   float *partial = nullptr, *att_part = nullptr;
   size_t partial_floats = 0, att_part_floats = 0;
   int att_slots = 1;
+  // passes through separate kernels (prefill chunks, stream mode) run the projections as batched
+  // tensor-core GEMMs over all the pass's rows: f16 operands in the bt layout, split-K scratch
+  bool use_bg = false;
+  uint16_t *bt_a = nullptr, *bt_h = nullptr;
+  float* bg_partial = nullptr;
+  unsigned* bg_tickets = nullptr;
   Ctl* ctl = nullptr;
   Ctl* ctl_host = nullptr;
 
@@ -531,6 +537,7 @@ struct LsModel {
     tickets = dalloc<unsigned>(max_tiles * (kMaxT / 16 + 1));
     partial_floats = (size_t)max_tiles * 32 * 16 * 32 * (kMaxT / 16 + 1);
     partial = dalloc<float>(partial_floats);
+    setup_bgemm();
     arg_ticket = dalloc<unsigned>(1);
     // context splits of the attention of one sequence: up to 64 (the tensor-core kernel's bound; the
     // CUDA-core kernel takes at most 16), so that long contexts spread over the SMs
@@ -549,6 +556,7 @@ struct LsModel {
   // per head, K slices per GEMV phase and dynamic shared memory.
   struct PassPlan {
     int grid = 0, slots = 1, ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_down = 1, kv_off = 0, stages = 0;
+    bool xs = false;
     size_t smem = 0;
   };
   PassPlan pk_plan[3];
@@ -576,11 +584,17 @@ struct LsModel {
       };
       // one CTA per SM (it takes the whole tensor memory); the weight ring takes the shared memory
       // the rest leaves (LS_PASS_STAGES caps it)
+      // the staging reads x from the RMS statistics' shared-memory copy when that leaves room for a
+      // ring of at least 4 stages (LS_PASS_XS=0 reads it from L2 again)
       P.ks_down = plan(layers[0].down, num_sms);
-      P.stages = pass_kernel_stages(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, pass_kernel_smem_budget(cfg.format, T));
+      const size_t budget = pass_kernel_smem_budget(cfg.format, T);
+      const char* xe = getenv("LS_PASS_XS");
+      P.xs = !(xe && std::string(xe) == "0") &&
+             pass_kernel_stages(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, budget, true) >= 4;
+      P.stages = pass_kernel_stages(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, budget, P.xs);
       if (const char* st = getenv("LS_PASS_STAGES")) P.stages = std::min(P.stages, std::max(2, atoi(st)));
       if (P.stages == 0) continue;
-      const size_t smem = pass_kernel_smem(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, P.stages);
+      const size_t smem = pass_kernel_smem(cfg.format, T, h, I, (int)cfg.head_dim, P.ks_down, P.stages, P.xs);
       const int per_sm = pass_kernel_blocks_per_sm(cfg.format, T, smem, max_per_sm);
       if (per_sm < 1) continue;
       P.grid = per_sm * num_sms;
@@ -594,10 +608,9 @@ struct LsModel {
     }
     if (getenv("LS_PASS_VERBOSE"))
       for (int c = 0; c < 3; c++)
-        fprintf(stderr, "pass plan T<=%d: grid %d slots %d stages %d ks qkv %d o %d gu %d down %d smem %zu\n",
-                16 * (c + 1), pk_plan[c].grid, pk_plan[c].slots, pk_plan[c].stages, pk_plan[c].ks_qkv, pk_plan[c].ks_o,
-                pk_plan[c].ks_gu, pk_plan[c].ks_down,
-                pk_plan[c].smem);
+        fprintf(stderr, "pass plan T<=%d: grid %d slots %d stages %d xs %d ks qkv %d o %d gu %d down %d smem %zu\n",
+                16 * (c + 1), pk_plan[c].grid, pk_plan[c].slots, pk_plan[c].stages, (int)pk_plan[c].xs, pk_plan[c].ks_qkv,
+                pk_plan[c].ks_o, pk_plan[c].ks_gu, pk_plan[c].ks_down, pk_plan[c].smem);
     if (pk_plan[0].grid == 0) return;
     pk_max_grid = max_grid;
     // TMA descriptors of every matrix: [layer][qkv, o, gate/up, down], then the embedding/head
@@ -665,6 +678,7 @@ struct LsModel {
     a.trace_sub = (int)pk_trace_sub();
     a.kv_off = P.kv_off;
     a.stages = P.stages;
+    a.xs = P.xs ? 1 : 0;
     a.poll_limit = 1u << 21;  // polls of ~0.5 us: about a second
     if (stall_barrier) {      // test hook: one barrier wait runs out after ~5 ms
       a.stall_barrier = stall_barrier;
@@ -839,6 +853,46 @@ struct LsModel {
 
   int pick_ksplit(const QMat& w, int M) const { return choose_ksplit(w, M, num_sms); }
 
+  // The batched GEMM path of passes through separate kernels, when every matrix's format allows it
+  // (LS_BGEMM=0 keeps the per-token-group GEMV): operand and scratch buffers for up to kMaxT rows.
+  void setup_bgemm() {
+    const char* e = getenv("LS_BGEMM");
+    const size_t h = cfg.hidden, I = cfg.inter;
+    const LayerW& W = layers[0];
+    use_bg = !(e && std::string(e) == "0") && (I % 8) == 0;
+    for (const QMat* w : {&W.qkv, &W.o, &W.gu, &W.down}) use_bg = use_bg && bgemm_supported(*w);
+    if (!use_bg) return;
+    size_t bpf = 0, btk = 0, rows_bt = 0;
+    for (int rows = 1; rows <= kMaxT; rows++) {
+      for (const QMat* w : {&W.qkv, &W.o, &W.gu, &W.down}) {
+        const BgemmPlan p = bgemm_plan(*w, rows, num_sms, false);
+        bpf = std::max(bpf, p.partial_floats);
+        btk = std::max(btk, p.tickets);
+      }
+      rows_bt = std::max(rows_bt, bt_elems(rows, 1));
+    }
+    bt_a = dalloc<uint16_t>(rows_bt * h);
+    bt_h = dalloc<uint16_t>(rows_bt * I);
+    bg_partial = dalloc<float>(bpf);
+    bg_tickets = dalloc<unsigned>(btk);
+  }
+  void bg(const QMat& w, const uint16_t* xin, int M, int epi, float* y, int y_stride, uint16_t* yh, const uint16_t* bias,
+          cudaStream_t s) {
+    BgemmLaunch g;
+    g.w = w;
+    g.x = xin;
+    g.M = M;
+    g.epi = epi;
+    g.y = y;
+    g.y_stride = y_stride;
+    g.yh = yh;
+    g.bias = bias;
+    g.partial = bg_partial;
+    g.tickets = bg_tickets;
+    g.err = &ctl->err;
+    launch_bgemm(g, bgemm_plan(w, M, num_sms, false), s);
+  }
+
   void gemv(const QMat& w, const float* xin, int x_stride, int M, int epi, float* y, int y_stride, const uint16_t* norm_bf16,
             const float* norm_f32, const uint16_t* bias, cudaStream_t s) {
     GemvLaunch g;
@@ -903,7 +957,12 @@ struct LsModel {
     const bool sample = prof_on && (int)l == prof_layer();
     auto pb = [&](int cls, double b) { return sample ? prof_begin(cls, b, s) : -1; };
     int pi = pb(0, gemv_bytes(W.qkv, T, h + 2 * kv));
-    gemv(W.qkv, x, h, T, EPI_BIAS_STORE, qkv, h + 2 * kv, W.in_norm, nullptr, W.qkv_bias, s);
+    if (use_bg) {
+      launch_bt_prep(x, h, T, h, W.in_norm, nullptr, cfg.eps, bt_a, s);
+      bg(W.qkv, bt_a, T, EPI_BIAS_STORE, qkv, h + 2 * kv, nullptr, W.qkv_bias, s);
+    } else {
+      gemv(W.qkv, x, h, T, EPI_BIAS_STORE, qkv, h + 2 * kv, W.in_norm, nullptr, W.qkv_bias, s);
+    }
     prof_end(pi, s);
     AttnLaunch a;
     a.qkv = qkv;
@@ -929,8 +988,28 @@ struct LsModel {
     // attention bytes: new K/V rows written (f16) + q|k|v in and out (f32); the cached rows read are
     // added per replay from that pass's pos0 (prof_collect)
     pi = pb(1, (double)T * kv * 2 * 2 + (double)T * (h + 2 * kv) * 4 + (double)T * h * 4);
+    if (use_bg && attention_tc_supported(a)) {  // straight into the O GEMM's operand
+      int gn = 16, gg = 1;
+      bgemm_groups(T, &gn, &gg);
+      a.out_h = bt_a;
+      a.out_h_n = gn;
+    }
     launch_attention(a, s);
+    if (use_bg && !a.out_h) launch_bt_prep(attn, h, T, h, nullptr, nullptr, 0.f, bt_a, s);
     prof_end(pi, s);
+    if (use_bg) {
+      pi = pb(2, gemv_bytes(W.o, T, h) + (double)T * h * 4);
+      bg(W.o, bt_a, T, EPI_RESID, x, h, nullptr, nullptr, s);
+      prof_end(pi, s);
+      pi = pb(3, gemv_bytes(W.gu, T, I));
+      launch_bt_prep(x, h, T, h, W.post_norm, nullptr, cfg.eps, bt_a, s);
+      bg(W.gu, bt_a, T, EPI_SWIGLU_H, nullptr, 0, bt_h, nullptr, s);
+      prof_end(pi, s);
+      pi = pb(4, gemv_bytes(W.down, T, h) + (double)T * h * 4);
+      bg(W.down, bt_h, T, EPI_RESID, x, h, nullptr, nullptr, s);
+      prof_end(pi, s);
+      return;
+    }
     pi = pb(2, gemv_bytes(W.o, T, h) + (double)T * h * 4);
     gemv(W.o, attn, h, T, EPI_RESID, x, h, nullptr, nullptr, nullptr, s);
     prof_end(pi, s);
@@ -2426,6 +2505,20 @@ int ls_qgemv_device(const LsQWeights* w, const float* x_dev, uint64_t M, float* 
   });
 }
 
+int ls_aead_host(int seal, const uint8_t* key, const uint8_t* nonce, const uint8_t* aad, uint64_t aad_len, uint8_t* data,
+                 uint64_t len, uint64_t chunk_bytes, uint32_t first, uint8_t* tags, int iters, double* ms, int64_t* bad_chunk) {
+  return guard([&] {
+    NEED(key);
+    NEED(nonce);
+    NEED(tags);
+    if (len && !data) LS_THROW(LS_ERR_ARG, "data must not be NULL");
+    if (aad_len && !aad) LS_THROW(LS_ERR_ARG, "aad must not be NULL");
+    const int bad = aead_host(seal != 0, key, nonce, chunk_bytes != 0, first, aad, aad_len, data, len, chunk_bytes, tags, iters, ms);
+    if (bad_chunk) *bad_chunk = bad;
+    if (bad >= 0) LS_THROW(LS_ERR_IO, "authentication failed for chunk " + std::to_string(bad) + ": wrong key, or the data was modified");
+  });
+}
+
 int ls_qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t rows, uint64_t cols, const float* x_dev,
                           uint64_t M, float* y_dev, void* stream) {
   return guard([&] { qgemv_rows_noalloc(bits, group, rows_dev, rows, cols, x_dev, M, y_dev, reinterpret_cast<cudaStream_t>(stream)); });
@@ -2610,8 +2703,12 @@ void attention_host_impl(uint64_t heads, uint64_t kv_heads, uint64_t hd, float r
   auto* dtab = static_cast<int32_t*>(dmalloc(ctx_pages * 4));
   auto* dout = static_cast<float*>(dmalloc(M * H * 4));
   auto* drope = static_cast<float2*>(dmalloc(ctx * (hd / 2) * sizeof(float2)));
-  const int slots = (int)std::max<size_t>(1, std::min<size_t>(64, (ctx + 63) / 64));
-  auto* dpart = static_cast<float*>(dmalloc(heads * (size_t)slots * M * (hd + 2) * 4));
+  // context splits: up to one per 128-position chunk, at most 160 (two per SM for two kv heads)
+  // (the CUDA-core kernel, for head_dim 16 and 32, takes up to 16 slots of 64 positions)
+  const int slots = (int)std::max<size_t>(1, std::min<size_t>(160, (ctx + 127) / 128));
+  const int simt_slots = (int)std::min<size_t>(16, (ctx + 63) / 64);
+  const size_t part_floats = heads * (size_t)std::max(slots, simt_slots) * M * (hd + 2);
+  auto* dpart = static_cast<float*>(dmalloc(part_floats * 4));
   auto* dtick = static_cast<unsigned*>(dmalloc(heads * 4));
   auto* dctl = static_cast<Ctl*>(dmalloc(sizeof(Ctl)));
   LS_CUDA(cudaMemsetAsync(dtick, 0, heads * 4, st));
@@ -2635,39 +2732,103 @@ void attention_host_impl(uint64_t heads, uint64_t kv_heads, uint64_t hd, float r
   a.ctl = dctl;
   a.out = dout;
   a.part = dpart;
+  a.part_floats = part_floats;
   a.tickets = dtick;
   a.heads = (int)heads;
   a.kv_heads = (int)kv_heads;
   a.hd = (int)hd;
   a.max_ctx = (int)ctx;
   a.M = (int)M;
-  a.max_splits = slots;
+  a.max_splits = simt_slots;
   a.max_total = (int)(pos0 + M);
   a.err = &dctl->err;
+  // LS_ATT_TRACE=1 (profiling): the tensor-core kernel's per-CTA timeline of this launch, summarised
+  // on stderr as the median and maximum over CTAs of each step
+  const bool att_trace = getenv("LS_ATT_TRACE") != nullptr;
+  const size_t trace_ctas = (size_t)160 * kv_heads * ((heads / kv_heads * M + 127) / 128);
+  if (att_trace) {
+    a.trace = static_cast<unsigned*>(dmalloc(trace_ctas * AT_TRACE_SLOTS * 4));
+    LS_CUDA(cudaMemsetAsync(a.trace, 0, trace_ctas * AT_TRACE_SLOTS * 4, st));
+  }
   launch_attention(a, st);
+  if (att_trace) {
+    std::vector<unsigned> tr(trace_ctas * AT_TRACE_SLOTS);
+    LS_CUDA(cudaMemcpyAsync(tr.data(), a.trace, tr.size() * 4, cudaMemcpyDeviceToHost, st));
+    LS_CUDA(cudaStreamSynchronize(st));
+    int dev = 0, khz = 1;
+    LS_CUDA(cudaGetDevice(&dev));
+    LS_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev));
+    const char* names[] = {"loads issued + previous kernel", "Q staged", "chunk0 loads landed", "chunk0 scores",
+                           "chunk0 softmax", "chunk0 P.V + O", "chunk1 loads landed", "chunk1 scores",
+                           "chunk1 softmax", "chunk1 P.V + O"};
+    for (int k = 1; k <= 11; k++) {
+      if (k == 11) names[0] = "partials written";
+      std::vector<double> d;
+      for (size_t c = 0; c < trace_ctas; c++) {
+        const unsigned* t = &tr[c * AT_TRACE_SLOTS];
+        int prev = k == 11 ? (t[10] ? 10 : 6) : k - 1;
+        if (t[k] && t[prev]) d.push_back((double)(t[k] - t[prev]) / khz * 1e3);
+      }
+      if (d.empty()) continue;
+      std::sort(d.begin(), d.end());
+      fprintf(stderr, "attention trace %-32s ctas %4zu  median %7.3f us  max %7.3f us\n", names[k == 11 ? 0 : k - 1],
+              d.size(), d[d.size() / 2], d.back());
+    }
+    a.trace = nullptr;
+  }
   if (k_out) LS_CUDA(cudaMemcpyAsync(k_out, dk, pool_elems * 2, cudaMemcpyDeviceToHost, st));
   if (v_out) LS_CUDA(cudaMemcpyAsync(v_out, dv, pool_elems * 2, cudaMemcpyDeviceToHost, st));
   if (iters > 1) {
-    // every timed launch alone, after a 256 MB read that evicts L2 (K/V come from HBM) and leaves
-    // only clean lines behind
-    void* flush = dmalloc((size_t)256 << 20);
-    auto* sink = static_cast<unsigned*>(dmalloc(256 * 4));
-    LS_CUDA(cudaMemsetAsync(flush, 1, (size_t)256 << 20, st));
+    // Timing: back-to-back launches (one CUDA graph, so that host launch costs stay out), each over
+    // its own replica of the K/V pools, the replicas together at least 256 MB (twice L2), so that
+    // every launch reads its cached rows from HBM as a layer of a pass does; ms = the events' span /
+    // launches.
+    const size_t pool_bytes = pool_elems * 2;
+    const size_t reps = std::min<size_t>(4096, std::max<size_t>((size_t)iters, (((size_t)256 << 20) / (2 * pool_bytes)) + 1));
+    auto* rk = static_cast<uint8_t*>(dmalloc(reps * pool_bytes));
+    auto* rv = static_cast<uint8_t*>(dmalloc(reps * pool_bytes));
+    LS_CUDA(cudaMemcpyAsync(rk, dk, pool_bytes, cudaMemcpyDeviceToDevice, st));
+    LS_CUDA(cudaMemcpyAsync(rv, dv, pool_bytes, cudaMemcpyDeviceToDevice, st));
+    for (size_t have = 1; have < reps;) {  // doubling copies
+      const size_t n = std::min(have, reps - have);
+      LS_CUDA(cudaMemcpyAsync(rk + have * pool_bytes, rk, n * pool_bytes, cudaMemcpyDeviceToDevice, st));
+      LS_CUDA(cudaMemcpyAsync(rv + have * pool_bytes, rv, n * pool_bytes, cudaMemcpyDeviceToDevice, st));
+      have += n;
+    }
+    auto launch_rep = [&](size_t i) {
+      AttnLaunch r = a;
+      r.k_cache = reinterpret_cast<uint16_t*>(rk + i * pool_bytes);
+      r.v_cache = reinterpret_cast<uint16_t*>(rv + i * pool_bytes);
+      launch_attention(r, st);
+    };
+    cudaGraph_t graph;
+    LS_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    try {
+      for (size_t i = 0; i < reps; i++) launch_rep(i);
+    } catch (...) {
+      cudaStreamEndCapture(st, &graph);
+      throw;
+    }
+    LS_CUDA(cudaStreamEndCapture(st, &graph));
+    cudaGraphExec_t exec;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    LS_CUDA(ie);
+    struct ExecGuard {
+      cudaGraphExec_t e;
+      ~ExecGuard() { cudaGraphExecDestroy(e); }
+    } exec_guard{exec};
+    LS_CUDA(cudaGraphLaunch(exec, st));  // warm-up: every replica once
     cudaEvent_t e0, e1;
     LS_CUDA(cudaEventCreate(&e0));
     LS_CUDA(cudaEventCreate(&e1));
-    double total = 0;
-    for (int i = 0; i < iters; i++) {
-      launch_l2_evict(flush, (size_t)256 << 20, sink, st);
-      LS_CUDA(cudaEventRecord(e0, st));
-      launch_attention(a, st);
-      LS_CUDA(cudaEventRecord(e1, st));
-      LS_CUDA(cudaEventSynchronize(e1));
-      float t = 0;
-      LS_CUDA(cudaEventElapsedTime(&t, e0, e1));
-      total += t;
-    }
-    if (ms) *ms = total / iters;
+    LS_CUDA(cudaEventRecord(e0, st));
+    LS_CUDA(cudaGraphLaunch(exec, st));
+    LS_CUDA(cudaEventRecord(e1, st));
+    LS_CUDA(cudaEventSynchronize(e1));
+    float t = 0;
+    LS_CUDA(cudaEventElapsedTime(&t, e0, e1));
+    if (ms) *ms = (double)t / (double)reps;
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
   } else if (ms) {
@@ -2740,16 +2901,72 @@ int ls_qgemv_host(int bits, int group, const uint8_t* rows_raw, uint64_t rows, u
     qgemv_device(q.get(), dx, M, dy, 0);
     LS_CUDA(cudaDeviceSynchronize());
     if (iters > 1 && ms) {
+      // Timing: back-to-back launches (one CUDA graph), each over its own device replica of the
+      // weight planes, at least `iters` of them and together at least 256 MB (twice L2), so that
+      // every launch streams its weights from HBM; ms = the events' span / launches.
+      const size_t bytes = qmat_bytes((int)rows, (int)cols, WeightFormat{q->w.bits, q->w.group});
+      const size_t reps = std::min<size_t>(4096, std::max<size_t>((size_t)iters, ((size_t)256 << 20) / bytes + 1));
+      uint8_t* rep = nullptr;
+      LS_CUDA(cudaMalloc(&rep, reps * bytes));
+      std::unique_ptr<uint8_t, decltype(&cudaFree)> grep(rep, &cudaFree);
+      cudaStream_t st;
+      LS_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+      struct StreamGuard {
+        cudaStream_t s;
+        ~StreamGuard() {
+          cudaStreamSynchronize(s);
+          cudaStreamDestroy(s);
+        }
+      } sg{st};
+      const uint8_t* base = static_cast<const uint8_t*>(q->mem);
+      for (size_t i = 0; i < reps; i++)
+        LS_CUDA(cudaMemcpyAsync(rep + i * bytes, base, bytes, cudaMemcpyDeviceToDevice, st));
+      std::vector<LsQWeights> views(reps);
+      for (size_t i = 0; i < reps; i++) {  // the replica's planes at the same offsets (not owned)
+        LsQWeights& v = views[i];
+        v.device = q->device;
+        v.w = q->w;
+        v.w.data = rep + i * bytes + (q->w.data - base);
+        v.w.scales = reinterpret_cast<const uint16_t*>(rep + i * bytes + (reinterpret_cast<const uint8_t*>(q->w.scales) - base));
+        v.partial = q->partial;
+        v.tickets = q->tickets;
+        v.err = q->err;
+        v.num_sms = q->num_sms;
+      }
+      struct ViewGuard {  // the views own nothing
+        std::vector<LsQWeights>& v;
+        ~ViewGuard() {
+          for (auto& w : v) w.mem = w.partial = nullptr, w.tickets = nullptr, w.err = nullptr;
+        }
+      } vg{views};
+      cudaGraph_t graph;
+      LS_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      try {
+        for (size_t i = 0; i < reps; i++) qgemv_device(&views[i], dx, M, dy, st);
+      } catch (...) {
+        cudaStreamEndCapture(st, &graph);
+        throw;
+      }
+      LS_CUDA(cudaStreamEndCapture(st, &graph));
+      cudaGraphExec_t exec;
+      const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      LS_CUDA(ie);
+      struct ExecGuard {
+        cudaGraphExec_t e;
+        ~ExecGuard() { cudaGraphExecDestroy(e); }
+      } eg{exec};
+      LS_CUDA(cudaGraphLaunch(exec, st));  // warm-up
       cudaEvent_t a, b;
       LS_CUDA(cudaEventCreate(&a));
       LS_CUDA(cudaEventCreate(&b));
-      LS_CUDA(cudaEventRecord(a, 0));
-      for (int i = 0; i < iters; i++) qgemv_device(q.get(), dx, M, dy, 0);
-      LS_CUDA(cudaEventRecord(b, 0));
+      LS_CUDA(cudaEventRecord(a, st));
+      LS_CUDA(cudaGraphLaunch(exec, st));
+      LS_CUDA(cudaEventRecord(b, st));
       LS_CUDA(cudaEventSynchronize(b));
       float t = 0;
       LS_CUDA(cudaEventElapsedTime(&t, a, b));
-      *ms = t / iters;
+      *ms = (double)t / (double)reps;
       cudaEventDestroy(a);
       cudaEventDestroy(b);
     }

@@ -469,6 +469,42 @@ __device__ __forceinline__ void rms_stats(const long long* x, int T, int n, floa
   }
 }
 
+// The same statistics (same sums in the same order), the rows loaded into registers and kept in
+// shared memory as f32 (xs: [T][n]) together with the norm weights (wn: [n], from bf16 nb or f32
+// nf), so that the staging of every K slice of the phase reads shared memory only. Warp w takes
+// rows w, w + PK_NW, ...; lane l its column pairs l, l + 32, ..., loaded 16 at a time.
+__device__ __forceinline__ void rms_rows(const long long* x, int T, int n, float eps, float* s_inv, float* xs, float* wn,
+                                         const uint16_t* nb, const float* nf) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, np = n >> 1;
+  for (int c = threadIdx.x; c < n; c += PK_THREADS) wn[c] = nb ? bf16f(nb[c]) : nf[c];
+  for (int t = warp; t < T; t += PK_NW) {
+    const longlong2* r = reinterpret_cast<const longlong2*>(x + (size_t)t * n);
+    float2* o = reinterpret_cast<float2*>(xs + (size_t)t * n);
+    float ss = 0.f;
+    for (int p0 = 0; p0 < np; p0 += 32 * 16) {
+      longlong2 v[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        const int p = p0 + lane + 32 * k;
+        v[k] = p < np ? __ldcg(r + p) : make_longlong2(0, 0);
+      }
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        const int p = p0 + lane + 32 * k;
+        if (p < np) {
+          const float f0 = from_fix(v[k].x), f1 = from_fix(v[k].y);
+          o[p] = make_float2(f0, f1);
+          ss = fmaf(f0, f0, ss);
+          ss = fmaf(f1, f1, ss);
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) s_inv[t] = 1.0f / sqrtf(ss / (float)n + eps);
+  }
+  __syncthreads();
+}
+
 __device__ __forceinline__ void zero_ll(long long* p, size_t n) {
   for (size_t i = (size_t)blockIdx.x * PK_THREADS + threadIdx.x; i < n; i += (size_t)gridDim.x * PK_THREADS) p[i] = 0;
 }
@@ -794,6 +830,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   uint8_t* kvb = xb + a.kv_off;  // attention K/V tiles
   // the B operand and K/V regions are contiguous: the RMS statistics copy rows of x into both
   const size_t rms_bytes = (size_t)a.kv_off + pk_kv_smem(a.hd);
+  // or (a.xs) they keep the rows as f32 and the norm weights after the K/V region for the staging
+  float* xs = a.xs ? reinterpret_cast<float*>(kvb + pk_kv_smem(a.hd)) : nullptr;
+  float* wn = xs ? xs + (size_t)NT * h : nullptr;
   const uint32_t xb_addr = tc::su32(xb);
 
   if (threadIdx.x == 0) {
@@ -972,14 +1011,16 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
   for (int l = 0; l < a.L && ok; l++) {
     const PassLayer& W = a.layers[l];
     // ---- QKV: RMSNorm(x) -> q|k|v sums (+ bias once) ----
-    rms_stats(a.x, T, h, a.eps, s_inv, xb, rms_bytes);
+    if (xs) rms_rows(a.x, T, h, a.eps, s_inv, xs, wn, W.in_norm, nullptr);
+    else rms_stats(a.x, T, h, a.eps, s_inv, xb, rms_bytes);
     // cached K/V rows of this CTA's first attention item: they stream in during the QKV phase
     if ((int)blockIdx.x < a.heads * a.slots) attention_prefetch(a, pos0, l, blockIdx.x / a.slots, blockIdx.x % a.slots, kvb);
     gemv_phase(
         W.qkv, a.ks_qkv,
         [&](int col0, int ncol, uint32_t sbo) {
           stage_b<NT>(xb, sbo, T, col0, ncol, [&](int t, int c) {
-            return from_fix(ldcg_ll(a.x + (size_t)t * h + c)) * s_inv[t] * bf16f(W.in_norm[c]);
+            return xs ? xs[(size_t)t * h + c] * s_inv[t] * wn[c]
+                      : from_fix(ldcg_ll(a.x + (size_t)t * h + c)) * s_inv[t] * bf16f(W.in_norm[c]);
           });
         },
         [&](int r, int kslice, float (&tot)[NT]) {
@@ -1019,12 +1060,14 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     if (!barrier()) break;
 
     // ---- gate/up: RMSNorm(x) -> gate/up sums ----
-    rms_stats(a.x, T, h, a.eps, s_inv, xb, rms_bytes);
+    if (xs) rms_rows(a.x, T, h, a.eps, s_inv, xs, wn, W.post_norm, nullptr);
+    else rms_stats(a.x, T, h, a.eps, s_inv, xb, rms_bytes);
     gemv_phase(
         W.gu, a.ks_gu,
         [&](int col0, int ncol, uint32_t sbo) {
           stage_b<NT>(xb, sbo, T, col0, ncol, [&](int t, int c) {
-            return from_fix(ldcg_ll(a.x + (size_t)t * h + c)) * s_inv[t] * bf16f(W.post_norm[c]);
+            return xs ? xs[(size_t)t * h + c] * s_inv[t] * wn[c]
+                      : from_fix(ldcg_ll(a.x + (size_t)t * h + c)) * s_inv[t] * bf16f(W.post_norm[c]);
           });
         },
         [&](int r, int, float (&tot)[NT]) {
@@ -1064,12 +1107,14 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
       (&s_bv[0][0])[i] = -CUDART_INF_F;
       (&s_bi[0][0])[i] = 0xffffffffu;
     }
-    rms_stats(a.x + (size_t)r0 * h, n, h, a.eps, s_inv, xb, rms_bytes);
+    if (xs) rms_rows(a.x + (size_t)r0 * h, n, h, a.eps, s_inv, xs, wn, nullptr, a.final_norm);
+    else rms_stats(a.x + (size_t)r0 * h, n, h, a.eps, s_inv, xb, rms_bytes);
     gemv_phase(
         a.embed, 1,
         [&](int col0, int ncol, uint32_t sbo) {
           stage_b<NT>(xb, sbo, n, col0, ncol, [&](int t, int c) {
-            return from_fix(ldcg_ll(a.x + (size_t)(r0 + t) * h + c)) * s_inv[t] * a.final_norm[c];
+            return xs ? xs[(size_t)t * h + c] * s_inv[t] * wn[c]
+                      : from_fix(ldcg_ll(a.x + (size_t)(r0 + t) * h + c)) * s_inv[t] * a.final_norm[c];
           });
         },
         [&](int r, int, float (&tot)[NT]) {
@@ -1208,17 +1253,20 @@ size_t pass_kernel_kv_off(const WeightFormat& f, int T, int hidden, int inter, i
   return (b + 127) & ~(size_t)127;
 }
 
-size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, int stages) {
+// The x copy after the K/V region: [NT][hidden] f32 rows, then [hidden] f32 norm weights.
+size_t pass_kernel_xs_bytes(int T, int hidden) { return ((size_t)pass_kernel_nt(T) + 1) * hidden * 4; }
+
+size_t pass_kernel_smem(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, int stages, bool xs) {
   return 1024 + (size_t)stages * pass_stage_bytes(f) + pass_kernel_kv_off(f, T, hidden, inter, hd, ks_down) +
-         pk_kv_smem(hd);  // 1 KB for aligning the ring
+         pk_kv_smem(hd) + (xs ? pass_kernel_xs_bytes(T, hidden) : 0);  // 1 KB for aligning the ring
 }
 
 // The deepest weight ring (2 .. PK_MAX_STAGES stages) whose shared memory fits `budget` bytes; 0 if
 // none does. A deeper ring keeps more bytes in flight per SM (the LM head streams at the ring's
 // depth over the memory latency).
-int pass_kernel_stages(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, size_t budget) {
+int pass_kernel_stages(const WeightFormat& f, int T, int hidden, int inter, int hd, int ks_down, size_t budget, bool xs) {
   for (int st = PK_MAX_STAGES; st >= 2; st--)
-    if (pass_kernel_smem(f, T, hidden, inter, hd, ks_down, st) <= budget) return st;
+    if (pass_kernel_smem(f, T, hidden, inter, hd, ks_down, st, xs) <= budget) return st;
   return 0;
 }
 

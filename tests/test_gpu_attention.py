@@ -50,7 +50,8 @@ def reference(heads, kvh, hd, pos0, qkv, kc, vc):
 
 
 @pytest.mark.parametrize("heads,kvh,hd,pos0,M", [(14, 2, 64, 0, 9), (14, 2, 64, 100, 1), (14, 2, 64, 700, 9),
-                                                 (16, 2, 128, 300, 5), (4, 2, 16, 65, 33), (14, 2, 64, 4000, 16)])
+                                                 (16, 2, 128, 300, 5), (4, 2, 16, 65, 33), (14, 2, 64, 4000, 16),
+                                                 (14, 2, 64, 20000, 9), (16, 2, 128, 9000, 3)])
 def test_attention_kernel_matches_float64_restatement(heads, kvh, hd, pos0, M):
     import layerstream_b200 as ls
 
@@ -61,6 +62,21 @@ def test_attention_kernel_matches_float64_restatement(heads, kvh, hd, pos0, M):
     got, _ = ls.attention(heads, kvh, hd, pos0, qkv, kc, vc)
     want = reference(heads, kvh, hd, pos0, qkv, kc, vc)
     assert np.max(np.abs(got - want)) < 2e-4 * (1 + np.max(np.abs(want)))
+
+
+def test_timed_attention_over_cache_replicas_returns_the_same_output():
+    """The timing loop runs the kernel over replicas of the cache: the output stays the untimed one."""
+    import layerstream_b200 as ls
+
+    heads, kvh, hd, pos0, M = 14, 2, 64, 3000, 9
+    rng = np.random.default_rng(11)
+    qkv = rng.standard_normal((M, (heads + 2 * kvh) * hd)).astype(np.float32)
+    kc = rng.standard_normal((kvh, pos0, hd)).astype(np.float16)
+    vc = rng.standard_normal((kvh, pos0, hd)).astype(np.float16)
+    once, _ = ls.attention(heads, kvh, hd, pos0, qkv, kc, vc)
+    timed, ms = ls.attention(heads, kvh, hd, pos0, qkv, kc, vc, iters=4)
+    assert ms > 0
+    np.testing.assert_array_equal(once, timed)
 
 
 def test_attention_rejects_bad_shapes():

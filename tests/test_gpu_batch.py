@@ -73,6 +73,27 @@ def test_each_sequence_of_a_batch_decodes_as_it_would_alone(tiny, body):
         b.close()
 
 
+@pytest.mark.parametrize("body", [(8, 32), (4, 32)])
+def test_sixty_four_sequences_decode_as_they_would_alone(tiny, body):
+    # 64 sequences x 5 verify rows = 320 rows: two token groups of 160, the batched GEMM's large-group
+    # plan (int8: one MMA issuer, four tensor-memory A buffers) in every projection and the head
+    # (tokens must equal the CPU path's up to its first near tie, where the streams may diverge)
+    p = tiny[body]
+    prompts = [[(11 * i + 17 * s + 3) % 600 for i in range(6)] for s in range(64)]
+    b = ls.Batch(ls.Model(p, max_ctx=128), 64, max_ctx=64, max_block=5)
+    got, _ = b.spec(np.array(prompts, np.uint32), 8, 4)
+    checked = 0
+    for pr, g in zip(prompts, got):
+        toks, margins = cpu_greedy_with_margins(p, pr, 8)
+        for i, (t, mg) in enumerate(zip(toks, margins)):
+            if mg <= TOL:
+                break
+            assert g[i] == t, (pr, i)
+            checked += 1
+    assert checked >= 64
+    b.close()
+
+
 def test_batch_tokens_match_the_cpu_path_where_margins_allow(tiny):
     p = tiny[(4, 32)]
     b = ls.Batch(ls.Model(p, max_ctx=128), len(PROMPTS), max_ctx=64, max_block=5)
