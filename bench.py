@@ -79,6 +79,9 @@ def parse():
     ap.add_argument("--tp", action="store_true",
                     help="config 5 (b): the resident model split tensor-parallel over the launched ranks (NCCL), "
                          "instead of 2-slot streaming per GPU")
+    ap.add_argument("--sealed", action="store_true",
+                    help="config 5 (streaming): the model sealed (ChaCha20-Poly1305, src/seal.rs) and streamed from the "
+                         "sealed file, each layer block opened on the GPU after its host-to-device copy")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-sample-tokens", type=int, default=0, help="decode tokens per CPU sample (0: auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -569,7 +572,18 @@ def batch_bench(args, cfg):
     B, plen, max_new, k = cfg["batch"], cfg["prompt"], cfg["max_new"], cfg["k"]
     tp = bool(args.tp and cfg.get("stream_slots"))
     slots = None if tp else cfg.get("stream_slots")
-    if slots:
+    sealed = bool(args.sealed and slots)
+    if sealed:
+        # the bench model sealed once with the reference's default chunking (1 MiB layer chunks,
+        # 512-row table chunks) under a fixed bench key; the file is reused between runs
+        key = bytes(range(32))
+        spath = path[:-4] + ".sealed"
+        if rank == 0 and not os.path.exists(spath):
+            ls.seal_model(path, spath + ".tmp", key, b"benchsea", device=local)
+            os.replace(spath + ".tmp", spath)
+        barrier(dist)
+        model = ls.Model(spath, device=local, max_ctx=plen + 64, mode="stream", slots=slots, key=key)
+    elif slots:
         model = ls.Model(path, device=local, max_ctx=plen + 64, mode="stream", slots=slots)
     else:
         model = ls.Model(path, device=local, max_ctx=plen + 64)
@@ -657,7 +671,12 @@ def batch_bench(args, cfg):
                             "peak_source": "nominal PCIe 5.0 x16", "traffic": None,
                             "algorithmic_bytes_per_launch": info.weight_bytes, "avg_launch_us": pass_s * 1e6}
         line["config"]["workload"] = (f"config5: 3b Qwen2 random-init int4 g32, {B} sequences, {plen}-token prompts, "
-                                      f"{max_new} new tokens, k={k}, lookup drafter, {slots}-slot layer streaming from pinned host")
+                                      f"{max_new} new tokens, k={k}, lookup drafter, {slots}-slot layer streaming from pinned host"
+                                      + (", sealed file (ChaCha20-Poly1305 1 MiB chunks, opened on the GPU after each copy)"
+                                         if sealed else ""))
+        if sealed:
+            line["sealed"] = {"cipher": "ChaCha20-Poly1305 (RFC 8439), chunks opened on the GPU", "layer_chunk": 1 << 20,
+                              "embed_chunk_rows": 512}
         line["config"]["config"] = 5
         line["dtype"] = dtype_note(4)
     if tp:

@@ -132,6 +132,23 @@ int ls_last_error(char *buf, size_t cap);
  * max_ctx: KV-cache capacity in tokens, reserved up front (src/model.rs:67-68). */
 int ls_model_open(const char *lsq_path, int device, uint64_t max_ctx, int mode, int slots, LsModel **out);
 int ls_model_free(LsModel *m);
+
+/* A sealed model file (src/seal.rs: SealedSource::open + ResidentProvider::load / StreamProvider):
+ * ChaCha20-Poly1305 per chunk, key = 32 bytes. The ciphertext is copied to the GPU and opened
+ * there (tags checked, then decrypted) before the weights are repacked: resident mode opens every
+ * chunk once at load; stream mode opens each layer block in its HBM slot on every pass (the
+ * embedding table is opened once, into the pinned host copy the passes read). Opening checks the
+ * key on the final norm's chunk (LS_ERR_IO: "authentication failed", as src/seal.rs:894-902); a
+ * modified chunk fails the load (resident) or the pass that streams it (LS_ERR_IO). */
+int ls_model_open_sealed(const char *path, const uint8_t *key, int device, uint64_t max_ctx, int mode, int slots,
+                         LsModel **out);
+/* seal_model (src/seal.rs:726-827): seals the model at src (a .lsq file or a bf16 model directory)
+ * into a new file out_path (which must not exist) under key (32 bytes) and nonce_prefix (8 bytes),
+ * layer blocks cut into layer_chunk-byte chunks and the table into embed_chunk_rows-row chunks
+ * (the reference's defaults: 1 MiB and 512), the cipher run on GPU `device`. The file is
+ * byte-identical to the reference's for the same inputs. *n_chunks (optional): chunks written. */
+int ls_seal_model(const char *src, const char *out_path, const uint8_t *key, const uint8_t *nonce_prefix,
+                  uint64_t layer_chunk, uint64_t embed_chunk_rows, int device, uint64_t *n_chunks);
 int ls_model_info(const LsModel *m, LsModelInfo *out);
 int ls_model_report(const LsModel *m, LsReport *out);
 

@@ -69,6 +69,9 @@ _SIGS = {
     "ls_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
     "ls_model_open": (C.c_int, [C.c_char_p, C.c_int, C.c_uint64, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
     "ls_model_free": (C.c_int, [C.c_void_p]),
+    "ls_model_open_sealed": (C.c_int, [C.c_char_p, C.c_void_p, C.c_int, C.c_uint64, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "ls_seal_model": (C.c_int, [C.c_char_p, C.c_char_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_int,
+                                C.POINTER(C.c_uint64)]),
     "ls_model_info": (C.c_int, [C.c_void_p, C.POINTER(ModelInfo)]),
     "ls_model_report": (C.c_int, [C.c_void_p, C.POINTER(Report)]),
     "ls_model_stream": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
@@ -157,10 +160,16 @@ class Model:
     """``model::Model`` (src/model.rs) backed by CUDA: a `.lsq` model resident in HBM or streamed
     through ``slots`` HBM layer slots from pinned host memory."""
 
-    def __init__(self, path: str, device: int = 0, max_ctx: int = 1024, mode: str = "resident", slots: int = 2):
+    def __init__(self, path: str, device: int = 0, max_ctx: int = 1024, mode: str = "resident", slots: int = 2,
+                 key: bytes = None):
+        """key: the 32-byte key of a sealed file (bytes, or 64 hex digits; src/seal.rs:422-440)."""
         h = C.c_void_p()
         md = {"resident": MODE_RESIDENT, "stream": MODE_STREAM}[mode]
-        _check(lib().ls_model_open(str(path).encode(), device, max_ctx, md, slots, C.byref(h)))
+        if key is None:
+            _check(lib().ls_model_open(str(path).encode(), device, max_ctx, md, slots, C.byref(h)))
+        else:
+            k = _bytes_arr(_key_bytes(key), 32)
+            _check(lib().ls_model_open_sealed(str(path).encode(), _p(k), device, max_ctx, md, slots, C.byref(h)))
         self._h = h
         info = self.info
         self.vocab = info.vocab
@@ -440,6 +449,23 @@ def aead_open(key: bytes, nonce: bytes, aad: bytes, data: bytes, tags, chunk_byt
     _check(lib().ls_aead_host(0, _p(k), _p(nn), _p(a), len(aad), _p(buf), len(data), chunk_bytes, first, _p(t), 1,
                               C.byref(ms), C.byref(bad)))
     return buf.tobytes()
+
+
+def _key_bytes(key) -> bytes:
+    if isinstance(key, str):
+        key = bytes.fromhex(key.strip())
+    return bytes(key)
+
+
+def seal_model(src: str, out: str, key, nonce_prefix: bytes, layer_chunk: int = 1 << 20, embed_chunk_rows: int = 512,
+               device: int = 0) -> int:
+    """seal_model (src/seal.rs:726-827) with the cipher on the GPU: src is a .lsq file or a bf16
+    model directory, out a new file. Returns the number of chunks."""
+    k, p = _bytes_arr(_key_bytes(key), 32), _bytes_arr(bytes(nonce_prefix), 8)
+    n = C.c_uint64()
+    _check(lib().ls_seal_model(str(src).encode(), str(out).encode(), _p(k), _p(p), layer_chunk, embed_chunk_rows, device,
+                               C.byref(n)))
+    return n.value
 
 
 def _bytes_arr(b: bytes, n: int) -> np.ndarray:

@@ -488,6 +488,15 @@ std::string sealed_header_json(const std::string& config_text, const LayerLayout
          ",\"layer_layout\":[" + ranges + "]}";
 }
 
+bool is_sealed_file(const std::string& path) {
+  const int fd = ::open(path.c_str(), O_RDONLY);
+  if (fd < 0) return false;
+  char m[4] = {0, 0, 0, 0};
+  const ssize_t r = ::pread(fd, m, 4, 0);
+  ::close(fd);
+  return r == 4 && std::memcmp(m, "LSS1", 4) == 0;
+}
+
 // src/seal.rs:13-27 (layout), 593-627 (SealedLayout::from_json), 860-903 (SealedSource::open)
 SealedFile SealedFile::open(const std::string& path) {
   Fd f(path);

@@ -112,6 +112,11 @@ struct SealedFile {
 };
 std::string sealed_header_json(const std::string& config_text, const LayerLayout& layout, size_t layer_chunk,
                                size_t embed_chunk_rows, size_t final_norm_bytes);
+bool is_sealed_file(const std::string& path);  // starts with the magic bytes "LSS1"
+// Seals the model at src (a .lsq file or a bf16 safetensors directory) into a new file at out
+// (src/seal.rs:726-827, seal_model), the cipher on the GPU; returns the number of chunks.
+size_t seal_model_file(const std::string& src, const std::string& out, const uint8_t* key, const uint8_t* nonce_prefix,
+                       size_t layer_chunk, size_t embed_chunk_rows);
 
 std::string inject_quant(const std::string& config_text, WeightFormat body, WeightFormat embed);
 std::string lsq_header_bytes(const std::string& config_text, size_t layer_bytes, size_t embed_bytes, size_t norm_bytes);
@@ -307,7 +312,11 @@ struct BgemmLaunch {
   float* partial = nullptr;     // split-K scratch
   unsigned* tickets = nullptr;
   int* err = nullptr;
+  // profiling: clock() stamps of pipeline events of CTA (0, 0, 0), [kind 0..7][K block 0..63], then
+  // every CTA's start and end at BG_TRACE_CTA + 2 * cta; null = off
+  unsigned* trace = nullptr;
 };
+constexpr int BG_TRACE_CTA = 8 * 64;
 struct BgemmPlan {
   int N = 16, ngroups = 1, ks = 1, stages = 2, kstage = 1, tmem_cols = 256;
   int abuf = 4, niss = 2;  // A buffers in tensor memory (2 or 4); MMA issuers, each with its own accumulator (1 or 2)

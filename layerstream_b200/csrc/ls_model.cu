@@ -235,6 +235,20 @@ struct LsModel {
   std::vector<cudaEvent_t> ev_loaded, ev_free;
   size_t raw_slot_bytes = 0;
 
+  // sealed files (src/seal.rs): the ciphertext is copied to the device and opened there (tags
+  // checked, then decrypted) before it is repacked; a failed tag leaves *d_bad = chunk + 1
+  bool sealed = false;
+  SealedFile sfile;
+  uint32_t* d_key = nullptr;         // the 32-byte key
+  uint8_t* d_aad = nullptr;          // frame + header, the associated data's shared prefix
+  AeadChunk* d_layer_desc = nullptr; // stream mode: the messages of layer l in raw slot s, [l][s][chunk]
+  AeadChunk* d_desc_stage[2] = {nullptr, nullptr};  // resident load / one-off opens: per staging buffer
+  AeadChunk* h_desc_stage[2] = {nullptr, nullptr};
+  size_t desc_stage_cap = 0;
+  void* aead_scr = nullptr;
+  size_t aead_scr_bytes = 0;
+  int* d_bad = nullptr;
+
   // cache, tables and activations
   uint16_t *kc = nullptr, *vc = nullptr;  // page pools of every layer, kv_layer elements apart
   size_t kv_layer = 0;
@@ -385,7 +399,61 @@ struct LsModel {
     launch_repack(e, dst.bits, dst.group, dst.cols, d, sc, pad32(rows), s);
   }
 
-  void open(const char* path, int dev, uint64_t mctx, int md, int nslots) {
+  // The AEAD message of sealed chunk idx over len device bytes at data (src/seal.rs:341-350).
+  AeadChunk sealed_chunk(size_t idx, uint8_t* data, uint64_t len) const {
+    AeadChunk c{};
+    c.data = data;
+    c.len = len;
+    std::memcpy(c.nonce, sfile.nonce_prefix, 8);
+    c.nonce[2] = (uint32_t)idx;
+    c.tail = (uint32_t)idx;
+    c.tail_len = 4;
+    std::memcpy(c.tag, &sfile.tags[16 * idx], 16);
+    return c;
+  }
+  // Opens, on stream s, the sealed chunks first_chunk.. that make up the n plaintext bytes copied to
+  // data (chunks of clen bytes, the last one shorter), through staging descriptor set k (the caller
+  // has waited for the last step that used set k).
+  void open_range(int k, size_t first_chunk, uint8_t* data, uint64_t n, uint64_t clen, cudaStream_t s) {
+    const size_t nch = (size_t)((n + clen - 1) / clen);
+    if (nch > desc_stage_cap) LS_THROW(-1, "sealed open: too many chunks in one step");
+    for (size_t i = 0; i < nch; i++)
+      h_desc_stage[k][i] = sealed_chunk(first_chunk + i, data + i * clen, std::min<uint64_t>(clen, n - i * clen));
+    LS_CUDA(cudaMemcpyAsync(d_desc_stage[k], h_desc_stage[k], nch * sizeof(AeadChunk), cudaMemcpyHostToDevice, s));
+    launch_aead(d_desc_stage[k], (int)nch, clen, d_aad, (uint32_t)sfile.aad_prefix.size(), d_key, false, aead_scr, aead_scr_bytes,
+                d_bad, s);
+  }
+  // Throws when a sealed chunk failed its tag (a wrong key, or a modified file).
+  void sealed_check() const {
+    if (!sealed) return;
+    int b = 0;
+    LS_CUDA(cudaMemcpy(&b, d_bad, 4, cudaMemcpyDeviceToHost));
+    if (b != 0x7fffffff)
+      LS_THROW(LS_ERR_IO, "authentication failed for chunk " + std::to_string(b - 1) + ": wrong key, or the file was modified");
+  }
+  // Device state of a sealed model: key, associated data, descriptor staging, scratch, error word.
+  void setup_sealed(const uint8_t* key, size_t embed_step_rows) {
+    d_key = dalloc<uint32_t>(8);
+    LS_CUDA(cudaMemcpy(d_key, key, 32, cudaMemcpyHostToDevice));
+    d_aad = dalloc<uint8_t>(sfile.aad_prefix.size());
+    LS_CUDA(cudaMemcpy(d_aad, sfile.aad_prefix.data(), sfile.aad_prefix.size(), cudaMemcpyHostToDevice));
+    const size_t rb = cfg.embed_row_bytes(), ecr = sfile.embed_chunk_rows;
+    desc_stage_cap = std::max<size_t>({sfile.layer_chunks(), (embed_step_rows + ecr - 1) / ecr, 1});
+    for (int k = 0; k < 2; k++) {
+      d_desc_stage[k] = dalloc<AeadChunk>(desc_stage_cap);
+      h_desc_stage[k] = halloc<AeadChunk>(desc_stage_cap);
+    }
+    const uint32_t al = (uint32_t)sfile.aad_prefix.size();
+    aead_scr_bytes = std::max({aead_scratch_bytes((int)sfile.layer_chunks() * std::max(1, slots), sfile.layer_chunk, al),
+                               aead_scratch_bytes((int)desc_stage_cap, ecr * rb, al),
+                               aead_scratch_bytes(1, sfile.final_norm_bytes, al)});
+    aead_scr = dalloc<uint8_t>(aead_scr_bytes);
+    d_bad = dalloc<int>(1);
+    const int big = 0x7fffffff;
+    LS_CUDA(cudaMemcpy(d_bad, &big, 4, cudaMemcpyHostToDevice));
+  }
+
+  void open(const char* path, int dev, uint64_t mctx, int md, int nslots, const uint8_t* key = nullptr) {
     struct stat stt;
     const bool dir = ::stat(path, &stt) == 0 && S_ISDIR(stt.st_mode);
     std::string data_path = path;
@@ -404,7 +472,26 @@ struct LsModel {
       layer_off = st.layer_start;
       data_path = st.file;
       if (md != LS_MODE_RESIDENT) LS_THROW(LS_ERR_ARG, "streaming reads quantized (.lsq) files; open a bf16 model resident");
+    } else if (is_sealed_file(path)) {
+      // a sealed file (src/seal.rs:860-903): the plaintext's layers, table and norm lie at ct_base
+      if (!key) LS_THROW(LS_ERR_ARG, "a sealed model needs its key (ls_model_open_sealed)");
+      sfile = SealedFile::open(path);
+      sealed = true;
+      file = LsqFile();
+      file.path = path;
+      file.config_text = sfile.config_text;
+      file.cfg = sfile.cfg;
+      file.layout = sfile.layout;
+      file.data_start = sfile.ct_base;
+      file.embed_start = sfile.ct_base + sfile.embed_plain_off();
+      file.norm_start = file.embed_start + sfile.embed_bytes();
+      file.embed_bytes = sfile.embed_bytes();
+      file.norm_bytes = sfile.final_norm_bytes;
+      for (size_t l = 0; l < file.cfg.layers; l++) layer_off.push_back(sfile.ct_base + l * file.layout.total);
+      if (!file.cfg.format.quant() && md != LS_MODE_RESIDENT)
+        LS_THROW(LS_ERR_ARG, "streaming reads quantized weights; open a sealed bf16 model resident");
     } else {
+      if (key) LS_THROW(LS_ERR_ARG, "a key was given for a file that is not sealed");
       file = LsqFile::open(path);
       for (size_t l = 0; l < file.cfg.layers; l++) layer_off.push_back(file.data_start + l * file.layout.total);
     }
@@ -430,9 +517,25 @@ struct LsModel {
       ~FdGuard() { ::close(fd); }
     } guard{fd};
 
+    // sealed: embedding rows are opened in whole chunks, so a load step takes a multiple of them
+    size_t embed_step = std::min<size_t>(kHeadRows, V);
+    if (sealed) {
+      const size_t ecr = sfile.embed_chunk_rows;
+      embed_step = std::min(V, ecr >= kHeadRows ? ecr : kHeadRows / ecr * ecr);
+      setup_sealed(key, embed_step);
+    }
+
     // final norm (src/weights.rs:408-411): bf16 -> f32, resident in both modes
     std::vector<uint16_t> nb(h);
     pread_all(fd, nb.data(), h * 2, file.norm_start);
+    if (sealed) {  // opening the norm's chunk checks the key up front (src/seal.rs:894-902)
+      uint8_t* dn = dalloc<uint8_t>(h * 2);
+      LS_CUDA(cudaMemcpyAsync(dn, nb.data(), h * 2, cudaMemcpyHostToDevice, stream));
+      open_range(0, sfile.final_chunk(), dn, h * 2, h * 2, stream);
+      LS_CUDA(cudaMemcpyAsync(nb.data(), dn, h * 2, cudaMemcpyDeviceToHost, stream));
+      LS_CUDA(cudaStreamSynchronize(stream));
+      sealed_check();
+    }
     std::vector<float> nf(h);
     for (size_t i = 0; i < h; i++) {
       uint32_t u = (uint32_t)nb[i] << 16;
@@ -450,7 +553,7 @@ struct LsModel {
       for (size_t l = 0; l < L; l++) layers.push_back(carve_layer(p));
       embed = carve(p, (int)V, (int)h, cfg.embed_format);
       // load through two pinned staging buffers and one device raw buffer
-      const size_t chunk_rows = std::min<size_t>(kHeadRows, V);
+      const size_t chunk_rows = embed_step;
       const size_t stage = std::max(lt, chunk_rows * rb);
       uint8_t* hst[2] = {halloc<uint8_t>(stage), halloc<uint8_t>(stage)};
       uint8_t* raw[2] = {dalloc<uint8_t>(stage), dalloc<uint8_t>(stage)};
@@ -469,12 +572,21 @@ struct LsModel {
         k ^= 1;
       };
       for (size_t l = 0; l < L; l++)
-        step(layer_off[l], lt, [&](const uint8_t* r) { repack_layer(r, layers[l], stream); });
+        step(layer_off[l], lt, [&](const uint8_t* r) {
+          if (sealed) open_range(k, l * sfile.layer_chunks(), const_cast<uint8_t*>(r), lt, sfile.layer_chunk, stream);
+          repack_layer(r, layers[l], stream);
+        });
       for (size_t first = 0; first < V; first += chunk_rows) {
         const size_t rows = std::min(chunk_rows, V - first);
-        step(file.embed_start + first * rb, rows * rb, [&](const uint8_t* r) { repack_embed_rows(r, (int)first, (int)rows, embed, stream); });
+        step(file.embed_start + first * rb, rows * rb, [&](const uint8_t* r) {
+          if (sealed)
+            open_range(k, sfile.embed_first_chunk() + first / sfile.embed_chunk_rows, const_cast<uint8_t*>(r), rows * rb,
+                       sfile.embed_chunk_rows * rb, stream);
+          repack_embed_rows(r, (int)first, (int)rows, embed, stream);
+        });
       }
       LS_CUDA(cudaStreamSynchronize(stream));
+      sealed_check();
       cudaEventDestroy(done[0]);
       cudaEventDestroy(done[1]);
     } else {
@@ -488,7 +600,7 @@ struct LsModel {
       LS_CUDA(cudaHostGetDevicePointer(&dp, host_model + (file.embed_start - file.data_start), 0));
       host_embed_dev = reinterpret_cast<const uint8_t*>(dp);
       const size_t chunk_rows = std::min<size_t>(kHeadRows, V);
-      raw_slot_bytes = std::max(lt, chunk_rows * rb);
+      raw_slot_bytes = std::max({lt, chunk_rows * rb, sealed ? embed_step * rb : (size_t)0});
       // a slot holds either a layer or a head chunk, so their planes share one region
       const size_t per = std::max(layer_plane_bytes(), qmat_bytes((int)chunk_rows, (int)h, cfg.embed_format));
       for (int s = 0; s < slots; s++) {
@@ -504,6 +616,31 @@ struct LsModel {
         ev_free.push_back(b);
       }
       resident_weight_bytes = (size_t)slots * (raw_slot_bytes + per);
+      if (sealed) {
+        // layer blocks stay sealed in host memory and are opened in their raw slot on every pass:
+        // the messages of layer l in slot s, fixed for the model's life
+        const size_t lc = sfile.layer_chunks();
+        std::vector<AeadChunk> desc(L * slots * lc);
+        for (size_t l = 0; l < L; l++)
+          for (int s = 0; s < slots; s++)
+            for (size_t c = 0; c < lc; c++)
+              desc[(l * slots + s) * lc + c] = sealed_chunk(l * lc + c, raw_slot[s] + c * sfile.layer_chunk,
+                                                            std::min<uint64_t>(sfile.layer_chunk, lt - c * sfile.layer_chunk));
+        d_layer_desc = dalloc<AeadChunk>(desc.size());
+        LS_CUDA(cudaMemcpy(d_layer_desc, desc.data(), desc.size() * sizeof(AeadChunk), cudaMemcpyHostToDevice));
+        // the embedding table is opened once, in place in host memory: the input rows and the LM
+        // head chunks of every pass read it from there
+        uint8_t* he = host_model + (file.embed_start - file.data_start);
+        for (size_t first = 0; first < V; first += embed_step) {
+          const size_t rows = std::min(embed_step, V - first);
+          LS_CUDA(cudaMemcpyAsync(raw_slot[0], he + first * rb, rows * rb, cudaMemcpyHostToDevice, stream));
+          open_range(0, sfile.embed_first_chunk() + first / sfile.embed_chunk_rows, raw_slot[0], rows * rb,
+                     sfile.embed_chunk_rows * rb, stream);
+          LS_CUDA(cudaMemcpyAsync(he + first * rb, raw_slot[0], rows * rb, cudaMemcpyDeviceToHost, stream));
+          LS_CUDA(cudaStreamSynchronize(stream));
+        }
+        sealed_check();
+      }
     }
 
     // K/V cache: per layer a pool [kv_heads][pages][page][hd] f16 (src/model.rs:67-68 reserves the
@@ -1089,6 +1226,11 @@ struct LsModel {
       const int s = (int)(it % slots);
       LS_CUDA(cudaStreamWaitEvent(cs, ev_loaded[s], 0));
       if (it < L) {
+        if (sealed) {  // open the layer's chunks in the slot (src/seal.rs:977-986)
+          const size_t lc = sfile.layer_chunks();
+          launch_aead(d_layer_desc + (it * slots + s) * lc, (int)lc, sfile.layer_chunk, d_aad, (uint32_t)sfile.aad_prefix.size(),
+                      d_key, false, aead_scr, aead_scr_bytes, d_bad, cs);
+        }
         repack_layer(raw_slot[s], layers[s], cs);
         LS_CUDA(cudaEventRecord(ev_free[s], cs));  // the raw slot may be refilled now
         layer_fn(layers[s], it);
@@ -1169,6 +1311,7 @@ struct LsModel {
     d2h_bytes += sizeof(Ctl) - offsetof(Ctl, argmax);
     LS_CUDA(cudaStreamSynchronize(stream));
     prof_collect();
+    if (mode != LS_MODE_RESIDENT) sealed_check();
     if (ctl_host->err == 1) LS_THROW(LS_ERR_DEVICE, "a tensor-core kernel gave up waiting on an mbarrier (bounded wait)");
     if (ctl_host->err == 3) LS_THROW(LS_ERR_DEVICE, "the pass kernel gave up waiting at a grid barrier (bounded wait)");
     if (ctl_host->err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
@@ -1977,6 +2120,7 @@ struct LsBatch {
     if (head_mode) d2h_bytes += 2 * ns * 4;
     LS_CUDA(cudaStreamSynchronize(stream));
     if (prof_on) prof_collect();
+    if (m->mode != LS_MODE_RESIDENT) m->sealed_check();
     passes++;
     inject_err = 0;
     if (*h_err) tp_failed = tp;
@@ -2309,6 +2453,32 @@ int ls_model_open(const char* path, int device, uint64_t max_ctx, int mode, int 
     std::unique_ptr<LsModel> m(new LsModel);
     m->open(path, device, max_ctx, mode, slots);
     *out = m.release();
+  });
+}
+
+int ls_model_open_sealed(const char* path, const uint8_t* key, int device, uint64_t max_ctx, int mode, int slots, LsModel** out) {
+  return guard([&] {
+    NEED(path);
+    NEED(key);
+    NEED(out);
+    *out = nullptr;
+    if (!is_sealed_file(path)) LS_THROW(LS_ERR_IO, std::string(path) + ": not a sealed layerstream model (bad magic bytes)");
+    std::unique_ptr<LsModel> m(new LsModel);
+    m->open(path, device, max_ctx, mode, slots, key);
+    *out = m.release();
+  });
+}
+
+int ls_seal_model(const char* src, const char* out_path, const uint8_t* key, const uint8_t* nonce_prefix, uint64_t layer_chunk,
+                  uint64_t embed_chunk_rows, int device, uint64_t* n_chunks) {
+  return guard([&] {
+    NEED(src);
+    NEED(out_path);
+    NEED(key);
+    NEED(nonce_prefix);
+    LS_CUDA(cudaSetDevice(device));
+    const size_t n = seal_model_file(src, out_path, key, nonce_prefix, layer_chunk, embed_chunk_rows);
+    if (n_chunks) *n_chunks = n;
   });
 }
 
@@ -3024,6 +3194,43 @@ int ls_bgemm_host(int bits, int group, const uint8_t* rows_raw, uint64_t rows, u
     g.err = derr;
     launch_bgemm(g, p, 0);
     LS_CUDA(cudaDeviceSynchronize());
+    if (getenv("LS_BG_TRACE")) {
+      // profiling: one more launch with the pipeline timeline, summarised on stderr (CTA 0's events
+      // per K block relative to its start; every CTA's duration)
+      const int ctas = ((q->w.rows_pad / 32 + 3) / 4) * p.ngroups * p.ks;
+      auto* dtr = static_cast<unsigned*>(dal(((size_t)BG_TRACE_CTA + 2 * ctas) * 4));
+      BgemmLaunch gt = g;
+      gt.trace = dtr;
+      launch_bgemm(gt, p, 0);
+      LS_CUDA(cudaDeviceSynchronize());
+      std::vector<unsigned> tr((size_t)BG_TRACE_CTA + 2 * ctas);
+      LS_CUDA(cudaMemcpy(tr.data(), dtr, tr.size() * 4, cudaMemcpyDeviceToHost));
+      int khz = 1;
+      LS_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev));
+      const unsigned t0 = tr[BG_TRACE_CTA];
+      fprintf(stderr, "bgemm trace: N %d groups %d ks %d stages %d kstage %d abuf %d issuers %d tmem %d smem %zu\n", p.N,
+              p.ngroups, p.ks, p.stages, p.kstage, p.abuf, p.niss, p.tmem_cols, p.smem);
+      const char* kinds[] = {"produced", "A written", "MMAs issued", "data seen", "A store", "A stored", "issuer waits"};
+      for (int kb = 0; kb < 64; kb++) {
+        bool any = false;
+        char line[512];
+        int o = std::snprintf(line, sizeof line, "  block %2d:", kb);
+        for (int k = 0; k < 7; k++) {
+          const unsigned t = tr[k * 64 + kb];
+          if (!t) continue;
+          any = true;
+          o += std::snprintf(line + o, sizeof line - o, " %s %.2f", kinds[k], (double)(int)(t - t0) / khz * 1e3);
+        }
+        if (any) fprintf(stderr, "%s us\n", line);
+      }
+      fprintf(stderr, "  epilogue %.2f -> %.2f us\n", (double)(int)(tr[7 * 64] - t0) / khz * 1e3,
+              (double)(int)(tr[7 * 64 + 1] - t0) / khz * 1e3);
+      std::vector<double> d;
+      for (int c = 0; c < ctas; c++)
+        d.push_back((double)(tr[BG_TRACE_CTA + 2 * c + 1] - tr[BG_TRACE_CTA + 2 * c]) / khz * 1e3);
+      std::sort(d.begin(), d.end());
+      fprintf(stderr, "  CTA durations: min %.2f median %.2f max %.2f us over %d CTAs\n", d.front(), d[d.size() / 2], d.back(), ctas);
+    }
     if (iters > 1 && ms) {
       cudaEvent_t a, b;
       LS_CUDA(cudaEventCreate(&a));

@@ -18,7 +18,12 @@
 // of 32 x 32 -> 64-bit products, the bits above 2^130 folded back times 5 (2^130 = 5 mod p).
 // Integer arithmetic mod p is exact and associative, so the split into segments does not change
 // the tag.
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <algorithm>
+#include <cerrno>
 #include <cstring>
 #include <vector>
 
@@ -450,6 +455,128 @@ int aead_host(bool seal, const uint8_t* key, const uint8_t* nonce12, bool indexe
     cudaEventDestroy(e1);
   }
   return bad == big ? -1 : bad - 1;
+}
+
+size_t seal_model_file(const std::string& src, const std::string& out, const uint8_t* key, const uint8_t* nonce_prefix,
+                       size_t layer_chunk, size_t embed_chunk_rows) {
+  if (layer_chunk == 0 || embed_chunk_rows == 0) LS_THROW(LS_ERR_ARG, "chunk sizes must be positive");
+  // the plaintext: every layer block, the embedding table, the final norm (src/seal.rs:726-827)
+  std::string config_text, data_path;
+  Config cfg;
+  LayerLayout layout;
+  std::vector<uint64_t> layer_start;
+  uint64_t embed_start = 0, norm_start = 0;
+  struct stat st;
+  if (::stat(src.c_str(), &st) == 0 && S_ISDIR(st.st_mode)) {
+    const SafetensorsModel m = SafetensorsModel::open(src);
+    config_text = m.config_text, data_path = m.file, cfg = m.cfg, layout = m.layout, layer_start = m.layer_start;
+    embed_start = m.embed_start, norm_start = m.norm_start;
+  } else {
+    const LsqFile q = LsqFile::open(src);
+    config_text = q.config_text, data_path = q.path, cfg = q.cfg, layout = q.layout;
+    for (size_t l = 0; l < cfg.layers; l++) layer_start.push_back(q.data_start + l * layout.total);
+    embed_start = q.embed_start, norm_start = q.norm_start;
+  }
+  const size_t rb = cfg.embed_row_bytes(), norm_bytes = cfg.hidden * 2;
+  const std::string header = sealed_header_json(config_text, layout, layer_chunk, embed_chunk_rows, norm_bytes);
+  std::vector<uint8_t> frame(kSealFrame);
+  std::memcpy(frame.data(), "LSS1", 4);
+  const uint32_t ver = 1, hl = (uint32_t)header.size();
+  std::memcpy(frame.data() + 4, &ver, 4);
+  std::memcpy(frame.data() + 8, nonce_prefix, 8);
+  std::memcpy(frame.data() + 16, &hl, 4);
+  frame.insert(frame.end(), header.begin(), header.end());
+  const size_t lc = (layout.total + layer_chunk - 1) / layer_chunk, ec = (cfg.vocab + embed_chunk_rows - 1) / embed_chunk_rows;
+  const size_t n_chunks = cfg.layers * lc + ec + 1;
+  std::vector<uint8_t> tags(16 * n_chunks, 0);
+
+  const int in = ::open(data_path.c_str(), O_RDONLY);
+  if (in < 0) LS_THROW(LS_ERR_IO, data_path + ": cannot open");
+  const int fo = ::open(out.c_str(), O_WRONLY | O_CREAT | O_EXCL, 0644);
+  if (fo < 0) {
+    ::close(in);
+    LS_THROW(LS_ERR_IO, out + ": " + std::strerror(errno));
+  }
+  struct Files {
+    int a, b;
+    ~Files() {
+      ::close(a);
+      ::close(b);
+    }
+  } files{in, fo};
+  auto write_all = [&](const uint8_t* p, size_t n, uint64_t off) {
+    size_t done = 0;
+    while (done < n) {
+      const ssize_t w = ::pwrite(fo, p + done, n - done, (off_t)(off + done));
+      if (w < 0 && errno == EINTR) continue;
+      if (w <= 0) LS_THROW(LS_ERR_IO, out + ": write failed");
+      done += (size_t)w;
+    }
+  };
+  write_all(frame.data(), frame.size(), 0);
+  write_all(tags.data(), tags.size(), frame.size());
+  uint64_t wpos = frame.size() + tags.size();
+
+  // one section at a time through one host and one device buffer: a layer block, up to 16 chunks of
+  // table rows, the norm
+  const size_t erows = embed_chunk_rows * 16;
+  const size_t buf_bytes = std::max({layout.total, std::min(erows, cfg.vocab) * rb, norm_bytes});
+  std::vector<uint8_t> hbuf(buf_bytes);
+  uint8_t *dbuf = nullptr, *daad = nullptr;
+  uint32_t* dkey = nullptr;
+  AeadChunk* dch = nullptr;
+  void* scr = nullptr;
+  const size_t max_ch = std::max<size_t>({lc, 16, 1});
+  const size_t scr_bytes = std::max({aead_scratch_bytes((int)max_ch, layer_chunk, (uint32_t)frame.size()),
+                                     aead_scratch_bytes((int)max_ch, embed_chunk_rows * rb, (uint32_t)frame.size()),
+                                     aead_scratch_bytes(1, norm_bytes, (uint32_t)frame.size())});
+  LS_CUDA(cudaMalloc(&dbuf, buf_bytes));
+  LS_CUDA(cudaMalloc(&daad, frame.size()));
+  LS_CUDA(cudaMalloc(&dkey, 32));
+  LS_CUDA(cudaMalloc(&dch, max_ch * sizeof(AeadChunk)));
+  LS_CUDA(cudaMalloc(&scr, scr_bytes));
+  struct Dev {
+    void* p[5];
+    ~Dev() {
+      cudaDeviceSynchronize();
+      for (void* q : p) cudaFree(q);
+    }
+  } dev{{dbuf, daad, dkey, dch, scr}};
+  LS_CUDA(cudaMemcpy(daad, frame.data(), frame.size(), cudaMemcpyHostToDevice));
+  LS_CUDA(cudaMemcpy(dkey, key, 32, cudaMemcpyHostToDevice));
+  // seals n plaintext bytes read at file offset `off` as chunks first.. of clen bytes
+  auto seal_section = [&](uint64_t off, size_t n, size_t first, size_t clen) {
+    pread_all(in, hbuf.data(), n, off);
+    const size_t nch = (n + clen - 1) / clen;
+    std::vector<AeadChunk> ch(nch);
+    for (size_t i = 0; i < nch; i++) {
+      AeadChunk& c = ch[i];
+      c = AeadChunk{};
+      c.data = dbuf + i * clen;
+      c.len = std::min<uint64_t>(clen, n - i * clen);
+      std::memcpy(c.nonce, nonce_prefix, 8);
+      c.nonce[2] = (uint32_t)(first + i);
+      c.tail = (uint32_t)(first + i);
+      c.tail_len = 4;
+    }
+    LS_CUDA(cudaMemcpy(dbuf, hbuf.data(), n, cudaMemcpyHostToDevice));
+    LS_CUDA(cudaMemcpy(dch, ch.data(), nch * sizeof(AeadChunk), cudaMemcpyHostToDevice));
+    launch_aead(dch, (int)nch, clen, daad, (uint32_t)frame.size(), dkey, true, scr, scr_bytes, nullptr, 0);
+    LS_CUDA(cudaMemcpy(hbuf.data(), dbuf, n, cudaMemcpyDeviceToHost));
+    LS_CUDA(cudaMemcpy(ch.data(), dch, nch * sizeof(AeadChunk), cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < nch; i++) std::memcpy(&tags[16 * (first + i)], ch[i].tag, 16);
+    write_all(hbuf.data(), n, wpos);
+    wpos += n;
+  };
+  for (size_t l = 0; l < cfg.layers; l++) seal_section(layer_start[l], layout.total, l * lc, layer_chunk);
+  for (size_t first = 0; first < cfg.vocab; first += erows) {
+    const size_t rows = std::min(erows, cfg.vocab - first);
+    seal_section(embed_start + first * rb, rows * rb, cfg.layers * lc + first / embed_chunk_rows, embed_chunk_rows * rb);
+  }
+  seal_section(norm_start, norm_bytes, n_chunks - 1, norm_bytes);
+  write_all(tags.data(), tags.size(), frame.size());
+  if (::fsync(fo) != 0) LS_THROW(LS_ERR_IO, out + ": fsync failed");
+  return n_chunks;
 }
 
 }  // namespace ls

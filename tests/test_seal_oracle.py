@@ -32,3 +32,41 @@ def test_oracle_reproduces_the_tags_for_many_lengths():
     for n, tag in SV.VECTORS["many_lengths"]:
         out = aead.encrypt(SV.NONCE, SV.plaintext(n), SV.aad(n))
         assert out[-16:].hex() == tag, n
+
+
+def test_oracle_sealed_file_opens_to_the_source_bytes_and_refuses_changes(tmp_path):
+    # the CPU restatement of the sealed format (oracle/seal.py) round-trips a quantized and a bf16
+    # model, and a wrong key or a swapped pair of layer chunks fails (tests/pipeline.rs:61-166)
+    import os
+
+    import pytest
+
+    import fixtures as F
+    from oracle import oracle as O
+    from oracle import seal as OS
+
+    d = str(tmp_path)
+    F.write_tiny_model(d, 1)
+    lsq = os.path.join(d, "m.lsq")
+    O.quantize_model(d, lsq, (4, 32), (4, 32), clip=True)
+    for src in [lsq, d]:
+        out = os.path.join(d, "m.sealed" if src == lsq else "b.sealed")
+        n = OS.seal_model(src, out, bytes([7] * 32), b"abcdefgh", 1500, 64)
+        s = OS.source(src)
+        raw = open(s["path"], "rb").read()
+        want = b"".join(raw[st:st + s["layer_bytes"]] for st in s["starts"])
+        want += raw[s["embed_start"]:s["embed_start"] + s["embed_bytes"]] + raw[s["norm_start"]:s["norm_start"] + s["norm_bytes"]]
+        got = OS.open_sealed(out, bytes([7] * 32))
+        assert got["plain"] == want and got["header"]["layer_chunk"] == 1500
+        assert os.path.getsize(out) == 20 + int.from_bytes(open(out, "rb").read()[16:20], "little") + 16 * n + len(want)
+        with pytest.raises(Exception):
+            OS.open_sealed(out, bytes([8] * 32))
+    # swapped layer blocks (equal sizes) do not authenticate
+    buf = bytearray(open(os.path.join(d, "m.sealed"), "rb").read())
+    s = OS.source(lsq)
+    lb = s["layer_bytes"]
+    base = len(buf) - (len(s["starts"]) * lb + s["embed_bytes"] + s["norm_bytes"])
+    buf[base:base + lb], buf[base + lb:base + 2 * lb] = buf[base + lb:base + 2 * lb], buf[base:base + lb]
+    open(os.path.join(d, "s.sealed"), "wb").write(bytes(buf))
+    with pytest.raises(Exception):
+        OS.open_sealed(os.path.join(d, "s.sealed"), bytes([7] * 32))
