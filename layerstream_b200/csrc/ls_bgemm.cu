@@ -8,17 +8,18 @@
 //           group's activations (f16, already in the B-operand layout, one contiguous block) into a
 //           ring of shared-memory stages (full / empty mbarriers)
 //   warps 0-7 two warpgroups taking alternate K blocks, one weight row per thread: dequantise the
-//           block ((q - 8) * s or q * s, f16) into one of four A buffers in tensor memory
-//           (tcgen05.st), dequantising the next block while the store of this one completes
+//           block ((q - 8) * s or q * s, f16; int8 as exact hi + lo parts) into one of the A buffers
+//           in tensor memory (four for int4, two for int8's double width; tcgen05.st),
+//           dequantising the next block while the store of this one completes
 //   warps 9-10 one thread each issues tcgen05.mma for alternate stages (A = weights in tensor
 //           memory, B = activations in shared memory, N = the token group, f32 accumulator of its own
-//           in tensor memory), then commits the stage and the A buffer back to their producers; two
-//           issuers keep the tensor pipe fed for small groups, their two accumulators are summed in
-//           the epilogue. Large groups (whose MMAs are long) take one issuer and one accumulator,
-//           which leaves tensor memory for four A buffers: two per warpgroup, so a warpgroup
-//           dequantises and stores its next block while the MMAs of its last one run
-//   epilogue warps 0-3 read D (tcgen05.ld; thread = weight row) and store, add the residual, add
-//           the bias, apply SwiGLU into the next GEMM's f16 operand, or take per-token argmax parts.
+//           in tensor memory), then commits the stage and the A buffer back to their producers; one
+//           issuer's commits and waits overlap the other's MMAs, and the two accumulators are summed
+//           in the epilogue (plan options: one issuer with four int8 buffers, or the two issuers
+//           splitting the tokens of one accumulator; both measured slower on config 4's shapes)
+//   epilogue warps 0-7 read D (tcgen05.ld; thread = weight row, warpgroup = half of the tokens) and
+//           store, add the residual, add the bias, apply SwiGLU into the next GEMM's f16 operand,
+//           or take per-token argmax parts.
 // Each weight tile is dequantised once per pass for all tokens of the group. Small matrices split
 // K over CTAs; the last CTA of a tile sums the slices in order. Every wait is bounded: on a timeout
 // the kernel records the error and returns after releasing tensor memory.
@@ -59,8 +60,8 @@ constexpr int BG_MAX_N = 192;  // two accumulators of N columns next to the A bu
 
 namespace {
 
-// The four epilogue warps only (the producer and issuer warps may have left).
-__device__ __forceinline__ void deq_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// The eight epilogue (dequantising) warps only (the producer and issuer warps may have left).
+__device__ __forceinline__ void deq_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 }  // namespace
 
@@ -84,6 +85,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
   using SH = BgShape<BITS, G>;
   constexpr int KB = SH::KB, NS = SH::NS, CPB = SH::CPB, ACOLS = SH::ACOLS, HCOLS = SH::HCOLS;
   const int ABUF = p.abuf, NISS = p.niss;  // A buffers (2 or 4), issuers (1 or 2)
+  const bool NSPLIT = p.n0 > 0;  // issuers split the tokens (each takes every K block) instead of the K blocks
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t full[BG_MAX_STAGES], empty[BG_MAX_STAGES], bar_a[4], bar_af[4], bar_d, bar_fin[BG_NISS];
   __shared__ uint32_t s_tmem;
@@ -110,10 +112,10 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
       tc::mbar_init(&full[s], 1);
-      tc::mbar_init(&empty[s], 1);
+      tc::mbar_init(&empty[s], NSPLIT ? 2 : 1);
     }
     for (int b = 0; b < ABUF; b++) {
-      tc::mbar_init(&bar_a[b], 1);
+      tc::mbar_init(&bar_a[b], NSPLIT ? 2 : 1);
       tc::mbar_init(&bar_af[b], BG_DEQ_WARPS);
     }
     tc::mbar_init(&bar_d, NISS);
@@ -177,10 +179,14 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
   } else if (warp >= BG_ISSUER && warp < BG_ISSUER + NISS) {
     if (lane == 0) {
       const int ig = warp - BG_ISSUER;
-      const uint32_t idesc = tc::idesc_f16(N);
-      const uint32_t dacc = d_col + ig * N;
+      // token split: issuer ig runs tokens [ig n0, ...) of every K block into its columns of the one
+      // accumulator; K split: alternate stages into an accumulator of its own
+      const int ncols = NSPLIT ? (ig == 0 ? p.n0 : N - p.n0) : N;
+      const uint32_t idesc = tc::idesc_f16(ncols);
+      const uint32_t dacc = d_col + (NSPLIT ? ig * p.n0 : ig * N);
+      const uint32_t xoff = NSPLIT ? (uint32_t)(ig * p.n0) * 16u : 0u;  // the first of its tokens' 16-byte rows
       bool first = true;
-      for (int st_i = ig; st_i < nst && !failed; st_i += NISS) {
+      for (int st_i = NSPLIT ? 0 : ig; st_i < nst && !failed; st_i += NSPLIT ? 1 : NISS) {
         const int s = st_i % S;
         if (!tc::mbar_wait_fast(&full[s], (st_i / S) & 1, &s_abort)) {
           failed = true;
@@ -199,7 +205,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
           const uint32_t xa = tc::su32(smem + (size_t)s * STAGE + W_ST + S_ST) + (uint32_t)j * X_KB;
 #pragma unroll
           for (int jj = 0; jj < KB / 16; jj++) {
-            const uint64_t bd = tc::sdesc(xa + jj * 2u * N * 16u, (uint32_t)N * 16u, 128u);
+            const uint64_t bd = tc::sdesc(xa + xoff + jj * 2u * N * 16u, (uint32_t)N * 16u, 128u);
             tc::mma_f16_ts(dacc, tmem + b * ACOLS + jj * 8, bd, idesc, (!first || jj > 0) ? 1u : 0u);
             if constexpr (ACOLS > HCOLS) tc::mma_f16_ts(dacc, tmem + b * ACOLS + HCOLS + jj * 8, bd, idesc, 1u);
           }
@@ -263,10 +269,11 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
       for (int q = 0; q < ACOLS; q++) acur[q] = anext[q];
     }
     failed = __any_sync(0xffffffffu, failed);
-    if (wg == 1) {
-      // the epilogue belongs to warpgroup 0; a failure here shows up there as a missing commit
-    } else {
-    // ---- epilogue (the four warps agree on failure before their named barriers) ----
+    {
+    // ---- epilogue: both warpgroups, warpgroup wg taking tokens [n_lo, n_hi) of every row (the
+    // eight warps agree on failure before their named barriers) ----
+    const int nh = (N / 16 + 1) / 2 * 16;
+    const int n_lo = wg ? nh : 0, n_hi = wg ? N : nh;
     if (!failed && !tc::mbar_wait_fast(&bar_d, 0, &s_abort)) failed = true;
     failed = __any_sync(0xffffffffu, failed);
     if (failed && lane == 0) s_epi_fail = 1;
@@ -277,32 +284,35 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
       // columns [16 n16, 16 n16 + 16) of this thread's row: the issuers' accumulators summed in order
       auto acc_load = [&](int n16, float* v) {
         uint32_t u[16];
+        if (!NSPLIT && NISS > 1 && nst > 1) {  // both accumulators' loads in flight before one wait
+          uint32_t* u2 = reinterpret_cast<uint32_t*>(v);
+          tc::ld16(d_col + lane_base + n16 * 16, u);
+          tc::ld16(d_col + N + lane_base + n16 * 16, u2);
+          tc::wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; e++) v[e] = __uint_as_float(u[e]) + __uint_as_float(u2[e]);
+          return;
+        }
         tc::ld16(d_col + lane_base + n16 * 16, u);
         tc::wait_ld();
 #pragma unroll
         for (int e = 0; e < 16; e++) v[e] = __uint_as_float(u[e]);
-        if (NISS > 1 && nst > 1) {
-          tc::ld16(d_col + N + lane_base + n16 * 16, u);
-          tc::wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; e++) v[e] += __uint_as_float(u[e]);
-        }
       };
-      const int t32 = t128 * 4 + warp;
+      const int t32 = t128 * 4 + wq;
       const bool row_valid = t32 < tiles32;
       const int r = t32 * 32 + lane;
       if (p.ks > 1) {
         // this slice's accumulators; the last slice's CTA sums them all (after the teardown)
         float* part = g.partial + (((size_t)t128 * p.ngroups + grp) * p.ks + ks) * (size_t)N * 128;
-        for (int n16 = 0; n16 < N / 16; n16++) {
+        for (int n16 = n_lo / 16; n16 < n_hi / 16; n16++) {
           float v[16];
           acc_load(n16, v);
 #pragma unroll
-          for (int e = 0; e < 16; e++) part[(size_t)(n16 * 16 + e) * 128 + warp * 32 + lane] = v[e];
+          for (int e = 0; e < 16; e++) part[(size_t)(n16 * 16 + e) * 128 + wq * 32 + lane] = v[e];
         }
       }
       if (p.ks == 1) {
-        for (int n16 = 0; n16 < N / 16; n16++) {
+        for (int n16 = n_lo / 16; n16 < n_hi / 16; n16++) {
           if (n16 * 16 >= Mloc) break;
           float v16[16];
           acc_load(n16, v16);
@@ -317,8 +327,8 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
               uint32_t bi = (uint32_t)(r + g.row_offset);
               warp_argmax(bv, bi);
               if (lane == 0) {
-                s_bv[warp][n] = bv;
-                s_bi[warp][n] = bi;
+                s_bv[wq][n] = bv;
+                s_bi[wq][n] = bi;
               }
             } else if (g.epi == EPI_SWIGLU_H) {
               const float u = __shfl_down_sync(0xffffffffu, v, 16);
@@ -336,7 +346,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
         }
         if (g.epi == EPI_ARGMAX) {
           deq_sync();
-          for (int n = threadIdx.x; n < Mloc; n += BG_DEQ_WARPS * 32) {
+          for (int n = threadIdx.x; n < Mloc; n += 2 * BG_DEQ_WARPS * 32) {
             float bv = s_bv[0][n];
             uint32_t bi = s_bi[0][n];
             for (int w = 1; w < BG_DEQ_WARPS; w++)
@@ -351,7 +361,7 @@ __global__ void __launch_bounds__(BG_THREADS, BG_MIN_BLOCKS)
     } else {
       failed = true;
     }
-    }  // warpgroup 0
+    }  // epilogue
   }
 
   // ---- release tensor memory (also on the error path) ----
@@ -519,6 +529,24 @@ BgemmPlan bgemm_plan(const QMat& w, int M, int num_sms, bool argmax) {
   p.niss = issuers;
   p.abuf = (issuers == 1 || aw <= 32) ? 4 : 2;
   p.tmem_cols = p.abuf * aw + p.niss * p.N <= 256 ? 256 : 512;
+  // Opt-in (LS_BGEMM_NSPLIT = the smallest N that splits; default 0 = never): the two issuers split
+  // the tokens (multiples of 16) of one N-column accumulator, each issuing every K block's MMAs,
+  // which leaves tensor memory for four A buffers. Measured slower than the K split on config 4's
+  // gate/up (N = 160: 45.9 against 40.4 us): both issuers then pay their per-block commit and wait
+  // overhead at the same time, while alternating K blocks overlaps one's overhead with the other's
+  // MMAs.
+  static const int nsplit_min = [] {
+    const char* e = getenv("LS_BGEMM_NSPLIT");
+    return e ? atoi(e) : 0;
+  }();
+  if (issuers == 2 && nsplit_min > 0 && p.N >= std::max(32, nsplit_min)) {
+    const int n0 = (p.N / 2 + 15) / 16 * 16;
+    if (p.N - n0 >= 16 && 4 * aw + p.N <= 512) {
+      p.n0 = n0;
+      p.abuf = 4;
+      p.tmem_cols = 4 * aw + p.N <= 256 ? 256 : 512;
+    }
+  }
   // stages of kstage K blocks (~24 KB each, within the slice); two CTAs per SM when tensor memory
   // allows it: keep the ring near 96 KB, else up to ~200 KB
   const uint32_t per_kb = 4u * CPB * 512u + 4u * NS * 64u + (uint32_t)p.N * KB * 2u;
@@ -528,7 +556,7 @@ BgemmPlan bgemm_plan(const QMat& w, int M, int num_sms, bool argmax) {
   // blocks i and i + ABUF (consecutive uses of a buffer) must belong to the same issuer, which
   // waits for the buffer's mbarrier phases in order (a parity wait two phases ahead would read
   // the stale phase as complete). That holds when kstage divides ABUF / 2 (one issuer: always).
-  if (p.niss == 2)
+  if (p.niss == 2 && p.n0 == 0)
     while ((p.abuf / 2) % p.kstage) p.kstage--;
   const uint32_t st = per_kb * p.kstage;
   const uint32_t budget = p.tmem_cols == 256 ? 96u * 1024 : 200u * 1024;
@@ -578,8 +606,9 @@ void launch_bgemm(const BgemmLaunch& g, const BgemmPlan& p, cudaStream_t s) {
   if (p.N % 16 || p.N > BG_MAX_N || p.ngroups * p.N < g.M) LS_THROW(-1, "batched GEMM plan does not cover the tokens");
   if (p.stages < 2 || p.stages > BG_MAX_STAGES || p.kstage < 1) LS_THROW(-1, "batched GEMM plan: bad stage count");
   if ((p.abuf != 2 && p.abuf != 4) || (p.niss != 1 && p.niss != 2) ||
-      p.abuf * (tc_kb(g.w.bits, g.w.group) / 2 * tc_parts(g.w.bits)) + p.niss * p.N > p.tmem_cols ||
-      (p.niss == 2 && (p.abuf / 2) % p.kstage))
+      p.abuf * (tc_kb(g.w.bits, g.w.group) / 2 * tc_parts(g.w.bits)) + (p.n0 ? 1 : p.niss) * p.N > p.tmem_cols ||
+      (p.niss == 2 && p.n0 == 0 && (p.abuf / 2) % p.kstage) ||
+      (p.n0 && (p.niss != 2 || p.n0 % 16 || (p.N - p.n0) < 16 || (p.N - p.n0) % 16)))
     LS_THROW(-1, "batched GEMM plan: bad tensor-memory split");
   {
     int N = 0, ng = 0;

@@ -320,6 +320,7 @@ constexpr int BG_TRACE_CTA = 8 * 64;
 struct BgemmPlan {
   int N = 16, ngroups = 1, ks = 1, stages = 2, kstage = 1, tmem_cols = 256;
   int abuf = 4, niss = 2;  // A buffers in tensor memory (2 or 4); MMA issuers, each with its own accumulator (1 or 2)
+  int n0 = 0;              // > 0: the two issuers split the token columns (n0 and N - n0) of one accumulator
   size_t smem = 0, partial_floats = 0, tickets = 0;
 };
 // token groups of a pass of M rows (every GEMM of the pass uses the same): N rows each, ngroups
