@@ -19,10 +19,9 @@
 // warps busy. K/V chunks stream through a two-buffer cp.async ring; the block's own new rows (RoPE
 // on K, both rounded to f16 as the cache stores them) are computed from qkv in place of cache
 // reads and written to the cache by the CTA that owns their chunk. Splits of one (sequence, kv
-// head, row block) leave (m, l, O) partials. Up to AT_LAST_MERGE splits, the last of them merges
-// in split order; more splits (long contexts spread over every SM) are merged by
-// attention_merge_kernel, one CTA per query row, so that the partials (16 KB per split and kv head
-// at M = 9) are read by many SMs instead of one. Every mbarrier wait is bounded: on a timeout the
+// head, row block) leave (m, l, O) partials, merged by attention_merge_kernel, one CTA per query
+// row, so that the partials (16 KB per split and kv head at M = 9) are read by many SMs instead of
+// one; batches of up to AT_LAST_MERGE splits merge in their last CTA, in split order. Every mbarrier wait is bounded: on a timeout the
 // kernel records the error and returns after releasing tensor memory.
 //
 // Scores are exact f16 x f16 products accumulated in f32 (then scaled in f32); q and P are rounded
@@ -38,7 +37,7 @@ namespace ls {
 constexpr int AT_THREADS = 256;  // two warps per tensor-memory lane quadrant
 constexpr int AT_CH = 128;       // positions per chunk: N of the score MMA, K of the value MMA
 constexpr int AT_MAX_SPLITS = 160;  // > 148: a single sequence's two kv heads fill every SM twice
-constexpr int AT_LAST_MERGE = 8;    // splits merged by the last CTA; above, by attention_merge_kernel
+constexpr int AT_LAST_MERGE = 8;    // batches: splits merged by the last CTA; above, by attention_merge_kernel
 // tensor-memory columns: scores [0, 128), P as f16 pairs [128, 192), output [192, 192 + hd)
 constexpr int AT_COL_P = 128, AT_COL_O = 192;
 __host__ __device__ constexpr int at_tmem_cols(int hd) { return AT_COL_O + hd <= 256 ? 256 : 512; }
@@ -96,7 +95,7 @@ __device__ __forceinline__ int at_lane(int r) { return (r & 3) * 32 + (r >> 2); 
 __device__ __forceinline__ int at_row(int lane) { return (lane & 31) * 4 + (lane >> 5); }
 
 template <int HD>
-__global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_kernel(const AttnLaunch a, int nsplit, int nrb) {
+__global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_kernel(const AttnLaunch a, int nsplit, int nrb, int merge_kernel) {
   using SM = AtSmem<HD>;
   constexpr int HALF = HD / 2, C8 = HD / 8, HO = HD / 2;  // HO: output columns of each half
   constexpr uint32_t SBO_HD = C8 * 128u;                  // 8-row group stride of [rows][hd] tiles
@@ -481,7 +480,7 @@ __global__ void __launch_bounds__(AT_THREADS, HD == 64 ? 2 : 1) attention_tc_ker
     __syncthreads();
     mark(11);
   }
-  if (nsplit > AT_LAST_MERGE || !last_cta(a.tickets + unit * nrb + rb, (unsigned)nsplit)) return;
+  if (merge_kernel || !last_cta(a.tickets + unit * nrb + rb, (unsigned)nsplit)) return;
   // weight of every split for every row (shared memory is free: all MMAs have completed)
   // (the weights of a row are computed by the two threads of its lane, each for half the splits:
   // the max and the sum are combined through shared memory in a fixed order)
@@ -655,16 +654,20 @@ static void launch_att_tc_t(const AttnLaunch& a, cudaStream_t s) {
     nsplit = std::max(1, std::min(nsplit, a.max_splits));
   else
     while (nsplit > 1 && (size_t)a.nseq * a.kv_heads * nsplit * R * (HD + 2) > a.part_floats) nsplit--;
+  // the splits' merge: a kernel of its own (one CTA per query row) for one sequence whenever there
+  // are splits (measured: 16 against 19-20 us at 4-8 splits with the last-CTA merge), and for batches
+  // above AT_LAST_MERGE splits (their many small units merge cheaply in their last CTA)
+  const int merge_kernel = nsplit > (a.nseq == 1 ? 1 : AT_LAST_MERGE) ? 1 : 0;
   const size_t smem = AtSmem<HD>::kTotal;
   ensure_smem(attention_tc_kernel<HD>, smem);
   const dim3 grid(nsplit, a.kv_heads * nrb, a.nseq);
   if (a.pdl) {
-    launch_pdl(attention_tc_kernel<HD>, grid, dim3(AT_THREADS), smem, s, a, nsplit, nrb);
+    launch_pdl(attention_tc_kernel<HD>, grid, dim3(AT_THREADS), smem, s, a, nsplit, nrb, merge_kernel);
   } else {
-    attention_tc_kernel<HD><<<grid, AT_THREADS, smem, s>>>(a, nsplit, nrb);
+    attention_tc_kernel<HD><<<grid, AT_THREADS, smem, s>>>(a, nsplit, nrb, merge_kernel);
     LS_CUDA(cudaGetLastError());
   }
-  if (nsplit > AT_LAST_MERGE) launch_pdl(attention_merge_kernel<HD>, dim3(R, a.kv_heads, a.nseq), dim3(128), 0, s, a, nsplit);
+  if (merge_kernel) launch_pdl(attention_merge_kernel<HD>, dim3(R, a.kv_heads, a.nseq), dim3(128), 0, s, a, nsplit);
 }
 
 bool attention_tc_supported(const AttnLaunch& a) {
