@@ -249,6 +249,10 @@ int ls_batch_inject_error(LsBatch *b, int code);
 /* on: 0 off, 1 an event pair around every launch class of each pass; also clears the counters */
 int ls_batch_profile_enable(LsBatch *b, int on);
 int ls_batch_profile(const LsBatch *b, LsBatchProfile *out);
+/* *on = 1 when a tensor-parallel batch sums its row-parallel projections through the peers' memory
+ * (every rank on its own GPU, each peer reachable; environment LS_TP_P2P=0 turns it off), 0 when
+ * it uses the NCCL all-reduce or the batch is not tensor-parallel. */
+int ls_batch_tp_peer(const LsBatch *b, int *on);
 
 /* ---- kernel-level entry points (microbenchmarks and parity tests) ---------------------------- */
 
@@ -286,6 +290,21 @@ int ls_attention_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope
 int ls_attention_paged_host(uint64_t heads, uint64_t kv_heads, uint64_t hd, float rope_theta, uint64_t pos0, uint64_t M,
                             const float *qkv, uint16_t *k_pool, uint16_t *v_pool, uint64_t num_pages, uint64_t page,
                             const int32_t *table, float *out, int iters, double *ms);
+
+/* The tensor-parallel reduction kernel of the row-parallel projections (O and down), run on one GPU
+ * as rank `rank` of an emulated world of 2..8 ranks whose partials ys (world x n f32, this rank's own
+ * at [rank]) all sit in this GPU's memory: x_out = x + calls x (ys[0] + ... + ys[world-1]), summed
+ * in rank order as every rank sums them. preset = 1: the peers' ready flags are set before the
+ * launches, so no launch waits; preset = 0: nothing sets them, the kernel's first wait runs out
+ * after wait_ms, *status = 5 and LS_ERR_DEVICE is returned (the bounded-wait path). *ms = device
+ * time per call. K > 0: the fused form the batch uses before every batched GEMM, over n / K rows of
+ * K (K a multiple of 8): after the sum, op_out (n f16 values, row order) = f16(x_out * inv_rms * norm),
+ * inv_rms = 1 / sqrt(mean(x_out^2) + eps) per row (norm NULL: no normalisation). In a
+ * tensor-parallel batch the peers' partials and flags are the other ranks' buffers mapped over
+ * NVLink; the kernel replaces an all-reduce of the projections' partial sums before the residual
+ * adds after O and down (src/model.rs:283-297, on one device in the reference). */
+int ls_tp_reduce_host(const float *x, const float *ys, uint32_t world, uint32_t rank, uint64_t n, int preset, uint32_t wait_ms,
+                      int calls, float *x_out, int *status, double *ms, uint32_t K, const float *norm, float eps, uint16_t *op_out);
 
 /* ChaCha20-Poly1305 (RFC 8439 section 2.8) on the GPU: the cipher of sealed model files
  * (src/seal.rs:340-400, seal_in_place / open_in_place). data: len bytes in host memory. seal = 1:

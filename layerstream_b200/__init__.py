@@ -111,6 +111,7 @@ _SIGS = {
     "ls_batch_report": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "ls_batch_profile_enable": (C.c_int, [C.c_void_p, C.c_int]),
     "ls_batch_profile": (C.c_int, [C.c_void_p, C.POINTER(BatchProfile)]),
+    "ls_batch_tp_peer": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     "ls_attention_host": (C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_double)]),
     "ls_batch_inject_error": (C.c_int, [C.c_void_p, C.c_int]),
@@ -123,6 +124,9 @@ _SIGS = {
     "ls_dequant_rows_host": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p]),
     "ls_aead_host": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64, C.c_uint64,
                                C.c_uint32, C.c_void_p, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
+    "ls_tp_reduce_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint64, C.c_int, C.c_uint32, C.c_int,
+                                    C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_double), C.c_uint32, C.c_void_p, C.c_float,
+                                    C.c_void_p]),
 }
 
 
@@ -348,6 +352,12 @@ class Batch:
         _check(lib().ls_batch_profile(self._h, C.byref(p)))
         return {c: {"launches": p.launches[i], "ms": p.ms[i], "bytes": p.bytes[i]} for i, c in enumerate(BATCH_PROF_CLASSES)}
 
+    def tp_peer(self) -> bool:
+        """True when the tensor-parallel sums go through the peers' memory, False on NCCL."""
+        on = C.c_int()
+        _check(lib().ls_batch_tp_peer(self._h, C.byref(on)))
+        return bool(on.value)
+
     def close(self):
         if getattr(self, "_h", None):
             lib().ls_batch_free(self._h)
@@ -449,6 +459,28 @@ def aead_open(key: bytes, nonce: bytes, aad: bytes, data: bytes, tags, chunk_byt
     _check(lib().ls_aead_host(0, _p(k), _p(nn), _p(a), len(aad), _p(buf), len(data), chunk_bytes, first, _p(t), 1,
                               C.byref(ms), C.byref(bad)))
     return buf.tobytes()
+
+
+def tp_reduce(x, ys, rank: int, preset: bool = True, wait_ms: int = 1000, calls: int = 1, K: int = 0, norm=None,
+              eps: float = 1e-6):
+    """The tensor-parallel reduction kernel on one GPU, as rank `rank` of len(ys) emulated ranks
+    whose partials all sit in this GPU's memory: returns (x + calls * sum(ys), ms per call), and
+    with K > 0 the fused form's f16 operand (rows x K, RMSNorm-ed with norm) as a third item.
+    preset=False leaves the peers' flags unset: the kernel's wait runs out after wait_ms and
+    LayerstreamError (LS_ERR_DEVICE) is raised."""
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    ys = np.ascontiguousarray(ys, np.float32)
+    if ys.ndim != 2 or ys.shape[1] != x.size:
+        raise ValueError("ys must be world x n")
+    out = np.empty_like(x)
+    op = np.zeros(x.size if K else 1, np.uint16)
+    nw = None if norm is None else np.ascontiguousarray(norm, np.float32)
+    st, ms = C.c_int(), C.c_double()
+    _check(lib().ls_tp_reduce_host(_p(x), _p(ys), ys.shape[0], rank, x.size, int(preset), wait_ms, calls, _p(out), C.byref(st),
+                                   C.byref(ms), K, None if nw is None else _p(nw), eps, _p(op)))
+    if K:
+        return out, ms.value, op.view(np.float16).reshape(-1, K)
+    return out, ms.value
 
 
 def _key_bytes(key) -> bytes:

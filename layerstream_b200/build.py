@@ -14,7 +14,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "liblayerstream_b200.so")
 SOURCES = ["ls_pass.cu", "ls_noalloc.cu", "ls_gemv_tc.cu", "ls_attn_tc.cu", "ls_bgemm.cu", "ls_kernels.cu", "ls_model.cu", "ls_format.cpp", "ls_nccl.cpp",
-           "ls_seal.cu"]
+           "ls_seal.cu", "ls_p2p.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

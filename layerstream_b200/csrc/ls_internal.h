@@ -419,6 +419,34 @@ void launch_aead(AeadChunk* d_chunks, int nchunks, uint64_t max_len, const uint8
 int aead_host(bool seal, const uint8_t* key, const uint8_t* nonce12, bool indexed, uint32_t first, const uint8_t* aad,
               uint64_t aad_len, uint8_t* data, uint64_t len, uint64_t chunk_bytes, uint8_t* tags, int iters, double* ms);
 
+// ---- tensor-parallel reduction through peer memory (ls_p2p.cu) ----
+constexpr int kMaxTpWorld = 8;
+struct P2PReduce {
+  int world = 0, rank = 0;
+  const float* peer_y[kMaxTpWorld] = {};    // every rank's partial rows (this rank's own at [rank])
+  unsigned* peer_flags[kMaxTpWorld] = {};   // every rank's ready flags, mapped into this process
+  unsigned* flags = nullptr;   // this rank's [world] ready epochs, by rank
+  unsigned* seq = nullptr;     // reductions this rank has completed
+  unsigned* ticket = nullptr;  // last-CTA election
+  unsigned* arrive = nullptr;  // first-CTA election (who signals ready)
+  int* err = nullptr;          // error word (5: a peer did not answer in time)
+  unsigned long long limit_ns = 0;  // how long one wait may take before it gives up
+};
+// x[i] += sum over the ranks of y_r[off + i], i < n (all ranks in order).
+void launch_p2p_reduce_add(float* x, const P2PReduce& r, size_t off, size_t n, int num_sms, cudaStream_t s);
+// The same over M rows of K, fused with the RMSNorm (norm_bf16 or norm_f32 weights) and f16 packing
+// into the batched GEMM's operand layout, as launch_bt_prep(x, K, M, K, ...) after the add.
+void launch_p2p_reduce_prep(float* x, const P2PReduce& r, size_t off, int M, int K, const uint16_t* norm_bf16, const float* norm_f32,
+                            float eps, uint16_t* out, int num_sms, cudaStream_t s);
+// One process, one GPU: the reduction as rank `rank` of an emulated world whose peers' partials
+// (ys: world x n, this rank's own at [rank]) sit in this GPU's memory. preset: the peers' flags are
+// set before the launches, so no wait happens; otherwise nothing sets them and the first wait runs
+// out after wait_ms. Returns the error word (0 or 5); x_out = x + calls x the sum of ys. K > 0: the
+// fused form over n / K rows of K, op_out = the f16 operand (RMSNorm with norm, or none when NULL)
+// in row order.
+int tp_reduce_host(const float* x, const float* ys, int world, int rank, uint64_t n, bool preset, uint32_t wait_ms, int calls,
+                   float* x_out, double* ms, uint32_t K, const float* norm, float eps, uint16_t* op_out);
+
 // ---- NCCL, loaded at run time (ls_nccl.cpp) ----
 struct NcclApi {
   ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;

@@ -1517,6 +1517,16 @@ struct LsBatch {
   QMat tp_head;  // this rank's vocabulary rows of the tied head (a view into the model's table)
   ncclComm_t comm = nullptr;
   float* ybuf = nullptr;                            // partial sums of row-parallel projections
+  // peer-memory reduction of ybuf over NVLink instead of NCCL (LS_TP_P2P=0 keeps NCCL); ybuf then
+  // holds two buffers of partials, reduction e of a pass writing buffer e mod 2 (a pass makes an even
+  // number of reductions, so the alternation carries across passes and captured graphs)
+  bool p2p = false;
+  P2PReduce p2pr{};
+  std::vector<void*> ipc_maps;  // the peers' buffers mapped into this process
+  size_t yhalf = 0;             // floats in one buffer of partials
+  int red_idx = 0;              // reductions enqueued in the current pass
+  size_t pending = 0;           // elements of a peer reduction deferred into the next operand prep
+  float* ycur() const { return p2p ? ybuf + (size_t)(red_idx & 1) * yhalf : ybuf; }
   ArgPart *tp_best = nullptr, *tp_all = nullptr;    // per-row best of this rank / of all ranks
   const LayerW& layer(size_t l) const { return tp_world > 1 ? tp_layers[l] : m->layers[l]; }
   size_t kv_layer = 0;  // elements of one layer's page pool (K or V)
@@ -1737,7 +1747,7 @@ struct LsBatch {
     attn = dalloc<float>(max_rows * dm.q_dim);
     hbuf = dalloc<float>(max_rows * I);
     if (tp_world > 1) {
-      ybuf = dalloc<float>(max_rows * h);
+      ybuf = dalloc<float>(2 * max_rows * h);  // two buffers for the peer-memory path
       tp_best = dalloc<ArgPart>(max_rows);
       tp_all = dalloc<ArgPart>((size_t)tp_world * max_rows);
     }
@@ -1786,6 +1796,7 @@ struct LsBatch {
     d_next = dalloc<uint32_t>(B);
     d_pos0 = dalloc<int>(B);
     d_err = dalloc<int>(1);
+    if (tp_world > 1) setup_p2p();
     inv_rms = dalloc<float>(max_rows);
     h_tok = halloc<uint32_t>(max_rows);
     h_m = halloc<uint32_t>(B);
@@ -1802,6 +1813,7 @@ struct LsBatch {
     // a failed tensor-parallel pass may leave collectives in flight on a peer: abort, do not wait
     if (comm) (tp_failed ? nccl_api().comm_abort : nccl_api().comm_destroy)(comm);
     for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
+    for (void* p : ipc_maps) cudaIpcCloseMemHandle(p);
     for (void* p : dev_allocs) cudaFree(p);
     for (void* p : host_allocs) cudaFreeHost(p);
     if (stream) cudaStreamDestroy(stream);
@@ -1896,12 +1908,125 @@ struct LsBatch {
   // One pass over sequences [s0, s0 + ns), M rows each. head_mode 0: advance only; 1: argmax of
   // every row and the acceptance rule per sequence (pos += m + 1); 2: argmax of the last row
   // (prefill of one sequence), pos += M.
-  // Sum of the row-parallel partial y over the ranks, then the residual add into x.
+  // Sum of the row-parallel partials (ycur()) over the ranks, then the residual add into x. On the
+  // peer-memory path with the batched GEMMs the sum is deferred into the next operand prep (prep_x),
+  // which every consumer of x on that path is, or into flush_reduce.
   void reduce_into_x(size_t n) {
+    if (p2p && use_bg) {
+      if (pending) LS_THROW(LS_ERR_ARG, "internal: a peer reduction is already pending");
+      pending = n;
+      return;
+    }
     const int pi = prof_begin(6, (double)n * 4 * 2 * (tp_world - 1) / tp_world);
-    nccl_check(nccl_api().all_reduce(ybuf, ybuf, n, ncclFloat32, ncclSum, comm, stream), "ncclAllReduce");
-    launch_add(x, ybuf, n, stream);
+    if (p2p) {
+      launch_p2p_reduce_add(x, p2pr, (size_t)(red_idx & 1) * yhalf, n, m->num_sms, stream);
+      red_idx++;
+    } else {
+      nccl_check(nccl_api().all_reduce(ybuf, ybuf, n, ncclFloat32, ncclSum, comm, stream), "ncclAllReduce");
+      launch_add(x, ybuf, n, stream);
+    }
     prof_end(pi);
+  }
+  void flush_reduce() {
+    if (!pending) return;
+    const size_t n = pending;
+    pending = 0;
+    const int pi = prof_begin(6, (double)n * 4 * 2 * (tp_world - 1) / tp_world);
+    launch_p2p_reduce_add(x, p2pr, (size_t)(red_idx & 1) * yhalf, n, m->num_sms, stream);
+    red_idx++;
+    prof_end(pi);
+  }
+  // The batched GEMM's operand from `rows` rows of x (stride hidden), RMSNorm-ed with nb or nf; a
+  // pending peer reduction over the same rows is applied first, in the same kernel.
+  void prep_x(int rows, const uint16_t* nb, const float* nf) {
+    const int h = (int)m->cfg.hidden;
+    if (pending && pending == (size_t)rows * h) {
+      pending = 0;
+      const int pi = prof_begin(6, (double)rows * h * 4 * 2 * (tp_world - 1) / tp_world);
+      launch_p2p_reduce_prep(x, p2pr, (size_t)(red_idx & 1) * yhalf, rows, h, nb, nf, m->cfg.eps, bt_a, m->num_sms, stream);
+      red_idx++;
+      prof_end(pi);
+      return;
+    }
+    flush_reduce();
+    launch_bt_prep(x, h, rows, h, nb, nf, m->cfg.eps, bt_a, stream);
+  }
+
+  // Maps every rank's partial buffer and flag words into this process (CUDA IPC; the handles are
+  // exchanged with an NCCL all-gather) when every rank sits on its own GPU and can reach every
+  // peer's memory. A collective call: all ranks take the same decision (the check is reduced over
+  // the ranks). LS_TP_P2P=0 keeps the NCCL all-reduce; LS_TP_WAIT_MS bounds each wait of the
+  // reduction kernels (default 5000).
+  void setup_p2p() {
+    const char* pe = getenv("LS_TP_P2P");
+    if ((pe && std::string(pe) == "0") || tp_world > kMaxTpWorld) return;
+    struct Handles {
+      cudaIpcMemHandle_t y, f;
+      cudaUUID_t uuid;
+    };
+    P2PReduce r;
+    r.world = tp_world;
+    r.rank = tp_rank;
+    r.flags = dalloc<unsigned>((size_t)tp_world);
+    r.seq = dalloc<unsigned>(1);
+    r.ticket = dalloc<unsigned>(1);
+    r.arrive = dalloc<unsigned>(1);
+    r.err = d_err;
+    const char* we = getenv("LS_TP_WAIT_MS");
+    const long long wait_ms = we ? std::max(1ll, std::atoll(we)) : 5000;
+    r.limit_ns = (unsigned long long)wait_ms * 1000000ull;
+    Handles mine{};
+    LS_CUDA(cudaIpcGetMemHandle(&mine.y, ybuf));
+    LS_CUDA(cudaIpcGetMemHandle(&mine.f, r.flags));
+    cudaDeviceProp prop;
+    LS_CUDA(cudaGetDeviceProperties(&prop, m->device));
+    mine.uuid = prop.uuid;
+    auto* dsend = dalloc<uint8_t>(sizeof(Handles));
+    auto* drecv = dalloc<uint8_t>(sizeof(Handles) * tp_world);
+    LS_CUDA(cudaMemcpyAsync(dsend, &mine, sizeof(Handles), cudaMemcpyHostToDevice, stream));
+    nccl_check(nccl_api().all_gather(dsend, drecv, sizeof(Handles), ncclUint8, comm, stream), "ncclAllGather (handles)");
+    std::vector<Handles> all(tp_world);
+    LS_CUDA(cudaMemcpyAsync(all.data(), drecv, sizeof(Handles) * tp_world, cudaMemcpyDeviceToHost, stream));
+    LS_CUDA(cudaStreamSynchronize(stream));
+    // every peer on another GPU that this process sees and can reach: ranks that wait on one
+    // another must never share a GPU
+    int ok = 1, ndev = 0;
+    LS_CUDA(cudaGetDeviceCount(&ndev));
+    for (int p = 0; p < tp_world && ok; p++) {
+      if (p == tp_rank) continue;
+      if (std::memcmp(&all[p].uuid, &mine.uuid, sizeof(cudaUUID_t)) == 0) ok = 0;
+      int local = -1;
+      for (int d = 0; d < ndev && ok; d++) {
+        cudaDeviceProp q;
+        LS_CUDA(cudaGetDeviceProperties(&q, d));
+        if (std::memcmp(&q.uuid, &all[p].uuid, sizeof(cudaUUID_t)) == 0) local = d;
+      }
+      int can = 0;
+      if (local < 0 || cudaDeviceCanAccessPeer(&can, m->device, local) != cudaSuccess || !can) ok = 0;
+    }
+    auto* dok = dalloc<int>(1);
+    LS_CUDA(cudaMemcpyAsync(dok, &ok, 4, cudaMemcpyHostToDevice, stream));
+    nccl_check(nccl_api().all_reduce(dok, dok, 1, ncclInt32, ncclMin, comm, stream), "ncclAllReduce (peer access)");
+    LS_CUDA(cudaMemcpyAsync(&ok, dok, 4, cudaMemcpyDeviceToHost, stream));
+    LS_CUDA(cudaStreamSynchronize(stream));
+    if (!ok) return;
+    for (int p = 0; p < tp_world; p++) {
+      if (p == tp_rank) {
+        r.peer_y[p] = ybuf;
+        r.peer_flags[p] = r.flags;
+        continue;
+      }
+      void *py = nullptr, *pf = nullptr;
+      LS_CUDA(cudaIpcOpenMemHandle(&py, all[p].y, cudaIpcMemLazyEnablePeerAccess));
+      ipc_maps.push_back(py);
+      LS_CUDA(cudaIpcOpenMemHandle(&pf, all[p].f, cudaIpcMemLazyEnablePeerAccess));
+      ipc_maps.push_back(pf);
+      r.peer_y[p] = static_cast<const float*>(py);
+      r.peer_flags[p] = static_cast<unsigned*>(pf);
+    }
+    p2pr = r;
+    p2p = true;
+    yhalf = max_rows * (size_t)m->cfg.hidden;
   }
 
   // A sequence's length; the pages past it go back to the pool.
@@ -1936,6 +2061,8 @@ struct LsBatch {
     // sized for the whole context.
     const bool graphed = graphs_on && !streamed && !prof_on && use_bg && s0 == 0 && ns == B && head_mode == 1 && !inject_err;
     auto enqueue = [&](bool for_graph) {
+    red_idx = 0;
+    pending = 0;
     LS_CUDA(cudaMemcpyAsync(d_tok, h_tok, T * 4, cudaMemcpyHostToDevice, stream));
     LS_CUDA(cudaMemcpyAsync(d_pos0, h_pos0, ns * 4, cudaMemcpyHostToDevice, stream));
     LS_CUDA(cudaMemsetAsync(d_err, 0, 4, stream));
@@ -1955,7 +2082,7 @@ struct LsBatch {
     auto layer_fn = [&](const LayerW& W, size_t l) {
       int pi = prof_begin(0, qbytes(W.qkv) + act * (h + QS));
       if (use_bg) {
-        launch_bt_prep(x, h, (int)T, h, W.in_norm, nullptr, m->cfg.eps, bt_a, stream);
+        prep_x((int)T, W.in_norm, nullptr);
         bg(W.qkv, bt_a, (int)T, EPI_BIAS_STORE, qkv, QS, nullptr, W.qkv_bias);
       } else {
         gemv(W.qkv, x, h, (int)T, EPI_BIAS_STORE, qkv, QS, W.in_norm, W.qkv_bias);
@@ -1998,7 +2125,7 @@ struct LsBatch {
       pi = prof_begin(2, qbytes(W.o) + act * (dm.q_dim + 2 * h));
       if (use_bg) {
         if (tp) {
-          bg(W.o, bt_a, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+          bg(W.o, bt_a, (int)T, EPI_STORE, ycur(), h, nullptr, nullptr);
           prof_end(pi);
           reduce_into_x(T * h);
         } else {
@@ -2006,12 +2133,12 @@ struct LsBatch {
           prof_end(pi);
         }
         pi = prof_begin(3, qbytes(W.gu) + act * (h + I));
-        launch_bt_prep(x, h, (int)T, h, W.post_norm, nullptr, m->cfg.eps, bt_a, stream);
+        prep_x((int)T, W.post_norm, nullptr);
         bg(W.gu, bt_a, (int)T, EPI_SWIGLU_H, nullptr, 0, bt_h, nullptr);
         prof_end(pi);
         pi = prof_begin(4, qbytes(W.down) + act * (I + 2 * h));
         if (tp) {
-          bg(W.down, bt_h, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+          bg(W.down, bt_h, (int)T, EPI_STORE, ycur(), h, nullptr, nullptr);
           prof_end(pi);
           reduce_into_x(T * h);
         } else {
@@ -2021,7 +2148,7 @@ struct LsBatch {
         return;
       }
       if (tp) {  // row-parallel O: this rank's heads' share of every output, summed over the ranks
-        gemv(W.o, attn, dm.q_dim, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+        gemv(W.o, attn, dm.q_dim, (int)T, EPI_STORE, ycur(), h, nullptr, nullptr);
         prof_end(pi);
         reduce_into_x(T * h);
       } else {
@@ -2033,7 +2160,7 @@ struct LsBatch {
       prof_end(pi);
       pi = prof_begin(4, qbytes(W.down) + act * (I + 2 * h));
       if (tp) {  // row-parallel down over this rank's intermediate slice
-        gemv(W.down, hbuf, I, (int)T, EPI_STORE, ybuf, h, nullptr, nullptr);
+        gemv(W.down, hbuf, I, (int)T, EPI_STORE, ycur(), h, nullptr, nullptr);
         prof_end(pi);
         reduce_into_x(T * h);
       } else {
@@ -2050,9 +2177,17 @@ struct LsBatch {
     auto head_fn = [&](const QMat& w, int first, int rows) {
       const int pi = prof_begin(5, qbytes(w) + (double)hM * h * 4);
       if (use_bg) {
-        if (nparts == 0) launch_bt_prep(hx, hstride, hM, h, nullptr, m->final_norm, m->cfg.eps, bt_a, stream);
+        if (nparts == 0) {
+          if (hx == x && hstride == h && hM == (int)T) {
+            prep_x(hM, nullptr, m->final_norm);  // with the last layer's pending reduction, if any
+          } else {
+            flush_reduce();
+            launch_bt_prep(hx, hstride, hM, h, nullptr, m->final_norm, m->cfg.eps, bt_a, stream);
+          }
+        }
         nparts += bg_head(w, first, rows, hM, nparts);
       } else {
+        flush_reduce();
         nparts += head(w, first, rows, hx, hstride, hM, nparts);
       }
       prof_end(pi);
@@ -2066,6 +2201,8 @@ struct LsBatch {
         else head_fn(m->embed, 0, (int)c.vocab);
       }
     }
+    flush_reduce();  // a pass without a head still completes x (and every rank the same reductions)
+    if (red_idx & 1) LS_THROW(LS_ERR_ARG, "internal: a pass made an odd number of peer reductions");
     const ArgPart* fparts = parts;
     int fnparts = nparts;
     if (tp && head_mode) {
@@ -2126,6 +2263,7 @@ struct LsBatch {
     if (*h_err) tp_failed = tp;
     if (*h_err == 1) LS_THROW(LS_ERR_DEVICE, "a tensor-core kernel gave up waiting on an mbarrier (bounded wait)");
     if (*h_err == 4) LS_THROW(LS_ERR_DEVICE, "a pass reported an injected error (test hook)");
+    if (*h_err == 5) LS_THROW(LS_ERR_DEVICE, "a peer rank did not answer the tensor-parallel reduction in time (bounded wait)");
     if (*h_err) LS_THROW(LS_ERR_DEVICE, "a kernel rejected a token id outside the vocabulary");
     for (size_t i = 0; i < ns; i++) set_pos(s0 + i, pos[s0 + i] + (head_mode == 1 ? h_m[i] + 1 : (uint64_t)M));
   }
@@ -2689,6 +2827,19 @@ int ls_aead_host(int seal, const uint8_t* key, const uint8_t* nonce, const uint8
   });
 }
 
+int ls_tp_reduce_host(const float* x, const float* ys, uint32_t world, uint32_t rank, uint64_t n, int preset, uint32_t wait_ms,
+                      int calls, float* x_out, int* status, double* ms, uint32_t K, const float* norm, float eps, uint16_t* op_out) {
+  return guard([&] {
+    NEED(x);
+    NEED(ys);
+    NEED(x_out);
+    const int e = tp_reduce_host(x, ys, (int)world, (int)rank, n, preset != 0, wait_ms, calls, x_out, ms, K, norm, eps, op_out);
+    if (status) *status = e;
+    if (e == 5) LS_THROW(LS_ERR_DEVICE, "a peer rank did not answer the tensor-parallel reduction in time (bounded wait)");
+    if (e) LS_THROW(LS_ERR_DEVICE, "peer reduction: error " + std::to_string(e));
+  });
+}
+
 int ls_qgemv_rows_noalloc(int bits, int group, const uint8_t* rows_dev, uint64_t rows, uint64_t cols, const float* x_dev,
                           uint64_t M, float* y_dev, void* stream) {
   return guard([&] { qgemv_rows_noalloc(bits, group, rows_dev, rows, cols, x_dev, M, y_dev, reinterpret_cast<cudaStream_t>(stream)); });
@@ -2828,6 +2979,14 @@ int ls_batch_profile(const LsBatch* b, LsBatchProfile* out) {
     NEED(b);
     NEED(out);
     *out = b->prof;
+  });
+}
+
+int ls_batch_tp_peer(const LsBatch* b, int* on) {
+  return guard([&] {
+    NEED(b);
+    NEED(on);
+    *on = b->p2p ? 1 : 0;
   });
 }
 

@@ -1,8 +1,9 @@
 """Tensor-parallel batch (config 5b) on two GPUs against the CPU path (needs 2 B200s).
 
 Each rank holds its q heads (and their kv head), half of the intermediate dimension and half of
-the vocabulary; O and down are summed over the ranks (NCCL all-reduce) and the LM head's per-rank
-first maxima are gathered. Every rank must emit the same tokens, and they must match the CPU path
+the vocabulary; O and down are summed over the ranks (by default through the peers' memory over
+NVLink, with LS_TP_P2P=0 by the NCCL all-reduce) and the LM head's per-rank first maxima are
+gathered. Every rank must emit the same tokens, and they must match the CPU path
 wherever the top-2 logit margin exceeds the north-star tolerance.
 """
 import os
@@ -19,7 +20,8 @@ TOL = 2e-2
 WORLD = 2
 
 
-def _rank(rank, world, path, uid_q, out_q, prompts, max_new, k):
+def _rank(rank, world, path, uid_q, out_q, prompts, max_new, k, peer):
+    os.environ["LS_TP_P2P"] = "1" if peer else "0"
     import torch
 
     import layerstream_b200 as ls
@@ -34,6 +36,8 @@ def _rank(rank, world, path, uid_q, out_q, prompts, max_new, k):
     try:
         m = ls.Model(path, device=rank, max_ctx=64)
         b = ls.Batch(m, len(prompts), max_ctx=64, max_block=k + 1, tp=(rank, world, uid))
+        if b.tp_peer() != peer:
+            raise AssertionError(f"peer reduction {'off' if peer else 'on'} against LS_TP_P2P")
         got, st = b.spec(np.array(prompts, np.uint32), max_new, k)
         out_q.put((rank, got, None))
     except Exception as e:  # reported to the parent, which fails the test
@@ -53,14 +57,36 @@ def _cpu_tokens(path, prompt, n):
     return toks, margins
 
 
+def _run_tp(path, prompts, max_new, k, peer):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    uid_q, out_q = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, WORLD, path, uid_q, out_q, prompts, max_new, k, peer)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(WORLD):
+            r, got, err = out_q.get(timeout=600)
+            res[r] = (got, err)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    for r in range(WORLD):
+        assert res[r][1] is None, res[r][1]
+    assert res[0][0] == res[1][0]  # every rank emits the same tokens
+    return res[0][0]
+
+
 def test_two_rank_tensor_parallel_batch_matches_the_cpu_path():
     import torch
-    import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < WORLD:
         pytest.skip("needs 2 GPUs")
     from layerstream_b200 import synth
-    import layerstream_b200 as ls
 
     synth.SHAPES["tp-test"] = dict(hidden_size=2048, num_attention_heads=16, num_key_value_heads=2,
                                    intermediate_size=256, num_hidden_layers=2, vocab_size=1000, rope_theta=1e6,
@@ -71,21 +97,11 @@ def test_two_rank_tensor_parallel_batch_matches_the_cpu_path():
     O.quantize_model(d, path, (4, 32), (4, 32), clip=True)
     prompts = [[(11 * i + 17 * s + 3) % 1000 for i in range(10)] for s in range(4)]
     max_new, k = 12, 4
-    ctx = mp.get_context("spawn")
-    uid_q, out_q = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, WORLD, path, uid_q, out_q, prompts, max_new, k)) for r in range(WORLD)]
-    for p in procs:
-        p.start()
-    res = {}
-    for _ in range(WORLD):
-        r, got, err = out_q.get(timeout=600)
-        res[r] = (got, err)
-    for p in procs:
-        p.join(timeout=120)
-    for r in range(WORLD):
-        assert res[r][1] is None, res[r][1]
-    assert res[0][0] == res[1][0]  # every rank emits the same tokens
-    for pr, g in zip(prompts, res[0][0]):
+    peer = _run_tp(path, prompts, max_new, k, True)
+    nccl = _run_tp(path, prompts, max_new, k, False)
+    # two ranks: the peer sum y0 + y1 and the fused norm equal NCCL's sum and the separate prep
+    assert peer == nccl
+    for pr, g in zip(prompts, peer):
         toks, margins = _cpu_tokens(path, pr, max_new)
         for i, (t, mg) in enumerate(zip(toks, margins)):
             if mg <= TOL:
