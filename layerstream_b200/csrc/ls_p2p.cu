@@ -140,6 +140,8 @@ __global__ void __launch_bounds__(256) p2p_reduce_add_kernel(float* __restrict__
 // then out[t] = f16(x[t] * inv_rms(x[t]) * w). Launched with programmatic dependent launch: the
 // partials are the previous kernel's output. The squares are summed in the same order as
 // bt_prep_kernel (128 threads, float4 steps), so the result equals reduce-then-prep bit for bit.
+constexpr int PREP_ITEMS = 4;  // float4s of a row per thread and step: K = 2048 in one step
+
 __global__ void __launch_bounds__(128) p2p_reduce_prep_kernel(float* __restrict__ x, P2PReduce r, size_t off, int M, int K, int N,
                                                               int rows, const uint16_t* __restrict__ nb, const float* __restrict__ nf,
                                                               float eps, uint16_t* __restrict__ out) {
@@ -155,17 +157,56 @@ __global__ void __launch_bounds__(128) p2p_reduce_prep_kernel(float* __restrict_
     float* xr = x + (size_t)t * K;
     float ss = 0.f;
     if (live) {
-      for (int c4 = threadIdx.x; c4 < K / 4; c4 += blockDim.x) {
-        float4 v = reinterpret_cast<float4*>(xr)[c4];
-        if (ok) {
-          const float4 acc = rank_sum4(r, off, (size_t)t * (K / 4) + c4);
-          v.x += acc.x;
-          v.y += acc.y;
-          v.z += acc.z;
-          v.w += acc.w;
-          reinterpret_cast<float4*>(xr)[c4] = v;
+      // PREP_ITEMS float4s per thread at a time, every rank's loads of them issued before any sum
+      // (a remote load costs about a microsecond; issued one after another they would add up)
+      const int n4 = K / 4;
+      const float4* yrow = nullptr;
+      for (int base = 0; base < n4; base += PREP_ITEMS * 128) {
+        float4 v[PREP_ITEMS], acc[PREP_ITEMS];
+#pragma unroll
+        for (int j = 0; j < PREP_ITEMS; j++) {
+          const int c4 = base + j * 128 + (int)threadIdx.x;
+          if (c4 < n4) v[j] = reinterpret_cast<const float4*>(xr)[c4];
         }
-        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        if (ok) {
+#pragma unroll 2
+          for (int p = 0; p < r.world; p++) {
+            yrow = reinterpret_cast<const float4*>(r.peer_y[p] + off) + (size_t)t * n4;
+            float4 y[PREP_ITEMS];
+#pragma unroll
+            for (int j = 0; j < PREP_ITEMS; j++) {
+              const int c4 = base + j * 128 + (int)threadIdx.x;
+              if (c4 < n4) y[j] = (p == r.rank) ? yrow[c4] : __ldcv(yrow + c4);
+            }
+#pragma unroll
+            for (int j = 0; j < PREP_ITEMS; j++) {
+              if (p == 0) {
+                acc[j] = y[j];
+              } else {
+                acc[j].x += y[j].x;
+                acc[j].y += y[j].y;
+                acc[j].z += y[j].z;
+                acc[j].w += y[j].w;
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < PREP_ITEMS; j++) {
+            const int c4 = base + j * 128 + (int)threadIdx.x;
+            if (c4 < n4) {
+              v[j].x += acc[j].x;
+              v[j].y += acc[j].y;
+              v[j].z += acc[j].z;
+              v[j].w += acc[j].w;
+              reinterpret_cast<float4*>(xr)[c4] = v[j];
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < PREP_ITEMS; j++) {
+          const int c4 = base + j * 128 + (int)threadIdx.x;
+          if (c4 < n4) ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
+        }
       }
     }
     ss = warp_sum(ss);
