@@ -625,6 +625,7 @@ def batch_bench(args, cfg):
         _, nxt = batch.verify(np.array([[t] * (k + 1) for t in nxt], np.uint32))
     prof = batch.profile()
     batch.profile_enable(0)
+    peer = tp and world > 1 and batch.tp_peer()
     barrier(dist)
     # tensor parallel: every rank emits the same tokens, counted once
     ms_max, tok_all = reduce_over_ranks(dist, decode_s * 1e3, tokens if (rank == 0 or not tp) else 0, device="cuda")
@@ -691,11 +692,16 @@ def batch_bench(args, cfg):
             "workload": (f"config5b: 3b Qwen2 random-init int4 g32, {B} sequences, {plen}-token prompts, {max_new} new "
                          f"tokens, k={k}, lookup drafter, resident, tensor parallel over {world} GPU(s)"),
             "config": 5, "global_batch": B, "batch_per_gpu": B,
-            "parallelism": (f"tp{world}: column-parallel QKV (q heads) and gate/up, row-parallel O and down with NCCL "
-                            "all-reduce, vocabulary-parallel head with an all-gather of per-rank maxima")
+            "parallelism": (f"tp{world}: column-parallel QKV (q heads) and gate/up, row-parallel O and down summed "
+                            + ("through the peers' memory over NVLink (reduction fused into the next RMSNorm/operand kernel)"
+                               if peer else "with NCCL all-reduce")
+                            + ", vocabulary-parallel head with an all-gather of per-rank maxima")
                            if world > 1 else "single GPU (tp1)"})
         line["dtype"] = dtype_note(4)
-        line["gpu_launches"] = int(passes * (7 * info.layers + 5 if world > 1 else 5 * info.layers + 4))
+        # per layer: prep, QKV, attention, O, prep, gate/up, down (+ 2 adds with NCCL); per pass:
+        # embedding, head prep, head, row maxima, acceptance
+        per_layer = 7 if (world == 1 or peer) else 9
+        line["gpu_launches"] = int(passes * (per_layer * info.layers + 5))
         line["roofline"] = {"bound": "hbm", "kernel": "tensor-parallel verify pass on the busiest rank (separate kernels)",
                             "achieved": (w_r + kv_r) / pass_s / 1e9, "peak": peak, "unit": "GB/s",
                             "frac": (w_r + kv_r) / pass_s / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
