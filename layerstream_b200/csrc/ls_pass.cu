@@ -55,7 +55,11 @@ __device__ __forceinline__ long long to_fix(float v) {
   v = fminf(fmaxf(v, -1.0e9f), 1.0e9f);
   return __float2ll_rn(v * 4294967296.0f);
 }
-__device__ __forceinline__ float from_fix(long long f) { return (float)((double)f * 2.3283064365386962890625e-10); }
+// One conversion, rounded to nearest, then an exact power-of-two scale: for |f| < 2^53 (|value| <
+// 2^21) the same float as converting through double and scaling there, without the two
+// double-precision operations per value (the activations' staging runs tens of thousands of these
+// per phase).
+__device__ __forceinline__ float from_fix(long long f) { return __ll2float_rn(f) * 2.3283064365386962890625e-10f; }
 __device__ __forceinline__ void fix_add(long long* p, float v) {
   atomicAdd(reinterpret_cast<unsigned long long*>(p), (unsigned long long)to_fix(v));
 }
@@ -755,11 +759,12 @@ __device__ __forceinline__ void stage_attention(const PassArgs& a, uint8_t* xb, 
 #pragma unroll
     for (int s2 = 0; s2 < kMaxSlots; s2++)
       v[s2] = s2 < S ? __ldcg(reinterpret_cast<const float2*>(base + s2 * sstride + 2 + d)) : make_float2(0.f, 0.f);
+    // the slot (m, l) pair of lane `lane` < S, loaded with the values (one L2 round trip); used
+    // when the warp's 32 pairs lie in one head
+    const float2 ml = lane < S ? __ldcg(reinterpret_cast<const float2*>(base + lane * sstride)) : make_float2(-CUDART_INF_F, 0.f);
     const bool one_head = __all_sync(0xffffffffu, hh == __shfl_sync(0xffffffffu, hh, 0));
     float ox = 0.f, oy = 0.f;
     if (one_head) {
-      const float2 ml = lane < S ? __ldcg(reinterpret_cast<const float2*>(base + lane * sstride))
-                                 : make_float2(-CUDART_INF_F, 0.f);
       const float mx = warp_max(ml.x);
       const float e = (ml.x == -CUDART_INF_F) ? 0.f : __expf(ml.x - mx);
       const float w = __fdividef(e, warp_sum(ml.y * e));
