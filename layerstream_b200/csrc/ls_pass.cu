@@ -538,15 +538,16 @@ __device__ __forceinline__ int att_row_pos(int slot, int S, int ti, int cpt, int
 }
 
 // Starts the cp.async copies of the cached K/V rows (positions < pos0, which no phase of this pass
-// writes) of tile 0 of item (hh, slot) into the K/V region. Every thread commits one group.
-__device__ void attention_prefetch(const PassArgs& a, int pos0, int l, int hh, int slot, uint8_t* kvb) {
+// writes) of tile 0 of item (hh, slot) into the K/V region, spread over `nthr` threads (this one
+// is `tid`); each of them commits one group, which attention_item's wait covers.
+__device__ void attention_prefetch(const PassArgs& a, int pos0, int l, int hh, int slot, uint8_t* kvb, int tid, int nthr) {
   const int HD = a.hd, HPK = pk_hpk(HD), AT = pk_at(HD), c8 = HD / 8;
   const int g = hh / (a.heads / a.kv_heads);
   const uint16_t* kc = a.kc + (size_t)l * a.kv_layer;
   const uint16_t* vc = a.vc + (size_t)l * a.kv_layer;
   __half* Ks = reinterpret_cast<__half*>(kvb);
   __half* Vs = Ks + AT * HPK;
-  for (int i = threadIdx.x; i < AT * c8; i += PK_THREADS) {
+  for (int i = tid; i < AT * c8; i += nthr) {
     const int r = i / c8, ch = i - r * c8;
     const int p = att_row_pos(slot, a.slots, 0, AT / PK_CHUNK, r);
     if (p < pos0) {
@@ -1018,8 +1019,11 @@ __global__ void __launch_bounds__(PK_THREADS, 1) pass_kernel(const PassArgs a) {
     // ---- QKV: RMSNorm(x) -> q|k|v sums (+ bias once) ----
     if (xs) rms_rows(a.x, T, h, a.eps, s_inv, xs, wn, W.in_norm, nullptr);
     else rms_stats(a.x, T, h, a.eps, s_inv, xb, rms_bytes);
-    // cached K/V rows of this CTA's first attention item: they stream in during the QKV phase
-    if ((int)blockIdx.x < a.heads * a.slots) attention_prefetch(a, pos0, l, blockIdx.x / a.slots, blockIdx.x % a.slots, kvb);
+    // cached K/V rows of this CTA's first attention item: they stream in during the QKV phase,
+    // issued by the producer warp's lanes 1..31 (idle while lane 0 streams the weights), so their
+    // page-table lookups stay off the phase's critical path
+    if ((int)blockIdx.x < a.heads * a.slots && warp == PK_PRODUCER && lane != 0)
+      attention_prefetch(a, pos0, l, blockIdx.x / a.slots, blockIdx.x % a.slots, kvb, lane - 1, 31);
     gemv_phase(
         W.qkv, a.ks_qkv,
         [&](int col0, int ncol, uint32_t sbo) {
