@@ -2010,19 +2010,37 @@ struct LsBatch {
     LS_CUDA(cudaMemcpyAsync(&ok, dok, 4, cudaMemcpyDeviceToHost, stream));
     LS_CUDA(cudaStreamSynchronize(stream));
     if (!ok) return;
-    for (int p = 0; p < tp_world; p++) {
+    // map the peers' buffers; a failure on any rank sends every rank back to NCCL (a rank that
+    // threw here alone would leave the others waiting for it in their first pass)
+    for (int p = 0; p < tp_world && ok; p++) {
       if (p == tp_rank) {
         r.peer_y[p] = ybuf;
         r.peer_flags[p] = r.flags;
         continue;
       }
       void *py = nullptr, *pf = nullptr;
-      LS_CUDA(cudaIpcOpenMemHandle(&py, all[p].y, cudaIpcMemLazyEnablePeerAccess));
+      if (cudaIpcOpenMemHandle(&py, all[p].y, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        ok = 0;
+        break;
+      }
       ipc_maps.push_back(py);
-      LS_CUDA(cudaIpcOpenMemHandle(&pf, all[p].f, cudaIpcMemLazyEnablePeerAccess));
+      if (cudaIpcOpenMemHandle(&pf, all[p].f, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        ok = 0;
+        break;
+      }
       ipc_maps.push_back(pf);
       r.peer_y[p] = static_cast<const float*>(py);
       r.peer_flags[p] = static_cast<unsigned*>(pf);
+    }
+    if (!ok) cudaGetLastError();  // clear the failed open's error
+    LS_CUDA(cudaMemcpyAsync(dok, &ok, 4, cudaMemcpyHostToDevice, stream));
+    nccl_check(nccl_api().all_reduce(dok, dok, 1, ncclInt32, ncclMin, comm, stream), "ncclAllReduce (peer mappings)");
+    LS_CUDA(cudaMemcpyAsync(&ok, dok, 4, cudaMemcpyDeviceToHost, stream));
+    LS_CUDA(cudaStreamSynchronize(stream));
+    if (!ok) {
+      for (void* q : ipc_maps) cudaIpcCloseMemHandle(q);
+      ipc_maps.clear();
+      return;
     }
     p2pr = r;
     p2p = true;
