@@ -147,7 +147,7 @@ def _rank_fail(rank, world, path, uid_q, out_q, inject_rank):
 
 
 def test_an_error_on_one_rank_stops_every_rank_on_the_same_pass():
-    # ADVICE: one rank's device error must not leave its peer waiting in the next collective
+    # one rank's device error must not leave its peer waiting in the next collective
     import torch
     import torch.multiprocessing as mp
 
